@@ -1,0 +1,309 @@
+"""MoE-layer throughput on B200: tokens/s of rusty-engine's moe_layer_forward hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3b1|c3b8|c3b32|c3b64|c5]
+                    [--impl ours|reference]
+
+One step = one forward of the whole MoE layer (router, dispatch, gate/up+SwiGLU, down,
+combine) over one batch of synthetic tokens already resident in HBM; the timed region is
+bracketed by a barrier + synchronize, each step by CUDA events on the forward's stream, and
+L2 is flushed (a 256 MiB write) between steps outside the events.  ``e2e`` is the same metric
+through the public host-buffer entry point (pinned host x in, host out, copies inside).
+``--impl reference`` times the CPU restatement of rusty-engine's pooled path (oracle/, all
+host threads) on the same config.  N > 1 runs one rank per GPU (torchrun); each rank serves
+its own batch (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (builder, tokens, workload label)
+    "c1": ("config_c1", 128, "c1 moe_layer_forward H1024 E16 k4 I512 Q4_0, 128 tokens"),
+    "c2": ("config_c2", 4096, "c2 Qwen3-30B-A3B MoE layer prefill H2048 E128 k8 I768 Q4_K/Q6_K, 4096 tokens"),
+    "c3b1": ("config_c2", 1, "c3 Qwen3-30B-A3B MoE layer decode batch 1"),
+    "c3b8": ("config_c2", 8, "c3 Qwen3-30B-A3B MoE layer decode batch 8"),
+    "c3b32": ("config_c2", 32, "c3 Qwen3-30B-A3B MoE layer decode batch 32"),
+    "c3b64": ("config_c2", 64, "c3 Qwen3-30B-A3B MoE layer decode batch 64"),
+    "c5": ("config_c5", 8192, "c5 Qwen3-235B-A22B MoE layer H4096 E128 k8 I1536 Q4_K/Q6_K, 8192 tokens"),
+}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(cfg_name, lw, x, budget_s=15.0):
+    """The oracle's pooled restatement of rusty-engine's CPU path on all host threads."""
+    from oracle import oracle as O
+
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    O.pool_init(threads)
+    T = x.shape[0]
+    probe = min(T, 256)
+    t0 = time.perf_counter()
+    O.moe_layer_pooled(x[:probe], lw)
+    dt = time.perf_counter() - t0
+    n = probe
+    if T > probe and dt * T / probe < budget_s:
+        t0 = time.perf_counter()
+        O.moe_layer_pooled(x, lw)
+        dt, n = time.perf_counter() - t0, T
+    return {"value": n / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} of {T} tokens of the {cfg_name} layer, one pooled pass ({dt:.2f} s)"}
+
+
+def algorithmic(lw, T, ids=None):
+    """FLOPs of the expert products and the bytes a layer must read (weights of distinct
+    experts touched + router + activations in/out)."""
+    from rusty_engine_b200.synth import row_bytes
+
+    H, I, E, k = lw.H, lw.I, lw.E, lw.k
+    flops_gateup = 4.0 * T * k * H * I
+    flops_down = 2.0 * T * k * H * I
+    per_expert = 2 * I * row_bytes(lw.gate_exps.ggml_type, H) + H * row_bytes(lw.down_exps.ggml_type, I)
+    touched = E if ids is None else len(np.unique(ids))
+    bytes_total = touched * per_expert + E * H * 4 + 2 * T * H * 4
+    gu_bytes = touched * 2 * I * row_bytes(lw.gate_exps.ggml_type, H)
+    return flops_gateup, flops_down, bytes_total, gu_bytes, touched
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    from rusty_engine_b200 import synth
+
+    builder, T, label = CONFIGS[args.config]
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        lw = getattr(synth, builder)()
+        x = synth.activations(T, lw.H)
+        from oracle import oracle as O
+
+        threads = len(os.sched_getaffinity(0))
+        O.pool_init(threads)
+        sample = min(T, 512)
+        for _ in range(max(1, min(args.warmup, 1))):
+            O.moe_layer_pooled(x[:sample], lw)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            O.moe_layer_pooled(x[:sample], lw)
+            times.append(time.perf_counter() - t0)
+        ms = statistics.mean(times) * 1e3
+        val = sample / (ms / 1e3)
+        print(json.dumps({
+            "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": val, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": label, "tokens": T, "sample_tokens": sample},
+            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"{sample} of {T} tokens per step (C restatement of the pooled AVX2 path)"},
+            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist_mod
+
+        dist = dist_mod
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    from rusty_engine_b200 import _lib
+    from rusty_engine_b200.moe import MoELayer
+
+    lw = getattr(synth, builder)()
+    x_np = synth.activations(T, lw.H, seed=1 + rank)
+    layer = MoELayer(lw, device=local)
+    x = torch.from_numpy(x_np).cuda()
+    out = torch.empty_like(x)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        layer.forward(x, out)
+    layer.forward(x, out, flags=_lib.FLAG_ROUTING_OUT)
+    torch.cuda.synchronize()
+    ids, _ = layer.routing(T)
+
+    sampler = ClockSampler(local)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stage = np.zeros(4)
+    barrier()
+    sampler.start()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        starts[i].record(stream)
+        layer.forward(x, out, flags=_lib.FLAG_STAGE_TIMING)
+        ends[i].record(stream)
+        stage += np.array(layer.stage_ms())
+    barrier()
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = statistics.mean(step_ms)
+    stage /= args.steps
+    if dist is not None:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # end to end: pinned host x in, host out, copies inside the timed call
+    xh = torch.from_numpy(x_np).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    import ctypes as C
+
+    L = _lib.load()
+    sptr = C.c_void_p(stream.cuda_stream)
+    for _ in range(2):
+        _lib.check(L.rmoe_layer_forward(layer._h, xh.data_ptr(), T, oh.data_ptr(), sptr, _lib.FLAG_HOST_IO))
+    barrier()
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_times = []
+    for _ in range(e2e_steps):
+        flush.fill_(0.0)
+        torch.cuda.synchronize()
+        s0 = time.perf_counter()
+        _lib.check(L.rmoe_layer_forward(layer._h, xh.data_ptr(), T, oh.data_ptr(), sptr, _lib.FLAG_HOST_IO))
+        e2e_times.append(time.perf_counter() - s0)
+    e2e_s = statistics.mean(e2e_times)
+    if dist is not None:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    if rank == 0:
+        peaks = load_peaks()
+        fg, fd, nbytes, gu_bytes, touched = algorithmic(lw, T, ids)
+        value = T * world / (ms / 1e3)
+        # dominant kernel by measured time share
+        names = ["route_dispatch", "gateup", "down", "combine"]
+        dom = int(np.argmax(stage))
+        if T >= 256:
+            work = {1: fg, 2: fd}.get(dom, fg)
+            ach = work / (stage[dom] / 1e3) / 1e12
+            roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                    "frac": ach / peaks["bf16_tflops"], "traffic": None, "kernel": names[dom],
+                    "peak_src": peaks["src"] + " burst bf16"}
+        else:
+            gb = (gu_bytes if dom == 1 else nbytes - gu_bytes) / (stage[dom] / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": gb, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": gb / peaks["hbm_gbs"], "traffic": None, "kernel": names[dom],
+                    "peak_src": peaks["src"] + " copy"}
+        line = {
+            "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16-mma/f32-router", "data": "synthetic",
+            "config": {"workload": label, "tokens_per_gpu": T, "experts_touched": int(touched),
+                       "l2": "flushed between steps (256 MiB write outside the events)",
+                       "parallelism": f"replicas{world}" if world > 1 else "single"},
+            "stage_ms": {n: float(v) for n, v in zip(names, stage)},
+            "roofline": roof,
+            "e2e": {"value": T * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * lw.H * 4,
+                    "d2h_bytes_per_step": T * lw.H * 4},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.config, lw, x_np)
+        print(json.dumps(line), flush=True)
+    layer.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

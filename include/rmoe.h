@@ -1,0 +1,166 @@
+/*
+ * rmoe.h -- C ABI of the B200-native MoE-layer path (router, dispatch, grouped expert
+ * products over GGUF-quantized experts, combine).
+ *
+ * Every entry point is plain C: pointers, sizes and status codes; no CUDA, NCCL or torch
+ * types cross this boundary (streams are passed as void*, NCCL ids as 128 raw bytes).
+ * Citations are to the rusty-engine function each entry point replaces.
+ *
+ * Error convention: every call returns rmoe_status; RMOE_OK is 0.  On failure the
+ * thread-local message is in rmoe_last_error() (rusty-engine returns
+ * EngineError{message}, src/core.rs:56-68, where it does not panic).  No call aborts or
+ * unwinds across the boundary.  Calls on one handle are stream-ordered; use one handle
+ * per device per host thread.
+ */
+#ifndef RMOE_H
+#define RMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RMOE_API __attribute__((visibility("default")))
+#else
+#define RMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    RMOE_OK = 0,
+    RMOE_ERR_INVALID = 1,     /* bad argument: shape, type, size, null pointer, k > E ... */
+    RMOE_ERR_UNSUPPORTED = 2, /* a ggml type / shape this build has no kernel for */
+    RMOE_ERR_CUDA = 3,        /* a CUDA runtime error (message carries cudaGetErrorString) */
+    RMOE_ERR_NCCL = 4,        /* an NCCL error in the expert-parallel path */
+    RMOE_ERR_DEVICE = 5,      /* a device-side check failed (kernel status word) */
+    RMOE_ERR_OOM = 6
+} rmoe_status;
+
+/* Gate (src/moe.rs:19-25): softmax over the chosen k logits, or per-expert sigmoid
+ * renormalised over the chosen k. */
+typedef enum { RMOE_GATE_SOFTMAX = 0, RMOE_GATE_SIGMOID = 1 } rmoe_gate;
+
+/* ggml type codes accepted for expert tensors (src/quant.rs:75-88). */
+enum {
+    RMOE_GGML_F32 = 0, RMOE_GGML_F16 = 1, RMOE_GGML_Q4_0 = 2, RMOE_GGML_Q5_0 = 6,
+    RMOE_GGML_Q8_0 = 8, RMOE_GGML_Q4_K = 12, RMOE_GGML_Q5_K = 13, RMOE_GGML_Q6_K = 14,
+    RMOE_GGML_BF16 = 30
+};
+
+/* One GGUF tensor as it lies in the file (src/gguf.rs:102-124 TensorEntry): type, the raw
+ * bytes (host memory), their length, and the GGUF dims, innermost first.
+ * ffn_{gate,up}_exps: dims {H, I, E}; ffn_down_exps: {I, H, E} (src/model.rs:366-391).
+ * Shared-expert tensors (*_shexp): {H, I} / {I, H}. */
+typedef struct {
+    uint32_t ggml_type;
+    const void* data;
+    uint64_t nbytes;
+    uint64_t dims[3];
+} rmoe_tensor;
+
+/* Layer description: the arguments of moe_layer_forward (src/moe.rs:360-368) with the
+ * experts given as GGUF tensors instead of f32 ExpertWeights. */
+typedef struct {
+    uint32_t hidden;      /* H (dmodel) */
+    uint32_t inter;       /* I (expert SwiGLU width) */
+    uint32_t n_experts;   /* E */
+    uint32_t top_k;       /* k (RouterConfig.top_k) */
+    uint32_t gate;        /* rmoe_gate (RouterConfig.gate) */
+    const float* router_w;/* ffn_gate_inp, E rows x H f32, host memory */
+    rmoe_tensor gate_exps, up_exps, down_exps;
+    uint32_t has_shared;  /* shared expert added at weight 1 (src/moe.rs:381-386) */
+    rmoe_tensor gate_shexp, up_shexp, down_shexp;
+    int32_t device;       /* CUDA ordinal the handle lives on */
+} rmoe_layer_desc;
+
+typedef struct rmoe_layer rmoe_layer;
+
+/* Forward flags. */
+enum {
+    RMOE_FLAG_HOST_IO = 1u << 0,       /* x / out are host pointers: copied in and out inside
+                                          the call, which then synchronises the stream */
+    RMOE_FLAG_DETERMINISTIC = 1u << 1, /* combine sums expert outputs per token in chosen
+                                          order (the reference order) instead of atomics */
+    RMOE_FLAG_FORCE_SMALL = 1u << 2,   /* always use the small-batch (decode) kernels */
+    RMOE_FLAG_FORCE_LARGE = 1u << 3,   /* always use the large-batch (prefill) kernels */
+    RMOE_FLAG_ROUTING_OUT = 1u << 4,   /* also fill the routing buffers (rmoe_layer_routing) */
+    RMOE_FLAG_STAGE_TIMING = 1u << 5   /* record CUDA events between the pipeline stages
+                                          (read back with rmoe_layer_stage_ms) */
+};
+
+/* Create a layer handle: validates the description on the host, copies router and expert
+ * bytes to HBM once (re-strided into the device layout) and owns that memory.
+ * Replaces building ExpertWeights for moe_layer_forward (src/moe.rs:348-353) and
+ * QMat::from_bytes for the expert tensors (src/qmat.rs:51-58). */
+RMOE_API rmoe_status rmoe_layer_create(const rmoe_layer_desc* desc, rmoe_layer** out);
+
+/* moe_layer_forward (src/moe.rs:360-388) for T tokens at once: out[t] = sum over the top-k
+ * routed experts of weight * down(swiglu(gate x_t, up x_t)) (+ the shared expert).
+ * x: T x H f32, out: T x H f32 (device pointers unless RMOE_FLAG_HOST_IO).  stream is a
+ * cudaStream_t (NULL = legacy default stream).  T = 0 is a no-op. */
+RMOE_API rmoe_status rmoe_layer_forward(rmoe_layer* layer, const float* x, uint32_t T, float* out,
+                               void* stream, uint32_t flags);
+
+/* Routing of the last forward with RMOE_FLAG_ROUTING_OUT: expert ids (T x k, chosen order)
+ * and weights (T x k), copied to host buffers.  Mirrors route() (src/moe.rs:120-125). */
+RMOE_API rmoe_status rmoe_layer_routing(rmoe_layer* layer, uint32_t T, uint32_t* ids, float* weights);
+
+/* Router logits (T x E f32, the exact moe::matvec values) of the last forward that had
+ * RMOE_FLAG_ROUTING_OUT, copied to a host buffer.  A debugging aid with no counterpart in
+ * the reference (its logits never leave moe_layer_forward). */
+RMOE_API rmoe_status rmoe_layer_logits(rmoe_layer* layer, uint32_t T, float* logits);
+
+/* Stage durations of the last forward that had RMOE_FLAG_STAGE_TIMING, in milliseconds,
+ * from CUDA events recorded on the forward's stream: ms[0] route+dispatch, ms[1] gate/up
+ * (+SwiGLU), ms[2] down (+atomic combine), ms[3] deterministic combine (0 if not run).
+ * Synchronises on the last event.  No counterpart in the reference (its RUSTY_PROFILE stage
+ * timers, src/profile.rs:15-89, are the analogue). */
+RMOE_API rmoe_status rmoe_layer_stage_ms(rmoe_layer* layer, float ms[4]);
+
+/* Release the handle and all device memory it owns. */
+RMOE_API void rmoe_layer_destroy(rmoe_layer* layer);
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+RMOE_API const char* rmoe_last_error(void);
+
+/* ---- stand-alone operators (the reference functions the layer is built from) --------- */
+
+/* quant::dequant (src/quant.rs:363-453) on the GPU: n GGUF bytes of type t -> f32.
+ * src/dst are device pointers; dst holds numel(t, nbytes) floats. */
+RMOE_API rmoe_status rmoe_dequant(uint32_t ggml_type, const void* src, uint64_t nbytes, float* dst,
+                         void* stream);
+
+/* QMat::matmul (src/qmat.rs:169-182) on the GPU: W[m x n] (GGUF bytes, host pointer, type t)
+ * times X[rows x n] f32 -> Out[rows x m] f32.  X/Out are device pointers.  rows = 1 is
+ * QMat::matvec (src/qmat.rs:80-82).  Weights are uploaded per call (a convenience path;
+ * the layer handle keeps its weights resident). */
+RMOE_API rmoe_status rmoe_qmat_matmul(uint32_t ggml_type, const void* w_host, uint64_t w_nbytes,
+                             uint32_t m, uint32_t n, const float* x, uint32_t rows, float* out,
+                             void* stream);
+
+/* route() (src/moe.rs:120-125) over T rows of E logits (device pointers): ids/weights are
+ * T x k in chosen order. */
+RMOE_API rmoe_status rmoe_route(const float* logits, uint32_t T, uint32_t E, uint32_t k, uint32_t gate,
+                       uint32_t* ids, float* weights, void* stream);
+
+/* ---- expert parallelism (no counterpart in the reference: its B9 dist-MoE is planned,
+ *      docs/roadmap.md:235-246) ---------------------------------------------------------- */
+
+/* 128-byte NCCL unique id, made on one rank and shared with all ranks out of band. */
+RMOE_API rmoe_status rmoe_ep_unique_id(uint8_t id[128]);
+
+/* Create this rank's shard of an expert-parallel layer: experts are placed contiguously,
+ * E / world_size per rank (rank r holds [r*E/W, (r+1)*E/W)); the router is replicated.
+ * desc carries the FULL tensors (each rank uploads only its slice). */
+RMOE_API rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* desc, int32_t rank, int32_t world_size,
+                                 const uint8_t id[128], rmoe_layer** out);
+
+/* Build info: "sm_100a <git-describe> <kernels...>". */
+RMOE_API const char* rmoe_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RMOE_H */

@@ -1,0 +1,299 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes wrapper over the CPU oracle (``liboracle.so``).
+
+The oracle restates rusty-engine's CPU algorithm for the MoE-layer path (see the header of
+``rmoe_oracle.c`` for the function-by-function citations).  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may import this module; it
+is the checker, never the product.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+F32P = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+F64P = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+U32P = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+U8P = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+
+
+def build() -> str:
+    """Compile liboracle.so from rmoe_oracle.c (gcc; no reference sources involved)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(
+        os.path.join(_HERE, "rmoe_oracle.c")
+    ):
+        build()
+    L = C.CDLL(_LIB_PATH)
+    u64, i64 = C.c_uint64, C.c_int64
+    L.orc_f16_to_f32.argtypes = [C.c_uint16]
+    L.orc_f16_to_f32.restype = C.c_float
+    L.orc_block_info.argtypes = [C.c_uint32, C.POINTER(u64), C.POINTER(u64)]
+    L.orc_block_info.restype = C.c_int
+    L.orc_bytes_for_numel.argtypes = [C.c_uint32, u64, C.POINTER(C.c_int)]
+    L.orc_bytes_for_numel.restype = u64
+    L.orc_dequant.argtypes = [C.c_uint32, U8P, u64, F32P]
+    L.orc_dequant.restype = i64
+    L.orc_last_error.restype = C.c_char_p
+    L.orc_sigmoid.argtypes = [C.c_float]
+    L.orc_sigmoid.restype = C.c_float
+    L.orc_silu.argtypes = [C.c_float]
+    L.orc_silu.restype = C.c_float
+    L.orc_softmax_in_place.argtypes = [F32P, u64]
+    for fn in (L.orc_top_k, L.orc_top_k_sigmoid):
+        fn.argtypes = [F32P, u64, u64, U32P, F32P]
+        fn.restype = u64
+    L.orc_route.argtypes = [F32P, u64, C.c_int, u64, U32P, F32P]
+    L.orc_route.restype = u64
+    L.orc_route_grouped.argtypes = [F32P, F32P, u64, u64, u64, u64, i64, C.c_int, U32P, F32P]
+    L.orc_route_grouped.restype = u64
+    L.orc_matvec.argtypes = [F32P, u64, u64, F32P, F32P]
+    L.orc_expert_ffn.argtypes = [F32P, F32P, F32P, F32P, u64, u64, F32P]
+    L.orc_combine.argtypes = [F32P, F32P, u64, u64, C.c_void_p, F32P]
+    L.orc_moe_layer_forward.argtypes = [
+        F32P, u64, F32P, u64, C.c_void_p, C.c_void_p, C.c_void_p,
+        C.c_void_p, C.c_void_p, C.c_void_p, u64, C.c_int, u64, F32P, U32P, F32P,
+    ]
+    L.orc_moe_layer_q_exact.argtypes = [
+        F32P, u64, u64, u64, u64, u64, C.c_int, F32P,
+        C.c_uint32, U8P, C.c_uint32, U8P, C.c_uint32, U8P,
+        C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p, C.c_uint32, C.c_void_p,
+        F32P, U32P, F32P, F32P, C.c_int,
+    ]
+    L.orc_router_logits.argtypes = [F32P, u64, u64, F32P, u64, F32P, C.c_int]
+    L.orc_route_batch.argtypes = [F32P, u64, u64, C.c_int, u64, U32P, F32P]
+    L.orc_router_logits_f64.argtypes = [F32P, u64, u64, F32P, u64, F64P]
+    L.orc_pool_init.argtypes = [C.c_int]
+    L.orc_pool_init.restype = C.c_int
+    L.orc_qmat_matmul.argtypes = [C.c_uint32, U8P, u64, u64, F32P, u64, F32P]
+    L.orc_moe_layer_pooled.argtypes = [
+        F32P, u64, u64, u64, u64, u64, C.c_int, F32P,
+        C.c_uint32, U8P, C.c_uint32, U8P, C.c_uint32, U8P, F32P,
+    ]
+    _lib = L
+    return L
+
+
+class OracleError(Exception):
+    """Mirrors rusty-engine's EngineError{message} for the dequant dispatch."""
+
+
+def f16_to_f32(h: int) -> float:
+    return lib().orc_f16_to_f32(h)
+
+
+def f16_to_f32_all() -> np.ndarray:
+    """Widen all 65536 binary16 patterns (quant.rs:25-45)."""
+    L = lib()
+    return np.array([L.orc_f16_to_f32(h) for h in range(65536)], dtype=np.float32)
+
+
+def block_info(t: int):
+    e, b = C.c_uint64(), C.c_uint64()
+    if not lib().orc_block_info(t, C.byref(e), C.byref(b)):
+        return None
+    return (e.value, b.value)
+
+
+def bytes_for_numel(t: int, numel: int):
+    ok = C.c_int()
+    v = lib().orc_bytes_for_numel(t, numel, C.byref(ok))
+    return v if ok.value else None
+
+
+def dequant(t: int, data) -> np.ndarray:
+    """quant::dequant (quant.rs:363-453): raises OracleError with the reference message."""
+    data = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8) if not isinstance(data, np.ndarray) else data, dtype=np.uint8)
+    n_max = max(len(data) * 2, 1) * 8
+    out = np.empty(n_max, dtype=np.float32)
+    n = lib().orc_dequant(t, data, len(data), out)
+    if n < 0:
+        raise OracleError(lib().orc_last_error().decode())
+    return out[:n].copy()
+
+
+def sigmoid(x: float) -> float:
+    return lib().orc_sigmoid(x)
+
+
+def silu(x: float) -> float:
+    return lib().orc_silu(x)
+
+
+def softmax(x) -> np.ndarray:
+    a = np.ascontiguousarray(x, dtype=np.float32).copy()
+    lib().orc_softmax_in_place(a, len(a))
+    return a
+
+
+def _routed(fn, scores, k, *extra):
+    s = np.ascontiguousarray(scores, dtype=np.float32)
+    ids = np.zeros(max(len(s), 1), dtype=np.uint32)
+    w = np.zeros(max(len(s), 1), dtype=np.float32)
+    n = fn(s, len(s), *extra, k, ids, w) if extra else fn(s, len(s), k, ids, w)
+    return [(int(ids[i]), float(w[i])) for i in range(n)]
+
+
+def top_k(scores, k):
+    return _routed(lib().orc_top_k, scores, k)
+
+
+def top_k_sigmoid(scores, k):
+    return _routed(lib().orc_top_k_sigmoid, scores, k)
+
+
+def route(logits, gate: int, k: int):
+    s = np.ascontiguousarray(logits, dtype=np.float32)
+    ids = np.zeros(max(len(s), 1), dtype=np.uint32)
+    w = np.zeros(max(len(s), 1), dtype=np.float32)
+    n = lib().orc_route(s, len(s), gate, k, ids, w)
+    return [(int(ids[i]), float(w[i])) for i in range(n)]
+
+
+def route_grouped(logits, bias, n_groups, top_k, top_k_group, noaux):
+    s = np.ascontiguousarray(logits, dtype=np.float32)
+    b = np.ascontiguousarray(bias if len(bias) else [0.0], dtype=np.float32)
+    ids = np.zeros(max(len(s), 1), dtype=np.uint32)
+    w = np.zeros(max(len(s), 1), dtype=np.float32)
+    n = lib().orc_route_grouped(
+        s, b, len(bias), len(s), n_groups, top_k, -1 if top_k_group is None else top_k_group,
+        1 if noaux else 0, ids, w,
+    )
+    return [(int(ids[i]), float(w[i])) for i in range(n)]
+
+
+def matvec(w, m, n, x) -> np.ndarray:
+    out = np.zeros(m, dtype=np.float32)
+    lib().orc_matvec(np.ascontiguousarray(w, dtype=np.float32), m, n, np.ascontiguousarray(x, dtype=np.float32), out)
+    return out
+
+
+def expert_ffn(x, g, u, d, hidden, inter) -> np.ndarray:
+    out = np.zeros(hidden, dtype=np.float32)
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+    lib().orc_expert_ffn(f(x), f(g), f(u), f(d), hidden, inter, out)
+    return out
+
+
+def _ptr_array(arrs):
+    ptrs = (C.c_void_p * len(arrs))()
+    for i, a in enumerate(arrs):
+        ptrs[i] = None if a is None else a.ctypes.data
+    return ptrs
+
+
+def moe_layer_forward(hidden, router_w, n_experts, experts, shared, inter, gate, top_k):
+    """moe_layer_forward (moe.rs:360-388) over f32 ExpertWeights (list of (gate, up, down))."""
+    f = lambda a: np.ascontiguousarray(a, dtype=np.float32)
+    hidden = f(hidden)
+    H = len(hidden)
+    keep = [tuple(f(a) for a in e) for e in experts]
+    gp = _ptr_array([e[0] for e in keep] + [None] * (n_experts - len(keep)))
+    up = _ptr_array([e[1] for e in keep] + [None] * (n_experts - len(keep)))
+    dp = _ptr_array([e[2] for e in keep] + [None] * (n_experts - len(keep)))
+    sh = tuple(f(a) for a in shared) if shared is not None else (None, None, None)
+    out = np.zeros(H, dtype=np.float32)
+    ids = np.zeros(max(n_experts, 1), dtype=np.uint32)
+    w = np.zeros(max(n_experts, 1), dtype=np.float32)
+    lib().orc_moe_layer_forward(
+        hidden, H, f(router_w), n_experts, gp, up, dp,
+        None if sh[0] is None else sh[0].ctypes.data,
+        None if sh[1] is None else sh[1].ctypes.data,
+        None if sh[2] is None else sh[2].ctypes.data,
+        inter, gate, top_k, out, ids, w,
+    )
+    return out
+
+
+def moe_layer_q_exact(x, layer, threads=None):
+    """Exact-f32 quantized layer: returns (out[T,H], ids[T,k], wts[T,k], logits[T,E]).
+
+    ``layer`` is a ``rusty_engine_b200.synth.LayerWeights``-like object exposing H, I, E, k,
+    gate, router_w, and (type, bytes) for gate/up/down (+ optional shared tensors).
+    """
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T = x.shape[0]
+    H, I, E, k = layer.H, layer.I, layer.E, layer.k
+    out = np.zeros((T, H), dtype=np.float32)
+    ids = np.zeros((T, k), dtype=np.uint32)
+    wts = np.zeros((T, k), dtype=np.float32)
+    logits = np.zeros((T, E), dtype=np.float32)
+    sh = layer.shared if getattr(layer, "shared", None) is not None else None
+    threads = threads or os.cpu_count() or 1
+    lib().orc_moe_layer_q_exact(
+        x, T, H, I, E, k, layer.gate, np.ascontiguousarray(layer.router_w, dtype=np.float32),
+        layer.gate_exps.ggml_type, layer.gate_exps.data,
+        layer.up_exps.ggml_type, layer.up_exps.data,
+        layer.down_exps.ggml_type, layer.down_exps.data,
+        sh[0].ggml_type if sh else 0, sh[0].data.ctypes.data if sh else None,
+        sh[1].ggml_type if sh else 0, sh[1].data.ctypes.data if sh else None,
+        sh[2].ggml_type if sh else 0, sh[2].data.ctypes.data if sh else None,
+        out, ids, wts, logits, int(threads),
+    )
+    return out, ids, wts, logits
+
+
+def router_logits(x, router_w, E, threads=None):
+    """moe::matvec logits (bit-exact f32 sequential sums) for every token: [T, E]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T, H = x.shape
+    out = np.zeros((T, E), dtype=np.float32)
+    lib().orc_router_logits(x, T, H, np.ascontiguousarray(router_w, dtype=np.float32), E, out,
+                            int(threads or os.cpu_count() or 1))
+    return out
+
+
+def route_batch(logits, gate, k):
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    T, E = lg.shape
+    k = min(k, E)
+    ids = np.zeros((T, k), dtype=np.uint32)
+    w = np.zeros((T, k), dtype=np.float32)
+    lib().orc_route_batch(lg, T, E, gate, k, ids, w)
+    return ids, w
+
+
+def router_logits_f64(x, router_w, E):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T, H = x.shape
+    out = np.zeros((T, E), dtype=np.float64)
+    lib().orc_router_logits_f64(x, T, H, np.ascontiguousarray(router_w, dtype=np.float32), E, out)
+    return out
+
+
+def pool_init(n: int) -> int:
+    return lib().orc_pool_init(int(n))
+
+
+def qmat_matmul(t, w, m, n, x, rows) -> np.ndarray:
+    out = np.zeros((rows, m), dtype=np.float32)
+    lib().orc_qmat_matmul(t, np.ascontiguousarray(w, dtype=np.uint8), m, n, np.ascontiguousarray(x, dtype=np.float32), rows, out)
+    return out
+
+
+def moe_layer_pooled(x, layer) -> np.ndarray:
+    """Pooled fused baseline (QMat::matmul composition); call pool_init first."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    T = x.shape[0]
+    out = np.zeros((T, layer.H), dtype=np.float32)
+    lib().orc_moe_layer_pooled(
+        x, T, layer.H, layer.I, layer.E, layer.k, layer.gate,
+        np.ascontiguousarray(layer.router_w, dtype=np.float32),
+        layer.gate_exps.ggml_type, layer.gate_exps.data,
+        layer.up_exps.ggml_type, layer.up_exps.data,
+        layer.down_exps.ggml_type, layer.down_exps.data, out,
+    )
+    return out

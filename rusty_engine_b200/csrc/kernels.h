@@ -1,0 +1,78 @@
+// kernels.h -- parameter blocks and launchers shared by the host orchestration (layer.cu)
+// and the kernel translation units.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace rmoe {
+
+static constexpr int MAX_E = 512;  // experts per layer this build supports
+static constexpr int MAX_K = 32;   // top-k this build supports
+
+struct RouteParams {
+    const float* x;         // [T, H] f32
+    const float* router_w;  // [E, H] f32
+    int T, H, E, k, gate, has_shared;
+    __nv_bfloat16* xb;      // [T, H] bf16 copy of x (GEMM B operand)
+    float* logits_out;      // optional [T, E]
+    float* out_zero;        // optional: rows of `out` to zero (atomic combine)
+    int* topk_id;           // [T, k]
+    float* topk_w;          // [T, k]
+    int* local_rank;        // [T, k] scratch
+    int* cta_cnt;           // [ceil(T/32), E] scratch
+    unsigned int* ticket;   // last-CTA counter (0 between launches)
+    int* expert_off;        // [E + 2]
+    int* row_tok;           // [rows] token of each expert-sorted row
+    int* row_slot;          // [rows] slot (k for the shared expert)
+    int* slot_row;          // [T, k] row of each (token, slot)
+    int* n_rows;            // total rows
+    int4* tiles;            // (expert, first row, rows, 0)
+    int* n_tiles;
+    int max_tiles;
+    int tile_rows;          // rows per tile
+    unsigned int* status;   // device status word (DevErr bits)
+};
+
+// Grouped expert products over the expert-sorted rows.
+struct GroupedParams {
+    DevMat gate, up, down;        // routed experts
+    DevMat sgate, sup, sdown;     // shared expert (type < 0 when absent)
+    int H, I, E, k;
+    const __nv_bfloat16* xb;      // [T, H]
+    const int* row_tok;
+    const int* row_slot;
+    const int4* tiles;
+    const int* n_tiles;
+    const float* topk_w;          // [T, k]
+    __nv_bfloat16* h;             // [rows, I] SwiGLU activations
+    float* y;                     // [rows, H] expert outputs (deterministic combine) or null
+    float* out;                   // [T, H] atomic combine target (when y is null)
+    unsigned int* status;
+};
+
+struct CombineParams {
+    const float* y;       // [rows, H]
+    const int* slot_row;  // [T, k]
+    const float* topk_w;  // [T, k]
+    int T, H, k, has_shared, shared_row0;
+    float* out;
+};
+
+size_t route_smem_bytes(int E);
+int route_grid(int T);
+cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s);
+
+// small-batch (mma.sync) grouped kernels; tile_rows = tokens per tile
+int small_tile_rows();
+cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s);
+cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, cudaStream_t s);
+
+cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
+cudaError_t launch_dequant_raw(int type, const void* src, uint64_t nblocks, float* dst, cudaStream_t s);
+cudaError_t launch_route_only(const float* logits, int T, int E, int k, int gate, int* ids, float* w, cudaStream_t s);
+cudaError_t launch_f32_to_bf16(const float* x, __nv_bfloat16* y, uint64_t n, cudaStream_t s);
+
+}  // namespace rmoe

@@ -1,0 +1,530 @@
+// layer.cu -- C ABI (include/rmoe.h): layer handles, host-side validation, load-time
+// re-striding of GGUF expert tensors into the device planes, and the forward pipeline
+//   route+dispatch -> grouped gate/up (+SwiGLU) -> grouped down (+combine)
+// all stream-ordered on the caller's stream.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/rmoe.h"
+#include "kernels.h"
+#include "layer_impl.h"
+
+namespace rmoe {
+
+static thread_local std::string g_err;
+
+rmoe_status fail(rmoe_status s, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return s;
+}
+
+rmoe_status cuda_fail(cudaError_t e, const char* what) {
+    return fail(RMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// (elements, bytes) per block, src/quant.rs:75-88
+bool block_geom(uint32_t t, uint32_t& el, uint32_t& by) {
+    switch (t) {
+        case T_F32: el = 1; by = 4; return true;
+        case T_F16: case T_BF16: el = 1; by = 2; return true;
+        case T_Q4_0: el = 32; by = 18; return true;
+        case T_Q5_0: el = 32; by = 22; return true;
+        case T_Q8_0: el = 32; by = 34; return true;
+        case T_Q4_K: el = 256; by = 144; return true;
+        case T_Q5_K: el = 256; by = 176; return true;
+        case T_Q6_K: el = 256; by = 210; return true;
+        default: return false;
+    }
+}
+
+static const char* type_name(uint32_t t) {
+    switch (t) {
+        case T_F32: return "F32"; case T_F16: return "F16"; case T_BF16: return "BF16";
+        case T_Q4_0: return "Q4_0"; case T_Q5_0: return "Q5_0"; case T_Q8_0: return "Q8_0";
+        case T_Q4_K: return "Q4_K"; case T_Q5_K: return "Q5_K"; case T_Q6_K: return "Q6_K";
+        default: return "?";
+    }
+}
+
+static uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) return (uint16_t)((u >> 16) | 0x40);  // NaN
+    uint32_t r = 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)((u + r) >> 16);
+}
+
+static float f16_to_f32_host(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16, exp = (h >> 10) & 0x1Fu, frac = h & 0x3FFu, bits;
+    if (exp == 0 && frac == 0) bits = sign;
+    else if (exp == 0) {
+        uint32_t e = 113, f = frac;
+        while (!(f & 0x400u)) { f <<= 1; e--; }
+        bits = sign | (e << 23) | ((f & 0x3FFu) << 13);
+    } else if (exp == 0x1F) bits = sign | 0x7F800000u | (frac << 13);
+    else bits = sign | ((exp + 112) << 23) | (frac << 13);
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+DeviceGuard::DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (dev != prev) cudaSetDevice(dev);
+    cur = dev;
+}
+DeviceGuard::~DeviceGuard() {
+    if (cur != prev) cudaSetDevice(prev);
+}
+
+void* Owned::alloc(size_t n) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, n ? n : 16) != cudaSuccess) return nullptr;
+    ptrs.push_back(p);
+    return p;
+}
+Owned::~Owned() {
+    for (void* p : ptrs) cudaFree(p);
+}
+
+// Re-stride `experts` matrices of `rows` x `K` GGUF rows into the device planes and upload.
+rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t experts, const char* name,
+                       Owned& own, DevMat& out) {
+    uint32_t el, by;
+    if (!block_geom(t.ggml_type, el, by)) return fail(RMOE_ERR_UNSUPPORTED, "%s: ggml type %u has no kernel", name, t.ggml_type);
+    if (K % 256 != 0)
+        return fail(RMOE_ERR_UNSUPPORTED, "%s: row width %u is not a multiple of 256 (GPU tile constraint)", name, K);
+    if (!t.data) return fail(RMOE_ERR_INVALID, "%s: null data", name);
+    const uint64_t total_rows = (uint64_t)rows * experts;
+    const uint64_t rb = (uint64_t)K / el * by;
+    if (t.nbytes != rb * total_rows)
+        return fail(RMOE_ERR_INVALID, "%s: %llu bytes, expected %llu for %s [%u x %u x %u]", name,
+                    (unsigned long long)t.nbytes, (unsigned long long)(rb * total_rows), type_name(t.ggml_type), K,
+                    rows, experts);
+    const uint8_t* src = static_cast<const uint8_t*>(t.data);
+    const uint64_t nblk = (uint64_t)K / el;
+    std::vector<uint8_t> mainp;
+    std::vector<uint16_t> dpl;
+    std::vector<uint32_t> aux;
+    out = DevMat{};
+    out.rows = rows;
+    out.K = K;
+    out.dstride = (uint32_t)nblk;
+    switch (t.ggml_type) {
+        case T_Q4_K: case T_Q5_K:
+            out.type = (int)t.ggml_type;
+            out.main_stride = rb;
+            mainp.assign(src, src + t.nbytes);
+            break;
+        case T_Q6_K:
+            out.type = T_Q6_K;
+            out.main_stride = nblk * 208;
+            mainp.resize(total_rows * nblk * 208);
+            dpl.resize(total_rows * nblk);
+            for (uint64_t r = 0; r < total_rows; r++)
+                for (uint64_t b = 0; b < nblk; b++) {
+                    const uint8_t* s = src + r * rb + b * 210;
+                    memcpy(&mainp[(r * nblk + b) * 208], s, 208);
+                    dpl[r * nblk + b] = (uint16_t)(s[208] | (s[209] << 8));
+                }
+            break;
+        case T_Q4_0: case T_Q8_0: {
+            const uint32_t qb = t.ggml_type == T_Q4_0 ? 16 : 32;
+            out.type = (int)t.ggml_type;
+            out.main_stride = nblk * qb;
+            mainp.resize(total_rows * nblk * qb);
+            dpl.resize(total_rows * nblk);
+            for (uint64_t r = 0; r < total_rows; r++)
+                for (uint64_t b = 0; b < nblk; b++) {
+                    const uint8_t* s = src + r * rb + b * by;
+                    memcpy(&mainp[(r * nblk + b) * qb], s + 2, qb);
+                    dpl[r * nblk + b] = (uint16_t)(s[0] | (s[1] << 8));
+                }
+            break;
+        }
+        case T_Q5_0:
+            out.type = T_Q5_0;
+            out.main_stride = nblk * 16;
+            mainp.resize(total_rows * nblk * 16);
+            dpl.resize(total_rows * nblk);
+            aux.resize(total_rows * nblk);
+            for (uint64_t r = 0; r < total_rows; r++)
+                for (uint64_t b = 0; b < nblk; b++) {
+                    const uint8_t* s = src + r * rb + b * 22;
+                    memcpy(&mainp[(r * nblk + b) * 16], s + 6, 16);
+                    dpl[r * nblk + b] = (uint16_t)(s[0] | (s[1] << 8));
+                    aux[r * nblk + b] = (uint32_t)s[2] | ((uint32_t)s[3] << 8) | ((uint32_t)s[4] << 16) | ((uint32_t)s[5] << 24);
+                }
+            break;
+        case T_F32: case T_F16: case T_BF16: {
+            out.type = T_BF16;
+            out.main_stride = (uint64_t)K * 2;
+            mainp.resize(total_rows * K * 2);
+            uint16_t* d = reinterpret_cast<uint16_t*>(mainp.data());
+            const uint64_t n = total_rows * K;
+            for (uint64_t i = 0; i < n; i++) {
+                if (t.ggml_type == T_BF16) d[i] = (uint16_t)(src[2 * i] | (src[2 * i + 1] << 8));
+                else if (t.ggml_type == T_F16) d[i] = f32_to_bf16_rne(f16_to_f32_host((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8))));
+                else { float f; memcpy(&f, src + 4 * i, 4); d[i] = f32_to_bf16_rne(f); }
+            }
+            break;
+        }
+        default:
+            return fail(RMOE_ERR_UNSUPPORTED, "%s: ggml type %u has no kernel", name, t.ggml_type);
+    }
+    void* dm = own.alloc(mainp.size());
+    if (!dm) return fail(RMOE_ERR_OOM, "%s: cudaMalloc(%zu) failed", name, mainp.size());
+    cudaError_t e = cudaMemcpy(dm, mainp.data(), mainp.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, name);
+    out.main = static_cast<const uint8_t*>(dm);
+    if (!dpl.empty()) {
+        void* dd = own.alloc(dpl.size() * 2);
+        if (!dd) return fail(RMOE_ERR_OOM, "%s: cudaMalloc failed", name);
+        if ((e = cudaMemcpy(dd, dpl.data(), dpl.size() * 2, cudaMemcpyHostToDevice)) != cudaSuccess) return cuda_fail(e, name);
+        out.dpl = static_cast<const __half*>(dd);
+    }
+    if (!aux.empty()) {
+        void* da = own.alloc(aux.size() * 4);
+        if (!da) return fail(RMOE_ERR_OOM, "%s: cudaMalloc failed", name);
+        if ((e = cudaMemcpy(da, aux.data(), aux.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return cuda_fail(e, name);
+        out.aux = static_cast<const uint32_t*>(da);
+    }
+    return RMOE_OK;
+}
+
+static rmoe_status check_dims(const rmoe_tensor& t, uint64_t d0, uint64_t d1, uint64_t d2, const char* name) {
+    uint64_t e2 = t.dims[2] ? t.dims[2] : 1;
+    if (t.dims[0] != d0 || t.dims[1] != d1 || e2 != d2)
+        return fail(RMOE_ERR_INVALID, "%s: dims [%llu, %llu, %llu], expected [%llu, %llu, %llu]", name,
+                    (unsigned long long)t.dims[0], (unsigned long long)t.dims[1], (unsigned long long)t.dims[2],
+                    (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2);
+    return RMOE_OK;
+}
+
+rmoe_status validate_desc(const rmoe_layer_desc* d) {
+    if (!d) return fail(RMOE_ERR_INVALID, "null layer description");
+    if (d->hidden == 0 || d->inter == 0 || d->n_experts == 0)
+        return fail(RMOE_ERR_INVALID, "hidden, inter and n_experts must be non-zero");
+    if (d->n_experts > (uint32_t)MAX_E) return fail(RMOE_ERR_UNSUPPORTED, "n_experts %u > %d", d->n_experts, MAX_E);
+    if (d->top_k == 0) return fail(RMOE_ERR_INVALID, "top_k must be >= 1");
+    if (d->top_k > (uint32_t)MAX_K) return fail(RMOE_ERR_UNSUPPORTED, "top_k %u > %d", d->top_k, MAX_K);
+    if (d->gate > 1) return fail(RMOE_ERR_INVALID, "gate %u is not softmax (0) or sigmoid (1)", d->gate);
+    if (!d->router_w) return fail(RMOE_ERR_INVALID, "null router weights");
+    if (d->hidden % 256 || d->inter % 256)
+        return fail(RMOE_ERR_UNSUPPORTED, "hidden %u / inter %u must be multiples of 256", d->hidden, d->inter);
+    rmoe_status s;
+    if ((s = check_dims(d->gate_exps, d->hidden, d->inter, d->n_experts, "ffn_gate_exps"))) return s;
+    if ((s = check_dims(d->up_exps, d->hidden, d->inter, d->n_experts, "ffn_up_exps"))) return s;
+    if ((s = check_dims(d->down_exps, d->inter, d->hidden, d->n_experts, "ffn_down_exps"))) return s;
+    if (d->has_shared) {
+        if ((s = check_dims(d->gate_shexp, d->hidden, d->inter, 1, "ffn_gate_shexp"))) return s;
+        if ((s = check_dims(d->up_shexp, d->hidden, d->inter, 1, "ffn_up_shexp"))) return s;
+        if ((s = check_dims(d->down_shexp, d->inter, d->hidden, 1, "ffn_down_shexp"))) return s;
+    }
+    return RMOE_OK;
+}
+
+static int canon_type(uint32_t t) { return (t == T_F32 || t == T_F16 || t == T_BF16) ? T_BF16 : (int)t; }
+
+rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_count, rmoe_layer* L) {
+    const uint32_t H = d->hidden, I = d->inter;
+    if (canon_type(d->gate_exps.ggml_type) != canon_type(d->up_exps.ggml_type))
+        return fail(RMOE_ERR_UNSUPPORTED, "gate (%s) and up (%s) expert types differ", type_name(d->gate_exps.ggml_type),
+                    type_name(d->up_exps.ggml_type));
+    uint32_t el, by;
+    rmoe_status s;
+    auto slice = [&](const rmoe_tensor& t, uint32_t rows, uint32_t K) {
+        rmoe_tensor u = t;
+        block_geom(t.ggml_type, el, by);
+        uint64_t per = (uint64_t)rows * (K / el) * by;
+        if (t.nbytes == per * d->n_experts) {
+            u.data = static_cast<const uint8_t*>(t.data) + per * e_begin;
+            u.nbytes = per * e_count;
+        }
+        return u;
+    };
+    if ((s = upload_mat(slice(d->gate_exps, I, H), I, H, e_count, "ffn_gate_exps", L->own, L->wg))) return s;
+    if ((s = upload_mat(slice(d->up_exps, I, H), I, H, e_count, "ffn_up_exps", L->own, L->wu))) return s;
+    if ((s = upload_mat(slice(d->down_exps, H, I), H, I, e_count, "ffn_down_exps", L->own, L->wd))) return s;
+    L->swg.type = L->swu.type = L->swd.type = -1;
+    if (d->has_shared) {
+        if (canon_type(d->gate_shexp.ggml_type) != L->wg.type || canon_type(d->up_shexp.ggml_type) != L->wu.type ||
+            canon_type(d->down_shexp.ggml_type) != L->wd.type)
+            return fail(RMOE_ERR_UNSUPPORTED, "shared-expert tensor types must match the routed experts' types");
+        if ((s = upload_mat(d->gate_shexp, I, H, 1, "ffn_gate_shexp", L->own, L->swg))) return s;
+        if ((s = upload_mat(d->up_shexp, I, H, 1, "ffn_up_shexp", L->own, L->swu))) return s;
+        if ((s = upload_mat(d->down_shexp, H, I, 1, "ffn_down_shexp", L->own, L->swd))) return s;
+    }
+    void* rw = L->own.alloc((size_t)d->n_experts * H * 4);
+    if (!rw) return fail(RMOE_ERR_OOM, "router cudaMalloc failed");
+    cudaError_t e = cudaMemcpy(rw, d->router_w, (size_t)d->n_experts * H * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(e, "router upload");
+    L->router_w = static_cast<float*>(rw);
+    return RMOE_OK;
+}
+
+// Workspace for T tokens (grows; a grow synchronises the device).
+rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
+    if (T <= L->ws_T && (!need_y || L->ws.y)) return RMOE_OK;
+    uint32_t cap = T > L->ws_T ? (T + 255) / 256 * 256 : L->ws_T;
+    cudaDeviceSynchronize();
+    L->ws_own.~Owned();
+    new (&L->ws_own) Owned();
+    L->ws = Workspace{};
+    Owned& o = L->ws_own;
+    const uint32_t H = L->H, I = L->I, E = L->E, k = L->k;
+    const uint64_t rows = (uint64_t)cap * k + (L->has_shared ? cap : 0);
+    const int NT = small_tile_rows();
+    L->max_tiles = (int)(rows / NT + E + 2);
+    Workspace& w = L->ws;
+    bool ok = true;
+    auto A = [&](size_t n) { void* p = o.alloc(n); ok = ok && p; return p; };
+    w.xin = (float*)A((size_t)cap * H * 4);
+    w.xout = (float*)A((size_t)cap * H * 4);
+    w.xb = (__nv_bfloat16*)A((size_t)cap * H * 2);
+    w.topk_id = (int*)A((size_t)cap * k * 4);
+    w.topk_w = (float*)A((size_t)cap * k * 4);
+    w.local_rank = (int*)A((size_t)cap * k * 4);
+    w.cta_cnt = (int*)A((size_t)((cap + 31) / 32) * E * 4);
+    w.ticket = (unsigned*)A(16);
+    w.status = (unsigned*)A(16);
+    w.expert_off = (int*)A((size_t)(E + 2) * 4);
+    w.row_tok = (int*)A(rows * 4);
+    w.row_slot = (int*)A(rows * 4);
+    w.slot_row = (int*)A((size_t)cap * k * 4);
+    w.n_rows = (int*)A(16);
+    w.n_tiles = (int*)A(16);
+    w.tiles = (int4*)A((size_t)L->max_tiles * 16);
+    w.h = (__nv_bfloat16*)A(rows * I * 2);
+    w.logits = (float*)A((size_t)cap * E * 4);
+    if (need_y || L->ws_had_y) w.y = (float*)A(rows * H * 4);
+    if (!ok) return fail(RMOE_ERR_OOM, "workspace cudaMalloc failed for %u tokens", cap);
+    cudaMemset(w.ticket, 0, 16);
+    cudaMemset(w.status, 0, 16);
+    L->ws_T = cap;
+    L->ws_had_y = w.y != nullptr;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "workspace init");
+    return RMOE_OK;
+}
+
+rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s,
+                                 uint32_t flags) {
+    const bool det = flags & RMOE_FLAG_DETERMINISTIC;
+    rmoe_status st = ensure_workspace(L, T, det);
+    if (st) return st;
+    Workspace& w = L->ws;
+    RouteParams rp{};
+    rp.x = x;
+    rp.router_w = L->router_w;
+    rp.T = (int)T; rp.H = (int)L->H; rp.E = (int)L->E; rp.k = (int)L->k; rp.gate = (int)L->gate_kind;
+    rp.has_shared = L->has_shared;
+    rp.xb = w.xb;
+    rp.logits_out = (flags & RMOE_FLAG_ROUTING_OUT) ? w.logits : nullptr;
+    rp.out_zero = det ? nullptr : out;
+    rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;
+    rp.ticket = w.ticket; rp.expert_off = w.expert_off; rp.row_tok = w.row_tok; rp.row_slot = w.row_slot;
+    rp.slot_row = w.slot_row; rp.n_rows = w.n_rows; rp.tiles = w.tiles; rp.n_tiles = w.n_tiles;
+    rp.max_tiles = L->max_tiles; rp.tile_rows = small_tile_rows(); rp.status = w.status;
+    const bool timing = flags & RMOE_FLAG_STAGE_TIMING;
+    if (timing && !L->ev[0])
+        for (auto& ev : L->ev) cudaEventCreate(&ev);
+    auto mark = [&](int i) {
+        if (timing) cudaEventRecord(L->ev[i], s);
+    };
+    mark(0);
+    cudaError_t e = launch_route_dispatch(rp, s);
+    if (e != cudaSuccess) return cuda_fail(e, "route_dispatch launch");
+    mark(1);
+
+    GroupedParams gp{};
+    gp.gate = L->wg; gp.up = L->wu; gp.down = L->wd;
+    gp.sgate = L->swg; gp.sup = L->swu; gp.sdown = L->swd;
+    gp.H = (int)L->H; gp.I = (int)L->I; gp.E = (int)L->E; gp.k = (int)L->k;
+    gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
+    gp.topk_w = w.topk_w; gp.h = w.h; gp.y = det ? w.y : nullptr; gp.out = out; gp.status = w.status;
+    if ((e = launch_small_gateup(gp, L->max_tiles, s)) != cudaSuccess) return cuda_fail(e, "gate/up launch");
+    mark(2);
+    if ((e = launch_small_down(gp, L->max_tiles, s)) != cudaSuccess) return cuda_fail(e, "down launch");
+    mark(3);
+    if (det) {
+        CombineParams cp{};
+        cp.y = w.y; cp.slot_row = w.slot_row; cp.topk_w = w.topk_w;
+        cp.T = (int)T; cp.H = (int)L->H; cp.k = (int)L->k; cp.has_shared = L->has_shared;
+        cp.shared_row0 = (int)(T * L->k);
+        cp.out = out;
+        if ((e = launch_combine(cp, s)) != cudaSuccess) return cuda_fail(e, "combine launch");
+    }
+    mark(4);
+    L->ev_valid = timing;
+    L->ev_combine = det;
+    L->last_T = T;
+    return RMOE_OK;
+}
+
+}  // namespace rmoe
+
+using namespace rmoe;
+
+extern "C" {
+
+const char* rmoe_last_error(void) { return g_err.c_str(); }
+
+const char* rmoe_build_info(void) { return "rmoe sm_100a: route_dispatch, small_gateup/down (mma.sync bf16), combine"; }
+
+rmoe_status rmoe_layer_create(const rmoe_layer_desc* d, rmoe_layer** out) {
+    if (!out) return fail(RMOE_ERR_INVALID, "null output handle pointer");
+    *out = nullptr;
+    rmoe_status s = validate_desc(d);
+    if (s) return s;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(RMOE_ERR_CUDA, "no CUDA device");
+    if (d->device < 0 || d->device >= ndev) return fail(RMOE_ERR_INVALID, "device %d out of range", d->device);
+    DeviceGuard g(d->device);
+    rmoe_layer* L = new rmoe_layer();
+    L->device = d->device;
+    L->H = d->hidden; L->I = d->inter; L->E = d->n_experts;
+    L->k = d->top_k < d->n_experts ? d->top_k : d->n_experts;  // top_k clamps to E (src/moe.rs:79)
+    L->gate_kind = d->gate;
+    L->has_shared = d->has_shared ? 1 : 0;
+    L->E_local = L->E;
+    if ((s = layer_upload(d, 0, d->n_experts, L))) { delete L; return s; }
+    *out = L;
+    return RMOE_OK;
+}
+
+rmoe_status rmoe_layer_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, void* stream, uint32_t flags) {
+    if (!L) return fail(RMOE_ERR_INVALID, "null layer");
+    if (T == 0) return RMOE_OK;
+    if (!x || !out) return fail(RMOE_ERR_INVALID, "null x / out");
+    DeviceGuard g(L->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (flags & RMOE_FLAG_HOST_IO) {
+        rmoe_status st = ensure_workspace(L, T, flags & RMOE_FLAG_DETERMINISTIC);
+        if (st) return st;
+        cudaError_t e = cudaMemcpyAsync(L->ws.xin, x, (size_t)T * L->H * 4, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "x upload");
+        st = layer_forward_device(L, L->ws.xin, T, L->ws.xout, s, flags);
+        if (st) return st;
+        e = cudaMemcpyAsync(out, L->ws.xout, (size_t)T * L->H * 4, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_fail(e, "out download");
+        if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "forward");
+        unsigned status = 0;
+        cudaMemcpy(&status, L->ws.status, 4, cudaMemcpyDeviceToHost);
+        if (status) return fail(RMOE_ERR_DEVICE, "device status 0x%x", status);
+        return RMOE_OK;
+    }
+    return layer_forward_device(L, x, T, out, s, flags);
+}
+
+rmoe_status rmoe_layer_routing(rmoe_layer* L, uint32_t T, uint32_t* ids, float* weights) {
+    if (!L) return fail(RMOE_ERR_INVALID, "null layer");
+    if (T > L->last_T) return fail(RMOE_ERR_INVALID, "routing of %u tokens requested, last forward had %u", T, L->last_T);
+    DeviceGuard g(L->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "sync");
+    if (ids && (e = cudaMemcpy(ids, L->ws.topk_id, (size_t)T * L->k * 4, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "routing ids");
+    if (weights && (e = cudaMemcpy(weights, L->ws.topk_w, (size_t)T * L->k * 4, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "routing weights");
+    return RMOE_OK;
+}
+
+rmoe_status rmoe_layer_logits(rmoe_layer* L, uint32_t T, float* logits) {
+    if (!L || !logits) return fail(RMOE_ERR_INVALID, "null layer / buffer");
+    if (T > L->last_T) return fail(RMOE_ERR_INVALID, "logits of %u tokens requested, last forward had %u", T, L->last_T);
+    DeviceGuard g(L->device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(logits, L->ws.logits, (size_t)T * L->E * 4, cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "logits");
+}
+
+rmoe_status rmoe_layer_stage_ms(rmoe_layer* L, float ms[4]) {
+    if (!L || !ms) return fail(RMOE_ERR_INVALID, "null layer / buffer");
+    if (!L->ev_valid) return fail(RMOE_ERR_INVALID, "last forward did not set RMOE_FLAG_STAGE_TIMING");
+    DeviceGuard g(L->device);
+    cudaError_t e = cudaEventSynchronize(L->ev[4]);
+    if (e != cudaSuccess) return cuda_fail(e, "stage events");
+    for (int i = 0; i < 4; i++) {
+        ms[i] = 0.0f;
+        cudaEventElapsedTime(&ms[i], L->ev[i], L->ev[i + 1]);
+    }
+    if (!L->ev_combine) ms[3] = 0.0f;
+    return RMOE_OK;
+}
+
+void rmoe_layer_destroy(rmoe_layer* L) {
+    if (!L) return;
+    DeviceGuard g(L->device);
+    cudaDeviceSynchronize();
+    delete L;
+}
+
+rmoe_status rmoe_dequant(uint32_t t, const void* src, uint64_t nbytes, float* dst, void* stream) {
+    uint32_t el, by;
+    if (!block_geom(t, el, by)) return fail(RMOE_ERR_UNSUPPORTED, "no scalar dequant for ggml type %u", t);
+    if (nbytes % by) return fail(RMOE_ERR_INVALID, "%s data len %llu not a multiple of %u", type_name(t), (unsigned long long)nbytes, by);
+    if (nbytes && (!src || !dst)) return fail(RMOE_ERR_INVALID, "null src / dst");
+    cudaError_t e = launch_dequant_raw((int)t, src, nbytes / by, dst, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "dequant launch");
+}
+
+rmoe_status rmoe_route(const float* logits, uint32_t T, uint32_t E, uint32_t k, uint32_t gate, uint32_t* ids,
+                       float* weights, void* stream) {
+    if (E == 0 || T == 0) return RMOE_OK;
+    if (E > (uint32_t)MAX_E) return fail(RMOE_ERR_UNSUPPORTED, "E %u > %d", E, MAX_E);
+    if (k > E) k = E;
+    if (k == 0 || k > (uint32_t)MAX_K) return fail(RMOE_ERR_UNSUPPORTED, "k %u unsupported", k);
+    if (gate > 1) return fail(RMOE_ERR_INVALID, "gate %u", gate);
+    cudaError_t e = launch_route_only(logits, (int)T, (int)E, (int)k, (int)gate, reinterpret_cast<int*>(ids), weights,
+                                      static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "route launch");
+}
+
+rmoe_status rmoe_qmat_matmul(uint32_t t, const void* w_host, uint64_t w_nbytes, uint32_t m, uint32_t n, const float* x,
+                             uint32_t rows, float* out, void* stream) {
+    if (m % 64) return fail(RMOE_ERR_UNSUPPORTED, "m %u must be a multiple of 64", m);
+    rmoe_tensor tt{t, w_host, w_nbytes, {n, m, 1}};
+    Owned own;
+    DevMat W;
+    rmoe_status s = upload_mat(tt, m, n, 1, "qmat", own, W);
+    if (s) return s;
+    if (rows == 0) return RMOE_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int NT = small_tile_rows();
+    const int ntiles = (int)((rows + NT - 1) / NT);
+    __nv_bfloat16* xb = (__nv_bfloat16*)own.alloc((size_t)rows * n * 2);
+    int* rowtok = (int*)own.alloc((size_t)rows * 4);
+    int4* tiles = (int4*)own.alloc((size_t)ntiles * 16);
+    int* nt = (int*)own.alloc(16);
+    if (!xb || !rowtok || !tiles || !nt) return fail(RMOE_ERR_OOM, "qmat workspace");
+    std::vector<int4> ht(ntiles);
+    std::vector<int> hr(rows);
+    for (uint32_t i = 0; i < rows; i++) hr[i] = (int)i;
+    for (int i = 0; i < ntiles; i++) ht[i] = make_int4(0, i * NT, (int)std::min<uint32_t>(NT, rows - i * NT), 0);
+    cudaMemcpy(rowtok, hr.data(), rows * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(tiles, ht.data(), ntiles * 16, cudaMemcpyHostToDevice);
+    cudaMemcpy(nt, &ntiles, 4, cudaMemcpyHostToDevice);
+    cudaError_t e = launch_f32_to_bf16(x, xb, (uint64_t)rows * n, st);
+    if (e != cudaSuccess) return cuda_fail(e, "convert");
+    GroupedParams gp{};
+    gp.down = W;
+    gp.sdown.type = -1;
+    gp.H = (int)m; gp.I = (int)n; gp.E = 1; gp.k = 1;
+    gp.h = xb; gp.row_tok = rowtok; gp.tiles = tiles; gp.n_tiles = nt; gp.y = out;
+    if ((e = launch_small_down(gp, ntiles, st)) != cudaSuccess) return cuda_fail(e, "qmat launch");
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "qmat");
+    return RMOE_OK;
+}
+
+}  // extern "C"

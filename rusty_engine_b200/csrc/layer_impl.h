@@ -1,0 +1,87 @@
+// layer_impl.h -- host-side layer handle and helpers shared by layer.cu and ep.cu.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <new>
+#include <vector>
+
+#include "../../include/rmoe.h"
+#include "kernels.h"
+
+namespace rmoe {
+
+// cudaMalloc'd blocks owned by a handle, freed together.
+struct Owned {
+    std::vector<void*> ptrs;
+    void* alloc(size_t n);
+    Owned() = default;
+    Owned(const Owned&) = delete;
+    Owned& operator=(const Owned&) = delete;
+    ~Owned();
+};
+
+// Makes `dev` current for the scope and restores the caller's device afterwards.
+struct DeviceGuard {
+    int prev = 0, cur = 0;
+    explicit DeviceGuard(int dev);
+    ~DeviceGuard();
+};
+
+// Per-forward scratch, sized for ws_T tokens.
+struct Workspace {
+    float* xin = nullptr;     // host-IO staging of x
+    float* xout = nullptr;    // host-IO staging of out
+    __nv_bfloat16* xb = nullptr;
+    int* topk_id = nullptr;
+    float* topk_w = nullptr;
+    int* local_rank = nullptr;
+    int* cta_cnt = nullptr;
+    unsigned* ticket = nullptr;
+    unsigned* status = nullptr;
+    int* expert_off = nullptr;
+    int* row_tok = nullptr;
+    int* row_slot = nullptr;
+    int* slot_row = nullptr;
+    int* n_rows = nullptr;
+    int* n_tiles = nullptr;
+    int4* tiles = nullptr;
+    __nv_bfloat16* h = nullptr;
+    float* y = nullptr;
+    float* logits = nullptr;
+};
+
+}  // namespace rmoe
+
+struct rmoe_layer {
+    int device = 0;
+    uint32_t H = 0, I = 0, E = 0, k = 0, gate_kind = 0;
+    int has_shared = 0;
+    uint32_t E_local = 0;
+    rmoe::DevMat wg{}, wu{}, wd{}, swg{}, swu{}, swd{};
+    float* router_w = nullptr;
+    rmoe::Owned own;       // weights
+    rmoe::Owned ws_own;    // workspace
+    rmoe::Workspace ws;
+    uint32_t ws_T = 0;
+    bool ws_had_y = false;
+    int max_tiles = 0;
+    uint32_t last_T = 0;
+    cudaEvent_t ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    bool ev_valid = false, ev_combine = false;
+    ~rmoe_layer() {
+        for (auto& e : ev)
+            if (e) cudaEventDestroy(e);
+    }
+};
+
+namespace rmoe {
+rmoe_status fail(rmoe_status s, const char* fmt, ...);
+rmoe_status cuda_fail(cudaError_t e, const char* what);
+bool block_geom(uint32_t t, uint32_t& el, uint32_t& by);
+rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t experts, const char* name, Owned& own,
+                       DevMat& out);
+rmoe_status validate_desc(const rmoe_layer_desc* d);
+rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_count, rmoe_layer* L);
+rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y);
+rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags);
+}  // namespace rmoe

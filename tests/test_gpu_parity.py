@@ -1,0 +1,217 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle on identical seeded
+inputs.
+
+Contract:
+* router logits and top-k expert ids: bit-exact with moe::matvec / top_k (the GPU computes
+  the same sequential f32 sums), so no near-tie exceptions are needed;
+* routing weights: within 2 ulp-scale (expf differs between CUDA and glibc by <= 2 ulp);
+* layer outputs: max-abs <= 2e-2 and relative L2 <= 5e-3 (bf16 MMA on dequantised values).
+  Where the output scale makes an absolute 2e-2 meaningless (Qwen-shaped Q4_K layers have
+  outputs ~1e5), max-abs is checked relative to the output RMS instead: <= 2e-2 * RMS.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from rusty_engine_b200 import _lib, synth
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 5e-3
+MAX_ABS = 2e-2
+
+
+def rel_l2(a, b):
+    return float(np.linalg.norm(a.astype(np.float64) - b) / max(np.linalg.norm(b.astype(np.float64)), 1e-30))
+
+
+def assert_layer_close(got, want, what=""):
+    err = np.abs(got.astype(np.float64) - want)
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    r = rel_l2(got, want)
+    assert r <= REL_L2, f"{what}: rel-L2 {r:.3e} > {REL_L2}"
+    bound = MAX_ABS if rms < 1.0 / MAX_ABS else MAX_ABS * rms
+    assert err.max() <= max(MAX_ABS, bound), f"{what}: max-abs {err.max():.3e} (rms {rms:.3e})"
+
+
+@pytest.fixture(scope="module")
+def torch_cuda(gpu):
+    import torch
+
+    return torch
+
+
+def run_layer(torch, lw, x, flags=0, routing=True):
+    from rusty_engine_b200.moe import MoELayer
+
+    layer = MoELayer(lw, device=0)
+    xd = torch.from_numpy(x).cuda()
+    out = layer.forward(xd, flags=flags | (_lib.FLAG_ROUTING_OUT if routing else 0))
+    torch.cuda.synchronize()
+    res = {"out": out.cpu().numpy()}
+    if routing:
+        res["ids"], res["w"] = layer.routing(x.shape[0])
+        res["logits"] = layer.logits(x.shape[0])
+    layer.close()
+    return res
+
+
+# ---- stand-alone operators -------------------------------------------------------------------
+@pytest.mark.parametrize("t", [2, 6, 8, 12, 13, 14, 0, 1, 30])
+def test_dequant_bit_exact(torch_cuda, t):
+    from rusty_engine_b200.moe import dequant
+
+    rng = np.random.default_rng(t)
+    el, _ = synth.BLOCK[t]
+    raw = synth.gen_blocks(rng, t, 64 if el > 1 else 4096, 0.001, 0.05)
+    got = dequant(t, raw)
+    want = O.dequant(t, raw.tobytes())
+    assert got.shape == want.shape
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_dequant_errors(torch_cuda):
+    from rusty_engine_b200.moe import EngineError, dequant
+
+    with pytest.raises(EngineError, match="Q4_0 data len 17 not a multiple of 18"):
+        dequant(2, bytes(17))
+
+
+def test_route_reference_kats(torch_cuda):
+    from rusty_engine_b200.moe import Gate, RouterConfig, route, top_k, top_k_sigmoid
+
+    s = top_k([0.1, 0.9, 0.2, 0.8], 2)  # src/moe.rs:632-641
+    assert [e.id for e in s] == [1, 3] and abs(sum(e.weight for e in s) - 1) < 1e-5
+    assert len(top_k([0.5, 0.4], 8)) == 2  # src/moe.rs:643-646
+    s = top_k_sigmoid([1.0, 5.0, 2.0, 4.0], 2)  # src/moe.rs:656-663
+    assert [e.id for e in s] == [1, 3] and abs(sum(e.weight for e in s) - 1) < 1e-5
+    assert [e.id for e in route([0.0, 3.0, 1.0, 2.0], RouterConfig(Gate.Sigmoid, 2))] == [1, 3]
+    assert route([], RouterConfig()) == []
+
+
+@pytest.mark.parametrize("gate", [0, 1])
+def test_route_random_with_ties_bit_exact(torch_cuda, gate):
+    from rusty_engine_b200.moe import Gate, RouterConfig, route_batch
+
+    rng = np.random.default_rng(11 + gate)
+    T, E, k = 257, 128, 8
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    lg[:, 5] = lg[:, 9]  # exact ties: the lower index must win
+    lg[::3, 100:110] = 1.5
+    ids, w = route_batch(lg, RouterConfig(Gate(gate), k))
+    wids, ww = O.route_batch(lg, gate, k)
+    assert np.array_equal(ids.astype(np.uint32), wids)
+    assert np.allclose(w, ww, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("t", [2, 6, 8, 12, 13, 14, 0])
+def test_qmat_matmul_parity(torch_cuda, t):
+    from rusty_engine_b200.moe import QMat
+
+    rng = np.random.default_rng(100 + t)
+    m, n, rows = 128, 512, 37
+    el, _ = synth.BLOCK[t]
+    raw = synth.gen_blocks(rng, t, m * n // el, 0.001, 0.01)
+    x = rng.standard_normal((rows, n)).astype(np.float32)
+    got = QMat.from_bytes(t, raw, m, n).matmul(x, rows)
+    deq = O.dequant(t, raw.tobytes()).reshape(m, n)
+    want = np.stack([O.matvec(deq, m, n, x[r]) for r in range(rows)])
+    assert rel_l2(got, want) <= REL_L2
+
+
+# ---- the layer --------------------------------------------------------------------------------
+def test_c1_layer_parity(torch_cuda):
+    """H 1024, E 16, top-4, I 512, Q4_0, 128 tokens, seed 0."""
+    lw = synth.config_c1()
+    x = synth.activations(128, lw.H)
+    got = run_layer(torch_cuda, lw, x)
+    out, ids, w, logits = O.moe_layer_q_exact(x, lw)
+    assert np.array_equal(got["logits"].view(np.uint32), logits.view(np.uint32)), "router logits not bit-exact"
+    assert np.array_equal(got["ids"], ids), "top-k ids not bit-exact"
+    assert np.allclose(got["w"], w, rtol=2e-6, atol=1e-7)
+    assert_layer_close(got["out"], out, "c1")
+
+
+def test_c1_deterministic_mode_reproducible(torch_cuda):
+    lw = synth.config_c1()
+    x = synth.activations(128, lw.H)
+    a = run_layer(torch_cuda, lw, x, flags=_lib.FLAG_DETERMINISTIC, routing=False)["out"]
+    b = run_layer(torch_cuda, lw, x, flags=_lib.FLAG_DETERMINISTIC, routing=False)["out"]
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    want = O.moe_layer_q_exact(x, lw)[0]
+    assert_layer_close(a, want, "c1 deterministic")
+
+
+def test_c2_layer_parity(torch_cuda):
+    """BASELINE config 2 (Qwen3-30B-A3B layer, Q4_K gate/up, Q6_K down), 4096 tokens:
+    router logits and ids bit-exact on all tokens; outputs on a 96-token sample."""
+    lw = synth.config_c2()
+    x = synth.activations(4096, lw.H)
+    got = run_layer(torch_cuda, lw, x)
+    logits = O.router_logits(x, lw.router_w, lw.E)
+    assert np.array_equal(got["logits"].view(np.uint32), logits.view(np.uint32)), "router logits not bit-exact"
+    ids, w = O.route_batch(logits, 0, lw.k)
+    assert np.array_equal(got["ids"], ids)
+    assert np.allclose(got["w"], w, rtol=2e-6, atol=1e-7)
+    sample = np.r_[0:48, 4048:4096]
+    out = O.moe_layer_q_exact(x[sample], lw)[0]
+    assert_layer_close(got["out"][sample], out, "c2")
+
+
+@pytest.mark.parametrize("T", [1, 3, 127])
+def test_ragged_token_counts(torch_cuda, T):
+    lw = synth.config_c1()
+    x = synth.activations(T, lw.H, seed=T)
+    got = run_layer(torch_cuda, lw, x)
+    out, ids, w, _ = O.moe_layer_q_exact(x, lw)
+    assert np.array_equal(got["ids"], ids)
+    assert_layer_close(got["out"], out, f"T={T}")
+
+
+@pytest.mark.parametrize("gt,dt", [(2, 2), (6, 6), (8, 8), (12, 14), (13, 13), (14, 14), (12, 12), (0, 0)])
+def test_formats_small_layer(torch_cuda, gt, dt):
+    lw = synth.make_layer(512, 256, 8, 2, gate_t=gt, up_t=gt, down_t=dt, dlo=0.002, dhi=0.02, seed=gt * 16 + dt)
+    x = synth.activations(40, lw.H, seed=7)
+    got = run_layer(torch_cuda, lw, x)
+    out, ids, w, _ = O.moe_layer_q_exact(x, lw)
+    assert np.array_equal(got["ids"], ids)
+    assert_layer_close(got["out"], out, f"types {gt}/{dt}")
+
+
+def test_sigmoid_gate_and_shared_expert(torch_cuda):
+    lw = synth.make_layer(512, 256, 16, 4, gate_t=12, up_t=12, down_t=14, dlo=0.001, dhi=0.01, seed=9, gate=1,
+                          shared=True)
+    x = synth.activations(33, lw.H, seed=9)
+    for flags in (0, _lib.FLAG_DETERMINISTIC):
+        got = run_layer(torch_cuda, lw, x, flags=flags)
+        out, ids, w, _ = O.moe_layer_q_exact(x, lw)
+        assert np.array_equal(got["ids"], ids)
+        assert np.allclose(got["w"], w, rtol=2e-6, atol=1e-7)
+        assert_layer_close(got["out"], out, "sigmoid+shared")
+
+
+def test_host_io_matches_device_path(torch_cuda):
+    from rusty_engine_b200.moe import MoELayer
+
+    lw = synth.config_c1()
+    x = synth.activations(64, lw.H, seed=3)
+    layer = MoELayer(lw, device=0)
+    a = layer.forward_host(x, flags=_lib.FLAG_DETERMINISTIC)
+    b = layer.forward(torch_cuda.from_numpy(x).cuda(), flags=_lib.FLAG_DETERMINISTIC).cpu().numpy()
+    layer.close()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_reference_layer_kats_f32_experts(torch_cuda):
+    """moe_layer_routes_to_best_expert / moe_layer_adds_shared_expert (src/moe.rs:773-801)
+    through the f32-ExpertWeights signature (zero-padded to the kernel widths)."""
+    from rusty_engine_b200.moe import ExpertWeights, Gate, RouterConfig, moe_layer_forward
+
+    silu1 = O.silu(1.0)
+    ide = lambda s: ExpertWeights(np.array([1.0, 0, 0, 1.0]), np.array([1.0, 0, 0, 1.0]), np.array([s, 0, 0, s]))
+    out = moe_layer_forward([1.0, 0.0], [0.0, 0.0, 10.0, 0.0], 2, [ide(1.0), ide(2.0)], None, 2,
+                            RouterConfig(Gate.Softmax, 1))
+    assert abs(out[0] - 2 * silu1) <= MAX_ABS and abs(out[1]) <= MAX_ABS
+    out = moe_layer_forward([1.0, 0.0], [10.0, 0.0, 0.0, 0.0], 2, [ide(1.0), ide(1.0)], ide(1.0), 2,
+                            RouterConfig(Gate.Sigmoid, 1))
+    assert abs(out[0] - 2 * silu1) <= MAX_ABS and abs(out[1]) <= MAX_ABS
