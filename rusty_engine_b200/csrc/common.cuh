@@ -8,9 +8,13 @@
 //   Q4_0 (2):  main plane [row][blk] of 16 B qs, d plane [row][blk] f16.
 //   Q5_0 (6):  main plane [row][blk] of 16 B qs, aux plane [row][blk] u32 qh, d plane.
 //   Q8_0 (8):  main plane [row][blk] of 32 B int8, d plane.
-//   F32/F16/BF16 (0/1/30): main plane [row][K] bf16 (the MMA operand type).
+//   F32/F16/BF16 (0/1/30): main plane [row][K] fp16 (the MMA operand type), internal code T_DENSE.
 // Element values decoded from these planes are bit-identical (in f32) to quant::dequant
-// (rusty-engine src/quant.rs:106-357); the kernels then round them to bf16 for the MMA.
+// (rusty-engine src/quant.rs:106-357); the kernels then round them to fp16 (round to nearest
+// even) for the tensor-core MMA.  fp16 keeps 11 significant bits against bf16's 8, and every
+// operand is range-checked: weights at layer creation, activations by the router, and the
+// SwiGLU activations carry a power-of-two scale per (row, 64-feature block) so they never
+// overflow fp16.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -20,12 +24,16 @@ namespace rmoe {
 
 enum GgmlType : int {
     T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q5_0 = 6, T_Q8_0 = 8,
-    T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_BF16 = 30
+    T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_BF16 = 30,
+    T_DENSE = 100  // device-only: an fp16 plane holding F32/F16/BF16 experts
 };
 
 // Status word bits written by kernels when a device-side check fails (never trap).
 enum DevErr : uint32_t { DERR_NONE = 0, DERR_BAD_EXPERT = 1, DERR_ROWS_OVERFLOW = 2, DERR_TILES_OVERFLOW = 4,
-                         DERR_TIMEOUT = 8 };
+                         DERR_TIMEOUT = 8, DERR_FP16_RANGE = 16 };
+
+// Rows of SwiGLU activations are stored as fp16 * 2^e per 64-feature block.
+static constexpr int HBLK = 64;
 
 // One stack of expert matrices (E experts x rows x K) in the device layout above.
 struct DevMat {
@@ -51,6 +59,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// 2^e as an exact float for e in [-126, 127].
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
+
 // get_scale_min_k4 (src/quant.rs:250-258) on the 12-byte scale array.
 __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, int& m) {
     if (j < 4) {
@@ -64,8 +80,8 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, i
 
 // --------------------------------------------------------------------------------------
 // chunk8: decode 8 consecutive elements [8*c8, 8*c8+8) of row `row` (global row index in
-// the stack) into 4 packed bf16x2 words.  The f32 value of each element is computed with
-// the same operation order as quant::dequant, then rounded to bf16 (round-to-nearest-even).
+// the stack) into 4 packed fp16x2 words.  The f32 value of each element is computed with
+// the same operation order as quant::dequant, then rounded to fp16 (round-to-nearest-even).
 // --------------------------------------------------------------------------------------
 template <int TYPE>
 __device__ __forceinline__ uint4 chunk8(const DevMat& M, uint64_t row, uint32_t c8);
@@ -88,8 +104,8 @@ __device__ __forceinline__ uint4 chunk8<T_Q4_K>(const DevMat& M, uint64_t row, u
         v[i] = __fsub_rn(__fmul_rn(d1, (float)((qs.x >> (8 * i + sh)) & 0xF)), dm1);
         v[4 + i] = __fsub_rn(__fmul_rn(d1, (float)((qs.y >> (8 * i + sh)) & 0xF)), dm1);
     }
-    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                      pack_bf16x2(v[6], v[7]));
+    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                      pack_f16x2(v[6], v[7]));
 }
 
 // Q5_K: Q4_K plus a 5th bit from qh (src/quant.rs:294-323), 176-B superblocks.
@@ -113,8 +129,8 @@ __device__ __forceinline__ uint4 chunk8<T_Q5_K>(const DevMat& M, uint64_t row, u
         v[i] = __fsub_rn(__fmul_rn(d1, (float)q0), dm1);
         v[4 + i] = __fsub_rn(__fmul_rn(d1, (float)q1), dm1);
     }
-    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                      pack_bf16x2(v[6], v[7]));
+    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                      pack_f16x2(v[6], v[7]));
 }
 
 // Q6_K: y = d*sc*(q6 - 32) (src/quant.rs:328-357); main plane 208 B/superblock, d plane.
@@ -140,8 +156,8 @@ __device__ __forceinline__ uint4 chunk8<T_Q6_K>(const DevMat& M, uint64_t row, u
         v[i] = __fmul_rn(ds, (float)q0);
         v[4 + i] = __fmul_rn(ds, (float)q1);
     }
-    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                      pack_bf16x2(v[6], v[7]));
+    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                      pack_f16x2(v[6], v[7]));
 }
 
 // Q4_0: y = (nibble - 8) * d, split-half (src/quant.rs:106-119); 16-B qs plane + d plane.
@@ -157,8 +173,8 @@ __device__ __forceinline__ uint4 chunk8<T_Q4_0>(const DevMat& M, uint64_t row, u
         v[i] = __fmul_rn((float)((int)((qs.x >> (8 * i + sh)) & 0xF) - 8), d);
         v[4 + i] = __fmul_rn((float)((int)((qs.y >> (8 * i + sh)) & 0xF) - 8), d);
     }
-    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                      pack_bf16x2(v[6], v[7]));
+    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                      pack_f16x2(v[6], v[7]));
 }
 
 // Q5_0: y = ((nibble | bit<<4) - 16) * d (src/quant.rs:126-144); qs, qh and d planes.
@@ -178,8 +194,8 @@ __device__ __forceinline__ uint4 chunk8<T_Q5_0>(const DevMat& M, uint64_t row, u
         v[i] = __fmul_rn((float)x0, d);
         v[4 + i] = __fmul_rn((float)x1, d);
     }
-    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                      pack_bf16x2(v[6], v[7]));
+    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                      pack_f16x2(v[6], v[7]));
 }
 
 // Q8_0: y = (int8) * d (src/quant.rs:147-158); 32-B qs plane + d plane.
@@ -194,13 +210,13 @@ __device__ __forceinline__ uint4 chunk8<T_Q8_0>(const DevMat& M, uint64_t row, u
         v[i] = __fmul_rn((float)(int8_t)((qs.x >> (8 * i)) & 0xFF), d);
         v[4 + i] = __fmul_rn((float)(int8_t)((qs.y >> (8 * i)) & 0xFF), d);
     }
-    return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                      pack_bf16x2(v[6], v[7]));
+    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
+                      pack_f16x2(v[6], v[7]));
 }
 
-// Unquantized experts (F32/F16/BF16 in GGUF) are held as a bf16 plane.
+// Unquantized experts (F32/F16/BF16 in GGUF) are held as an fp16 plane.
 template <>
-__device__ __forceinline__ uint4 chunk8<T_BF16>(const DevMat& M, uint64_t row, uint32_t c8) {
+__device__ __forceinline__ uint4 chunk8<T_DENSE>(const DevMat& M, uint64_t row, uint32_t c8) {
     return __ldg(reinterpret_cast<const uint4*>(M.main + row * M.main_stride + (uint64_t)c8 * 16u));
 }
 
@@ -225,10 +241,10 @@ __device__ __forceinline__ void ldmatrix_x2(uint32_t addr, uint32_t& r0, uint32_
     asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
 
-// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D (fp32)
-__device__ __forceinline__ void mma_bf16_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+// D = A(16x16 fp16, row) * B(16x8 fp16, col) + D (fp32)
+__device__ __forceinline__ void mma_f16_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
     asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));

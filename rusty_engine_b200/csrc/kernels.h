@@ -16,7 +16,8 @@ struct RouteParams {
     const float* x;         // [T, H] f32
     const float* router_w;  // [E, H] f32
     int T, H, E, k, gate, has_shared;
-    __nv_bfloat16* xb;      // [T, H] bf16 copy of x (GEMM B operand)
+    __half* xb;             // [T, H] fp16 copy of x (GEMM B operand)
+    int* rowexp;            // [rows] SwiGLU row exponents, set to -127 by the dispatch
     float* logits_out;      // optional [T, E]
     float* out_zero;        // optional: rows of `out` to zero (atomic combine)
     int* topk_id;           // [T, k]
@@ -41,13 +42,15 @@ struct GroupedParams {
     DevMat gate, up, down;        // routed experts
     DevMat sgate, sup, sdown;     // shared expert (type < 0 when absent)
     int H, I, E, k;
-    const __nv_bfloat16* xb;      // [T, H]
+    const __half* xb;             // [T, H]
     const int* row_tok;
     const int* row_slot;
     const int4* tiles;
     const int* n_tiles;
     const float* topk_w;          // [T, k]
-    __nv_bfloat16* h;             // [rows, I] SwiGLU activations
+    __half* h;                    // [rows, I] SwiGLU activations, fp16 * 2^hexp
+    int8_t* hexp;                 // [rows, I / 64] block exponents
+    int* rowexp;                  // [rows] max block exponent per row
     float* y;                     // [rows, H] expert outputs (deterministic combine) or null
     float* out;                   // [T, H] atomic combine target (when y is null)
     unsigned int* status;
@@ -73,6 +76,6 @@ cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, cudaStream_
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_dequant_raw(int type, const void* src, uint64_t nblocks, float* dst, cudaStream_t s);
 cudaError_t launch_route_only(const float* logits, int T, int E, int k, int gate, int* ids, float* w, cudaStream_t s);
-cudaError_t launch_f32_to_bf16(const float* x, __nv_bfloat16* y, uint64_t n, cudaStream_t s);
+cudaError_t launch_f32_to_f16(const float* x, __half* y, uint64_t n, cudaStream_t s);
 
 }  // namespace rmoe

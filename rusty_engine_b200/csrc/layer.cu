@@ -3,6 +3,7 @@
 //   route+dispatch -> grouped gate/up (+SwiGLU) -> grouped down (+combine)
 // all stream-ordered on the caller's stream.
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -56,12 +57,30 @@ static const char* type_name(uint32_t t) {
     }
 }
 
-static uint16_t f32_to_bf16_rne(float f) {
+// f32 -> binary16, round to nearest even; returns false when |f| is beyond the fp16 range.
+static bool f32_to_f16_rne(float f, uint16_t& out) {
     uint32_t u;
     memcpy(&u, &f, 4);
-    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) return (uint16_t)((u >> 16) | 0x40);  // NaN
-    uint32_t r = 0x7fffu + ((u >> 16) & 1u);
-    return (uint16_t)((u + r) >> 16);
+    uint32_t sign = (u >> 16) & 0x8000u, a = u & 0x7fffffffu;
+    if (a >= 0x477ff000u) {  // >= 65520 rounds to inf (or inf/NaN itself)
+        out = (uint16_t)(sign | 0x7c00u);
+        return false;
+    }
+    if (a < 0x33000000u) { out = (uint16_t)sign; return true; }  // < 2^-25 rounds to zero
+    int e = (int)(a >> 23) - 127;
+    uint32_t mant = (a & 0x7fffffu) | 0x800000u;
+    if (e < -14) {  // subnormal half: value = mant * 2^(e-23), unit 2^-24
+        int shift = 13 + (-14 - e);  // bits of the 24-bit significand below the 2^-24 unit
+        uint32_t q = mant >> shift, rem = mant & ((1u << shift) - 1u), halfway = 1u << (shift - 1);
+        if (rem > halfway || (rem == halfway && (q & 1u))) q++;
+        out = (uint16_t)(sign | q);
+        return true;
+    }
+    uint32_t q = ((uint32_t)(e + 15) << 10) | ((mant >> 13) & 0x3ffu);
+    uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) q++;  // carry may round up into the exponent
+    out = (uint16_t)(sign | q);
+    return (q & 0x7c00u) != 0x7c00u;
 }
 
 static float f16_to_f32_host(uint16_t h) {
@@ -120,6 +139,29 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
     out.rows = rows;
     out.K = K;
     out.dstride = (uint32_t)nblk;
+    // fp16 operand range: bound |w| per block from its scales (d * 63 * 15 + dmin * 63 for
+    // the K-quants, d * 32 / 16 / 128 for the others) and refuse layers that could overflow.
+    double wmax = 0.0;
+    if (t.ggml_type != T_F32 && t.ggml_type != T_F16 && t.ggml_type != T_BF16) {
+        const uint64_t nb_all = total_rows * nblk;
+        for (uint64_t b = 0; b < nb_all; b++) {
+            const uint8_t* s = src + b * by;
+            double bound;
+            switch (t.ggml_type) {
+                case T_Q4_K: case T_Q5_K:
+                    bound = fabs(f16_to_f32_host((uint16_t)(s[0] | (s[1] << 8)))) * 63.0 * 31.0 +
+                            fabs(f16_to_f32_host((uint16_t)(s[2] | (s[3] << 8)))) * 63.0;
+                    break;
+                case T_Q6_K: bound = fabs(f16_to_f32_host((uint16_t)(s[208] | (s[209] << 8)))) * 128.0 * 32.0; break;
+                case T_Q8_0: bound = fabs(f16_to_f32_host((uint16_t)(s[0] | (s[1] << 8)))) * 128.0; break;
+                default: bound = fabs(f16_to_f32_host((uint16_t)(s[0] | (s[1] << 8)))) * 16.0; break;
+            }
+            if (!(bound <= wmax)) wmax = bound;  // also catches NaN scales
+        }
+        if (!(wmax < 65504.0))
+            return fail(RMOE_ERR_UNSUPPORTED, "%s: block scales allow |w| up to %g, beyond the fp16 operand range", name,
+                        wmax);
+    }
     switch (t.ggml_type) {
         case T_Q4_K: case T_Q5_K:
             out.type = (int)t.ggml_type;
@@ -167,16 +209,25 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
                 }
             break;
         case T_F32: case T_F16: case T_BF16: {
-            out.type = T_BF16;
+            out.type = T_DENSE;
             out.main_stride = (uint64_t)K * 2;
             mainp.resize(total_rows * K * 2);
             uint16_t* d = reinterpret_cast<uint16_t*>(mainp.data());
             const uint64_t n = total_rows * K;
+            bool range_ok = true;
             for (uint64_t i = 0; i < n; i++) {
-                if (t.ggml_type == T_BF16) d[i] = (uint16_t)(src[2 * i] | (src[2 * i + 1] << 8));
-                else if (t.ggml_type == T_F16) d[i] = f32_to_bf16_rne(f16_to_f32_host((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8))));
-                else { float f; memcpy(&f, src + 4 * i, 4); d[i] = f32_to_bf16_rne(f); }
+                float f;
+                if (t.ggml_type == T_BF16) {
+                    uint32_t b = (uint32_t)(src[2 * i] | (src[2 * i + 1] << 8)) << 16;
+                    memcpy(&f, &b, 4);
+                } else if (t.ggml_type == T_F16) {
+                    f = f16_to_f32_host((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8)));
+                } else {
+                    memcpy(&f, src + 4 * i, 4);
+                }
+                range_ok &= f32_to_f16_rne(f, d[i]);
             }
+            if (!range_ok) return fail(RMOE_ERR_UNSUPPORTED, "%s: a weight exceeds the fp16 operand range", name);
             break;
         }
         default:
@@ -291,7 +342,7 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     auto A = [&](size_t n) { void* p = o.alloc(n); ok = ok && p; return p; };
     w.xin = (float*)A((size_t)cap * H * 4);
     w.xout = (float*)A((size_t)cap * H * 4);
-    w.xb = (__nv_bfloat16*)A((size_t)cap * H * 2);
+    w.xb = (__half*)A((size_t)cap * H * 2);
     w.topk_id = (int*)A((size_t)cap * k * 4);
     w.topk_w = (float*)A((size_t)cap * k * 4);
     w.local_rank = (int*)A((size_t)cap * k * 4);
@@ -305,7 +356,9 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.n_rows = (int*)A(16);
     w.n_tiles = (int*)A(16);
     w.tiles = (int4*)A((size_t)L->max_tiles * 16);
-    w.h = (__nv_bfloat16*)A(rows * I * 2);
+    w.h = (__half*)A(rows * I * 2);
+    w.hexp = (int8_t*)A(rows * (I / HBLK));
+    w.rowexp = (int*)A(rows * 4);
     w.logits = (float*)A((size_t)cap * E * 4);
     if (need_y || L->ws_had_y) w.y = (float*)A(rows * H * 4);
     if (!ok) return fail(RMOE_ERR_OOM, "workspace cudaMalloc failed for %u tokens", cap);
@@ -330,6 +383,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.T = (int)T; rp.H = (int)L->H; rp.E = (int)L->E; rp.k = (int)L->k; rp.gate = (int)L->gate_kind;
     rp.has_shared = L->has_shared;
     rp.xb = w.xb;
+    rp.rowexp = w.rowexp;
     rp.logits_out = (flags & RMOE_FLAG_ROUTING_OUT) ? w.logits : nullptr;
     rp.out_zero = det ? nullptr : out;
     rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;
@@ -352,7 +406,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     gp.sgate = L->swg; gp.sup = L->swu; gp.sdown = L->swd;
     gp.H = (int)L->H; gp.I = (int)L->I; gp.E = (int)L->E; gp.k = (int)L->k;
     gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
-    gp.topk_w = w.topk_w; gp.h = w.h; gp.y = det ? w.y : nullptr; gp.out = out; gp.status = w.status;
+    gp.topk_w = w.topk_w; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp; gp.y = det ? w.y : nullptr; gp.out = out; gp.status = w.status;
     if ((e = launch_small_gateup(gp, L->max_tiles, s)) != cudaSuccess) return cuda_fail(e, "gate/up launch");
     mark(2);
     if ((e = launch_small_down(gp, L->max_tiles, s)) != cudaSuccess) return cuda_fail(e, "down launch");
@@ -380,7 +434,7 @@ extern "C" {
 
 const char* rmoe_last_error(void) { return g_err.c_str(); }
 
-const char* rmoe_build_info(void) { return "rmoe sm_100a: route_dispatch, small_gateup/down (mma.sync bf16), combine"; }
+const char* rmoe_build_info(void) { return "rmoe sm_100a: route_dispatch, small_gateup/down (mma.sync fp16), combine"; }
 
 rmoe_status rmoe_layer_create(const rmoe_layer_desc* d, rmoe_layer** out) {
     if (!out) return fail(RMOE_ERR_INVALID, "null output handle pointer");
@@ -503,11 +557,15 @@ rmoe_status rmoe_qmat_matmul(uint32_t t, const void* w_host, uint64_t w_nbytes, 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int NT = small_tile_rows();
     const int ntiles = (int)((rows + NT - 1) / NT);
-    __nv_bfloat16* xb = (__nv_bfloat16*)own.alloc((size_t)rows * n * 2);
+    __half* xb = (__half*)own.alloc((size_t)rows * n * 2);
     int* rowtok = (int*)own.alloc((size_t)rows * 4);
+    int8_t* hexp = (int8_t*)own.alloc((size_t)rows * (n / HBLK));
+    int* rexp = (int*)own.alloc((size_t)rows * 4);
     int4* tiles = (int4*)own.alloc((size_t)ntiles * 16);
     int* nt = (int*)own.alloc(16);
-    if (!xb || !rowtok || !tiles || !nt) return fail(RMOE_ERR_OOM, "qmat workspace");
+    if (!xb || !rowtok || !tiles || !nt || !hexp || !rexp) return fail(RMOE_ERR_OOM, "qmat workspace");
+    cudaMemsetAsync(hexp, 0, (size_t)rows * (n / HBLK), st);
+    cudaMemsetAsync(rexp, 0, (size_t)rows * 4, st);
     std::vector<int4> ht(ntiles);
     std::vector<int> hr(rows);
     for (uint32_t i = 0; i < rows; i++) hr[i] = (int)i;
@@ -515,13 +573,13 @@ rmoe_status rmoe_qmat_matmul(uint32_t t, const void* w_host, uint64_t w_nbytes, 
     cudaMemcpy(rowtok, hr.data(), rows * 4, cudaMemcpyHostToDevice);
     cudaMemcpy(tiles, ht.data(), ntiles * 16, cudaMemcpyHostToDevice);
     cudaMemcpy(nt, &ntiles, 4, cudaMemcpyHostToDevice);
-    cudaError_t e = launch_f32_to_bf16(x, xb, (uint64_t)rows * n, st);
+    cudaError_t e = launch_f32_to_f16(x, xb, (uint64_t)rows * n, st);
     if (e != cudaSuccess) return cuda_fail(e, "convert");
     GroupedParams gp{};
     gp.down = W;
     gp.sdown.type = -1;
     gp.H = (int)m; gp.I = (int)n; gp.E = 1; gp.k = 1;
-    gp.h = xb; gp.row_tok = rowtok; gp.tiles = tiles; gp.n_tiles = nt; gp.y = out;
+    gp.h = xb; gp.hexp = hexp; gp.rowexp = rexp; gp.row_tok = rowtok; gp.tiles = tiles; gp.n_tiles = nt; gp.y = out;
     if ((e = launch_small_down(gp, ntiles, st)) != cudaSuccess) return cuda_fail(e, "qmat launch");
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "qmat");
     return RMOE_OK;

@@ -31,7 +31,7 @@ struct DeviceGuard {
 struct Workspace {
     float* xin = nullptr;     // host-IO staging of x
     float* xout = nullptr;    // host-IO staging of out
-    __nv_bfloat16* xb = nullptr;
+    __half* xb = nullptr;
     int* topk_id = nullptr;
     float* topk_w = nullptr;
     int* local_rank = nullptr;
@@ -45,7 +45,9 @@ struct Workspace {
     int* n_rows = nullptr;
     int* n_tiles = nullptr;
     int4* tiles = nullptr;
-    __nv_bfloat16* h = nullptr;
+    __half* h = nullptr;
+    int8_t* hexp = nullptr;
+    int* rowexp = nullptr;
     float* y = nullptr;
     float* logits = nullptr;
 };

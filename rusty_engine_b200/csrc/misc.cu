@@ -131,14 +131,14 @@ cudaError_t launch_dequant_raw(int type, const void* src, uint64_t nblocks, floa
     return cudaGetLastError();
 }
 
-__global__ void f32_to_bf16_kernel(const float* x, __nv_bfloat16* y, uint64_t n) {
+__global__ void f32_to_f16_kernel(const float* x, __half* y, uint64_t n) {
     uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
-    if (i < n) y[i] = __float2bfloat16_rn(x[i]);
+    if (i < n) y[i] = __float2half_rn(x[i]);
 }
 
-cudaError_t launch_f32_to_bf16(const float* x, __nv_bfloat16* y, uint64_t n, cudaStream_t s) {
+cudaError_t launch_f32_to_f16(const float* x, __half* y, uint64_t n, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
-    f32_to_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, y, n);
+    f32_to_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(x, y, n);
     return cudaGetLastError();
 }
 

@@ -105,13 +105,17 @@ __global__ void __launch_bounds__(RT_THREADS) route_dispatch_kernel(RouteParams 
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
         for (int k0 = 0; k0 < H; k0 += RT_K) {
-            // x tile: 32 tokens x 32 k (and the bf16 copy of x, written once when e0 == 0)
+            // x tile: 32 tokens x 32 k (and the fp16 copy of x, written once when e0 == 0)
             for (int i = tid; i < RT_TOK * RT_K; i += RT_THREADS) {
                 int tl = i / RT_K, kk = i % RT_K;
                 int t = t0 + tl;
                 float v = (t < p.T) ? p.x[(size_t)t * H + k0 + kk] : 0.0f;
                 xs[kk][tl] = v;
-                if (e0 == 0 && t < p.T && p.xb) p.xb[(size_t)t * H + k0 + kk] = __float2bfloat16_rn(v);
+                if (e0 == 0 && t < p.T && p.xb) {
+                    // fp16 MMA operand; |x| beyond the fp16 range is reported, never silently inf
+                    if (!(fabsf(v) <= 65504.0f)) atomicOr(p.status, (unsigned)DERR_FP16_RANGE);
+                    p.xb[(size_t)t * H + k0 + kk] = __float2half_rn(v);
+                }
             }
             // w tile: 128 experts x 32 k, transposed into ws[k][e]
             for (int i = tid; i < RT_EXP * RT_K / 4; i += RT_THREADS) {
@@ -243,11 +247,13 @@ __global__ void __launch_bounds__(RT_THREADS) route_dispatch_kernel(RouteParams 
         p.row_tok[pos] = t;
         p.row_slot[pos] = i - t * k;
         p.slot_row[i] = pos;
+        p.rowexp[pos] = -127;
     }
     if (p.has_shared) {
         for (int t = tid; t < p.T; t += RT_THREADS) {
             p.row_tok[off_s[E] + t] = t;
             p.row_slot[off_s[E] + t] = k;
+            p.rowexp[off_s[E] + t] = -127;
         }
     }
     // tile list: (expert, first row, rows) with at most tile_rows rows per tile
