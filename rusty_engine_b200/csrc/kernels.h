@@ -18,7 +18,7 @@ struct RouteParams {
     int T, H, E, k, gate, has_shared;
     __half* xb;             // [T, H] fp16 copy of x (GEMM B operand)
     int* rowexp;            // [rows] SwiGLU row exponents, set to -127 by the dispatch
-    float* logits_out;      // optional [T, E]
+    float* logits;          // [T, E] router logits (the exact moe::matvec values)
     float* out_zero;        // optional: rows of `out` to zero (atomic combine)
     int* topk_id;           // [T, k]
     float* topk_w;          // [T, k]
@@ -64,7 +64,6 @@ struct CombineParams {
     float* out;
 };
 
-size_t route_smem_bytes(int E);
 int route_grid(int T);
 cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s);
 

@@ -285,7 +285,8 @@ rmoe_status validate_desc(const rmoe_layer_desc* d) {
     return RMOE_OK;
 }
 
-static int canon_type(uint32_t t) { return (t == T_F32 || t == T_F16 || t == T_BF16) ? T_BF16 : (int)t; }
+// Device type a GGUF type is held as (unquantized experts become one fp16 plane).
+static int canon_type(uint32_t t) { return (t == T_F32 || t == T_F16 || t == T_BF16) ? T_DENSE : (int)t; }
 
 rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_count, rmoe_layer* L) {
     const uint32_t H = d->hidden, I = d->inter;
@@ -384,7 +385,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.has_shared = L->has_shared;
     rp.xb = w.xb;
     rp.rowexp = w.rowexp;
-    rp.logits_out = (flags & RMOE_FLAG_ROUTING_OUT) ? w.logits : nullptr;
+    rp.logits = w.logits;
     rp.out_zero = det ? nullptr : out;
     rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;
     rp.ticket = w.ticket; rp.expert_off = w.expert_off; rp.row_tok = w.row_tok; rp.row_slot = w.row_slot;

@@ -1,28 +1,156 @@
-// route.cu -- router GEMV + top-k + dispatch in one launch.
+// route.cu -- router logits, top-k and dispatch (expert-sorted rows + GEMM tile list).
 //
 // Router logits are bit-identical to rusty-engine's moe::matvec (src/moe.rs:271-277): each
 // logit is a sequential f32 sum over H of w*x with separate multiply and add roundings (Rust
-// never contracts), accumulated in ascending k.  The GEMV is register-tiled (32 tokens x 128
-// experts per CTA, 4x4 outputs per thread) but every output keeps that exact order.
+// never contracts), accumulated in ascending k.  Two kernels compute them:
+//   * small batches: one lane per (token, expert), streaming the expert's weight row with
+//     128-bit loads while the token's activations are broadcast across the warp;
+//   * large batches: a register-tiled product (64 tokens x 64 experts per CTA, 4 x 4 outputs
+//     per thread, cp.async double-buffered k-tiles), every output keeping the same order.
 // Top-k is rusty-engine's stable descending argsort (src/moe.rs:75-93): larger score first,
 // equal scores by lower expert index; softmax over the chosen k (src/moe.rs:61-72) or the
 // sigmoid renormalisation (src/moe.rs:97-117).
 //
-// Dispatch: each CTA counts its tokens' picks per expert and the in-CTA rank of every pick
-// in token order; the last CTA to finish (atomic ticket, no spin-wait) scans the counts and
-// writes the expert-sorted row list (ascending token order inside each expert, so the layout
-// is deterministic) and the GEMM tile list.
+// Dispatch: the top-k kernel counts each CTA's picks per expert and the in-CTA rank of every
+// pick in token order; the last CTA to finish (atomic ticket, no spin-wait) scans the counts
+// into per-(CTA, expert) offsets and writes the tile list; a scatter kernel then places every
+// (token, slot) at offset + rank, so rows are in ascending token order inside each expert.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace rmoe {
 
-static constexpr int RT_TOK = 32;   // tokens per CTA
-static constexpr int RT_EXP = 128;  // experts per register tile pass
-static constexpr int RT_K = 32;     // k-tile
-static constexpr int RT_THREADS = 256;
+static constexpr int TK_TOK = 32;  // tokens per top-k CTA
+static constexpr int TK_THREADS = 256;
 
-// Top-k of one token's E logits held in `lg` (shared or global memory), one warp.
+// ---------------------------------------------------------------------------------------
+// logits, small batches: warp = (token t, 32 experts), lane = expert
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) logits_small_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                                           int T, int H, int E, float* __restrict__ logits,
+                                                           __half* __restrict__ xb, unsigned* status) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int groups = (E + 31) / 32;
+    const int t = warp / groups, g = warp % groups;
+    if (t >= T) return;
+    const int e = g * 32 + lane;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * H);
+    const float4* wr = reinterpret_cast<const float4*>(w + (size_t)min(e, E - 1) * H);
+    float s = 0.0f;
+#pragma unroll 8
+    for (int i = 0; i < H / 4; i++) {
+        float4 xv = __ldg(xr + i);
+        float4 wv = __ldg(wr + i);
+        s = __fadd_rn(s, __fmul_rn(wv.x, xv.x));
+        s = __fadd_rn(s, __fmul_rn(wv.y, xv.y));
+        s = __fadd_rn(s, __fmul_rn(wv.z, xv.z));
+        s = __fadd_rn(s, __fmul_rn(wv.w, xv.w));
+        if (g == 0 && xb && (i & 31) == lane) {
+            // fp16 MMA operand; |x| beyond the fp16 range is reported, never silently inf
+            if (!(fabsf(xv.x) <= 65504.f && fabsf(xv.y) <= 65504.f && fabsf(xv.z) <= 65504.f &&
+                  fabsf(xv.w) <= 65504.f))
+                atomicOr(status, (unsigned)DERR_FP16_RANGE);
+            uint2 pk = make_uint2(pack_f16x2(xv.x, xv.y), pack_f16x2(xv.z, xv.w));
+            *reinterpret_cast<uint2*>(xb + (size_t)t * H + i * 4) = pk;
+        }
+    }
+    if (e < E) logits[(size_t)t * E + e] = s;
+}
+
+// ---------------------------------------------------------------------------------------
+// logits, large batches: CTA = 64 tokens x 64 experts, 256 threads, 4 x 4 outputs each
+// (thread (tx, ty) owns experts e0 + tx + 16j and tokens t0 + ty + 16i, so the 16-B shared
+// loads of one warp touch distinct banks up to a 2-way conflict)
+// ---------------------------------------------------------------------------------------
+static constexpr int LT_TOK = 64, LT_EXP = 64, LT_K = 32, LT_THREADS = 256, LT_LD = LT_K + 4;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ w, int T, int H, int E,
+                                                                  float* __restrict__ logits, __half* __restrict__ xb,
+                                                                  unsigned* status) {
+    __shared__ __align__(16) float xs[2][LT_TOK][LT_LD];
+    __shared__ __align__(16) float ws[2][LT_EXP][LT_LD];
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.x * LT_TOK, e0 = blockIdx.y * LT_EXP;
+    const int tx = tid & 15, ty = tid >> 4;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+
+    auto issue = [&](int buf, int k0) {
+        for (int q = tid; q < LT_TOK * LT_K / 4; q += LT_THREADS) {
+            int r = q / (LT_K / 4), c = (q % (LT_K / 4)) * 4;
+            cp_async16(&xs[buf][r][c], x + (size_t)min(t0 + r, T - 1) * H + k0 + c);
+            cp_async16(&ws[buf][r][c], w + (size_t)min(e0 + r, E - 1) * H + k0 + c);
+        }
+        cp_async_commit();
+    };
+    const int nk = H / LT_K;
+    issue(0, 0);
+    for (int kt = 0; kt < nk; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) {
+            issue(buf ^ 1, (kt + 1) * LT_K);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        if (blockIdx.y == 0 && xb) {  // the fp16 copy of x (GEMM operand), once per token tile
+            for (int q = tid; q < LT_TOK * LT_K; q += LT_THREADS) {
+                int r = q / LT_K, c = q % LT_K;
+                if (t0 + r < T) {
+                    float xv = xs[buf][r][c];
+                    if (!(fabsf(xv) <= 65504.0f)) atomicOr(status, (unsigned)DERR_FP16_RANGE);
+                    xb[(size_t)(t0 + r) * H + kt * LT_K + c] = __float2half_rn(xv);
+                }
+            }
+        }
+#pragma unroll 2
+        for (int kq = 0; kq < LT_K; kq += 4) {
+            float4 xv[4], wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) xv[i] = *reinterpret_cast<const float4*>(&xs[buf][ty + 16 * i][kq]);
+#pragma unroll
+            for (int j = 0; j < 4; j++) wv[j] = *reinterpret_cast<const float4*>(&ws[buf][tx + 16 * j][kq]);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float a = acc[i][j];
+                    a = __fadd_rn(a, __fmul_rn(wv[j].x, xv[i].x));
+                    a = __fadd_rn(a, __fmul_rn(wv[j].y, xv[i].y));
+                    a = __fadd_rn(a, __fmul_rn(wv[j].z, xv[i].z));
+                    a = __fadd_rn(a, __fmul_rn(wv[j].w, xv[i].w));
+                    acc[i][j] = a;
+                }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int t = t0 + ty + 16 * i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int e = e0 + tx + 16 * j;
+            if (e < E) logits[(size_t)t * E + e] = acc[i][j];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// top-k of one token's E logits (one warp)
+// ---------------------------------------------------------------------------------------
 // Order = stable descending argsort (larger first, ties to the lower index), the rusty-engine
 // top_k / top_k_sigmoid contract (src/moe.rs:75-117).  Lane j < k returns the j-th expert id;
 // lane 0 writes the k weights to w_out in chosen order.
@@ -32,9 +160,9 @@ __device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, floa
 #pragma unroll
     for (int s = 0; s < MAX_E / 32; s++) {
         int e = lane + 32 * s;
-        float x = (e < E) ? lg[e] : 0.0f;
-        if (gate == 1 && e < E) x = 1.0f / (1.0f + expf(-x));  // sigmoid (src/moe.rs:44-46)
-        v[s] = x;
+        float xv = (e < E) ? lg[e] : 0.0f;
+        if (gate == 1 && e < E) xv = 1.0f / (1.0f + expf(-xv));  // sigmoid (src/moe.rs:44-46)
+        v[s] = xv;
         if (e >= E) taken |= 1u << s;
     }
     const int NONE = 0x7fffffff;
@@ -84,88 +212,22 @@ __device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, floa
     return chosen_id;
 }
 
-__global__ void __launch_bounds__(RT_THREADS) route_dispatch_kernel(RouteParams p) {
-    __shared__ float xs[RT_K][RT_TOK + 4];
-    __shared__ __align__(16) float ws[RT_K][RT_EXP + 4];
-    extern __shared__ float dyn[];  // logits [RT_TOK][E + 1]
-    __shared__ int ids_s[RT_TOK * 32];
+// ---------------------------------------------------------------------------------------
+// top-k + counts (+ last-CTA scan and tile list)
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
+    __shared__ int ids_s[TK_TOK * MAX_K];
+    __shared__ int cnt_s[MAX_E + 2];
+    __shared__ int off_s[MAX_E + 2];
     __shared__ unsigned int ticket_s;
-
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int t0 = blockIdx.x * RT_TOK;
+    const int t0 = blockIdx.x * TK_TOK;
     const int E = p.E, H = p.H, k = p.k;
-    const int LS = E + 1;
+    const int ntok = min(TK_TOK, p.T - t0);
 
-    // ---- logits: exact sequential-order f32 sums ----
-    const int tx = tid & 31, ty = tid >> 5;  // experts 4tx..4tx+3, tokens 4ty..4ty+3
-    for (int e0 = 0; e0 < E; e0 += RT_EXP) {
-        float acc[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-        for (int k0 = 0; k0 < H; k0 += RT_K) {
-            // x tile: 32 tokens x 32 k (and the fp16 copy of x, written once when e0 == 0)
-            for (int i = tid; i < RT_TOK * RT_K; i += RT_THREADS) {
-                int tl = i / RT_K, kk = i % RT_K;
-                int t = t0 + tl;
-                float v = (t < p.T) ? p.x[(size_t)t * H + k0 + kk] : 0.0f;
-                xs[kk][tl] = v;
-                if (e0 == 0 && t < p.T && p.xb) {
-                    // fp16 MMA operand; |x| beyond the fp16 range is reported, never silently inf
-                    if (!(fabsf(v) <= 65504.0f)) atomicOr(p.status, (unsigned)DERR_FP16_RANGE);
-                    p.xb[(size_t)t * H + k0 + kk] = __float2half_rn(v);
-                }
-            }
-            // w tile: 128 experts x 32 k, transposed into ws[k][e]
-            for (int i = tid; i < RT_EXP * RT_K / 4; i += RT_THREADS) {
-                int el = i / (RT_K / 4), kq = (i % (RT_K / 4)) * 4;
-                int e = e0 + el;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (e < E) v = __ldg(reinterpret_cast<const float4*>(p.router_w + (size_t)e * H + k0 + kq));
-                ws[kq + 0][el] = v.x;
-                ws[kq + 1][el] = v.y;
-                ws[kq + 2][el] = v.z;
-                ws[kq + 3][el] = v.w;
-            }
-            __syncthreads();
-#pragma unroll 4
-            for (int kk = 0; kk < RT_K; kk++) {
-                float4 w4 = *reinterpret_cast<const float4*>(&ws[kk][tx * 4]);
-                float xv[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) xv[i] = xs[kk][ty * 4 + i];
-                float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-                for (int i = 0; i < 4; i++)
-#pragma unroll
-                    for (int j = 0; j < 4; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(wv[j], xv[i]));
-            }
-            __syncthreads();
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                int e = e0 + tx * 4 + j;
-                if (e < E) dyn[(ty * 4 + i) * LS + e] = acc[i][j];
-            }
-    }
-    __syncthreads();
-
-    // optional logits dump (tests)
-    if (p.logits_out) {
-        for (int i = tid; i < RT_TOK * E; i += RT_THREADS) {
-            int tl = i / E, e = i % E;
-            if (t0 + tl < p.T) p.logits_out[(size_t)(t0 + tl) * E + e] = dyn[tl * LS + e];
-        }
-    }
-
-    // ---- top-k per token: one warp per token ----
-    for (int tl = warp; tl < RT_TOK; tl += RT_THREADS / 32) {
+    for (int tl = warp; tl < ntok; tl += TK_THREADS / 32) {
         int t = t0 + tl;
-        if (t >= p.T) break;
-        int id = warp_topk(dyn + tl * LS, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+        int id = warp_topk(p.logits + (size_t)t * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
         if (lane < k) {
             p.topk_id[(size_t)t * k + lane] = id;
             ids_s[tl * k + lane] = id;
@@ -173,25 +235,21 @@ __global__ void __launch_bounds__(RT_THREADS) route_dispatch_kernel(RouteParams 
     }
     // zero the output rows this CTA owns when the combine accumulates with atomics
     if (p.out_zero) {
-        for (int tl = 0; tl < RT_TOK; tl++) {
-            int t = t0 + tl;
-            if (t >= p.T) break;
-            for (int i = tid * 4; i < H; i += RT_THREADS * 4)
-                *reinterpret_cast<float4*>(p.out_zero + (size_t)t * H + i) = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        for (int tl = 0; tl < ntok; tl++)
+            for (int i = tid * 4; i < H; i += TK_THREADS * 4)
+                *reinterpret_cast<float4*>(p.out_zero + (size_t)(t0 + tl) * H + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncthreads();
-
-    // ---- per-CTA counts and in-CTA ranks (token order) ----
-    const int ntok = min(RT_TOK, p.T - t0);
-    for (int e = tid; e < E; e += RT_THREADS) {
+    // in-CTA rank of every pick in token order: one thread per expert scans the CTA's
+    // TK_TOK * k picks in order
+    for (int e = tid; e < E; e += TK_THREADS) {
         int c = 0;
         for (int i = 0; i < ntok * k; i++)
             if (ids_s[i] == e) p.local_rank[(size_t)t0 * k + i] = c++;
         p.cta_cnt[(size_t)blockIdx.x * E + e] = c;
     }
 
-    // ---- last CTA: scan + expert-sorted rows + tile list ----
+    // ---- last CTA: per-(CTA, expert) offsets, expert offsets, tile list ----
     __threadfence();
     __syncthreads();
     if (tid == 0) ticket_s = atomicAdd(p.ticket, 1u);
@@ -201,10 +259,9 @@ __global__ void __launch_bounds__(RT_THREADS) route_dispatch_kernel(RouteParams 
 
     const int ncta = gridDim.x;
     const int NE = E + (p.has_shared ? 1 : 0);
-    __shared__ int off_s[MAX_E + 2];
-    __shared__ int cnt_s[MAX_E + 2];
-    for (int e = tid; e < E; e += RT_THREADS) {
+    for (int e = tid; e < E; e += TK_THREADS) {
         int c = 0;
+#pragma unroll 8
         for (int b = 0; b < ncta; b++) c += __ldcg(p.cta_cnt + (size_t)b * E + e);
         cnt_s[e] = c;
     }
@@ -228,37 +285,17 @@ __global__ void __launch_bounds__(RT_THREADS) route_dispatch_kernel(RouteParams 
         *p.n_tiles = tiles;
     }
     __syncthreads();
-    // per-(cta, expert) offsets, expert-major so rows stay in token order
-    for (int e = tid; e < E; e += RT_THREADS) {
+    // counts -> offsets in place (expert-major, CTA-minor keeps token order inside an expert)
+    for (int e = tid; e < E; e += TK_THREADS) {
         int run = off_s[e];
         for (int b = 0; b < ncta; b++) {
             int c = __ldcg(p.cta_cnt + (size_t)b * E + e);
-            p.cta_cnt[(size_t)b * E + e] = run;  // reuse as offsets
+            p.cta_cnt[(size_t)b * E + e] = run;
             run += c;
-        }
-    }
-    __syncthreads();
-    __threadfence_block();
-    const int nent = p.T * k;
-    for (int i = tid; i < nent; i += RT_THREADS) {
-        int t = i / k;
-        int e = __ldcg(p.topk_id + i);
-        int pos = __ldcg(p.cta_cnt + (size_t)(t / RT_TOK) * E + e) + __ldcg(p.local_rank + i);
-        p.row_tok[pos] = t;
-        p.row_slot[pos] = i - t * k;
-        p.slot_row[i] = pos;
-        p.rowexp[pos] = -127;
-    }
-    if (p.has_shared) {
-        for (int t = tid; t < p.T; t += RT_THREADS) {
-            p.row_tok[off_s[E] + t] = t;
-            p.row_slot[off_s[E] + t] = k;
-            p.rowexp[off_s[E] + t] = -127;
         }
     }
     // tile list: (expert, first row, rows) with at most tile_rows rows per tile
     if (tid < 32) {
-        // warp-serial over experts keeps this simple; NE <= MAX_E + 1
         int base = 0;
         for (int e = 0; e < NE; e++) {
             int c = cnt_s[e];
@@ -276,13 +313,48 @@ __global__ void __launch_bounds__(RT_THREADS) route_dispatch_kernel(RouteParams 
     if (tid == 0) *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
 }
 
-size_t route_smem_bytes(int E) { return (size_t)RT_TOK * (E + 1) * sizeof(float); }
-int route_grid(int T) { return (T + RT_TOK - 1) / RT_TOK; }
+// Place every (token, slot) at its expert-sorted row; one CTA per top-k CTA's tokens.
+__global__ void __launch_bounds__(TK_THREADS) scatter_rows_kernel(RouteParams p) {
+    const int t0 = blockIdx.x * TK_TOK, k = p.k, E = p.E;
+    const int nent = min(TK_TOK, p.T - t0) * k;
+    const int* off = p.cta_cnt + (size_t)blockIdx.x * E;
+    for (int i = threadIdx.x; i < nent; i += TK_THREADS) {
+        int gi = t0 * k + i;
+        int t = gi / k;
+        int pos = off[p.topk_id[gi]] + p.local_rank[gi];
+        p.row_tok[pos] = t;
+        p.row_slot[pos] = gi - t * k;
+        p.slot_row[gi] = pos;
+        p.rowexp[pos] = -127;
+    }
+    if (p.has_shared) {
+        const int base = p.expert_off[E];
+        for (int tl = threadIdx.x; tl < TK_TOK && t0 + tl < p.T; tl += TK_THREADS) {
+            int t = t0 + tl;
+            p.row_tok[base + t] = t;
+            p.row_slot[base + t] = k;
+            p.rowexp[base + t] = -127;
+        }
+    }
+}
+
+int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
+
+static constexpr int SMALL_T = 64;  // lane-per-logit path up to this batch
 
 cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
-    size_t smem = route_smem_bytes(p.E);
-    cudaFuncSetAttribute(route_dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    route_dispatch_kernel<<<route_grid(p.T), RT_THREADS, smem, s>>>(p);
+    if (p.T <= SMALL_T) {
+        int warps = p.T * ((p.E + 31) / 32);
+        logits_small_kernel<<<(warps + 3) / 4, 128, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+    } else {
+        dim3 grid((p.T + LT_TOK - 1) / LT_TOK, (p.E + LT_EXP - 1) / LT_EXP);
+        logits_tiled_kernel<<<grid, LT_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
     return cudaGetLastError();
 }
 
