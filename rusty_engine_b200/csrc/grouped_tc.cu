@@ -1,0 +1,571 @@
+// grouped_tc.cu -- tensor-core (tcgen05) grouped expert products for large batches (prefill).
+//
+// One CTA computes a 128-feature block of one expert for a tile of <= 128 expert-sorted rows:
+//   gate/up: h[row, f] = silu(gate_f . x_row) * (up_f . x_row)   (src/moe.rs:280-299)
+//   down:    out[tok] += w_slot * (down . h_row)                  (src/moe.rs:373-380)
+//
+// Warp roles (one CTA per SM, everything stream-ordered through mbarriers):
+//   warp 0      bulk-copies the raw GGUF bytes of the CTA's weight rows into a shared ring,
+//               one 256-element superblock (or 8 blocks of 32) per stage;
+//   warp 1      allocates tensor memory and issues tcgen05.mma (one elected thread): A is the
+//               dequantized weight tile held in TMEM, B the token tile in shared memory;
+//   warps 2-3   gather the token rows (fp16) into 128-B-swizzled shared tiles with cp.async;
+//   warps 4..   one thread per weight row decodes 64 K-elements of its row per stage from the
+//               raw ring (bit-identical f32 values to quant::dequant, rounded to fp16) and
+//               stores them into its TMEM lane with tcgen05.st; after the last stage the same
+//               warps drain the f32 accumulators from TMEM and run the epilogue.
+// The fp16 weights never touch shared memory; shared memory carries the raw bytes and the
+// token tiles only.  Every wait is bounded: on a timeout the kernel records DERR_TIMEOUT in the
+// status word, skips the remaining work, waits for its own MMAs and frees its tensor memory.
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_ptx.cuh"
+
+namespace rmoe {
+using namespace tc;
+
+static constexpr int TC_M = 128;   // weight rows per matrix per CTA (= TMEM lanes)
+static constexpr int TC_BN = 128;  // expert-sorted rows per tile (MMA N, rounded to 16 per tile)
+static constexpr int TC_KS = 64;   // K elements per MMA stage (one 128-B swizzle row of fp16)
+static constexpr int TC_NST = 4;   // MMA stages in flight
+static constexpr int TC_RST = 2;   // raw weight stages in flight
+static constexpr int TC_BLOOK = 2; // token-tile copies kept in flight per loader thread
+
+int tc_tile_rows() { return TC_BN; }
+
+// Raw-stage geometry: RK K-elements per stage; BYTES copied per row; STRIDE = shared pitch
+// (an odd number of 16-B units, so 16-B loads of 8 consecutive rows hit distinct banks).
+template <int TYPE> struct Raw;
+template <> struct Raw<T_Q4_K> { static constexpr int RK = 256, BYTES = 144, STRIDE = 144; };
+template <> struct Raw<T_Q5_K> { static constexpr int RK = 256, BYTES = 176, STRIDE = 176; };
+template <> struct Raw<T_Q6_K> { static constexpr int RK = 256, BYTES = 208, STRIDE = 208; };
+template <> struct Raw<T_Q4_0> { static constexpr int RK = 256, BYTES = 144, STRIDE = 144; };
+template <> struct Raw<T_Q5_0> { static constexpr int RK = 256, BYTES = 176, STRIDE = 176; };
+template <> struct Raw<T_Q8_0> { static constexpr int RK = 256, BYTES = 272, STRIDE = 272; };
+template <> struct Raw<T_DENSE> { static constexpr int RK = 128, BYTES = 256, STRIDE = 272; };
+
+// Copy raw stage j of global row `grow` (all planes) to shared address dst.
+template <int TYPE>
+__device__ __forceinline__ void raw_copy(const DevMat& M, uint64_t grow, int j, uint32_t dst, uint32_t bar) {
+    const uint8_t* rowp = M.main + grow * M.main_stride;
+    const uint64_t blk0 = grow * M.dstride + (uint64_t)j * 8;  // first 32-element block (32-formats)
+    if constexpr (TYPE == T_Q4_K) bulk_g2s(dst, rowp + (uint64_t)j * 144, 144, bar);
+    if constexpr (TYPE == T_Q5_K) bulk_g2s(dst, rowp + (uint64_t)j * 176, 176, bar);
+    if constexpr (TYPE == T_Q6_K) bulk_g2s(dst, rowp + (uint64_t)j * 208, 208, bar);
+    if constexpr (TYPE == T_Q4_0) {
+        bulk_g2s(dst, rowp + (uint64_t)j * 128, 128, bar);
+        bulk_g2s(dst + 128, reinterpret_cast<const uint8_t*>(M.dpl) + blk0 * 2, 16, bar);
+    }
+    if constexpr (TYPE == T_Q5_0) {
+        bulk_g2s(dst, rowp + (uint64_t)j * 128, 128, bar);
+        bulk_g2s(dst + 128, reinterpret_cast<const uint8_t*>(M.aux) + blk0 * 4, 32, bar);
+        bulk_g2s(dst + 160, reinterpret_cast<const uint8_t*>(M.dpl) + blk0 * 2, 16, bar);
+    }
+    if constexpr (TYPE == T_Q8_0) {
+        bulk_g2s(dst, rowp + (uint64_t)j * 256, 256, bar);
+        bulk_g2s(dst + 256, reinterpret_cast<const uint8_t*>(M.dpl) + blk0 * 2, 16, bar);
+    }
+    if constexpr (TYPE == T_DENSE) bulk_g2s(dst, rowp + (uint64_t)j * 256, 256, bar);
+}
+
+__device__ __forceinline__ float nib(uint32_t w, int sh) { return (float)((w >> sh) & 0xFu); }
+
+// Decode K-elements [64*sub, 64*sub + 64) of one raw row into 32 packed fp16 pairs (k, k+1).
+template <int TYPE>
+__device__ __forceinline__ void slice64(const uint8_t* p, int sub, float q6d, uint32_t* v);
+
+template <>
+__device__ __forceinline__ void slice64<T_Q4_K>(const uint8_t* p, int sub, float, uint32_t* v) {
+    uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
+    float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
+    int sc0, m0, sc1, m1;
+    scale_min_k4(2 * sub, p + 4, sc0, m0);
+    scale_min_k4(2 * sub + 1, p + 4, sc1, m1);
+    const float d1 = __fmul_rn(d, (float)sc0), dm1 = __fmul_rn(dmin, (float)m0);
+    const float d2 = __fmul_rn(d, (float)sc1), dm2 = __fmul_rn(dmin, (float)m1);
+    const uint4* q = reinterpret_cast<const uint4*>(p + 16 + sub * 32);
+    uint4 a = q[0], b = q[1];
+    uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        auto lo = [&](int sh) { return __fsub_rn(__fmul_rn(d1, nib(w[i], sh)), dm1); };
+        auto hi = [&](int sh) { return __fsub_rn(__fmul_rn(d2, nib(w[i], sh)), dm2); };
+        v[2 * i] = pack_f16x2(lo(0), lo(8));
+        v[2 * i + 1] = pack_f16x2(lo(16), lo(24));
+        v[16 + 2 * i] = pack_f16x2(hi(4), hi(12));
+        v[16 + 2 * i + 1] = pack_f16x2(hi(20), hi(28));
+    }
+}
+
+template <>
+__device__ __forceinline__ void slice64<T_Q5_K>(const uint8_t* p, int sub, float, uint32_t* v) {
+    uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
+    float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
+    int sc0, m0, sc1, m1;
+    scale_min_k4(2 * sub, p + 4, sc0, m0);
+    scale_min_k4(2 * sub + 1, p + 4, sc1, m1);
+    const float d1 = __fmul_rn(d, (float)sc0), dm1 = __fmul_rn(dmin, (float)m0);
+    const float d2 = __fmul_rn(d, (float)sc1), dm2 = __fmul_rn(dmin, (float)m1);
+    const uint4* q = reinterpret_cast<const uint4*>(p + 48 + sub * 32);
+    const uint4* hq = reinterpret_cast<const uint4*>(p + 16);
+    uint4 a = q[0], b = q[1], ha = hq[0], hb = hq[1];
+    uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+    const int ul = 2 * sub, uh = 2 * sub + 1;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        auto lo = [&](int byte) {
+            float qv = (float)(((w[i] >> (8 * byte)) & 0xFu) + (((hw[i] >> (8 * byte + ul)) & 1u) << 4));
+            return __fsub_rn(__fmul_rn(d1, qv), dm1);
+        };
+        auto hi = [&](int byte) {
+            float qv = (float)(((w[i] >> (8 * byte + 4)) & 0xFu) + (((hw[i] >> (8 * byte + uh)) & 1u) << 4));
+            return __fsub_rn(__fmul_rn(d2, qv), dm2);
+        };
+        v[2 * i] = pack_f16x2(lo(0), lo(1));
+        v[2 * i + 1] = pack_f16x2(lo(2), lo(3));
+        v[16 + 2 * i] = pack_f16x2(hi(0), hi(1));
+        v[16 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
+    }
+}
+
+// Q6_K raw row: ql[128] | qh[64] | scales[16]; d comes from the d plane (q6d).
+template <>
+__device__ __forceinline__ void slice64<T_Q6_K>(const uint8_t* p, int sub, float q6d, uint32_t* v) {
+    const int h = sub >> 1, odd = sub & 1;
+    const uint4* ql = reinterpret_cast<const uint4*>(p + h * 64);
+    const uint4* qh = reinterpret_cast<const uint4*>(p + 128 + h * 32);
+    uint4 l0 = ql[0], l1 = ql[1], l2 = ql[2], l3 = ql[3], h0 = qh[0], h1 = qh[1];
+    uint32_t la[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};  // ql[h*64 + l], l < 32
+    uint32_t lb[8] = {l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};  // ql[h*64 + 32 + l]
+    uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const int8_t* sc = reinterpret_cast<const int8_t*>(p + 192 + h * 8);
+    const int qa = 2 * odd, qb = 2 * odd + 1;  // quadrants of this slice
+    const int nsh = 4 * odd;                   // low nibbles for quadrants 0/1, high for 2/3
+    const float sa0 = __fmul_rn(q6d, (float)sc[qa * 2]), sa1 = __fmul_rn(q6d, (float)sc[qa * 2 + 1]);
+    const float sb0 = __fmul_rn(q6d, (float)sc[qb * 2]), sb1 = __fmul_rn(q6d, (float)sc[qb * 2 + 1]);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {  // l = 4i .. 4i+3
+        const float sa = (i < 4) ? sa0 : sa1, sb = (i < 4) ? sb0 : sb1;
+        auto va = [&](int byte) {
+            int q = (int)(((la[i] >> (8 * byte + nsh)) & 0xFu) | (((hw[i] >> (8 * byte + 2 * qa)) & 3u) << 4)) - 32;
+            return __fmul_rn(sa, (float)q);
+        };
+        auto vb = [&](int byte) {
+            int q = (int)(((lb[i] >> (8 * byte + nsh)) & 0xFu) | (((hw[i] >> (8 * byte + 2 * qb)) & 3u) << 4)) - 32;
+            return __fmul_rn(sb, (float)q);
+        };
+        v[2 * i] = pack_f16x2(va(0), va(1));
+        v[2 * i + 1] = pack_f16x2(va(2), va(3));
+        v[16 + 2 * i] = pack_f16x2(vb(0), vb(1));
+        v[16 + 2 * i + 1] = pack_f16x2(vb(2), vb(3));
+    }
+}
+
+// Q4_0 raw row: qs[8 x 16] | d[8 x f16]; slice = blocks 2*sub, 2*sub+1.
+template <>
+__device__ __forceinline__ void slice64<T_Q4_0>(const uint8_t* p, int sub, float, uint32_t* v) {
+#pragma unroll
+    for (int bb = 0; bb < 2; bb++) {
+        const int b = 2 * sub + bb;
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(p + 128 + 2 * b));
+        uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            auto lo = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte)) & 0xFu) - 8), d); };
+            auto hi = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte + 4)) & 0xFu) - 8), d); };
+            v[16 * bb + 2 * i] = pack_f16x2(lo(0), lo(1));
+            v[16 * bb + 2 * i + 1] = pack_f16x2(lo(2), lo(3));
+            v[16 * bb + 8 + 2 * i] = pack_f16x2(hi(0), hi(1));
+            v[16 * bb + 8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
+        }
+    }
+}
+
+// Q5_0 raw row: qs[8 x 16] | qh[8 x u32] | d[8 x f16].
+template <>
+__device__ __forceinline__ void slice64<T_Q5_0>(const uint8_t* p, int sub, float, uint32_t* v) {
+#pragma unroll
+    for (int bb = 0; bb < 2; bb++) {
+        const int b = 2 * sub + bb;
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(p + 160 + 2 * b));
+        const uint32_t qh = *reinterpret_cast<const uint32_t*>(p + 128 + 4 * b);
+        uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
+        uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            auto lo = [&](int byte) {
+                int j = 4 * i + byte;
+                int x = (int)(((w[i] >> (8 * byte)) & 0xFu) | (((qh >> j) & 1u) << 4)) - 16;
+                return __fmul_rn((float)x, d);
+            };
+            auto hi = [&](int byte) {
+                int j = 4 * i + byte;
+                int x = (int)(((w[i] >> (8 * byte + 4)) & 0xFu) | (((qh >> (j + 16)) & 1u) << 4)) - 16;
+                return __fmul_rn((float)x, d);
+            };
+            v[16 * bb + 2 * i] = pack_f16x2(lo(0), lo(1));
+            v[16 * bb + 2 * i + 1] = pack_f16x2(lo(2), lo(3));
+            v[16 * bb + 8 + 2 * i] = pack_f16x2(hi(0), hi(1));
+            v[16 * bb + 8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
+        }
+    }
+}
+
+// Q8_0 raw row: qs[8 x 32] | d[8 x f16].
+template <>
+__device__ __forceinline__ void slice64<T_Q8_0>(const uint8_t* p, int sub, float, uint32_t* v) {
+#pragma unroll
+    for (int bb = 0; bb < 2; bb++) {
+        const int b = 2 * sub + bb;
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(p + 256 + 2 * b));
+        const uint4* q = reinterpret_cast<const uint4*>(p + 32 * b);
+        uint4 a = q[0], c = q[1];
+        uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {  // word i holds elements 4i..4i+3 of the block
+            auto val = [&](int byte) { return __fmul_rn((float)(int8_t)((w[i] >> (8 * byte)) & 0xFFu), d); };
+            v[16 * bb + 2 * i] = pack_f16x2(val(0), val(1));
+            v[16 * bb + 2 * i + 1] = pack_f16x2(val(2), val(3));
+        }
+    }
+}
+
+template <>
+__device__ __forceinline__ void slice64<T_DENSE>(const uint8_t* p, int sub, float, uint32_t* v) {
+    const uint4* q = reinterpret_cast<const uint4*>(p + 128 * sub);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        uint4 a = q[i];
+        v[4 * i] = a.x;
+        v[4 * i + 1] = a.y;
+        v[4 * i + 2] = a.z;
+        v[4 * i + 3] = a.w;
+    }
+}
+
+template <int TYPE, int NMAT>
+struct TcGeom {
+    static constexpr int B_STAGE = TC_BN * 128;  // bytes per token tile stage
+    static constexpr int RAW_STAGE = NMAT * TC_M * Raw<TYPE>::STRIDE;
+    static constexpr int SMEM = TC_NST * B_STAGE + TC_RST * RAW_STAGE + 1024;
+    static constexpr int THREADS = 32 * (4 + 4 * NMAT);
+    static constexpr uint32_t TMEM_COLS = NMAT == 2 ? 512 : 256;
+    static constexpr int A_COL0 = NMAT * TC_BN;  // A ring after the accumulators
+};
+
+template <int TYPE, int NMAT>
+__global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(GroupedParams p) {
+    using G = TcGeom<TYPE, NMAT>;
+    constexpr int RK = Raw<TYPE>::RK, RSTRIDE = Raw<TYPE>::STRIDE, SUBS = RK / TC_KS;
+    extern __shared__ uint8_t dsmem[];
+    __shared__ __align__(8) uint64_t bar_raw_full[TC_RST], bar_raw_empty[TC_RST];
+    __shared__ __align__(8) uint64_t bar_a_full[TC_NST], bar_b_full[TC_NST], bar_empty[TC_NST], bar_acc;
+    __shared__ uint32_t tmem_holder;
+    __shared__ int s_tok[TC_BN], s_rexp[TC_BN];
+    __shared__ float s_w[TC_BN];
+    __shared__ volatile int s_abort;
+
+    const int tile = blockIdx.y;
+    if (tile >= *p.n_tiles) return;  // uniform exit before any barrier or TMEM use
+    const int4 ti = p.tiles[tile];
+    const int e = ti.x, row0 = ti.y, nrows = ti.z;
+    const int n_eff = (nrows + 15) & ~15;
+    const int fb = blockIdx.x;
+    const bool shared_e = e >= p.E;
+    const DevMat& M0 = NMAT == 2 ? (shared_e ? p.sgate : p.gate) : (shared_e ? p.sdown : p.down);
+    const DevMat& M1 = shared_e ? p.sup : p.up;
+    const uint64_t grow0 = (uint64_t)(shared_e ? 0 : e) * M0.rows + (uint64_t)fb * TC_M;
+    const int K = NMAT == 2 ? p.H : p.I;
+    const int nk = K / TC_KS, nraw = K / RK;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const uint32_t sbase = (smem_u32(dsmem) + 1023u) & ~1023u;  // 1024-B aligned (SW128 atoms)
+    uint8_t* gbase = dsmem + (sbase - smem_u32(dsmem));
+    const uint32_t bring = sbase, rawring = sbase + TC_NST * G::B_STAGE;
+    uint8_t* raw_g = gbase + TC_NST * G::B_STAGE;
+
+    if (tid == 0) {
+        for (int i = 0; i < TC_RST; i++) {
+            mbar_init(smem_u32(&bar_raw_full[i]), 1);
+            mbar_init(smem_u32(&bar_raw_empty[i]), 4 * NMAT);
+        }
+        for (int i = 0; i < TC_NST; i++) {
+            mbar_init(smem_u32(&bar_a_full[i]), 4 * NMAT);
+            mbar_init(smem_u32(&bar_b_full[i]), 64);
+            mbar_init(smem_u32(&bar_empty[i]), 1);
+        }
+        mbar_init(smem_u32(&bar_acc), 1);
+        s_abort = 0;
+        fence_mbar_init();
+    }
+    for (int n = tid; n < TC_BN; n += G::THREADS) {
+        int tok = 0, rexp = 0;
+        float w = 0.0f;
+        if (n < nrows) {
+            const int r = row0 + n;
+            tok = __ldg(p.row_tok + r);
+            const int slot = __ldg(p.row_slot + r);
+            w = (slot < p.k) ? __ldg(p.topk_w + (size_t)tok * p.k + slot) : 1.0f;
+            if (NMAT == 1) rexp = __ldg(p.rowexp + r);
+        }
+        s_tok[n] = tok;
+        s_w[n] = w;
+        s_rexp[n] = rexp;
+    }
+    if (warp == 1) tmem_alloc(smem_u32(&tmem_holder), G::TMEM_COLS);
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tbase = tmem_holder;
+
+    auto fail = [&]() {
+        s_abort = 1;
+        atomicOr(p.status, (unsigned)DERR_TIMEOUT);
+    };
+
+    if (warp == 0) {
+        // ---------------- raw weight producer ----------------
+        for (int j = 0; j < nraw; j++) {
+            const int s = j % TC_RST;
+            if (s_abort) break;
+            if (j >= TC_RST && !mbar_wait(smem_u32(&bar_raw_empty[s]), ((j / TC_RST) + 1) & 1)) {
+                fail();
+                break;
+            }
+            const uint32_t bar = smem_u32(&bar_raw_full[s]);
+            if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(NMAT * TC_M * Raw<TYPE>::BYTES));
+            __syncwarp();
+            for (int r = lane; r < TC_M; r += 32) {
+                raw_copy<TYPE>(M0, grow0 + r, j, rawring + (uint32_t)((s * NMAT + 0) * TC_M + r) * RSTRIDE, bar);
+                if (NMAT == 2)
+                    raw_copy<TYPE>(M1, grow0 + r, j, rawring + (uint32_t)((s * NMAT + 1) * TC_M + r) * RSTRIDE, bar);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(TC_M, n_eff);
+            for (int kt = 0; kt < nk; kt++) {
+                const int s = kt % TC_NST;
+                const uint32_t ph = (kt / TC_NST) & 1;
+                if (s_abort) break;
+                if (!mbar_wait(smem_u32(&bar_a_full[s]), ph) || !mbar_wait(smem_u32(&bar_b_full[s]), ph)) {
+                    fail();
+                    break;
+                }
+                fence_after_sync();
+                const uint32_t bst = bring + (uint32_t)s * G::B_STAGE;
+#pragma unroll
+                for (int m = 0; m < NMAT; m++)
+#pragma unroll
+                    for (int ks = 0; ks < TC_KS / 16; ks++)
+                        mma_ts(tbase + (uint32_t)(m * TC_BN), tbase + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32 + ks * 8),
+                               smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
+                mma_commit(smem_u32(&bar_empty[s]));
+            }
+            mma_commit(smem_u32(&bar_acc));  // also fires when aborted: every issued MMA has finished
+        }
+        __syncwarp();
+    } else if (warp < 4) {
+        // ---------------- token-tile loaders (64 threads, cp.async 16 B) ----------------
+        const int bt = tid - 64;
+        const int nblk = p.I / HBLK;
+        auto finish = [&](int st) {
+            if (NMAT == 1) {
+                // bring every h block of the stage to its row's common scale 2^rowexp
+                const uint32_t bst = bring + (uint32_t)(st % TC_NST) * G::B_STAGE;
+                for (int q = bt; q < nrows * 8; q += 64) {
+                    const int n = q >> 3, c = q & 7;
+                    const int dexp = (int)__ldg(p.hexp + (size_t)(row0 + n) * nblk + st) - s_rexp[n];
+                    if (dexp != 0) {
+                        uint8_t* ptr = gbase + (bst - sbase) + n * 128 + ((c ^ (n & 7)) << 4);
+                        uint4 v = *reinterpret_cast<uint4*>(ptr);
+                        float sc = dexp < -40 ? 0.0f : exp2i(dexp);
+                        uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            float2 f = __half22float2(*reinterpret_cast<__half2*>(&w4[i]));
+                            w4[i] = pack_f16x2(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc));
+                        }
+                        *reinterpret_cast<uint4*>(ptr) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+                }
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(smem_u32(&bar_b_full[st % TC_NST]));
+        };
+        int done = 0;
+        for (int kt = 0; kt < nk; kt++) {
+            const int s = kt % TC_NST;
+            if (s_abort) break;
+            if (kt >= TC_NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / TC_NST) + 1) & 1)) {
+                fail();
+                break;
+            }
+            const uint32_t bst = bring + (uint32_t)s * G::B_STAGE;
+            for (int q = bt; q < nrows * 8; q += 64) {
+                const int n = q >> 3, c = q & 7;
+                const __half* src = (NMAT == 2) ? p.xb + (size_t)s_tok[n] * p.H + kt * TC_KS + c * 8
+                                                : p.h + (size_t)(row0 + n) * p.I + kt * TC_KS + c * 8;
+                cp_async16(bst + (uint32_t)(n * 128 + ((c ^ (n & 7)) << 4)), src);
+            }
+            cp_async_commit();
+            if (kt >= TC_BLOOK) {
+                cp_async_wait<TC_BLOOK>();
+                finish(done++);
+            }
+        }
+        cp_async_wait<0>();
+        if (!s_abort)
+            while (done < nk) finish(done++);
+    } else {
+        // ---------------- converters: one thread per weight row ----------------
+        const int cw = warp - 4, m = cw >> 2, q = warp & 3;
+        const int r = q * 32 + lane;
+        const DevMat& Mm = (m == 0) ? M0 : M1;
+        const uint64_t grow = grow0 + r;
+        const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
+        float q6d = 0.0f;
+        bool ok = true;
+        for (int kt = 0; kt < nk && ok; kt++) {
+            const int j = kt / SUBS, sub = kt % SUBS, s = kt % TC_NST;
+            if (s_abort) { ok = false; break; }
+            if (sub == 0) {
+                if (!mbar_wait(smem_u32(&bar_raw_full[j % TC_RST]), (j / TC_RST) & 1)) { fail(); ok = false; break; }
+                if (TYPE == T_Q6_K) q6d = __half2float(Mm.dpl[grow * Mm.dstride + j]);
+            }
+            if (kt >= TC_NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / TC_NST) + 1) & 1)) {
+                fail();
+                ok = false;
+                break;
+            }
+            const uint8_t* rp = raw_g + (size_t)(((j % TC_RST) * NMAT + m) * TC_M + r) * RSTRIDE;
+            uint32_t v[32];
+            slice64<TYPE>(rp, sub, q6d, v);
+            tmem_st32(tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32), v);
+            tmem_st_wait();
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[s]));
+            if (sub == SUBS - 1) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % TC_RST]));
+            }
+        }
+        // ---------------- epilogue ----------------
+        const bool acc_ok = mbar_wait(smem_u32(&bar_acc), 0);
+        if (!acc_ok) fail();
+        fence_after_sync();
+        const bool work = acc_ok && !s_abort;
+        if (NMAT == 2) {
+            // SwiGLU in f32 into a shared staging tile hs[n][f] (the rings are free now)
+            float* hs = reinterpret_cast<float*>(gbase);
+            constexpr int HLD = TC_M + 1;
+            for (int c = 2 * m; c < 2 * m + 2; c++) {
+                if (c * 32 >= n_eff) break;
+                uint32_t g[32], u[32];
+                tmem_ld32(tlane + (uint32_t)(c * 32), g);
+                tmem_ld32(tlane + (uint32_t)(TC_BN + c * 32), u);
+                tmem_ld_wait();
+                if (work) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
+                        hs[(c * 32 + i) * HLD + r] = silu_ref(gv) * uv;
+                    }
+                }
+            }
+            asm volatile("bar.sync 1, %0;\n" ::"n"(32 * 4 * NMAT) : "memory");
+            if (work) {
+                // per (row, 64-feature block): exponent, fp16 values, block/row exponents
+                const int nblk = p.I / HBLK;
+                const int ct = tid - 128;
+                for (int pi = ct; pi < nrows * 2; pi += 32 * 4 * NMAT) {
+                    const int n = pi >> 1, blk = pi & 1;
+                    const float* src = hs + n * HLD + blk * 64;
+                    float amax = 0.0f;
+#pragma unroll 8
+                    for (int i = 0; i < 64; i++) amax = fmaxf(amax, fabsf(src[i]));
+                    int ex = -127;
+                    if (amax > 0.0f) {
+                        int e2;
+                        frexpf(amax, &e2);
+                        ex = max(-100, min(100, e2 - 14));
+                    }
+                    const float sc = exp2i(-ex);
+                    const size_t rr = (size_t)(row0 + n);
+                    uint4* dst = reinterpret_cast<uint4*>(p.h + rr * p.I + fb * TC_M + blk * 64);
+#pragma unroll
+                    for (int j2 = 0; j2 < 8; j2++) {
+                        const float* s8 = src + 8 * j2;
+                        dst[j2] = make_uint4(pack_f16x2(__fmul_rn(s8[0], sc), __fmul_rn(s8[1], sc)),
+                                             pack_f16x2(__fmul_rn(s8[2], sc), __fmul_rn(s8[3], sc)),
+                                             pack_f16x2(__fmul_rn(s8[4], sc), __fmul_rn(s8[5], sc)),
+                                             pack_f16x2(__fmul_rn(s8[6], sc), __fmul_rn(s8[7], sc)));
+                    }
+                    p.hexp[rr * nblk + fb * 2 + blk] = (int8_t)ex;
+                    atomicMax(p.rowexp + rr, ex);
+                }
+            }
+        } else {
+            const int f = fb * TC_M + r;
+            for (int c = 0; c * 32 < n_eff; c++) {
+                uint32_t a[32];
+                tmem_ld32(tlane + (uint32_t)(c * 32), a);
+                tmem_ld_wait();
+                if (!work) continue;
+#pragma unroll 4
+                for (int i = 0; i < 32; i++) {
+                    const int n = c * 32 + i;
+                    if (n >= nrows) break;
+                    const float yv = __fmul_rn(__uint_as_float(a[i]), exp2i(s_rexp[n]));
+                    if (p.y) p.y[(size_t)(row0 + n) * p.H + f] = yv;
+                    else atomicAdd(p.out + (size_t)s_tok[n] * p.H + f, __fmul_rn(s_w[n], yv));
+                }
+            }
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after_sync();
+        tmem_dealloc(tbase, G::TMEM_COLS);
+    }
+}
+
+template <int TYPE, int NMAT>
+static cudaError_t go_tc(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+    using G = TcGeom<TYPE, NMAT>;
+    auto k = tc_grouped_kernel<TYPE, NMAT>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+    if (e != cudaSuccess) return e;
+    dim3 grid((NMAT == 2 ? p.I : p.H) / TC_M, max_tiles);
+    k<<<grid, G::THREADS, G::SMEM, s>>>(p);
+    return cudaGetLastError();
+}
+
+#define RMOE_TC_SWITCH(T, ...)                                     \
+    switch (T) {                                                   \
+        case T_Q4_0: { constexpr int TT = T_Q4_0; __VA_ARGS__; }   \
+        case T_Q5_0: { constexpr int TT = T_Q5_0; __VA_ARGS__; }   \
+        case T_Q8_0: { constexpr int TT = T_Q8_0; __VA_ARGS__; }   \
+        case T_Q4_K: { constexpr int TT = T_Q4_K; __VA_ARGS__; }   \
+        case T_Q5_K: { constexpr int TT = T_Q5_K; __VA_ARGS__; }   \
+        case T_Q6_K: { constexpr int TT = T_Q6_K; __VA_ARGS__; }   \
+        case T_DENSE: { constexpr int TT = T_DENSE; __VA_ARGS__; } \
+        default: return cudaErrorInvalidValue;                     \
+    }
+
+cudaError_t launch_tc_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+    if (max_tiles <= 0) return cudaSuccess;
+    RMOE_TC_SWITCH(p.gate.type, return go_tc<TT, 2>(p, max_tiles, s))
+}
+
+cudaError_t launch_tc_down(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+    if (max_tiles <= 0) return cudaSuccess;
+    RMOE_TC_SWITCH(p.down.type, return go_tc<TT, 1>(p, max_tiles, s))
+}
+
+}  // namespace rmoe

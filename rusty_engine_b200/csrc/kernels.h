@@ -72,6 +72,11 @@ int small_tile_rows();
 cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s);
 cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, cudaStream_t s);
 
+// large-batch (tcgen05) grouped kernels; tile_rows = rows per tile
+int tc_tile_rows();
+cudaError_t launch_tc_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s);
+cudaError_t launch_tc_down(const GroupedParams& p, int max_tiles, cudaStream_t s);
+
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_dequant_raw(int type, const void* src, uint64_t nblocks, float* dst, cudaStream_t s);
 cudaError_t launch_route_only(const float* logits, int T, int E, int k, int gate, int* ids, float* w, cudaStream_t s);

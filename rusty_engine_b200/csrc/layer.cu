@@ -390,7 +390,15 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;
     rp.ticket = w.ticket; rp.expert_off = w.expert_off; rp.row_tok = w.row_tok; rp.row_slot = w.row_slot;
     rp.slot_row = w.slot_row; rp.n_rows = w.n_rows; rp.tiles = w.tiles; rp.n_tiles = w.n_tiles;
-    rp.max_tiles = L->max_tiles; rp.tile_rows = small_tile_rows(); rp.status = w.status;
+    // Large batches (>= 32 routed rows per expert on average) run the tcgen05 kernels, small
+    // ones the bandwidth-bound mma.sync kernels; the flags force either path.
+    bool use_tc = (uint64_t)T * L->k >= 32ull * L->E;
+    if (flags & RMOE_FLAG_FORCE_SMALL) use_tc = false;
+    if (flags & RMOE_FLAG_FORCE_LARGE) use_tc = true;
+    const int tile_rows = use_tc ? tc_tile_rows() : small_tile_rows();
+    const uint64_t rows_T = (uint64_t)T * L->k + (L->has_shared ? T : 0);
+    const int max_tiles = (int)std::min<uint64_t>((uint64_t)L->max_tiles, rows_T / tile_rows + L->E + 2);
+    rp.max_tiles = max_tiles; rp.tile_rows = tile_rows; rp.status = w.status;
     const bool timing = flags & RMOE_FLAG_STAGE_TIMING;
     if (timing && !L->ev[0])
         for (auto& ev : L->ev) cudaEventCreate(&ev);
@@ -408,9 +416,12 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     gp.H = (int)L->H; gp.I = (int)L->I; gp.E = (int)L->E; gp.k = (int)L->k;
     gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
     gp.topk_w = w.topk_w; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp; gp.y = det ? w.y : nullptr; gp.out = out; gp.status = w.status;
-    if ((e = launch_small_gateup(gp, L->max_tiles, s)) != cudaSuccess) return cuda_fail(e, "gate/up launch");
+    e = use_tc ? launch_tc_gateup(gp, max_tiles, s) : launch_small_gateup(gp, max_tiles, s);
+    if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
     mark(2);
-    if ((e = launch_small_down(gp, L->max_tiles, s)) != cudaSuccess) return cuda_fail(e, "down launch");
+    e = use_tc ? launch_tc_down(gp, max_tiles, s) : launch_small_down(gp, max_tiles, s);
+    if (e != cudaSuccess) return cuda_fail(e, "down launch");
+    L->last_tc = use_tc;
     mark(3);
     if (det) {
         CombineParams cp{};

@@ -68,6 +68,7 @@ struct rmoe_layer {
     bool ws_had_y = false;
     int max_tiles = 0;
     uint32_t last_T = 0;
+    bool last_tc = false;  // the last forward ran the tcgen05 kernels
     cudaEvent_t ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     bool ev_valid = false, ev_combine = false;
     ~rmoe_layer() {

@@ -168,14 +168,29 @@ def test_ragged_token_counts(torch_cuda, T):
     assert_layer_close(got["out"], out, f"T={T}")
 
 
+PATHS = {"mma_sync": _lib.FLAG_FORCE_SMALL, "tcgen05": _lib.FLAG_FORCE_LARGE}
+
+
+@pytest.mark.parametrize("path", sorted(PATHS))
 @pytest.mark.parametrize("gt,dt", [(2, 2), (6, 6), (8, 8), (12, 14), (13, 13), (14, 14), (12, 12), (0, 0)])
-def test_formats_small_layer(torch_cuda, gt, dt):
+def test_formats_small_layer(torch_cuda, gt, dt, path):
     lw = synth.make_layer(512, 256, 8, 2, gate_t=gt, up_t=gt, down_t=dt, dlo=0.002, dhi=0.02, seed=gt * 16 + dt)
     x = synth.activations(40, lw.H, seed=7)
-    got = run_layer(torch_cuda, lw, x)
+    got = run_layer(torch_cuda, lw, x, flags=PATHS[path])
     out, ids, w, _ = O.moe_layer_q_exact(x, lw)
     assert np.array_equal(got["ids"], ids)
-    assert_layer_close(got["out"], out, f"types {gt}/{dt}")
+    assert_layer_close(got["out"], out, f"types {gt}/{dt} {path}")
+
+
+@pytest.mark.parametrize("path", sorted(PATHS))
+def test_c1_both_paths(torch_cuda, path):
+    """Config 1 through each expert-product path, atomic and deterministic combine."""
+    lw = synth.config_c1()
+    x = synth.activations(128, lw.H)
+    want = O.moe_layer_q_exact(x, lw)[0]
+    for det in (0, _lib.FLAG_DETERMINISTIC):
+        got = run_layer(torch_cuda, lw, x, flags=PATHS[path] | det, routing=False)["out"]
+        assert_layer_close(got, want, f"c1 {path} det={det}")
 
 
 def test_sigmoid_gate_and_shared_expert(torch_cuda):
