@@ -71,7 +71,7 @@ def build(verbose: bool = False, jobs: int = 8) -> str:
                 print(log, file=sys.stderr)
     objs = [o for o, _ in results]
     if not os.path.exists(OUT) or os.path.getmtime(OUT) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc] + ARCH + ["-shared", "-o", OUT] + objs + link_nccl + ["-lcuda"]
+        cmd = [nvcc] + ARCH + ["-shared", "-o", OUT] + objs + link_nccl
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")

@@ -41,7 +41,8 @@ struct DevMat {
     const uint32_t* aux;   // Q5_0 qh plane (else null)
     const __half* dpl;     // block-scale plane (Q4_0/Q5_0/Q8_0/Q6_K; else null)
     uint64_t main_stride;  // bytes per row in the main plane
-    uint32_t dstride;      // halves per row in the d plane (= blocks per row)
+    uint32_t dstride;      // blocks per row (d / aux planes)
+    uint64_t trows;        // rows in the whole stack (experts x rows); d / aux planes are [block][trows]
     uint32_t rows;         // rows per expert
     uint32_t K;            // elements per row (multiple of 256)
     int32_t type;
@@ -145,7 +146,7 @@ __device__ __forceinline__ uint4 chunk8<T_Q6_K>(const DevMat& M, uint64_t row, u
     uint2 lo = __ldg(reinterpret_cast<const uint2*>(ql));
     uint2 hb = __ldg(reinterpret_cast<const uint2*>(sb + 128 + h * 32 + l0));
     int sc = (int)(int8_t)__ldg(sb + 192 + h * 8 + qd * 2 + (l0 >> 4));
-    float d = __half2float(M.dpl[row * M.dstride + sbi]);
+    float d = __half2float(M.dpl[(uint64_t)sbi * M.trows + row]);
     float ds = __fmul_rn(d, (float)sc);
     uint32_t nsh = (qd >> 1) * 4, hsh = qd * 2;
     float v[8];
@@ -165,7 +166,7 @@ template <>
 __device__ __forceinline__ uint4 chunk8<T_Q4_0>(const DevMat& M, uint64_t row, uint32_t c8) {
     uint32_t blk = c8 >> 2, q = c8 & 3u;
     uint2 qs = __ldg(reinterpret_cast<const uint2*>(M.main + row * M.main_stride + blk * 16u + (q & 1u) * 8u));
-    float d = __half2float(M.dpl[row * M.dstride + blk]);
+    float d = __half2float(M.dpl[(uint64_t)blk * M.trows + row]);
     uint32_t sh = (q >> 1) * 4;
     float v[8];
 #pragma unroll
@@ -182,8 +183,8 @@ template <>
 __device__ __forceinline__ uint4 chunk8<T_Q5_0>(const DevMat& M, uint64_t row, uint32_t c8) {
     uint32_t blk = c8 >> 2, q = c8 & 3u;
     uint2 qs = __ldg(reinterpret_cast<const uint2*>(M.main + row * M.main_stride + blk * 16u + (q & 1u) * 8u));
-    uint32_t qh = __ldg(M.aux + row * M.dstride + blk);
-    float d = __half2float(M.dpl[row * M.dstride + blk]);
+    uint32_t qh = __ldg(M.aux + (uint64_t)blk * M.trows + row);
+    float d = __half2float(M.dpl[(uint64_t)blk * M.trows + row]);
     uint32_t sh = (q >> 1) * 4;
     uint32_t e0 = (q & 1u) * 8u + (q >> 1) * 16u;  // first element index in the block
     float v[8];
@@ -203,7 +204,7 @@ template <>
 __device__ __forceinline__ uint4 chunk8<T_Q8_0>(const DevMat& M, uint64_t row, uint32_t c8) {
     uint32_t blk = c8 >> 2, q = c8 & 3u;
     uint2 qs = __ldg(reinterpret_cast<const uint2*>(M.main + row * M.main_stride + blk * 32u + q * 8u));
-    float d = __half2float(M.dpl[row * M.dstride + blk]);
+    float d = __half2float(M.dpl[(uint64_t)blk * M.trows + row]);
     float v[8];
 #pragma unroll
     for (int i = 0; i < 4; i++) {

@@ -5,11 +5,14 @@
 //   down:    out[tok] += w_slot * (down . h_row)                  (src/moe.rs:373-380)
 //
 // Warp roles (one CTA per SM, everything stream-ordered through mbarriers):
-//   warp 0      bulk-copies the raw GGUF bytes of the CTA's weight rows into a shared ring,
-//               one 256-element superblock (or 8 blocks of 32) per stage;
+//   warp 0      TMA producer: one 2-D tensor copy per matrix and plane brings the raw GGUF
+//               bytes of the CTA's 128 weight rows for one 256-element superblock (or 8 blocks
+//               of 32) into a shared ring;
 //   warp 1      allocates tensor memory and issues tcgen05.mma (one elected thread): A is the
 //               dequantized weight tile held in TMEM, B the token tile in shared memory;
-//   warps 2-3   gather the token rows (fp16) into 128-B-swizzled shared tiles with cp.async;
+//   warps 2-3   token tiles: for gate/up they gather x rows (fp16) by token with cp.async into
+//               128-B-swizzled shared tiles; for down one thread loads the h tile with a
+//               swizzled 2-D TMA and all 64 threads bring each row to its common scale;
 //   warps 4..   one thread per weight row decodes 64 K-elements of its row per stage from the
 //               raw ring (bit-identical f32 values to quant::dequant, rounded to fp16) and
 //               stores them into its TMEM lane with tcgen05.st; after the last stage the same
@@ -17,6 +20,8 @@
 // The fp16 weights never touch shared memory; shared memory carries the raw bytes and the
 // token tiles only.  Every wait is bounded: on a timeout the kernel records DERR_TIMEOUT in the
 // status word, skips the remaining work, waits for its own MMAs and frees its tensor memory.
+#include <string.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tc_ptx.cuh"
@@ -24,58 +29,129 @@
 namespace rmoe {
 using namespace tc;
 
-static constexpr int TC_M = 128;   // weight rows per matrix per CTA (= TMEM lanes)
+static constexpr int TC_M = 128;   // weight rows per matrix per CTA (= TMEM lanes, = TMA box rows)
 static constexpr int TC_BN = 128;  // expert-sorted rows per tile (MMA N, rounded to 16 per tile)
 static constexpr int TC_KS = 64;   // K elements per MMA stage (one 128-B swizzle row of fp16)
 static constexpr int TC_NST = 4;   // MMA stages in flight
 static constexpr int TC_RST = 2;   // raw weight stages in flight
-static constexpr int TC_BLOOK = 2; // token-tile copies kept in flight per loader thread
+static constexpr int TC_BLOOK = 2; // token-tile stages kept in flight by the loaders
 
 int tc_tile_rows() { return TC_BN; }
 
-// Raw-stage geometry: RK K-elements per stage; BYTES copied per row; STRIDE = shared pitch
-// (an odd number of 16-B units, so 16-B loads of 8 consecutive rows hit distinct banks).
+// Raw-stage geometry per type: RK K-elements per stage; PITCH = bytes per row of the main-plane
+// box (what each row needs, plus 16 B where that keeps the pitch an odd number of 16-B units so
+// 16-B loads of 8 consecutive rows hit distinct banks); DBLK = block scales per row per stage
+// ([block][row] plane); AUX = Q5_0 high-bit words ([block][row] plane).
 template <int TYPE> struct Raw;
-template <> struct Raw<T_Q4_K> { static constexpr int RK = 256, BYTES = 144, STRIDE = 144; };
-template <> struct Raw<T_Q5_K> { static constexpr int RK = 256, BYTES = 176, STRIDE = 176; };
-template <> struct Raw<T_Q6_K> { static constexpr int RK = 256, BYTES = 208, STRIDE = 208; };
-template <> struct Raw<T_Q4_0> { static constexpr int RK = 256, BYTES = 144, STRIDE = 144; };
-template <> struct Raw<T_Q5_0> { static constexpr int RK = 256, BYTES = 176, STRIDE = 176; };
-template <> struct Raw<T_Q8_0> { static constexpr int RK = 256, BYTES = 272, STRIDE = 272; };
-template <> struct Raw<T_DENSE> { static constexpr int RK = 128, BYTES = 256, STRIDE = 272; };
+template <> struct Raw<T_Q4_K> { static constexpr int RK = 256, PITCH = 144, MB = 144, DBLK = 0, AUX = 0; };
+template <> struct Raw<T_Q5_K> { static constexpr int RK = 256, PITCH = 176, MB = 176, DBLK = 0, AUX = 0; };
+template <> struct Raw<T_Q6_K> { static constexpr int RK = 256, PITCH = 208, MB = 208, DBLK = 1, AUX = 0; };
+template <> struct Raw<T_Q4_0> { static constexpr int RK = 256, PITCH = 144, MB = 128, DBLK = 8, AUX = 0; };
+template <> struct Raw<T_Q5_0> { static constexpr int RK = 256, PITCH = 144, MB = 128, DBLK = 8, AUX = 8; };
+template <> struct Raw<T_Q8_0> { static constexpr int RK = 256, PITCH = 272, MB = 256, DBLK = 8, AUX = 0; };
+template <> struct Raw<T_DENSE> { static constexpr int RK = 128, PITCH = 272, MB = 256, DBLK = 0, AUX = 0; };
 
-// Copy raw stage j of global row `grow` (all planes) to shared address dst.
 template <int TYPE>
-__device__ __forceinline__ void raw_copy(const DevMat& M, uint64_t grow, int j, uint32_t dst, uint32_t bar) {
-    const uint8_t* rowp = M.main + grow * M.main_stride;
-    const uint64_t blk0 = grow * M.dstride + (uint64_t)j * 8;  // first 32-element block (32-formats)
-    if constexpr (TYPE == T_Q4_K) bulk_g2s(dst, rowp + (uint64_t)j * 144, 144, bar);
-    if constexpr (TYPE == T_Q5_K) bulk_g2s(dst, rowp + (uint64_t)j * 176, 176, bar);
-    if constexpr (TYPE == T_Q6_K) bulk_g2s(dst, rowp + (uint64_t)j * 208, 208, bar);
-    if constexpr (TYPE == T_Q4_0) {
-        bulk_g2s(dst, rowp + (uint64_t)j * 128, 128, bar);
-        bulk_g2s(dst + 128, reinterpret_cast<const uint8_t*>(M.dpl) + blk0 * 2, 16, bar);
+struct RawStage {
+    using R = Raw<TYPE>;
+    static constexpr int MAIN = TC_M * R::PITCH;  // bytes per matrix: main box
+    static constexpr int DOFF = MAIN, DBYTES = R::DBLK * TC_M * 2;
+    static constexpr int AOFF = DOFF + DBYTES, ABYTES = R::AUX * TC_M * 4;
+    static constexpr int BYTES = AOFF + ABYTES;   // per matrix; every region 128-B aligned
+    static_assert(MAIN % 128 == 0 && DBYTES % 128 == 0 && ABYTES % 128 == 0, "TMA regions must be 128-B aligned");
+};
+
+// ---------------------------------------------------------------------------------------------
+// host: tensor maps
+// ---------------------------------------------------------------------------------------------
+// The driver's tensor-map encoder, resolved through the runtime so the library does not link
+// libcuda itself (it loads on hosts without a driver; only this call needs one).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encoder() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
     }
-    if constexpr (TYPE == T_Q5_0) {
-        bulk_g2s(dst, rowp + (uint64_t)j * 128, 128, bar);
-        bulk_g2s(dst + 128, reinterpret_cast<const uint8_t*>(M.aux) + blk0 * 4, 32, bar);
-        bulk_g2s(dst + 160, reinterpret_cast<const uint8_t*>(M.dpl) + blk0 * 2, 16, bar);
+    return fn;
+}
+
+static bool encode2d(CUtensorMap& m, CUtensorMapDataType dt, const void* base, uint64_t d0, uint64_t d1,
+                     uint64_t stride1_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swz) {
+    EncodeTiledFn fn = encoder();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {d0, d1};
+    cuuint64_t strides[1] = {stride1_bytes};
+    cuuint32_t box[2] = {b0, b1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int TYPE>
+static bool maps_for(const DevMat& M, WMaps& o) {
+    using R = Raw<TYPE>;
+    // main plane as u16 [trows][main_stride / 2]; box = PITCH bytes x 128 rows (past the row end
+    // the box reads zeros)
+    bool ok = encode2d(o.main, CU_TENSOR_MAP_DATA_TYPE_UINT16, M.main, M.main_stride / 2, M.trows, M.main_stride,
+                       R::PITCH / 2, TC_M, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (R::DBLK)
+        ok = ok && encode2d(o.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, M.dpl, M.trows, M.dstride, M.trows * 2, TC_M, R::DBLK,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (R::AUX)
+        ok = ok && encode2d(o.aux, CU_TENSOR_MAP_DATA_TYPE_UINT32, M.aux, M.trows, M.dstride, M.trows * 4, TC_M, R::AUX,
+                            CU_TENSOR_MAP_SWIZZLE_NONE);
+    return ok;
+}
+
+bool make_weight_maps(const DevMat& M, WMaps& out) {
+    memset(&out, 0, sizeof out);
+    switch (M.type) {
+        case T_Q4_K: return maps_for<T_Q4_K>(M, out);
+        case T_Q5_K: return maps_for<T_Q5_K>(M, out);
+        case T_Q6_K: return maps_for<T_Q6_K>(M, out);
+        case T_Q4_0: return maps_for<T_Q4_0>(M, out);
+        case T_Q5_0: return maps_for<T_Q5_0>(M, out);
+        case T_Q8_0: return maps_for<T_Q8_0>(M, out);
+        case T_DENSE: return maps_for<T_DENSE>(M, out);
+        default: return false;
     }
-    if constexpr (TYPE == T_Q8_0) {
-        bulk_g2s(dst, rowp + (uint64_t)j * 256, 256, bar);
-        bulk_g2s(dst + 256, reinterpret_cast<const uint8_t*>(M.dpl) + blk0 * 2, 16, bar);
-    }
-    if constexpr (TYPE == T_DENSE) bulk_g2s(dst, rowp + (uint64_t)j * 256, 256, bar);
+}
+
+bool make_h_map(const __half* h, uint64_t rows, uint32_t I, CUtensorMap& out) {
+    return encode2d(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, h, I, rows, (uint64_t)I * 2, TC_KS, TC_BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// ---------------------------------------------------------------------------------------------
+// device: TMA 2-D tile load (no multicast)
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
 }
 
 __device__ __forceinline__ float nib(uint32_t w, int sh) { return (float)((w >> sh) & 0xFu); }
 
-// Decode K-elements [64*sub, 64*sub + 64) of one raw row into 32 packed fp16 pairs (k, k+1).
+// Decode K-elements [64*sub, 64*sub + 64) of one weight row into 32 packed fp16 pairs (k, k+1).
+// p = the row's main-plane bytes for the stage; dq / aq = its block-scale / high-bit entries
+// (block b of the stage at dq + 256 b / aq + 512 b).
 template <int TYPE>
-__device__ __forceinline__ void slice64(const uint8_t* p, int sub, float q6d, uint32_t* v);
+__device__ __forceinline__ void slice64(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub, uint32_t* v);
 
 template <>
-__device__ __forceinline__ void slice64<T_Q4_K>(const uint8_t* p, int sub, float, uint32_t* v) {
+__device__ __forceinline__ void slice64<T_Q4_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub,
+                                                uint32_t* v) {
     uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
     float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
     int sc0, m0, sc1, m1;
@@ -98,7 +174,8 @@ __device__ __forceinline__ void slice64<T_Q4_K>(const uint8_t* p, int sub, float
 }
 
 template <>
-__device__ __forceinline__ void slice64<T_Q5_K>(const uint8_t* p, int sub, float, uint32_t* v) {
+__device__ __forceinline__ void slice64<T_Q5_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub,
+                                                uint32_t* v) {
     uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
     float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
     int sc0, m0, sc1, m1;
@@ -129,9 +206,11 @@ __device__ __forceinline__ void slice64<T_Q5_K>(const uint8_t* p, int sub, float
     }
 }
 
-// Q6_K raw row: ql[128] | qh[64] | scales[16]; d comes from the d plane (q6d).
+// Q6_K main plane row: ql[128] | qh[64] | scales[16]; d from the block-scale plane.
 template <>
-__device__ __forceinline__ void slice64<T_Q6_K>(const uint8_t* p, int sub, float q6d, uint32_t* v) {
+__device__ __forceinline__ void slice64<T_Q6_K>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub,
+                                                uint32_t* v) {
+    const float q6d = h2f(*reinterpret_cast<const uint16_t*>(dq));
     const int h = sub >> 1, odd = sub & 1;
     const uint4* ql = reinterpret_cast<const uint4*>(p + h * 64);
     const uint4* qh = reinterpret_cast<const uint4*>(p + 128 + h * 32);
@@ -162,13 +241,14 @@ __device__ __forceinline__ void slice64<T_Q6_K>(const uint8_t* p, int sub, float
     }
 }
 
-// Q4_0 raw row: qs[8 x 16] | d[8 x f16]; slice = blocks 2*sub, 2*sub+1.
+// Q4_0 main plane row: qs[8 x 16]; slice = blocks 2*sub, 2*sub+1.
 template <>
-__device__ __forceinline__ void slice64<T_Q4_0>(const uint8_t* p, int sub, float, uint32_t* v) {
+__device__ __forceinline__ void slice64<T_Q4_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub,
+                                                uint32_t* v) {
 #pragma unroll
     for (int bb = 0; bb < 2; bb++) {
         const int b = 2 * sub + bb;
-        const float d = h2f(*reinterpret_cast<const uint16_t*>(p + 128 + 2 * b));
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
         uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
         uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -183,14 +263,15 @@ __device__ __forceinline__ void slice64<T_Q4_0>(const uint8_t* p, int sub, float
     }
 }
 
-// Q5_0 raw row: qs[8 x 16] | qh[8 x u32] | d[8 x f16].
+// Q5_0 main plane row: qs[8 x 16]; high bits and scales from their planes.
 template <>
-__device__ __forceinline__ void slice64<T_Q5_0>(const uint8_t* p, int sub, float, uint32_t* v) {
+__device__ __forceinline__ void slice64<T_Q5_0>(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub,
+                                                uint32_t* v) {
 #pragma unroll
     for (int bb = 0; bb < 2; bb++) {
         const int b = 2 * sub + bb;
-        const float d = h2f(*reinterpret_cast<const uint16_t*>(p + 160 + 2 * b));
-        const uint32_t qh = *reinterpret_cast<const uint32_t*>(p + 128 + 4 * b);
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
+        const uint32_t qh = *reinterpret_cast<const uint32_t*>(aq + 512 * b);
         uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
         uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -213,13 +294,14 @@ __device__ __forceinline__ void slice64<T_Q5_0>(const uint8_t* p, int sub, float
     }
 }
 
-// Q8_0 raw row: qs[8 x 32] | d[8 x f16].
+// Q8_0 main plane row: qs[8 x 32].
 template <>
-__device__ __forceinline__ void slice64<T_Q8_0>(const uint8_t* p, int sub, float, uint32_t* v) {
+__device__ __forceinline__ void slice64<T_Q8_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub,
+                                                uint32_t* v) {
 #pragma unroll
     for (int bb = 0; bb < 2; bb++) {
         const int b = 2 * sub + bb;
-        const float d = h2f(*reinterpret_cast<const uint16_t*>(p + 256 + 2 * b));
+        const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
         const uint4* q = reinterpret_cast<const uint4*>(p + 32 * b);
         uint4 a = q[0], c = q[1];
         uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
@@ -233,7 +315,8 @@ __device__ __forceinline__ void slice64<T_Q8_0>(const uint8_t* p, int sub, float
 }
 
 template <>
-__device__ __forceinline__ void slice64<T_DENSE>(const uint8_t* p, int sub, float, uint32_t* v) {
+__device__ __forceinline__ void slice64<T_DENSE>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub,
+                                                 uint32_t* v) {
     const uint4* q = reinterpret_cast<const uint4*>(p + 128 * sub);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
@@ -248,7 +331,7 @@ __device__ __forceinline__ void slice64<T_DENSE>(const uint8_t* p, int sub, floa
 template <int TYPE, int NMAT>
 struct TcGeom {
     static constexpr int B_STAGE = TC_BN * 128;  // bytes per token tile stage
-    static constexpr int RAW_STAGE = NMAT * TC_M * Raw<TYPE>::STRIDE;
+    static constexpr int RAW_STAGE = NMAT * RawStage<TYPE>::BYTES;
     static constexpr int SMEM = TC_NST * B_STAGE + TC_RST * RAW_STAGE + 1024;
     static constexpr int THREADS = 32 * (4 + 4 * NMAT);
     static constexpr uint32_t TMEM_COLS = NMAT == 2 ? 512 : 256;
@@ -256,12 +339,15 @@ struct TcGeom {
 };
 
 template <int TYPE, int NMAT>
-__global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(GroupedParams p) {
+__global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
+    tc_grouped_kernel(const __grid_constant__ GroupedParams p, const __grid_constant__ TcMaps maps) {
     using G = TcGeom<TYPE, NMAT>;
-    constexpr int RK = Raw<TYPE>::RK, RSTRIDE = Raw<TYPE>::STRIDE, SUBS = RK / TC_KS;
+    using RS = RawStage<TYPE>;
+    constexpr int RK = Raw<TYPE>::RK, PITCH = Raw<TYPE>::PITCH, SUBS = RK / TC_KS;
     extern __shared__ uint8_t dsmem[];
     __shared__ __align__(8) uint64_t bar_raw_full[TC_RST], bar_raw_empty[TC_RST];
-    __shared__ __align__(8) uint64_t bar_a_full[TC_NST], bar_b_full[TC_NST], bar_empty[TC_NST], bar_acc;
+    __shared__ __align__(8) uint64_t bar_a_full[TC_NST], bar_b_full[TC_NST], bar_empty[TC_NST], bar_b_land[TC_NST];
+    __shared__ __align__(8) uint64_t bar_acc;
     __shared__ uint32_t tmem_holder;
     __shared__ int s_tok[TC_BN], s_rexp[TC_BN];
     __shared__ float s_w[TC_BN];
@@ -273,10 +359,9 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
     const int e = ti.x, row0 = ti.y, nrows = ti.z;
     const int n_eff = (nrows + 15) & ~15;
     const int fb = blockIdx.x;
-    const bool shared_e = e >= p.E;
-    const DevMat& M0 = NMAT == 2 ? (shared_e ? p.sgate : p.gate) : (shared_e ? p.sdown : p.down);
-    const DevMat& M1 = shared_e ? p.sup : p.up;
-    const uint64_t grow0 = (uint64_t)(shared_e ? 0 : e) * M0.rows + (uint64_t)fb * TC_M;
+    const int sh = e >= p.E ? 1 : 0;  // shared expert: its own single-expert stacks
+    const DevMat& M0 = NMAT == 2 ? (sh ? p.sgate : p.gate) : (sh ? p.sdown : p.down);
+    const int grow0 = (sh ? 0 : e) * (int)M0.rows + fb * TC_M;  // first weight row of the CTA
     const int K = NMAT == 2 ? p.H : p.I;
     const int nk = K / TC_KS, nraw = K / RK;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -295,6 +380,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
             mbar_init(smem_u32(&bar_a_full[i]), 4 * NMAT);
             mbar_init(smem_u32(&bar_b_full[i]), 64);
             mbar_init(smem_u32(&bar_empty[i]), 1);
+            mbar_init(smem_u32(&bar_b_land[i]), 1);
         }
         mbar_init(smem_u32(&bar_acc), 1);
         s_abort = 0;
@@ -326,23 +412,28 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
     };
 
     if (warp == 0) {
-        // ---------------- raw weight producer ----------------
-        for (int j = 0; j < nraw; j++) {
-            const int s = j % TC_RST;
-            if (s_abort) break;
-            if (j >= TC_RST && !mbar_wait(smem_u32(&bar_raw_empty[s]), ((j / TC_RST) + 1) & 1)) {
-                fail();
-                break;
-            }
-            const uint32_t bar = smem_u32(&bar_raw_full[s]);
-            if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(NMAT * TC_M * Raw<TYPE>::BYTES));
-            __syncwarp();
-            for (int r = lane; r < TC_M; r += 32) {
-                raw_copy<TYPE>(M0, grow0 + r, j, rawring + (uint32_t)((s * NMAT + 0) * TC_M + r) * RSTRIDE, bar);
-                if (NMAT == 2)
-                    raw_copy<TYPE>(M1, grow0 + r, j, rawring + (uint32_t)((s * NMAT + 1) * TC_M + r) * RSTRIDE, bar);
+        // ---------------- TMA producer: raw weight superblocks ----------------
+        if (lane == 0) {
+            for (int j = 0; j < nraw; j++) {
+                const int s = j % TC_RST;
+                if (s_abort) break;
+                if (j >= TC_RST && !mbar_wait(smem_u32(&bar_raw_empty[s]), ((j / TC_RST) + 1) & 1)) {
+                    fail();
+                    break;
+                }
+                const uint32_t bar = smem_u32(&bar_raw_full[s]);
+                mbar_arrive_expect_tx(bar, (uint32_t)G::RAW_STAGE);
+#pragma unroll
+                for (int m = 0; m < NMAT; m++) {
+                    const WMaps& wm = maps.w[sh][m];
+                    const uint32_t dst = rawring + (uint32_t)(s * NMAT + m) * RS::BYTES;
+                    tma_2d(dst, &wm.main, j * (Raw<TYPE>::MB / 2), grow0, bar);
+                    if (Raw<TYPE>::DBLK) tma_2d(dst + RS::DOFF, &wm.d, grow0, j * Raw<TYPE>::DBLK, bar);
+                    if (Raw<TYPE>::AUX) tma_2d(dst + RS::AOFF, &wm.aux, grow0, j * Raw<TYPE>::AUX, bar);
+                }
             }
         }
+        __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
@@ -369,13 +460,19 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
         }
         __syncwarp();
     } else if (warp < 4) {
-        // ---------------- token-tile loaders (64 threads, cp.async 16 B) ----------------
+        // ---------------- token tiles (64 threads) ----------------
         const int bt = tid - 64;
         const int nblk = p.I / HBLK;
+        bool ok = true;
+        // make stage st ready for the MMA: (down) common row scale, proxy fence, arrive
         auto finish = [&](int st) {
+            const uint32_t bst = bring + (uint32_t)(st % TC_NST) * G::B_STAGE;
             if (NMAT == 1) {
-                // bring every h block of the stage to its row's common scale 2^rowexp
-                const uint32_t bst = bring + (uint32_t)(st % TC_NST) * G::B_STAGE;
+                if (!mbar_wait(smem_u32(&bar_b_land[st % TC_NST]), (st / TC_NST) & 1)) {
+                    fail();
+                    ok = false;
+                    return;
+                }
                 for (int q = bt; q < nrows * 8; q += 64) {
                     const int n = q >> 3, c = q & 7;
                     const int dexp = (int)__ldg(p.hexp + (size_t)(row0 + n) * nblk + st) - s_rexp[n];
@@ -397,7 +494,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
             mbar_arrive(smem_u32(&bar_b_full[st % TC_NST]));
         };
         int done = 0;
-        for (int kt = 0; kt < nk; kt++) {
+        for (int kt = 0; kt < nk && ok; kt++) {
             const int s = kt % TC_NST;
             if (s_abort) break;
             if (kt >= TC_NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / TC_NST) + 1) & 1)) {
@@ -405,45 +502,50 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
                 break;
             }
             const uint32_t bst = bring + (uint32_t)s * G::B_STAGE;
-            for (int q = bt; q < nrows * 8; q += 64) {
-                const int n = q >> 3, c = q & 7;
-                const __half* src = (NMAT == 2) ? p.xb + (size_t)s_tok[n] * p.H + kt * TC_KS + c * 8
-                                                : p.h + (size_t)(row0 + n) * p.I + kt * TC_KS + c * 8;
-                cp_async16(bst + (uint32_t)(n * 128 + ((c ^ (n & 7)) << 4)), src);
-            }
-            cp_async_commit();
-            if (kt >= TC_BLOOK) {
-                cp_async_wait<TC_BLOOK>();
-                finish(done++);
+            if (NMAT == 2) {
+                for (int q = bt; q < nrows * 8; q += 64) {
+                    const int n = q >> 3, c = q & 7;
+                    const __half* src = p.xb + (size_t)s_tok[n] * p.H + kt * TC_KS + c * 8;
+                    cp_async16(bst + (uint32_t)(n * 128 + ((c ^ (n & 7)) << 4)), src);
+                }
+                cp_async_commit();
+                if (kt >= TC_BLOOK) {
+                    cp_async_wait<TC_BLOOK>();
+                    finish(done++);
+                }
+            } else {
+                if (bt == 0) {
+                    const uint32_t bar = smem_u32(&bar_b_land[s]);
+                    mbar_arrive_expect_tx(bar, (uint32_t)G::B_STAGE);
+                    tma_2d(bst, &maps.h, kt * TC_KS, row0, bar);
+                }
+                if (kt >= TC_BLOOK) finish(done++);
             }
         }
-        cp_async_wait<0>();
-        if (!s_abort)
-            while (done < nk) finish(done++);
+        if (NMAT == 2) cp_async_wait<0>();
+        while (ok && !s_abort && done < nk) finish(done++);
     } else {
         // ---------------- converters: one thread per weight row ----------------
         const int cw = warp - 4, m = cw >> 2, q = warp & 3;
         const int r = q * 32 + lane;
-        const DevMat& Mm = (m == 0) ? M0 : M1;
-        const uint64_t grow = grow0 + r;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
-        float q6d = 0.0f;
         bool ok = true;
         for (int kt = 0; kt < nk && ok; kt++) {
             const int j = kt / SUBS, sub = kt % SUBS, s = kt % TC_NST;
             if (s_abort) { ok = false; break; }
-            if (sub == 0) {
-                if (!mbar_wait(smem_u32(&bar_raw_full[j % TC_RST]), (j / TC_RST) & 1)) { fail(); ok = false; break; }
-                if (TYPE == T_Q6_K) q6d = __half2float(Mm.dpl[grow * Mm.dstride + j]);
+            if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % TC_RST]), (j / TC_RST) & 1)) {
+                fail();
+                ok = false;
+                break;
             }
             if (kt >= TC_NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / TC_NST) + 1) & 1)) {
                 fail();
                 ok = false;
                 break;
             }
-            const uint8_t* rp = raw_g + (size_t)(((j % TC_RST) * NMAT + m) * TC_M + r) * RSTRIDE;
+            const uint8_t* mat = raw_g + (size_t)((j % TC_RST) * NMAT + m) * RS::BYTES;
             uint32_t v[32];
-            slice64<TYPE>(rp, sub, q6d, v);
+            slice64<TYPE>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, v);
             tmem_st32(tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32), v);
             tmem_st_wait();
             fence_before_sync();
@@ -516,13 +618,14 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
                 tmem_ld32(tlane + (uint32_t)(c * 32), a);
                 tmem_ld_wait();
                 if (!work) continue;
-#pragma unroll 4
+#pragma unroll
                 for (int i = 0; i < 32; i++) {
                     const int n = c * 32 + i;
-                    if (n >= nrows) break;
-                    const float yv = __fmul_rn(__uint_as_float(a[i]), exp2i(s_rexp[n]));
-                    if (p.y) p.y[(size_t)(row0 + n) * p.H + f] = yv;
-                    else atomicAdd(p.out + (size_t)s_tok[n] * p.H + f, __fmul_rn(s_w[n], yv));
+                    if (n < nrows) {
+                        const float yv = __fmul_rn(__uint_as_float(a[i]), exp2i(s_rexp[n]));
+                        if (p.y) p.y[(size_t)(row0 + n) * p.H + f] = yv;
+                        else atomicAdd(p.out + (size_t)s_tok[n] * p.H + f, __fmul_rn(s_w[n], yv));
+                    }
                 }
             }
         }
@@ -536,13 +639,13 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1) tc_grouped_kernel(Grou
 }
 
 template <int TYPE, int NMAT>
-static cudaError_t go_tc(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+static cudaError_t go_tc(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s) {
     using G = TcGeom<TYPE, NMAT>;
     auto k = tc_grouped_kernel<TYPE, NMAT>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((NMAT == 2 ? p.I : p.H) / TC_M, max_tiles);
-    k<<<grid, G::THREADS, G::SMEM, s>>>(p);
+    k<<<grid, G::THREADS, G::SMEM, s>>>(p, maps);
     return cudaGetLastError();
 }
 
@@ -558,14 +661,14 @@ static cudaError_t go_tc(const GroupedParams& p, int max_tiles, cudaStream_t s) 
         default: return cudaErrorInvalidValue;                     \
     }
 
-cudaError_t launch_tc_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+cudaError_t launch_tc_gateup(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s) {
     if (max_tiles <= 0) return cudaSuccess;
-    RMOE_TC_SWITCH(p.gate.type, return go_tc<TT, 2>(p, max_tiles, s))
+    RMOE_TC_SWITCH(p.gate.type, return go_tc<TT, 2>(p, maps, max_tiles, s))
 }
 
-cudaError_t launch_tc_down(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+cudaError_t launch_tc_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s) {
     if (max_tiles <= 0) return cudaSuccess;
-    RMOE_TC_SWITCH(p.down.type, return go_tc<TT, 1>(p, max_tiles, s))
+    RMOE_TC_SWITCH(p.down.type, return go_tc<TT, 1>(p, maps, max_tiles, s))
 }
 
 }  // namespace rmoe

@@ -2,6 +2,7 @@
 // and the kernel translation units.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -72,10 +73,27 @@ int small_tile_rows();
 cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s);
 cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, cudaStream_t s);
 
+// TMA descriptors of one weight-matrix stack: main plane (viewed as u16, 128-row boxes), the
+// block-scale plane and the Q5_0 high-bit plane (both [block][row], 128-row boxes).
+struct WMaps {
+    CUtensorMap main, d, aux;
+};
+
+// Everything the tcgen05 kernels read through TMA: [routed | shared expert][matrix 0 | 1]
+// weight maps and the SwiGLU activations h ([rows, I] fp16, 64 x 128 boxes, 128-B swizzle).
+struct alignas(64) TcMaps {
+    WMaps w[2][2];
+    CUtensorMap h;
+};
+
+// Build the maps of one stack (after upload_mat) / of the h workspace; false on a driver error.
+bool make_weight_maps(const DevMat& M, WMaps& out);
+bool make_h_map(const __half* h, uint64_t rows, uint32_t I, CUtensorMap& out);
+
 // large-batch (tcgen05) grouped kernels; tile_rows = rows per tile
 int tc_tile_rows();
-cudaError_t launch_tc_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s);
-cudaError_t launch_tc_down(const GroupedParams& p, int max_tiles, cudaStream_t s);
+cudaError_t launch_tc_gateup(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s);
+cudaError_t launch_tc_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s);
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_dequant_raw(int type, const void* src, uint64_t nblocks, float* dst, cudaStream_t s);

@@ -139,6 +139,7 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
     out.rows = rows;
     out.K = K;
     out.dstride = (uint32_t)nblk;
+    out.trows = total_rows;
     // fp16 operand range: bound |w| per block from its scales (d * 63 * 15 + dmin * 63 for
     // the K-quants, d * 32 / 16 / 128 for the others) and refuse layers that could overflow.
     double wmax = 0.0;
@@ -177,7 +178,7 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
                 for (uint64_t b = 0; b < nblk; b++) {
                     const uint8_t* s = src + r * rb + b * 210;
                     memcpy(&mainp[(r * nblk + b) * 208], s, 208);
-                    dpl[r * nblk + b] = (uint16_t)(s[208] | (s[209] << 8));
+                    dpl[b * total_rows + r] = (uint16_t)(s[208] | (s[209] << 8));
                 }
             break;
         case T_Q4_0: case T_Q8_0: {
@@ -190,7 +191,7 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
                 for (uint64_t b = 0; b < nblk; b++) {
                     const uint8_t* s = src + r * rb + b * by;
                     memcpy(&mainp[(r * nblk + b) * qb], s + 2, qb);
-                    dpl[r * nblk + b] = (uint16_t)(s[0] | (s[1] << 8));
+                    dpl[b * total_rows + r] = (uint16_t)(s[0] | (s[1] << 8));
                 }
             break;
         }
@@ -204,8 +205,8 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
                 for (uint64_t b = 0; b < nblk; b++) {
                     const uint8_t* s = src + r * rb + b * 22;
                     memcpy(&mainp[(r * nblk + b) * 16], s + 6, 16);
-                    dpl[r * nblk + b] = (uint16_t)(s[0] | (s[1] << 8));
-                    aux[r * nblk + b] = (uint32_t)s[2] | ((uint32_t)s[3] << 8) | ((uint32_t)s[4] << 16) | ((uint32_t)s[5] << 24);
+                    dpl[b * total_rows + r] = (uint16_t)(s[0] | (s[1] << 8));
+                    aux[b * total_rows + r] = (uint32_t)s[2] | ((uint32_t)s[3] << 8) | ((uint32_t)s[4] << 16) | ((uint32_t)s[5] << 24);
                 }
             break;
         case T_F32: case T_F16: case T_BF16: {
@@ -317,6 +318,12 @@ rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_
         if ((s = upload_mat(d->up_shexp, I, H, 1, "ffn_up_shexp", L->own, L->swu))) return s;
         if ((s = upload_mat(d->down_shexp, H, I, 1, "ffn_down_shexp", L->own, L->swd))) return s;
     }
+    // TMA descriptors of every stack, for the tensor-core kernels
+    bool maps_ok = make_weight_maps(L->wg, L->mg) && make_weight_maps(L->wu, L->mu) && make_weight_maps(L->wd, L->md);
+    if (d->has_shared)
+        maps_ok = maps_ok && make_weight_maps(L->swg, L->smg) && make_weight_maps(L->swu, L->smu) &&
+                  make_weight_maps(L->swd, L->smd);
+    if (!maps_ok) return fail(RMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for an expert stack");
     void* rw = L->own.alloc((size_t)d->n_experts * H * 4);
     if (!rw) return fail(RMOE_ERR_OOM, "router cudaMalloc failed");
     cudaError_t e = cudaMemcpy(rw, d->router_w, (size_t)d->n_experts * H * 4, cudaMemcpyHostToDevice);
@@ -363,6 +370,7 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.logits = (float*)A((size_t)cap * E * 4);
     if (need_y || L->ws_had_y) w.y = (float*)A(rows * H * 4);
     if (!ok) return fail(RMOE_ERR_OOM, "workspace cudaMalloc failed for %u tokens", cap);
+    if (!make_h_map(w.h, rows, I, L->hmap)) return fail(RMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for h");
     cudaMemset(w.ticket, 0, 16);
     cudaMemset(w.status, 0, 16);
     L->ws_T = cap;
@@ -416,10 +424,23 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     gp.H = (int)L->H; gp.I = (int)L->I; gp.E = (int)L->E; gp.k = (int)L->k;
     gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
     gp.topk_w = w.topk_w; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp; gp.y = det ? w.y : nullptr; gp.out = out; gp.status = w.status;
-    e = use_tc ? launch_tc_gateup(gp, max_tiles, s) : launch_small_gateup(gp, max_tiles, s);
+    TcMaps maps;
+    if (use_tc) {
+        memset(&maps, 0, sizeof maps);
+        maps.w[0][0] = L->mg;
+        maps.w[0][1] = L->mu;
+        maps.w[1][0] = L->smg;
+        maps.w[1][1] = L->smu;
+        maps.h = L->hmap;
+    }
+    e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : launch_small_gateup(gp, max_tiles, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
     mark(2);
-    e = use_tc ? launch_tc_down(gp, max_tiles, s) : launch_small_down(gp, max_tiles, s);
+    if (use_tc) {
+        maps.w[0][0] = L->md;
+        maps.w[1][0] = L->smd;
+    }
+    e = use_tc ? launch_tc_down(gp, maps, max_tiles, s) : launch_small_down(gp, max_tiles, s);
     if (e != cudaSuccess) return cuda_fail(e, "down launch");
     L->last_tc = use_tc;
     mark(3);

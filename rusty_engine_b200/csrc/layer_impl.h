@@ -60,6 +60,8 @@ struct rmoe_layer {
     int has_shared = 0;
     uint32_t E_local = 0;
     rmoe::DevMat wg{}, wu{}, wd{}, swg{}, swu{}, swd{};
+    rmoe::WMaps mg{}, mu{}, md{}, smg{}, smu{}, smd{};  // TMA maps of the stacks above
+    CUtensorMap hmap{};                                   // TMA map of the workspace h
     float* router_w = nullptr;
     rmoe::Owned own;       // weights
     rmoe::Owned ws_own;    // workspace
