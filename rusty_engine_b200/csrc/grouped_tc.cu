@@ -4,15 +4,15 @@
 //   gate/up: h[row, f] = silu(gate_f . x_row) * (up_f . x_row)   (src/moe.rs:280-299)
 //   down:    out[tok] += w_slot * (down . h_row)                  (src/moe.rs:373-380)
 //
-// Warp roles (one CTA per SM, everything stream-ordered through mbarriers):
+// Warp roles (gate/up runs one CTA per SM, down two; everything is ordered through mbarriers):
 //   warp 0      TMA producer: one 2-D tensor copy per matrix and plane brings the raw GGUF
 //               bytes of the CTA's 128 weight rows for one 256-element superblock (or 8 blocks
 //               of 32) into a shared ring;
 //   warp 1      allocates tensor memory and issues tcgen05.mma (one elected thread): A is the
 //               dequantized weight tile held in TMEM, B the token tile in shared memory;
-//   warps 2-3   token tiles: for gate/up they gather x rows (fp16) by token with cp.async into
-//               128-B-swizzled shared tiles; for down one thread loads the h tile with a
-//               swizzled 2-D TMA and all 64 threads bring each row to its common scale;
+//   warps 2-3   token tiles: one thread loads each 64-column tile of the expert-sorted x rows
+//               (gate/up) or of the SwiGLU activations h (down) with a 128-B-swizzled 2-D TMA;
+//               for down, warp 3 then brings each h row of the tile to its row's common scale;
 //   warps 4..   one thread per weight row decodes 64 K-elements of its row per stage from the
 //               raw ring (bit-identical f32 values to quant::dequant, rounded to fp16) and
 //               stores them into its TMEM lane with tcgen05.st; after the last stage the same
@@ -34,7 +34,7 @@ static constexpr int TC_BN = 128;  // expert-sorted rows per tile (MMA N, rounde
 static constexpr int TC_KS = 64;   // K elements per MMA stage (one 128-B swizzle row of fp16)
 static constexpr int TC_NST = 4;   // MMA stages in flight
 static constexpr int TC_RST = 2;   // raw weight stages in flight
-static constexpr int TC_BLOOK = 2; // token-tile stages kept in flight by the loaders
+static constexpr int TC_MAX_HBLK = 48;  // I / 64 this path supports (I <= 3072)
 
 int tc_tile_rows() { return TC_BN; }
 
@@ -125,10 +125,12 @@ bool make_weight_maps(const DevMat& M, WMaps& out) {
     }
 }
 
-bool make_h_map(const __half* h, uint64_t rows, uint32_t I, CUtensorMap& out) {
-    return encode2d(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, h, I, rows, (uint64_t)I * 2, TC_KS, TC_BN,
+bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMap& out) {
+    return encode2d(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, width, rows, (uint64_t)width * 2, TC_KS, TC_BN,
                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
+
+int tc_max_inter() { return TC_MAX_HBLK * HBLK; }
 
 // ---------------------------------------------------------------------------------------------
 // device: TMA 2-D tile load (no multicast)
@@ -149,6 +151,20 @@ __device__ __forceinline__ float nib(uint32_t w, int sh) { return (float)((w >> 
 template <int TYPE>
 __device__ __forceinline__ void slice64(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub, uint32_t* v);
 
+// Packed-half helpers: a 4- or 6-bit code c placed in the low mantissa bits of 0x6400 is the
+// exact fp16 value 1024 + c, so code -> fp16 costs one byte permute and one logic op per pair.
+__device__ __forceinline__ __half2 as_h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
+__device__ __forceinline__ uint32_t as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ uint32_t lop_or3(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xFE;\n" : "=r"(r) : "r"(a), "r"(b), "r"(c));  // a | b | c
+    return r;
+}
+
+// Q4_K: y = d*sc*q - dmin*m.  Per pair: the two codes land in 1024 + q (exact), 1024 is
+// subtracted exactly, and one fused multiply-add by the fp16-rounded sub-block scale and min
+// gives the value (the scale, the min and the result each round once to fp16; the f32 path
+// rounds the result only, and the difference is well inside the layer tolerance).
 template <>
 __device__ __forceinline__ void slice64<T_Q4_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub,
                                                 uint32_t* v) {
@@ -157,19 +173,25 @@ __device__ __forceinline__ void slice64<T_Q4_K>(const uint8_t* p, const uint8_t*
     int sc0, m0, sc1, m1;
     scale_min_k4(2 * sub, p + 4, sc0, m0);
     scale_min_k4(2 * sub + 1, p + 4, sc1, m1);
-    const float d1 = __fmul_rn(d, (float)sc0), dm1 = __fmul_rn(dmin, (float)m0);
-    const float d2 = __fmul_rn(d, (float)sc1), dm2 = __fmul_rn(dmin, (float)m1);
+    const __half2 D1 = __float2half2_rn(__fmul_rn(d, (float)sc0)), M1 = __float2half2_rn(-__fmul_rn(dmin, (float)m0));
+    const __half2 D2 = __float2half2_rn(__fmul_rn(d, (float)sc1)), M2 = __float2half2_rn(-__fmul_rn(dmin, (float)m1));
+    const __half2 K = __float2half2_rn(1024.0f);
     const uint4* q = reinterpret_cast<const uint4*>(p + 16 + sub * 32);
     uint4 a = q[0], b = q[1];
     uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        auto lo = [&](int sh) { return __fsub_rn(__fmul_rn(d1, nib(w[i], sh)), dm1); };
-        auto hi = [&](int sh) { return __fsub_rn(__fmul_rn(d2, nib(w[i], sh)), dm2); };
-        v[2 * i] = pack_f16x2(lo(0), lo(8));
-        v[2 * i + 1] = pack_f16x2(lo(16), lo(24));
-        v[16 + 2 * i] = pack_f16x2(hi(4), hi(12));
-        v[16 + 2 * i + 1] = pack_f16x2(hi(20), hi(28));
+        const uint32_t p01 = __byte_perm(w[i], 0, 0x4140), p23 = __byte_perm(w[i], 0, 0x4342);
+        auto lo = [&](uint32_t pp) {
+            return as_u32(__hfma2(__hsub2(as_h2((pp & 0x000F000Fu) | 0x64006400u), K), D1, M1));
+        };
+        auto hi = [&](uint32_t pp) {
+            return as_u32(__hfma2(__hsub2(as_h2(((pp >> 4) & 0x000F000Fu) | 0x64006400u), K), D2, M2));
+        };
+        v[2 * i] = lo(p01);
+        v[2 * i + 1] = lo(p23);
+        v[16 + 2 * i] = hi(p01);
+        v[16 + 2 * i + 1] = hi(p23);
     }
 }
 
@@ -221,23 +243,27 @@ __device__ __forceinline__ void slice64<T_Q6_K>(const uint8_t* p, const uint8_t*
     const int8_t* sc = reinterpret_cast<const int8_t*>(p + 192 + h * 8);
     const int qa = 2 * odd, qb = 2 * odd + 1;  // quadrants of this slice
     const int nsh = 4 * odd;                   // low nibbles for quadrants 0/1, high for 2/3
-    const float sa0 = __fmul_rn(q6d, (float)sc[qa * 2]), sa1 = __fmul_rn(q6d, (float)sc[qa * 2 + 1]);
-    const float sb0 = __fmul_rn(q6d, (float)sc[qb * 2]), sb1 = __fmul_rn(q6d, (float)sc[qb * 2 + 1]);
+    // scales rounded once to fp16; (q6 - 32) is exact in fp16 (1024 + q6 - 1056)
+    const __half2 sa0 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qa * 2]));
+    const __half2 sa1 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qa * 2 + 1]));
+    const __half2 sb0 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qb * 2]));
+    const __half2 sb1 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qb * 2 + 1]));
+    const __half2 K = __float2half2_rn(1056.0f);
+    // the two high bits of quadrant qa (bits 2qa..2qa+1 of qh) moved to bits 4..5: << (4 - 4*odd);
+    // of quadrant qb (bits 2qb..2qb+1): << 2 then >> 4*odd
 #pragma unroll
     for (int i = 0; i < 8; i++) {  // l = 4i .. 4i+3
-        const float sa = (i < 4) ? sa0 : sa1, sb = (i < 4) ? sb0 : sb1;
-        auto va = [&](int byte) {
-            int q = (int)(((la[i] >> (8 * byte + nsh)) & 0xFu) | (((hw[i] >> (8 * byte + 2 * qa)) & 3u) << 4)) - 32;
-            return __fmul_rn(sa, (float)q);
-        };
-        auto vb = [&](int byte) {
-            int q = (int)(((lb[i] >> (8 * byte + nsh)) & 0xFu) | (((hw[i] >> (8 * byte + 2 * qb)) & 3u) << 4)) - 32;
-            return __fmul_rn(sb, (float)q);
-        };
-        v[2 * i] = pack_f16x2(va(0), va(1));
-        v[2 * i + 1] = pack_f16x2(va(2), va(3));
-        v[16 + 2 * i] = pack_f16x2(vb(0), vb(1));
-        v[16 + 2 * i + 1] = pack_f16x2(vb(2), vb(3));
+        const __half2 sa = (i < 4) ? sa0 : sa1, sb = (i < 4) ? sb0 : sb1;
+#pragma unroll
+        for (int pr = 0; pr < 2; pr++) {  // byte pairs (0,1) and (2,3)
+            const uint32_t sel = pr ? 0x4342 : 0x4140;
+            const uint32_t pa = __byte_perm(la[i], 0, sel), pb = __byte_perm(lb[i], 0, sel);
+            const uint32_t ph = __byte_perm(hw[i], 0, sel);
+            const uint32_t ca = lop_or3((pa >> nsh) & 0x000F000Fu, (ph << (4 - nsh)) & 0x00300030u, 0x64006400u);
+            const uint32_t cb = lop_or3((pb >> nsh) & 0x000F000Fu, ((ph << 2) >> nsh) & 0x00300030u, 0x64006400u);
+            v[2 * i + pr] = as_u32(__hmul2(__hsub2(as_h2(ca), K), sa));
+            v[16 + 2 * i + pr] = as_u32(__hmul2(__hsub2(as_h2(cb), K), sb));
+        }
     }
 }
 
@@ -332,24 +358,29 @@ template <int TYPE, int NMAT>
 struct TcGeom {
     static constexpr int B_STAGE = TC_BN * 128;  // bytes per token tile stage
     static constexpr int RAW_STAGE = NMAT * RawStage<TYPE>::BYTES;
-    static constexpr int SMEM = TC_NST * B_STAGE + TC_RST * RAW_STAGE + 1024;
+    // down keeps one stage less so that two of its CTAs fit on an SM (one drains while the other
+    // computes); gate/up fills the tensor memory with its two accumulators and runs alone
+    static constexpr int NST = NMAT == 2 ? TC_NST : TC_NST - 1;
+    static constexpr int SMEM = NST * B_STAGE + TC_RST * RAW_STAGE + 1024;
     static constexpr int THREADS = 32 * (4 + 4 * NMAT);
     static constexpr uint32_t TMEM_COLS = NMAT == 2 ? 512 : 256;
     static constexpr int A_COL0 = NMAT * TC_BN;  // A ring after the accumulators
 };
 
 template <int TYPE, int NMAT>
-__global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
+__global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
     tc_grouped_kernel(const __grid_constant__ GroupedParams p, const __grid_constant__ TcMaps maps) {
     using G = TcGeom<TYPE, NMAT>;
     using RS = RawStage<TYPE>;
     constexpr int RK = Raw<TYPE>::RK, PITCH = Raw<TYPE>::PITCH, SUBS = RK / TC_KS;
+    constexpr int NST = G::NST;
     extern __shared__ uint8_t dsmem[];
     __shared__ __align__(8) uint64_t bar_raw_full[TC_RST], bar_raw_empty[TC_RST];
-    __shared__ __align__(8) uint64_t bar_a_full[TC_NST], bar_b_full[TC_NST], bar_empty[TC_NST], bar_b_land[TC_NST];
+    __shared__ __align__(8) uint64_t bar_a_full[NST], bar_b_full[NST], bar_empty[NST], bar_b_land[NST];
     __shared__ __align__(8) uint64_t bar_acc;
     __shared__ uint32_t tmem_holder;
     __shared__ int s_tok[TC_BN], s_rexp[TC_BN];
+    __shared__ int8_t s_hexp[NMAT == 1 ? TC_BN * TC_MAX_HBLK : 1];
     __shared__ float s_w[TC_BN];
     __shared__ volatile int s_abort;
 
@@ -368,17 +399,17 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
 
     const uint32_t sbase = (smem_u32(dsmem) + 1023u) & ~1023u;  // 1024-B aligned (SW128 atoms)
     uint8_t* gbase = dsmem + (sbase - smem_u32(dsmem));
-    const uint32_t bring = sbase, rawring = sbase + TC_NST * G::B_STAGE;
-    uint8_t* raw_g = gbase + TC_NST * G::B_STAGE;
+    const uint32_t bring = sbase, rawring = sbase + NST * G::B_STAGE;
+    uint8_t* raw_g = gbase + NST * G::B_STAGE;
 
     if (tid == 0) {
         for (int i = 0; i < TC_RST; i++) {
             mbar_init(smem_u32(&bar_raw_full[i]), 1);
             mbar_init(smem_u32(&bar_raw_empty[i]), 4 * NMAT);
         }
-        for (int i = 0; i < TC_NST; i++) {
+        for (int i = 0; i < NST; i++) {
             mbar_init(smem_u32(&bar_a_full[i]), 4 * NMAT);
-            mbar_init(smem_u32(&bar_b_full[i]), 64);
+            mbar_init(smem_u32(&bar_b_full[i]), NMAT == 2 ? 1 : 32);
             mbar_init(smem_u32(&bar_empty[i]), 1);
             mbar_init(smem_u32(&bar_b_land[i]), 1);
         }
@@ -399,6 +430,10 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
         s_tok[n] = tok;
         s_w[n] = w;
         s_rexp[n] = rexp;
+    }
+    if (NMAT == 1) {  // block exponents of the tile's h rows (the down kernel rescales B with them)
+        const int nblk = p.I / HBLK;
+        for (int i = tid; i < nrows * nblk; i += G::THREADS) s_hexp[i] = p.hexp[(size_t)row0 * nblk + i];
     }
     if (warp == 1) tmem_alloc(smem_u32(&tmem_holder), G::TMEM_COLS);
     fence_before_sync();
@@ -439,8 +474,8 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(TC_M, n_eff);
             for (int kt = 0; kt < nk; kt++) {
-                const int s = kt % TC_NST;
-                const uint32_t ph = (kt / TC_NST) & 1;
+                const int s = kt % NST;
+                const uint32_t ph = (kt / NST) & 1;
                 if (s_abort) break;
                 if (!mbar_wait(smem_u32(&bar_a_full[s]), ph) || !mbar_wait(smem_u32(&bar_b_full[s]), ph)) {
                     fail();
@@ -460,70 +495,78 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
         }
         __syncwarp();
     } else if (warp < 4) {
-        // ---------------- token tiles (64 threads) ----------------
+        // ---------------- token tiles ----------------
+        // gate/up: one thread streams the expert-sorted x tiles with TMA straight onto b_full.
+        // down: one thread loads the h tiles with TMA; then all 64 threads bring every row's
+        // 64-feature block to the row's common scale 2^rowexp (exact power-of-two multiplies).
         const int bt = tid - 64;
         const int nblk = p.I / HBLK;
         bool ok = true;
-        // make stage st ready for the MMA: (down) common row scale, proxy fence, arrive
-        auto finish = [&](int st) {
-            const uint32_t bst = bring + (uint32_t)(st % TC_NST) * G::B_STAGE;
-            if (NMAT == 1) {
-                if (!mbar_wait(smem_u32(&bar_b_land[st % TC_NST]), (st / TC_NST) & 1)) {
+        if (NMAT == 2) {
+            if (bt == 0) {
+                for (int kt = 0; kt < nk; kt++) {
+                    const int s = kt % NST;
+                    if (s_abort) break;
+                    if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
+                        fail();
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&bar_b_full[s]);
+                    mbar_arrive_expect_tx(bar, (uint32_t)G::B_STAGE);
+                    tma_2d(bring + (uint32_t)s * G::B_STAGE, &maps.b, kt * TC_KS, row0, bar);
+                }
+            }
+        } else if (bt == 0) {
+            // issuer: keeps every free stage loading, never waits for a rescale
+            for (int kt = 0; kt < nk; kt++) {
+                const int s = kt % NST;
+                if (s_abort) break;
+                if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
+                    fail();
+                    break;
+                }
+                const uint32_t bar = smem_u32(&bar_b_land[s]);
+                mbar_arrive_expect_tx(bar, (uint32_t)G::B_STAGE);
+                tma_2d(bring + (uint32_t)s * G::B_STAGE, &maps.b, kt * TC_KS, row0, bar);
+            }
+        } else if (bt >= 32) {
+            // rescalers (warp 3): bring each landed stage to the rows' common scales
+            const int rt = bt - 32;
+            for (int st = 0; st < nk && ok; st++) {
+                if (s_abort) break;
+                const uint32_t bst = bring + (uint32_t)(st % NST) * G::B_STAGE;
+                if (!mbar_wait(smem_u32(&bar_b_land[st % NST]), (st / NST) & 1)) {
                     fail();
                     ok = false;
-                    return;
+                    break;
                 }
-                for (int q = bt; q < nrows * 8; q += 64) {
-                    const int n = q >> 3, c = q & 7;
-                    const int dexp = (int)__ldg(p.hexp + (size_t)(row0 + n) * nblk + st) - s_rexp[n];
-                    if (dexp != 0) {
-                        uint8_t* ptr = gbase + (bst - sbase) + n * 128 + ((c ^ (n & 7)) << 4);
-                        uint4 v = *reinterpret_cast<uint4*>(ptr);
-                        float sc = dexp < -40 ? 0.0f : exp2i(dexp);
-                        uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+                // one 128-B row (64 fp16) per step; the 8 chunks are independent, so all loads issue
+                // before the multiplies (a row's swizzle permutes its chunks, the scale is per row)
+                for (int n = rt; n < nrows; n += 32) {
+                    const int dexp = (int)s_hexp[n * nblk + st] - s_rexp[n];
+                    if (dexp == 0) continue;
+                    uint4* row = reinterpret_cast<uint4*>(gbase + (bst - sbase) + n * 128);
+                    if (dexp < -24) {
 #pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            float2 f = __half22float2(*reinterpret_cast<__half2*>(&w4[i]));
-                            w4[i] = pack_f16x2(__fmul_rn(f.x, sc), __fmul_rn(f.y, sc));
-                        }
-                        *reinterpret_cast<uint4*>(ptr) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                        for (int c = 0; c < 8; c++) row[c] = make_uint4(0, 0, 0, 0);
+                        continue;
+                    }
+                    const __half2 sc = __float2half2_rn(exp2i(dexp));  // exact: 2^-24 .. 1
+                    uint4 v[8];
+#pragma unroll
+                    for (int c = 0; c < 8; c++) v[c] = row[c];
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        __half2* h2 = reinterpret_cast<__half2*>(&v[c]);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) h2[i] = __hmul2(h2[i], sc);
+                        row[c] = v[c];
                     }
                 }
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(smem_u32(&bar_b_full[st % TC_NST]));
-        };
-        int done = 0;
-        for (int kt = 0; kt < nk && ok; kt++) {
-            const int s = kt % TC_NST;
-            if (s_abort) break;
-            if (kt >= TC_NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / TC_NST) + 1) & 1)) {
-                fail();
-                break;
-            }
-            const uint32_t bst = bring + (uint32_t)s * G::B_STAGE;
-            if (NMAT == 2) {
-                for (int q = bt; q < nrows * 8; q += 64) {
-                    const int n = q >> 3, c = q & 7;
-                    const __half* src = p.xb + (size_t)s_tok[n] * p.H + kt * TC_KS + c * 8;
-                    cp_async16(bst + (uint32_t)(n * 128 + ((c ^ (n & 7)) << 4)), src);
-                }
-                cp_async_commit();
-                if (kt >= TC_BLOOK) {
-                    cp_async_wait<TC_BLOOK>();
-                    finish(done++);
-                }
-            } else {
-                if (bt == 0) {
-                    const uint32_t bar = smem_u32(&bar_b_land[s]);
-                    mbar_arrive_expect_tx(bar, (uint32_t)G::B_STAGE);
-                    tma_2d(bst, &maps.h, kt * TC_KS, row0, bar);
-                }
-                if (kt >= TC_BLOOK) finish(done++);
+                fence_proxy_async_smem();
+                mbar_arrive(smem_u32(&bar_b_full[st % NST]));
             }
         }
-        if (NMAT == 2) cp_async_wait<0>();
-        while (ok && !s_abort && done < nk) finish(done++);
     } else {
         // ---------------- converters: one thread per weight row ----------------
         const int cw = warp - 4, m = cw >> 2, q = warp & 3;
@@ -531,14 +574,14 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
         bool ok = true;
         for (int kt = 0; kt < nk && ok; kt++) {
-            const int j = kt / SUBS, sub = kt % SUBS, s = kt % TC_NST;
+            const int j = kt / SUBS, sub = kt % SUBS, s = kt % NST;
             if (s_abort) { ok = false; break; }
             if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % TC_RST]), (j / TC_RST) & 1)) {
                 fail();
                 ok = false;
                 break;
             }
-            if (kt >= TC_NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / TC_NST) + 1) & 1)) {
+            if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
                 fail();
                 ok = false;
                 break;
@@ -575,7 +618,9 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
                         float gv = __uint_as_float(g[i]), uv = __uint_as_float(u[i]);
-                        hs[(c * 32 + i) * HLD + r] = silu_ref(gv) * uv;
+                        // SiLU (src/moe.rs:44-51) with the fast exponential: the result is
+                        // rounded to fp16 next, far coarser than the approximation
+                        hs[(c * 32 + i) * HLD + r] = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
                     }
                 }
             }
@@ -612,7 +657,11 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
                 }
             }
         } else {
-            const int f = fb * TC_M + r;
+            // y tile through shared memory, ys[n][f] (the rings are idle once bar_acc has fired),
+            // so that each warp then writes whole 512-B token rows with 16-B stores or vector
+            // reductions. Scaling by 2^rowexp is exact, so w * (acc * 2^e) == acc * (w * 2^e).
+            float* ys = reinterpret_cast<float*>(gbase);
+            constexpr int YLD = TC_M + 4;
             for (int c = 0; c * 32 < n_eff; c++) {
                 uint32_t a[32];
                 tmem_ld32(tlane + (uint32_t)(c * 32), a);
@@ -621,11 +670,17 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), 1)
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
                     const int n = c * 32 + i;
-                    if (n < nrows) {
-                        const float yv = __fmul_rn(__uint_as_float(a[i]), exp2i(s_rexp[n]));
-                        if (p.y) p.y[(size_t)(row0 + n) * p.H + f] = yv;
-                        else atomicAdd(p.out + (size_t)s_tok[n] * p.H + f, __fmul_rn(s_w[n], yv));
-                    }
+                    const float sc = p.y ? exp2i(s_rexp[n]) : __fmul_rn(s_w[n], exp2i(s_rexp[n]));
+                    ys[n * YLD + r] = __fmul_rn(__uint_as_float(a[i]), sc);
+                }
+            }
+            asm volatile("bar.sync 1, %0;\n" ::"n"(32 * 4 * NMAT) : "memory");
+            if (work) {
+                const int f = fb * TC_M + 4 * lane;
+                for (int n = q; n < nrows; n += 4) {  // warp q of the four epilogue warps
+                    const float4 v = *reinterpret_cast<const float4*>(ys + n * YLD + 4 * lane);
+                    if (p.y) *reinterpret_cast<float4*>(p.y + (size_t)(row0 + n) * p.H + f) = v;
+                    else atomicAdd(reinterpret_cast<float4*>(p.out + (size_t)s_tok[n] * p.H + f), v);
                 }
             }
         }

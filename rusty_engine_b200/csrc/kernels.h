@@ -19,6 +19,7 @@ struct RouteParams {
     int T, H, E, k, gate, has_shared;
     __half* xb;             // [T, H] fp16 copy of x (GEMM B operand)
     int* rowexp;            // [rows] SwiGLU row exponents, set to -127 by the dispatch
+    __half* xs;             // optional [rows, H]: x rows in expert-sorted order (tensor-core path)
     float* logits;          // [T, E] router logits (the exact moe::matvec values)
     float* out_zero;        // optional: rows of `out` to zero (atomic combine)
     int* topk_id;           // [T, k]
@@ -80,15 +81,17 @@ struct WMaps {
 };
 
 // Everything the tcgen05 kernels read through TMA: [routed | shared expert][matrix 0 | 1]
-// weight maps and the SwiGLU activations h ([rows, I] fp16, 64 x 128 boxes, 128-B swizzle).
+// weight maps and the token operand b: the expert-sorted x rows (gate/up) or the SwiGLU
+// activations h (down), [rows, width] fp16 in 64 x 128 boxes with the 128-B swizzle.
 struct alignas(64) TcMaps {
     WMaps w[2][2];
-    CUtensorMap h;
+    CUtensorMap b;
 };
 
 // Build the maps of one stack (after upload_mat) / of the h workspace; false on a driver error.
 bool make_weight_maps(const DevMat& M, WMaps& out);
-bool make_h_map(const __half* h, uint64_t rows, uint32_t I, CUtensorMap& out);
+bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMap& out);
+int tc_max_inter();  // largest I the tensor-core down kernel supports
 
 // large-batch (tcgen05) grouped kernels; tile_rows = rows per tile
 int tc_tile_rows();

@@ -365,12 +365,14 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.n_tiles = (int*)A(16);
     w.tiles = (int4*)A((size_t)L->max_tiles * 16);
     w.h = (__half*)A(rows * I * 2);
+    w.xs = (__half*)A(rows * H * 2);
     w.hexp = (int8_t*)A(rows * (I / HBLK));
     w.rowexp = (int*)A(rows * 4);
     w.logits = (float*)A((size_t)cap * E * 4);
     if (need_y || L->ws_had_y) w.y = (float*)A(rows * H * 4);
     if (!ok) return fail(RMOE_ERR_OOM, "workspace cudaMalloc failed for %u tokens", cap);
-    if (!make_h_map(w.h, rows, I, L->hmap)) return fail(RMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for h");
+    if (!make_rows_map(w.h, rows, I, L->hmap) || !make_rows_map(w.xs, rows, H, L->xsmap))
+        return fail(RMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the token operands");
     cudaMemset(w.ticket, 0, 16);
     cudaMemset(w.status, 0, 16);
     L->ws_T = cap;
@@ -400,9 +402,10 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.slot_row = w.slot_row; rp.n_rows = w.n_rows; rp.tiles = w.tiles; rp.n_tiles = w.n_tiles;
     // Large batches (>= 32 routed rows per expert on average) run the tcgen05 kernels, small
     // ones the bandwidth-bound mma.sync kernels; the flags force either path.
-    bool use_tc = (uint64_t)T * L->k >= 32ull * L->E;
+    bool use_tc = (uint64_t)T * L->k >= 32ull * L->E && L->I <= (uint32_t)tc_max_inter();
     if (flags & RMOE_FLAG_FORCE_SMALL) use_tc = false;
-    if (flags & RMOE_FLAG_FORCE_LARGE) use_tc = true;
+    if ((flags & RMOE_FLAG_FORCE_LARGE) && L->I <= (uint32_t)tc_max_inter()) use_tc = true;
+    rp.xs = use_tc ? w.xs : nullptr;
     const int tile_rows = use_tc ? tc_tile_rows() : small_tile_rows();
     const uint64_t rows_T = (uint64_t)T * L->k + (L->has_shared ? T : 0);
     const int max_tiles = (int)std::min<uint64_t>((uint64_t)L->max_tiles, rows_T / tile_rows + L->E + 2);
@@ -431,7 +434,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         maps.w[0][1] = L->mu;
         maps.w[1][0] = L->smg;
         maps.w[1][1] = L->smu;
-        maps.h = L->hmap;
+        maps.b = L->xsmap;
     }
     e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : launch_small_gateup(gp, max_tiles, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
@@ -439,6 +442,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     if (use_tc) {
         maps.w[0][0] = L->md;
         maps.w[1][0] = L->smd;
+        maps.b = L->hmap;
     }
     e = use_tc ? launch_tc_down(gp, maps, max_tiles, s) : launch_small_down(gp, max_tiles, s);
     if (e != cudaSuccess) return cuda_fail(e, "down launch");
@@ -511,6 +515,9 @@ rmoe_status rmoe_layer_forward(rmoe_layer* L, const float* x, uint32_t T, float*
         if (status) return fail(RMOE_ERR_DEVICE, "device status 0x%x", status);
         return RMOE_OK;
     }
+    // the router streams x and the combine writes out with 16-B vector accesses
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
+        return fail(RMOE_ERR_INVALID, "device x / out must be 16-byte aligned");
     return layer_forward_device(L, x, T, out, s, flags);
 }
 

@@ -48,6 +48,7 @@ struct Workspace {
     __half* h = nullptr;
     int8_t* hexp = nullptr;
     int* rowexp = nullptr;
+    __half* xs = nullptr;   // expert-sorted x (tensor-core path)
     float* y = nullptr;
     float* logits = nullptr;
 };
@@ -61,7 +62,7 @@ struct rmoe_layer {
     uint32_t E_local = 0;
     rmoe::DevMat wg{}, wu{}, wd{}, swg{}, swu{}, swd{};
     rmoe::WMaps mg{}, mu{}, md{}, smg{}, smu{}, smd{};  // TMA maps of the stacks above
-    CUtensorMap hmap{};                                   // TMA map of the workspace h
+    CUtensorMap hmap{}, xsmap{};                          // TMA maps of the workspace h and xs
     float* router_w = nullptr;
     rmoe::Owned own;       // weights
     rmoe::Owned ws_own;    // workspace

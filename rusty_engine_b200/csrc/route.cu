@@ -336,6 +336,21 @@ __global__ void __launch_bounds__(TK_THREADS) scatter_rows_kernel(RouteParams p)
             p.rowexp[base + t] = -127;
         }
     }
+    if (p.xs) {
+        // expert-sorted fp16 copy of x: each (token, slot) row (and the shared expert's row)
+        // goes to its sorted position, 16 B per lane, one warp per row
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        const int per = k + (p.has_shared ? 1 : 0);
+        const int nrow = min(TK_TOK, p.T - t0) * per;
+        const int base = p.has_shared ? p.expert_off[E] : 0;
+        for (int i = warp; i < nrow; i += TK_THREADS / 32) {
+            const int tl = i / per, j = i - tl * per, t = t0 + tl;
+            const int pos = (j < k) ? off[p.topk_id[(size_t)t * k + j]] + p.local_rank[(size_t)t * k + j] : base + t;
+            const uint4* src = reinterpret_cast<const uint4*>(p.xb + (size_t)t * p.H);
+            uint4* dst = reinterpret_cast<uint4*>(p.xs + (size_t)pos * p.H);
+            for (int c = lane; c < p.H / 8; c += 32) dst[c] = src[c];
+        }
+    }
 }
 
 int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
