@@ -103,6 +103,25 @@ RMOE_API rmoe_status rmoe_layer_create(const rmoe_layer_desc* desc, rmoe_layer**
 RMOE_API rmoe_status rmoe_layer_forward(rmoe_layer* layer, const float* x, uint32_t T, float* out,
                                void* stream, uint32_t flags);
 
+/* Size of the library's static device scratch used by rmoe_layer_forward_noalloc: 8 MiB, held
+ * on every GPU that loads the library until the process exits. */
+#define RMOE_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* No counterpart in the reference.  The same layer forward as rmoe_layer_forward for a small
+ * batch, allocating no device memory: for callers that cannot call cudaMalloc at forward time
+ * (serving runtimes that reserved the device's memory up front for their own pool, decode
+ * loops that must not take cudaMalloc's implicit device synchronisation).  x and out are
+ * 16-byte-aligned device pointers (T x H f32); it runs the small-batch kernels with the atomic
+ * combine, in-stream and without synchronising.  Its scratch is one static device array of
+ * RMOE_NOALLOC_SCRATCH_BYTES; a batch whose scratch would not fit is rejected with
+ * RMOE_ERR_INVALID and a message giving the bytes it needs (about 2.4 MB for 64 tokens of an
+ * H 2048 / E 128 / k 8 / I 768 layer).  The first call on a device looks up the array's
+ * address (cudaGetSymbolAddress), so make that first call before any stream capture.  Every
+ * call on a device shares the array: calls that overlap on the GPU race on it.  It does not
+ * update what rmoe_layer_routing / rmoe_layer_logits / rmoe_layer_stage_ms report. */
+RMOE_API rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* layer, const float* x, uint32_t T, float* out,
+                                                void* stream);
+
 /* Routing of the last forward with RMOE_FLAG_ROUTING_OUT: expert ids (T x k, chosen order)
  * and weights (T x k), copied to host buffers.  Mirrors route() (src/moe.rs:120-125). */
 RMOE_API rmoe_status rmoe_layer_routing(rmoe_layer* layer, uint32_t T, uint32_t* ids, float* weights);

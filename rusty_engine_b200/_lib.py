@@ -51,8 +51,10 @@ class LayerDesc(C.Structure):
 EXPORTS = [
     "rmoe_layer_create", "rmoe_layer_forward", "rmoe_layer_routing", "rmoe_layer_logits", "rmoe_layer_destroy",
     "rmoe_last_error", "rmoe_dequant", "rmoe_qmat_matmul", "rmoe_route", "rmoe_ep_unique_id",
-    "rmoe_ep_layer_create", "rmoe_build_info", "rmoe_layer_stage_ms",
+    "rmoe_ep_layer_create", "rmoe_build_info", "rmoe_layer_stage_ms", "rmoe_layer_forward_noalloc",
 ]
+
+NOALLOC_SCRATCH_BYTES = 8 << 20  # RMOE_NOALLOC_SCRATCH_BYTES
 
 _lib = None
 _lock = threading.Lock()
@@ -70,6 +72,7 @@ def load():
         vp, u32, u64, i32 = C.c_void_p, C.c_uint32, C.c_uint64, C.c_int32
         L.rmoe_layer_create.argtypes = [C.POINTER(LayerDesc), C.POINTER(vp)]
         L.rmoe_layer_forward.argtypes = [vp, vp, u32, vp, vp, u32]
+        L.rmoe_layer_forward_noalloc.argtypes = [vp, vp, u32, vp, vp]
         L.rmoe_layer_routing.argtypes = [vp, u32, vp, vp]
         L.rmoe_layer_logits.argtypes = [vp, u32, vp]
         L.rmoe_layer_stage_ms.argtypes = [vp, vp]
