@@ -18,7 +18,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -40,6 +39,13 @@ CONFIGS = {
 }
 
 
+def kernels_per_forward(lw, T):
+    """Kernels of this library one forward launches: router logits, top-k + dispatch scan, row
+    scatter, gate/up (+SwiGLU), down (+atomic weighted combine); the tensor-core path (T*k >=
+    32*E) adds the expert-sorted x gather and the h rescale between gate/up and down."""
+    return 7 if T * lw.k >= 32 * lw.E else 5
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -50,53 +56,64 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event reasons of this rank's GPU, read through NVML every 2 ms while
+    the timed region runs (read-only queries; nothing is set).  The GPU is found by UUID so the
+    NVML index need not match the CUDA index."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, index: int):
-        self.index, self.proc, self.lines = index, None, []
+    def __init__(self, cuda_index: int):
+        self.h, self.samples, self.reasons, self.err = None, [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml as N
+            import torch
+
+            N.nvmlInit()
+            self.N = N
+            uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+            try:
+                self.h = N.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                pr = torch.cuda.get_device_properties(cuda_index)
+                self.h = N.nvmlDeviceGetHandleByPciBusId(
+                    f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0")
+            self.smax = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: reported, not fatal
+            self.err = f"nvml unavailable: {type(e).__name__}"
+
+    def _sample(self):
+        N = self.N
+        self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+        r = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        for name, bit in self.REASONS.items():
+            if r & bit:
+                self.reasons.add(name)
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        if self.h is None:
+            return
+        self._sample()
+        self.t = threading.Thread(target=self._loop, daemon=True)
+        self.t.start()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.h is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "nvml unavailable"]}
+        self._stop.set()
+        self.t.join(timeout=1)
+        self._sample()
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.smax,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "src": "nvml, 2 ms poll"}
 
 
 def cpu_baseline(cfg_name, lw, x, budget_s=15.0):
@@ -285,7 +302,7 @@ def main():
         line = {
             "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16-mma/f32-router", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16-mma/f32-acc/f32-router", "data": "synthetic",
             "config": {"workload": label, "tokens_per_gpu": T, "experts_touched": int(touched),
                        "l2": "flushed between steps (256 MiB write outside the events)",
                        "parallelism": f"replicas{world}" if world > 1 else "single"},
@@ -293,7 +310,7 @@ def main():
             "roofline": roof,
             "e2e": {"value": T * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * lw.H * 4,
                     "d2h_bytes_per_step": T * lw.H * 4},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": kernels_per_forward(lw, T) * args.steps,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -34,7 +34,6 @@ static constexpr int TC_BN = 128;  // expert-sorted rows per tile (MMA N, rounde
 static constexpr int TC_KS = 64;   // K elements per MMA stage (one 128-B swizzle row of fp16)
 static constexpr int TC_NST = 4;   // MMA stages in flight
 static constexpr int TC_RST = 2;   // raw weight stages in flight
-static constexpr int TC_MAX_HBLK = 48;  // I / 64 this path supports (I <= 3072)
 
 int tc_tile_rows() { return TC_BN; }
 
@@ -130,8 +129,6 @@ bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMa
                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int tc_max_inter() { return TC_MAX_HBLK * HBLK; }
-
 // ---------------------------------------------------------------------------------------------
 // device: TMA 2-D tile load (no multicast)
 // ---------------------------------------------------------------------------------------------
@@ -143,13 +140,12 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
         : "memory");
 }
 
-__device__ __forceinline__ float nib(uint32_t w, int sh) { return (float)((w >> sh) & 0xFu); }
-
-// Decode K-elements [64*sub, 64*sub + 64) of one weight row into 32 packed fp16 pairs (k, k+1).
+// Decode K-elements [64*sub + 32*half, +32) of one weight row into 16 packed fp16 pairs (k, k+1).
 // p = the row's main-plane bytes for the stage; dq / aq = its block-scale / high-bit entries
-// (block b of the stage at dq + 256 b / aq + 512 b).
+// (block b of the stage at dq + 256 b / aq + 512 b).  half is warp-uniform.
 template <int TYPE>
-__device__ __forceinline__ void slice64(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub, uint32_t* v);
+__device__ __forceinline__ void slice32(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub, int half,
+                                        uint32_t* v);
 
 // Packed-half helpers: a 4- or 6-bit code c placed in the low mantissa bits of 0x6400 is the
 // exact fp16 value 1024 + c, so code -> fp16 costs one byte permute and one logic op per pair.
@@ -161,192 +157,164 @@ __device__ __forceinline__ uint32_t lop_or3(uint32_t a, uint32_t b, uint32_t c) 
     return r;
 }
 
-// Q4_K: y = d*sc*q - dmin*m.  Per pair: the two codes land in 1024 + q (exact), 1024 is
-// subtracted exactly, and one fused multiply-add by the fp16-rounded sub-block scale and min
-// gives the value (the scale, the min and the result each round once to fp16; the f32 path
-// rounds the result only, and the difference is well inside the layer tolerance).
+// Q4_K: y = d*sc*q - dmin*m over sub-block 2*sub + half (the low nibbles of the slice's 32 qs
+// bytes for half 0, the high nibbles for half 1).  Per pair: the two codes land in 1024 + q
+// (exact), 1024 is subtracted exactly, and one fused multiply-add by the fp16-rounded sub-block
+// scale and min gives the value (the scale, the min and the result each round once to fp16;
+// the f32 path rounds the result only, and the difference is well inside the layer tolerance).
 template <>
-__device__ __forceinline__ void slice64<T_Q4_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub,
+__device__ __forceinline__ void slice32<T_Q4_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub, int half,
                                                 uint32_t* v) {
-    uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
-    float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
-    int sc0, m0, sc1, m1;
-    scale_min_k4(2 * sub, p + 4, sc0, m0);
-    scale_min_k4(2 * sub + 1, p + 4, sc1, m1);
-    const __half2 D1 = __float2half2_rn(__fmul_rn(d, (float)sc0)), M1 = __float2half2_rn(-__fmul_rn(dmin, (float)m0));
-    const __half2 D2 = __float2half2_rn(__fmul_rn(d, (float)sc1)), M2 = __float2half2_rn(-__fmul_rn(dmin, (float)m1));
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
+    const float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
+    int sc, mn;
+    scale_min_k4(2 * sub + half, p + 4, sc, mn);
+    const __half2 D = __float2half2_rn(__fmul_rn(d, (float)sc)), M = __float2half2_rn(-__fmul_rn(dmin, (float)mn));
     const __half2 K = __float2half2_rn(1024.0f);
     const uint4* q = reinterpret_cast<const uint4*>(p + 16 + sub * 32);
-    uint4 a = q[0], b = q[1];
-    uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const uint4 a = q[0], b = q[1];
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const int sh = 4 * half;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const uint32_t p01 = __byte_perm(w[i], 0, 0x4140), p23 = __byte_perm(w[i], 0, 0x4342);
-        auto lo = [&](uint32_t pp) {
-            return as_u32(__hfma2(__hsub2(as_h2((pp & 0x000F000Fu) | 0x64006400u), K), D1, M1));
-        };
-        auto hi = [&](uint32_t pp) {
-            return as_u32(__hfma2(__hsub2(as_h2(((pp >> 4) & 0x000F000Fu) | 0x64006400u), K), D2, M2));
-        };
-        v[2 * i] = lo(p01);
-        v[2 * i + 1] = lo(p23);
-        v[16 + 2 * i] = hi(p01);
-        v[16 + 2 * i + 1] = hi(p23);
+        v[2 * i] = as_u32(__hfma2(__hsub2(as_h2(((p01 >> sh) & 0x000F000Fu) | 0x64006400u), K), D, M));
+        v[2 * i + 1] = as_u32(__hfma2(__hsub2(as_h2(((p23 >> sh) & 0x000F000Fu) | 0x64006400u), K), D, M));
     }
 }
 
 template <>
-__device__ __forceinline__ void slice64<T_Q5_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub,
+__device__ __forceinline__ void slice32<T_Q5_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub, int half,
                                                 uint32_t* v) {
-    uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
-    float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
-    int sc0, m0, sc1, m1;
-    scale_min_k4(2 * sub, p + 4, sc0, m0);
-    scale_min_k4(2 * sub + 1, p + 4, sc1, m1);
-    const float d1 = __fmul_rn(d, (float)sc0), dm1 = __fmul_rn(dmin, (float)m0);
-    const float d2 = __fmul_rn(d, (float)sc1), dm2 = __fmul_rn(dmin, (float)m1);
+    const uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
+    const float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
+    int sc, mn;
+    scale_min_k4(2 * sub + half, p + 4, sc, mn);
+    const float d1 = __fmul_rn(d, (float)sc), dm1 = __fmul_rn(dmin, (float)mn);
     const uint4* q = reinterpret_cast<const uint4*>(p + 48 + sub * 32);
     const uint4* hq = reinterpret_cast<const uint4*>(p + 16);
-    uint4 a = q[0], b = q[1], ha = hq[0], hb = hq[1];
-    uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    const int ul = 2 * sub, uh = 2 * sub + 1;
+    const uint4 a = q[0], b = q[1], ha = hq[0], hb = hq[1];
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
+    const int sh = 4 * half, ub = 2 * sub + half;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        auto lo = [&](int byte) {
-            float qv = (float)(((w[i] >> (8 * byte)) & 0xFu) + (((hw[i] >> (8 * byte + ul)) & 1u) << 4));
+        auto val = [&](int byte) {
+            float qv = (float)(((w[i] >> (8 * byte + sh)) & 0xFu) + (((hw[i] >> (8 * byte + ub)) & 1u) << 4));
             return __fsub_rn(__fmul_rn(d1, qv), dm1);
         };
-        auto hi = [&](int byte) {
-            float qv = (float)(((w[i] >> (8 * byte + 4)) & 0xFu) + (((hw[i] >> (8 * byte + uh)) & 1u) << 4));
-            return __fsub_rn(__fmul_rn(d2, qv), dm2);
-        };
-        v[2 * i] = pack_f16x2(lo(0), lo(1));
-        v[2 * i + 1] = pack_f16x2(lo(2), lo(3));
-        v[16 + 2 * i] = pack_f16x2(hi(0), hi(1));
-        v[16 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
+        v[2 * i] = pack_f16x2(val(0), val(1));
+        v[2 * i + 1] = pack_f16x2(val(2), val(3));
     }
 }
 
-// Q6_K main plane row: ql[128] | qh[64] | scales[16]; d from the block-scale plane.
+// Q6_K main plane row: ql[128] | qh[64] | scales[16]; d from the block-scale plane.  Slice
+// `sub` covers quadrants 2*(sub&1) and 2*(sub&1)+1 of the 128-element half sub>>1; `half`
+// picks one: its low bits are the low (sub even) or high (sub odd) nibbles of ql[0..31]
+// (half 0) or ql[32..63] (half 1) of that half, its two high bits sit at bits 2*quadrant of qh.
 template <>
-__device__ __forceinline__ void slice64<T_Q6_K>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub,
+__device__ __forceinline__ void slice32<T_Q6_K>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub, int half,
                                                 uint32_t* v) {
     const float q6d = h2f(*reinterpret_cast<const uint16_t*>(dq));
-    const int h = sub >> 1, odd = sub & 1;
-    const uint4* ql = reinterpret_cast<const uint4*>(p + h * 64);
+    const int h = sub >> 1, odd = sub & 1, qd = 2 * odd + half;
+    const uint4* ql = reinterpret_cast<const uint4*>(p + h * 64 + half * 32);
     const uint4* qh = reinterpret_cast<const uint4*>(p + 128 + h * 32);
-    uint4 l0 = ql[0], l1 = ql[1], l2 = ql[2], l3 = ql[3], h0 = qh[0], h1 = qh[1];
-    uint32_t la[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};  // ql[h*64 + l], l < 32
-    uint32_t lb[8] = {l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};  // ql[h*64 + 32 + l]
-    uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const uint4 l0 = ql[0], l1 = ql[1], h0 = qh[0], h1 = qh[1];
+    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
     const int8_t* sc = reinterpret_cast<const int8_t*>(p + 192 + h * 8);
-    const int qa = 2 * odd, qb = 2 * odd + 1;  // quadrants of this slice
-    const int nsh = 4 * odd;                   // low nibbles for quadrants 0/1, high for 2/3
+    const int nsh = 4 * odd;
     // scales rounded once to fp16; (q6 - 32) is exact in fp16 (1024 + q6 - 1056)
-    const __half2 sa0 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qa * 2]));
-    const __half2 sa1 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qa * 2 + 1]));
-    const __half2 sb0 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qb * 2]));
-    const __half2 sb1 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qb * 2 + 1]));
+    const __half2 s0 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qd * 2]));
+    const __half2 s1 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qd * 2 + 1]));
     const __half2 K = __float2half2_rn(1056.0f);
-    // the two high bits of quadrant qa (bits 2qa..2qa+1 of qh) moved to bits 4..5: << (4 - 4*odd);
-    // of quadrant qb (bits 2qb..2qb+1): << 2 then >> 4*odd
 #pragma unroll
     for (int i = 0; i < 8; i++) {  // l = 4i .. 4i+3
-        const __half2 sa = (i < 4) ? sa0 : sa1, sb = (i < 4) ? sb0 : sb1;
+        const __half2 s = (i < 4) ? s0 : s1;
 #pragma unroll
         for (int pr = 0; pr < 2; pr++) {  // byte pairs (0,1) and (2,3)
             const uint32_t sel = pr ? 0x4342 : 0x4140;
-            const uint32_t pa = __byte_perm(la[i], 0, sel), pb = __byte_perm(lb[i], 0, sel);
-            const uint32_t ph = __byte_perm(hw[i], 0, sel);
-            const uint32_t ca = lop_or3((pa >> nsh) & 0x000F000Fu, (ph << (4 - nsh)) & 0x00300030u, 0x64006400u);
-            const uint32_t cb = lop_or3((pb >> nsh) & 0x000F000Fu, ((ph << 2) >> nsh) & 0x00300030u, 0x64006400u);
-            v[2 * i + pr] = as_u32(__hmul2(__hsub2(as_h2(ca), K), sa));
-            v[16 + 2 * i + pr] = as_u32(__hmul2(__hsub2(as_h2(cb), K), sb));
+            const uint32_t pl = __byte_perm(lw[i], 0, sel), ph = __byte_perm(hw[i], 0, sel);
+            // the quadrant's two high bits (2*qd, 2*qd+1) moved to bits 4..5
+            const uint32_t hb = qd <= 2 ? (ph << (4 - 2 * qd)) : (ph >> 2);
+            const uint32_t c = lop_or3((pl >> nsh) & 0x000F000Fu, hb & 0x00300030u, 0x64006400u);
+            v[2 * i + pr] = as_u32(__hmul2(__hsub2(as_h2(c), K), s));
         }
     }
 }
 
-// Q4_0 main plane row: qs[8 x 16]; slice = blocks 2*sub, 2*sub+1.
+// Q4_0 main plane row: qs[8 x 16]; half = block 2*sub + half (low nibbles -> elements 0..15,
+// high nibbles -> 16..31).
 template <>
-__device__ __forceinline__ void slice64<T_Q4_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub,
+__device__ __forceinline__ void slice32<T_Q4_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub, int half,
                                                 uint32_t* v) {
+    const int b = 2 * sub + half;
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
+    const uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int bb = 0; bb < 2; bb++) {
-        const int b = 2 * sub + bb;
-        const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
-        uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
-        uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            auto lo = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte)) & 0xFu) - 8), d); };
-            auto hi = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte + 4)) & 0xFu) - 8), d); };
-            v[16 * bb + 2 * i] = pack_f16x2(lo(0), lo(1));
-            v[16 * bb + 2 * i + 1] = pack_f16x2(lo(2), lo(3));
-            v[16 * bb + 8 + 2 * i] = pack_f16x2(hi(0), hi(1));
-            v[16 * bb + 8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
-        }
+    for (int i = 0; i < 4; i++) {
+        auto lo = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte)) & 0xFu) - 8), d); };
+        auto hi = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte + 4)) & 0xFu) - 8), d); };
+        v[2 * i] = pack_f16x2(lo(0), lo(1));
+        v[2 * i + 1] = pack_f16x2(lo(2), lo(3));
+        v[8 + 2 * i] = pack_f16x2(hi(0), hi(1));
+        v[8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
     }
 }
 
 // Q5_0 main plane row: qs[8 x 16]; high bits and scales from their planes.
 template <>
-__device__ __forceinline__ void slice64<T_Q5_0>(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub,
-                                                uint32_t* v) {
+__device__ __forceinline__ void slice32<T_Q5_0>(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub,
+                                                int half, uint32_t* v) {
+    const int b = 2 * sub + half;
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
+    const uint32_t qh = *reinterpret_cast<const uint32_t*>(aq + 512 * b);
+    const uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int bb = 0; bb < 2; bb++) {
-        const int b = 2 * sub + bb;
-        const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
-        const uint32_t qh = *reinterpret_cast<const uint32_t*>(aq + 512 * b);
-        uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
-        uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            auto lo = [&](int byte) {
-                int j = 4 * i + byte;
-                int x = (int)(((w[i] >> (8 * byte)) & 0xFu) | (((qh >> j) & 1u) << 4)) - 16;
-                return __fmul_rn((float)x, d);
-            };
-            auto hi = [&](int byte) {
-                int j = 4 * i + byte;
-                int x = (int)(((w[i] >> (8 * byte + 4)) & 0xFu) | (((qh >> (j + 16)) & 1u) << 4)) - 16;
-                return __fmul_rn((float)x, d);
-            };
-            v[16 * bb + 2 * i] = pack_f16x2(lo(0), lo(1));
-            v[16 * bb + 2 * i + 1] = pack_f16x2(lo(2), lo(3));
-            v[16 * bb + 8 + 2 * i] = pack_f16x2(hi(0), hi(1));
-            v[16 * bb + 8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
-        }
+    for (int i = 0; i < 4; i++) {
+        auto lo = [&](int byte) {
+            int j = 4 * i + byte;
+            int x = (int)(((w[i] >> (8 * byte)) & 0xFu) | (((qh >> j) & 1u) << 4)) - 16;
+            return __fmul_rn((float)x, d);
+        };
+        auto hi = [&](int byte) {
+            int j = 4 * i + byte;
+            int x = (int)(((w[i] >> (8 * byte + 4)) & 0xFu) | (((qh >> (j + 16)) & 1u) << 4)) - 16;
+            return __fmul_rn((float)x, d);
+        };
+        v[2 * i] = pack_f16x2(lo(0), lo(1));
+        v[2 * i + 1] = pack_f16x2(lo(2), lo(3));
+        v[8 + 2 * i] = pack_f16x2(hi(0), hi(1));
+        v[8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
     }
 }
 
-// Q8_0 main plane row: qs[8 x 32].
+// Q8_0 main plane row: qs[8 x 32]; half = block 2*sub + half.
 template <>
-__device__ __forceinline__ void slice64<T_Q8_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub,
+__device__ __forceinline__ void slice32<T_Q8_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub, int half,
                                                 uint32_t* v) {
+    const int b = 2 * sub + half;
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
+    const uint4* q = reinterpret_cast<const uint4*>(p + 32 * b);
+    const uint4 a = q[0], c = q[1];
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
 #pragma unroll
-    for (int bb = 0; bb < 2; bb++) {
-        const int b = 2 * sub + bb;
-        const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
-        const uint4* q = reinterpret_cast<const uint4*>(p + 32 * b);
-        uint4 a = q[0], c = q[1];
-        uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-        for (int i = 0; i < 8; i++) {  // word i holds elements 4i..4i+3 of the block
-            auto val = [&](int byte) { return __fmul_rn((float)(int8_t)((w[i] >> (8 * byte)) & 0xFFu), d); };
-            v[16 * bb + 2 * i] = pack_f16x2(val(0), val(1));
-            v[16 * bb + 2 * i + 1] = pack_f16x2(val(2), val(3));
-        }
+    for (int i = 0; i < 8; i++) {  // word i holds elements 4i..4i+3 of the block
+        auto val = [&](int byte) { return __fmul_rn((float)(int8_t)((w[i] >> (8 * byte)) & 0xFFu), d); };
+        v[2 * i] = pack_f16x2(val(0), val(1));
+        v[2 * i + 1] = pack_f16x2(val(2), val(3));
     }
 }
 
 template <>
-__device__ __forceinline__ void slice64<T_DENSE>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub,
+__device__ __forceinline__ void slice32<T_DENSE>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub, int half,
                                                  uint32_t* v) {
-    const uint4* q = reinterpret_cast<const uint4*>(p + 128 * sub);
+    const uint4* q = reinterpret_cast<const uint4*>(p + 128 * sub + 64 * half);
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        uint4 a = q[i];
+    for (int i = 0; i < 4; i++) {
+        const uint4 a = q[i];
         v[4 * i] = a.x;
         v[4 * i + 1] = a.y;
         v[4 * i + 2] = a.z;
@@ -362,13 +330,19 @@ struct TcGeom {
     // computes); gate/up fills the tensor memory with its two accumulators and runs alone
     static constexpr int NST = NMAT == 2 ? TC_NST : TC_NST - 1;
     static constexpr int SMEM = NST * B_STAGE + TC_RST * RAW_STAGE + 1024;
-    static constexpr int THREADS = 32 * (4 + 4 * NMAT);
+    // converter warps per matrix: 4 decode whole 64-element slices; 8 would split each slice
+    // into two 32-element halves (measured slower on B200: the per-slice waits and arrivals
+    // double while the decode itself does not shrink)
+    static constexpr int CW = 4;
+    static constexpr int CONV = 32 * CW * NMAT;  // converter / epilogue threads
+    static constexpr int THREADS = 128 + CONV;
+    static constexpr int MIN_BLOCKS = NMAT == 2 ? 1 : 2;
     static constexpr uint32_t TMEM_COLS = NMAT == 2 ? 512 : 256;
     static constexpr int A_COL0 = NMAT * TC_BN;  // A ring after the accumulators
 };
 
 template <int TYPE, int NMAT>
-__global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
+__global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT>::MIN_BLOCKS)
     tc_grouped_kernel(const __grid_constant__ GroupedParams p, const __grid_constant__ TcMaps maps) {
     using G = TcGeom<TYPE, NMAT>;
     using RS = RawStage<TYPE>;
@@ -376,11 +350,10 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
     constexpr int NST = G::NST;
     extern __shared__ uint8_t dsmem[];
     __shared__ __align__(8) uint64_t bar_raw_full[TC_RST], bar_raw_empty[TC_RST];
-    __shared__ __align__(8) uint64_t bar_a_full[NST], bar_b_full[NST], bar_empty[NST], bar_b_land[NST];
+    __shared__ __align__(8) uint64_t bar_a_full[NST], bar_b_full[NST], bar_empty[NST];
     __shared__ __align__(8) uint64_t bar_acc;
     __shared__ uint32_t tmem_holder;
     __shared__ int s_tok[TC_BN], s_rexp[TC_BN];
-    __shared__ int8_t s_hexp[NMAT == 1 ? TC_BN * TC_MAX_HBLK : 1];
     __shared__ float s_w[TC_BN];
     __shared__ volatile int s_abort;
 
@@ -405,13 +378,12 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
     if (tid == 0) {
         for (int i = 0; i < TC_RST; i++) {
             mbar_init(smem_u32(&bar_raw_full[i]), 1);
-            mbar_init(smem_u32(&bar_raw_empty[i]), 4 * NMAT);
+            mbar_init(smem_u32(&bar_raw_empty[i]), G::CW * NMAT);
         }
         for (int i = 0; i < NST; i++) {
-            mbar_init(smem_u32(&bar_a_full[i]), 4 * NMAT);
-            mbar_init(smem_u32(&bar_b_full[i]), NMAT == 2 ? 1 : 32);
+            mbar_init(smem_u32(&bar_a_full[i]), G::CW * NMAT);
+            mbar_init(smem_u32(&bar_b_full[i]), 1);
             mbar_init(smem_u32(&bar_empty[i]), 1);
-            mbar_init(smem_u32(&bar_b_land[i]), 1);
         }
         mbar_init(smem_u32(&bar_acc), 1);
         s_abort = 0;
@@ -430,10 +402,6 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
         s_tok[n] = tok;
         s_w[n] = w;
         s_rexp[n] = rexp;
-    }
-    if (NMAT == 1) {  // block exponents of the tile's h rows (the down kernel rescales B with them)
-        const int nblk = p.I / HBLK;
-        for (int i = tid; i < nrows * nblk; i += G::THREADS) s_hexp[i] = p.hexp[(size_t)row0 * nblk + i];
     }
     if (warp == 1) tmem_alloc(smem_u32(&tmem_holder), G::TMEM_COLS);
     fence_before_sync();
@@ -495,29 +463,8 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
         }
         __syncwarp();
     } else if (warp < 4) {
-        // ---------------- token tiles ----------------
-        // gate/up: one thread streams the expert-sorted x tiles with TMA straight onto b_full.
-        // down: one thread loads the h tiles with TMA; then all 64 threads bring every row's
-        // 64-feature block to the row's common scale 2^rowexp (exact power-of-two multiplies).
-        const int bt = tid - 64;
-        const int nblk = p.I / HBLK;
-        bool ok = true;
-        if (NMAT == 2) {
-            if (bt == 0) {
-                for (int kt = 0; kt < nk; kt++) {
-                    const int s = kt % NST;
-                    if (s_abort) break;
-                    if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
-                        fail();
-                        break;
-                    }
-                    const uint32_t bar = smem_u32(&bar_b_full[s]);
-                    mbar_arrive_expect_tx(bar, (uint32_t)G::B_STAGE);
-                    tma_2d(bring + (uint32_t)s * G::B_STAGE, &maps.b, kt * TC_KS, row0, bar);
-                }
-            }
-        } else if (bt == 0) {
-            // issuer: keeps every free stage loading, never waits for a rescale
+        // ---------------- token tiles: one thread streams them with TMA onto b_full ----------------
+        if (tid == 64) {
             for (int kt = 0; kt < nk; kt++) {
                 const int s = kt % NST;
                 if (s_abort) break;
@@ -525,51 +472,16 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
                     fail();
                     break;
                 }
-                const uint32_t bar = smem_u32(&bar_b_land[s]);
+                const uint32_t bar = smem_u32(&bar_b_full[s]);
                 mbar_arrive_expect_tx(bar, (uint32_t)G::B_STAGE);
                 tma_2d(bring + (uint32_t)s * G::B_STAGE, &maps.b, kt * TC_KS, row0, bar);
-            }
-        } else if (bt >= 32) {
-            // rescalers (warp 3): bring each landed stage to the rows' common scales
-            const int rt = bt - 32;
-            for (int st = 0; st < nk && ok; st++) {
-                if (s_abort) break;
-                const uint32_t bst = bring + (uint32_t)(st % NST) * G::B_STAGE;
-                if (!mbar_wait(smem_u32(&bar_b_land[st % NST]), (st / NST) & 1)) {
-                    fail();
-                    ok = false;
-                    break;
-                }
-                // one 128-B row (64 fp16) per step; the 8 chunks are independent, so all loads issue
-                // before the multiplies (a row's swizzle permutes its chunks, the scale is per row)
-                for (int n = rt; n < nrows; n += 32) {
-                    const int dexp = (int)s_hexp[n * nblk + st] - s_rexp[n];
-                    if (dexp == 0) continue;
-                    uint4* row = reinterpret_cast<uint4*>(gbase + (bst - sbase) + n * 128);
-                    if (dexp < -24) {
-#pragma unroll
-                        for (int c = 0; c < 8; c++) row[c] = make_uint4(0, 0, 0, 0);
-                        continue;
-                    }
-                    const __half2 sc = __float2half2_rn(exp2i(dexp));  // exact: 2^-24 .. 1
-                    uint4 v[8];
-#pragma unroll
-                    for (int c = 0; c < 8; c++) v[c] = row[c];
-#pragma unroll
-                    for (int c = 0; c < 8; c++) {
-                        __half2* h2 = reinterpret_cast<__half2*>(&v[c]);
-#pragma unroll
-                        for (int i = 0; i < 4; i++) h2[i] = __hmul2(h2[i], sc);
-                        row[c] = v[c];
-                    }
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(smem_u32(&bar_b_full[st % NST]));
             }
         }
     } else {
         // ---------------- converters: one thread per weight row ----------------
-        const int cw = warp - 4, m = cw >> 2, q = warp & 3;
+        // warp (4 + cw) writes TMEM lanes 32 * (warp & 3) (a warp may only reach its quarter)
+        constexpr int CW = G::CW;
+        const int cw = warp - 4, m = cw / CW, q = warp & 3, part = (cw % CW) >> 2;  // part: slice half (CW 8)
         const int r = q * 32 + lane;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
         bool ok = true;
@@ -587,9 +499,18 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
                 break;
             }
             const uint8_t* mat = raw_g + (size_t)((j % TC_RST) * NMAT + m) * RS::BYTES;
-            uint32_t v[32];
-            slice64<TYPE>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, v);
-            tmem_st32(tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32), v);
+            const uint8_t *rp = mat + r * PITCH, *rd = mat + RS::DOFF + r * 2, *ra = mat + RS::AOFF + r * 4;
+            const uint32_t acol = tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32);
+            if (CW == 8) {
+                uint32_t v[16];
+                slice32<TYPE>(rp, rd, ra, sub, part, v);
+                tmem_st16(acol + 16 * part, v);
+            } else {
+                uint32_t v[32];
+                slice32<TYPE>(rp, rd, ra, sub, 0, v);
+                slice32<TYPE>(rp, rd, ra, sub, 1, v + 16);
+                tmem_st32(acol, v);
+            }
             tmem_st_wait();
             fence_before_sync();
             __syncwarp();
@@ -608,8 +529,8 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
             // SwiGLU in f32 into a shared staging tile hs[n][f] (the rings are free now)
             float* hs = reinterpret_cast<float*>(gbase);
             constexpr int HLD = TC_M + 1;
-            for (int c = 2 * m; c < 2 * m + 2; c++) {
-                if (c * 32 >= n_eff) break;
+            // token chunk c (32 columns) of the accumulators: warps of a lane quarter share them out
+            for (int c = cw >> 2; c * 32 < n_eff; c += G::CONV / 128) {
                 uint32_t g[32], u[32];
                 tmem_ld32(tlane + (uint32_t)(c * 32), g);
                 tmem_ld32(tlane + (uint32_t)(TC_BN + c * 32), u);
@@ -624,12 +545,12 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
                     }
                 }
             }
-            asm volatile("bar.sync 1, %0;\n" ::"n"(32 * 4 * NMAT) : "memory");
+            asm volatile("bar.sync 1, %0;\n" ::"n"(G::CONV) : "memory");
             if (work) {
                 // per (row, 64-feature block): exponent, fp16 values, block/row exponents
                 const int nblk = p.I / HBLK;
                 const int ct = tid - 128;
-                for (int pi = ct; pi < nrows * 2; pi += 32 * 4 * NMAT) {
+                for (int pi = ct; pi < nrows * 2; pi += G::CONV) {
                     const int n = pi >> 1, blk = pi & 1;
                     const float* src = hs + n * HLD + blk * 64;
                     float amax = 0.0f;
@@ -662,7 +583,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
             // reductions. Scaling by 2^rowexp is exact, so w * (acc * 2^e) == acc * (w * 2^e).
             float* ys = reinterpret_cast<float*>(gbase);
             constexpr int YLD = TC_M + 4;
-            for (int c = 0; c * 32 < n_eff; c++) {
+            for (int c = cw >> 2; c * 32 < n_eff; c += G::CONV / 128) {
                 uint32_t a[32];
                 tmem_ld32(tlane + (uint32_t)(c * 32), a);
                 tmem_ld_wait();
@@ -674,10 +595,10 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
                     ys[n * YLD + r] = __fmul_rn(__uint_as_float(a[i]), sc);
                 }
             }
-            asm volatile("bar.sync 1, %0;\n" ::"n"(32 * 4 * NMAT) : "memory");
+            asm volatile("bar.sync 1, %0;\n" ::"n"(G::CONV) : "memory");
             if (work) {
                 const int f = fb * TC_M + 4 * lane;
-                for (int n = q; n < nrows; n += 4) {  // warp q of the four epilogue warps
+                for (int n = cw; n < nrows; n += G::CONV / 32) {  // one token row per epilogue warp
                     const float4 v = *reinterpret_cast<const float4*>(ys + n * YLD + 4 * lane);
                     if (p.y) *reinterpret_cast<float4*>(p.y + (size_t)(row0 + n) * p.H + f) = v;
                     else atomicAdd(reinterpret_cast<float4*>(p.out + (size_t)s_tok[n] * p.H + f), v);
@@ -691,6 +612,42 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NMAT), NMAT == 2 ? 1 : 2)
         fence_after_sync();
         tmem_dealloc(tbase, G::TMEM_COLS);
     }
+}
+
+// ---------------------------------------------------------------------------------------------
+// h to one scale per row.  The gate/up CTAs each see 128 features of a row, so they store h as
+// fp16 x 2^hexp per 64-feature block; once all of them are done the row's common exponent
+// (rowexp = max over its blocks) is known and every block is brought to it here, once, so the
+// down kernel's token tiles go from global memory to the MMA untouched.  Multiplying by
+// 2^(hexp - rowexp) <= 1 is exact down to the fp16 subnormal range; blocks more than 24 binades
+// below the row's largest would be flushed by it anyway and are zeroed.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rescale_h_kernel(__half* __restrict__ h, const int8_t* __restrict__ hexp,
+                                                        const int* __restrict__ rowexp, const int* __restrict__ n_rows,
+                                                        int I) {
+    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (r >= *n_rows) return;
+    const int re = __ldg(rowexp + r), nblk = I / HBLK;
+    uint4* row = reinterpret_cast<uint4*>(h + (size_t)r * I);
+    for (int c = lane; c < I / 8; c += 32) {
+        const int dexp = (int)__ldg(hexp + (size_t)r * nblk + c / 8) - re;
+        if (dexp == 0) continue;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (dexp >= -24) {
+            v = row[c];
+            const __half2 sc = __float2half2_rn(exp2i(dexp));
+            __half2* h2 = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+            for (int i = 0; i < 4; i++) h2[i] = __hmul2(h2[i], sc);
+        }
+        row[c] = v;
+    }
+}
+
+cudaError_t launch_rescale_h(const GroupedParams& p, int max_rows, cudaStream_t s) {
+    if (max_rows <= 0) return cudaSuccess;
+    rescale_h_kernel<<<(max_rows + 7) / 8, 256, 0, s>>>(p.h, p.hexp, p.rowexp, p.n_rows, p.I);
+    return cudaGetLastError();
 }
 
 template <int TYPE, int NMAT>

@@ -25,7 +25,7 @@ struct RouteParams {
     int* topk_id;           // [T, k]
     float* topk_w;          // [T, k]
     int* local_rank;        // [T, k] scratch
-    int* cta_cnt;           // [ceil(T/32), E] scratch
+    int* cta_cnt;           // [E, route_cnt_stride(route_grid(T))] scratch: counts, then prefixes
     unsigned int* ticket;   // last-CTA counter (0 between launches)
     int* expert_off;        // [E + 2]
     int* row_tok;           // [rows] token of each expert-sorted row
@@ -49,6 +49,7 @@ struct GroupedParams {
     const int* row_slot;
     const int4* tiles;
     const int* n_tiles;
+    const int* n_rows;            // expert-sorted rows in use
     const float* topk_w;          // [T, k]
     __half* h;                    // [rows, I] SwiGLU activations, fp16 * 2^hexp
     int8_t* hexp;                 // [rows, I / 64] block exponents
@@ -67,6 +68,8 @@ struct CombineParams {
 };
 
 int route_grid(int T);
+// row stride of the per-(expert, top-k CTA) count table: CTAs rounded up to 16
+__host__ __device__ inline int route_cnt_stride(int ncta) { return (ncta + 15) & ~15; }
 cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s);
 
 // small-batch (mma.sync) grouped kernels; tile_rows = tokens per tile
@@ -91,12 +94,13 @@ struct alignas(64) TcMaps {
 // Build the maps of one stack (after upload_mat) / of the h workspace; false on a driver error.
 bool make_weight_maps(const DevMat& M, WMaps& out);
 bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMap& out);
-int tc_max_inter();  // largest I the tensor-core down kernel supports
 
 // large-batch (tcgen05) grouped kernels; tile_rows = rows per tile
 int tc_tile_rows();
 cudaError_t launch_tc_gateup(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s);
 cudaError_t launch_tc_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s);
+// between the two: h blocks to their row's common exponent (rows beyond *n_rows untouched)
+cudaError_t launch_rescale_h(const GroupedParams& p, int max_rows, cudaStream_t s);
 
 cudaError_t launch_combine(const CombineParams& p, cudaStream_t s);
 cudaError_t launch_dequant_raw(int type, const void* src, uint64_t nblocks, float* dst, cudaStream_t s);

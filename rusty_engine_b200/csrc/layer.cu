@@ -354,7 +354,7 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.topk_id = (int*)A((size_t)cap * k * 4);
     w.topk_w = (float*)A((size_t)cap * k * 4);
     w.local_rank = (int*)A((size_t)cap * k * 4);
-    w.cta_cnt = (int*)A((size_t)((cap + 31) / 32) * E * 4);
+    w.cta_cnt = (int*)A((size_t)route_cnt_stride(route_grid((int)cap)) * E * 4);
     w.ticket = (unsigned*)A(16);
     w.status = (unsigned*)A(16);
     w.expert_off = (int*)A((size_t)(E + 2) * 4);
@@ -402,9 +402,9 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.slot_row = w.slot_row; rp.n_rows = w.n_rows; rp.tiles = w.tiles; rp.n_tiles = w.n_tiles;
     // Large batches (>= 32 routed rows per expert on average) run the tcgen05 kernels, small
     // ones the bandwidth-bound mma.sync kernels; the flags force either path.
-    bool use_tc = (uint64_t)T * L->k >= 32ull * L->E && L->I <= (uint32_t)tc_max_inter();
+    bool use_tc = (uint64_t)T * L->k >= 32ull * L->E;
     if (flags & RMOE_FLAG_FORCE_SMALL) use_tc = false;
-    if ((flags & RMOE_FLAG_FORCE_LARGE) && L->I <= (uint32_t)tc_max_inter()) use_tc = true;
+    if (flags & RMOE_FLAG_FORCE_LARGE) use_tc = true;
     rp.xs = use_tc ? w.xs : nullptr;
     const int tile_rows = use_tc ? tc_tile_rows() : small_tile_rows();
     const uint64_t rows_T = (uint64_t)T * L->k + (L->has_shared ? T : 0);
@@ -426,6 +426,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     gp.sgate = L->swg; gp.sup = L->swu; gp.sdown = L->swd;
     gp.H = (int)L->H; gp.I = (int)L->I; gp.E = (int)L->E; gp.k = (int)L->k;
     gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
+    gp.n_rows = w.n_rows;
     gp.topk_w = w.topk_w; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp; gp.y = det ? w.y : nullptr; gp.out = out; gp.status = w.status;
     TcMaps maps;
     if (use_tc) {
@@ -439,6 +440,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : launch_small_gateup(gp, max_tiles, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
     mark(2);
+    if (use_tc && (e = launch_rescale_h(gp, (int)rows_T, s)) != cudaSuccess) return cuda_fail(e, "h rescale launch");
     if (use_tc) {
         maps.w[0][0] = L->md;
         maps.w[1][0] = L->smd;

@@ -70,7 +70,7 @@ static void carve(Carver& c, const rmoe_layer* L, uint32_t T, uint64_t rows, int
     w.topk_w = c.take<float>((size_t)T * k * 4);
     w.local_rank = c.take<int>((size_t)T * k * 4);
     w.slot_row = c.take<int>((size_t)T * k * 4);
-    w.cta_cnt = c.take<int>((size_t)route_grid((int)T) * E * 4);
+    w.cta_cnt = c.take<int>((size_t)route_cnt_stride(route_grid((int)T)) * E * 4);
     w.expert_off = c.take<int>((E + 2) * 4);
     w.row_tok = c.take<int>(rows * 4);
     w.row_slot = c.take<int>(rows * 4);

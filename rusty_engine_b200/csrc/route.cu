@@ -153,12 +153,13 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
 // ---------------------------------------------------------------------------------------
 // Order = stable descending argsort (larger first, ties to the lower index), the rusty-engine
 // top_k / top_k_sigmoid contract (src/moe.rs:75-117).  Lane j < k returns the j-th expert id;
-// lane 0 writes the k weights to w_out in chosen order.
-__device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, float* w_out) {
-    float v[MAX_E / 32];
+// lane j < k writes pick j's weight to w_out[j].
+template <int NS>  // NS >= ceil(E / 32) logits per lane
+__device__ int warp_topk_n(const float* lg, int E, int k, int gate, int lane, float* w_out) {
+    float v[NS];
     unsigned taken = 0;
 #pragma unroll
-    for (int s = 0; s < MAX_E / 32; s++) {
+    for (int s = 0; s < NS; s++) {
         int e = lane + 32 * s;
         float xv = (e < E) ? lg[e] : 0.0f;
         if (gate == 1 && e < E) xv = 1.0f / (1.0f + expf(-xv));  // sigmoid (src/moe.rs:44-46)
@@ -172,7 +173,7 @@ __device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, floa
         float best = 0.0f;
         int bid = NONE;
 #pragma unroll
-        for (int s = 0; s < MAX_E / 32; s++) {
+        for (int s = 0; s < NS; s++) {
             // s ascending = index ascending, so a strict '>' keeps the lowest index on ties
             if (!((taken >> s) & 1u) && (bid == NONE || v[s] > best)) {
                 best = v[s];
@@ -189,41 +190,58 @@ __device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, floa
         if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
         if (lane == j) { chosen_score = best; chosen_id = bid; }
     }
-    float sc[MAX_K];
-#pragma unroll
-    for (int j = 0; j < MAX_K; j++) sc[j] = __shfl_sync(0xffffffffu, chosen_score, j);
-    if (lane == 0) {
-        if (gate == 1) {
-            float wsum = 0.0f;
-            for (int j = 0; j < k; j++) wsum = __fadd_rn(wsum, sc[j]);
-            for (int j = 0; j < k; j++) w_out[j] = (wsum == 0.0f) ? 0.0f : __fdiv_rn(sc[j], wsum);
-        } else {
-            // softmax_in_place (src/moe.rs:61-72): max fold, exp(v - max), sequential sum, divide
-            float mx = -INFINITY;
-            for (int j = 0; j < k; j++) mx = fmaxf(mx, sc[j]);
-            float sum = 0.0f;
-            for (int j = 0; j < k; j++) sum = __fadd_rn(sum, expf(__fsub_rn(sc[j], mx)));
-            for (int j = 0; j < k; j++) {
-                float ex = expf(__fsub_rn(sc[j], mx));
-                w_out[j] = (sum != 0.0f) ? __fdiv_rn(ex, sum) : ex;
-            }
-        }
+    // lane j < k holds pick j's score; the sums run in pick order on every lane (the same
+    // sequential f32 additions as the reference), each lane then forms its own weight
+    if (gate == 1) {
+        float wsum = 0.0f;
+        for (int j = 0; j < k; j++) wsum = __fadd_rn(wsum, __shfl_sync(0xffffffffu, chosen_score, j));
+        if (lane < k) w_out[lane] = (wsum == 0.0f) ? 0.0f : __fdiv_rn(chosen_score, wsum);
+    } else {
+        // softmax_in_place (src/moe.rs:61-72): max fold, exp(v - max), sequential sum, divide
+        float mx = -INFINITY;
+        for (int j = 0; j < k; j++) mx = fmaxf(mx, __shfl_sync(0xffffffffu, chosen_score, j));
+        const float ex = (lane < k) ? expf(__fsub_rn(chosen_score, mx)) : 0.0f;
+        float sum = 0.0f;
+        for (int j = 0; j < k; j++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, j));
+        if (lane < k) w_out[lane] = (sum != 0.0f) ? __fdiv_rn(ex, sum) : ex;
     }
     return chosen_id;
+}
+
+__device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, float* w_out) {
+    const int ns = (E + 31) / 32;
+    if (ns <= 1) return warp_topk_n<1>(lg, E, k, gate, lane, w_out);
+    if (ns <= 2) return warp_topk_n<2>(lg, E, k, gate, lane, w_out);
+    if (ns <= 4) return warp_topk_n<4>(lg, E, k, gate, lane, w_out);
+    if (ns <= 8) return warp_topk_n<8>(lg, E, k, gate, lane, w_out);
+    return warp_topk_n<MAX_E / 32>(lg, E, k, gate, lane, w_out);
 }
 
 // ---------------------------------------------------------------------------------------
 // top-k + counts (+ last-CTA scan and tile list)
 // ---------------------------------------------------------------------------------------
+// cta_cnt is expert-major, [E][ncp] with ncp = ncta rounded up to 16 (zero padding): CTA b's
+// pick count for expert e at e * ncp + b; the last CTA turns every expert's run of counts into
+// exclusive prefixes (rows before CTA b's first row of that expert), so a pick's row =
+// expert_off[e] + cta_cnt[e * ncp + b] + local rank.
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        int o = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += o;
+    }
+    return v;
+}
+
 __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     __shared__ int ids_s[TK_TOK * MAX_K];
     __shared__ int cnt_s[MAX_E + 2];
-    __shared__ int off_s[MAX_E + 2];
     __shared__ unsigned int ticket_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = blockIdx.x * TK_TOK;
     const int E = p.E, H = p.H, k = p.k;
     const int ntok = min(TK_TOK, p.T - t0);
+    const int ncta = gridDim.x;
 
     for (int tl = warp; tl < ntok; tl += TK_THREADS / 32) {
         int t = t0 + tl;
@@ -233,8 +251,9 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
             ids_s[tl * k + lane] = id;
         }
     }
-    // zero the output rows this CTA owns when the combine accumulates with atomics
-    if (p.out_zero) {
+    // zero the output rows this CTA owns when the combine accumulates with atomics (the x
+    // gather kernel does it instead when it runs)
+    if (p.out_zero && !p.xs) {
         for (int tl = 0; tl < ntok; tl++)
             for (int i = tid * 4; i < H; i += TK_THREADS * 4)
                 *reinterpret_cast<float4*>(p.out_zero + (size_t)(t0 + tl) * H + i) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -242,14 +261,17 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     __syncthreads();
     // in-CTA rank of every pick in token order: one thread per expert scans the CTA's
     // TK_TOK * k picks in order
+    const int ncp = route_cnt_stride(ncta);
     for (int e = tid; e < E; e += TK_THREADS) {
         int c = 0;
         for (int i = 0; i < ntok * k; i++)
             if (ids_s[i] == e) p.local_rank[(size_t)t0 * k + i] = c++;
-        p.cta_cnt[(size_t)blockIdx.x * E + e] = c;
+        p.cta_cnt[(size_t)e * ncp + blockIdx.x] = c;
+        if (blockIdx.x == 0)
+            for (int b = ncta; b < ncp; b++) p.cta_cnt[(size_t)e * ncp + b] = 0;
     }
 
-    // ---- last CTA: per-(CTA, expert) offsets, expert offsets, tile list ----
+    // ---- last CTA: per-(expert, CTA) prefixes, expert offsets, tile list ----
     __threadfence();
     __syncthreads();
     if (tid == 0) ticket_s = atomicAdd(p.ticket, 1u);
@@ -257,78 +279,103 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     if (ticket_s != gridDim.x - 1) return;
     __threadfence();
 
-    const int ncta = gridDim.x;
-    const int NE = E + (p.has_shared ? 1 : 0);
-    for (int e = tid; e < E; e += TK_THREADS) {
-        int c = 0;
-#pragma unroll 8
-        for (int b = 0; b < ncta; b++) c += __ldcg(p.cta_cnt + (size_t)b * E + e);
-        cnt_s[e] = c;
+    // TPE threads per expert (a power of two), each owning a run of consecutive CTAs (a multiple
+    // of 16): sum the run with 16-B loads (64 counts in flight), scan the runs' sums across the
+    // group, then rewrite the run as exclusive prefixes
+    int E2 = 1;
+    while (E2 < E) E2 <<= 1;
+    const int TPE = max(1, min(32, TK_THREADS / E2));
+    const int seg = (ncp / 16 + TPE - 1) / TPE * 16;
+    for (int e0 = 0; e0 < E; e0 += TK_THREADS / TPE) {
+        const int e = e0 + tid / TPE, part = tid % TPE;
+        const int b_lo = min(ncp, part * seg), b_hi = min(ncp, b_lo + seg);
+        int4* row = reinterpret_cast<int4*>(p.cta_cnt + (size_t)min(e, E - 1) * ncp);
+        int sum = 0;
+        int4 first[16];
+        for (int b = b_lo; b < b_hi; b += 64) {
+            int4 v[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) v[u] = (e < E && b + 4 * u < b_hi) ? __ldcg(row + b / 4 + u) : make_int4(0, 0, 0, 0);
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                sum += v[u].x + v[u].y + v[u].z + v[u].w;
+                if (b == b_lo) first[u] = v[u];
+            }
+        }
+        int incl = sum;
+        for (int off = 1; off < TPE; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, incl, off, TPE);
+            if (part >= off) incl += o;
+        }
+        if (e < E) {
+            int run = incl - sum;
+            for (int b = b_lo; b < b_hi; b += 64) {
+                int4 v[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++)
+                    v[u] = (b == b_lo) ? first[u] : (b + 4 * u < b_hi) ? __ldcg(row + b / 4 + u) : make_int4(0, 0, 0, 0);
+#pragma unroll
+                for (int u = 0; u < 16; u++) {
+                    if (b + 4 * u < b_hi) {
+                        const int4 c = v[u];
+                        row[b / 4 + u] = make_int4(run, run + c.x, run + c.x + c.y, run + c.x + c.y + c.z);
+                        run += c.x + c.y + c.z + c.w;
+                    }
+                }
+            }
+            if (part == TPE - 1) cnt_s[e] = incl;
+        }
     }
     if (tid == 0 && p.has_shared) cnt_s[E] = p.T;
     __syncthreads();
-    if (tid == 0) {
+    // warp 0: expert offsets and the tile list (expert, first row, rows), <= tile_rows rows each
+    if (warp == 0) {
+        const int NE = E + (p.has_shared ? 1 : 0);
         int run = 0, tiles = 0;
-        for (int e = 0; e < NE; e++) {
-            off_s[e] = run;
-            p.expert_off[e] = run;
-            run += cnt_s[e];
-            tiles += (cnt_s[e] + p.tile_rows - 1) / p.tile_rows;
-        }
-        off_s[NE] = run;
-        p.expert_off[NE] = run;
-        *p.n_rows = run;
-        if (tiles > p.max_tiles) {
-            atomicOr(p.status, (unsigned)DERR_TILES_OVERFLOW);
-            tiles = p.max_tiles;
-        }
-        *p.n_tiles = tiles;
-    }
-    __syncthreads();
-    // counts -> offsets in place (expert-major, CTA-minor keeps token order inside an expert)
-    for (int e = tid; e < E; e += TK_THREADS) {
-        int run = off_s[e];
-        for (int b = 0; b < ncta; b++) {
-            int c = __ldcg(p.cta_cnt + (size_t)b * E + e);
-            p.cta_cnt[(size_t)b * E + e] = run;
-            run += c;
-        }
-    }
-    // tile list: (expert, first row, rows) with at most tile_rows rows per tile
-    if (tid < 32) {
-        int base = 0;
-        for (int e = 0; e < NE; e++) {
-            int c = cnt_s[e];
-            int nt = (c + p.tile_rows - 1) / p.tile_rows;
-            for (int j = lane; j < nt; j += 32) {
-                int ti = base + j;
-                if (ti < p.max_tiles) {
-                    int r0 = j * p.tile_rows;
-                    p.tiles[ti] = make_int4(e, off_s[e] + r0, min(p.tile_rows, c - r0), 0);
-                }
+        for (int e0 = 0; e0 < NE; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < NE ? cnt_s[e] : 0;
+            const int nt = (c + p.tile_rows - 1) / p.tile_rows;
+            const int ic = warp_incl_scan(c, lane), itl = warp_incl_scan(nt, lane);
+            const int off = run + ic - c, tb = tiles + itl - nt;
+            if (e < NE) {
+                p.expert_off[e] = off;
+                for (int j = 0; j < nt; j++)
+                    if (tb + j < p.max_tiles)
+                        p.tiles[tb + j] = make_int4(e, off + j * p.tile_rows, min(p.tile_rows, c - j * p.tile_rows), 0);
             }
-            base += nt;
+            run += __shfl_sync(0xffffffffu, ic, 31);
+            tiles += __shfl_sync(0xffffffffu, itl, 31);
+        }
+        if (lane == 0) {
+            p.expert_off[NE] = run;
+            *p.n_rows = run;
+            if (tiles > p.max_tiles) {
+                atomicOr(p.status, (unsigned)DERR_TILES_OVERFLOW);
+                tiles = p.max_tiles;
+            }
+            *p.n_tiles = tiles;
+            *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
         }
     }
-    if (tid == 0) *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
 }
 
-// Place every (token, slot) at its expert-sorted row; one CTA per top-k CTA's tokens.
+// Place every (token, slot) at its expert-sorted row; CTA b handles the picks top-k CTA b made.
 __global__ void __launch_bounds__(TK_THREADS) scatter_rows_kernel(RouteParams p) {
-    const int t0 = blockIdx.x * TK_TOK, k = p.k, E = p.E;
+    const int t0 = blockIdx.x * TK_TOK, k = p.k, ncp = route_cnt_stride(gridDim.x);
     const int nent = min(TK_TOK, p.T - t0) * k;
-    const int* off = p.cta_cnt + (size_t)blockIdx.x * E;
     for (int i = threadIdx.x; i < nent; i += TK_THREADS) {
         int gi = t0 * k + i;
         int t = gi / k;
-        int pos = off[p.topk_id[gi]] + p.local_rank[gi];
+        const int e = p.topk_id[gi];
+        int pos = p.expert_off[e] + p.cta_cnt[(size_t)e * ncp + blockIdx.x] + p.local_rank[gi];
         p.row_tok[pos] = t;
         p.row_slot[pos] = gi - t * k;
         p.slot_row[gi] = pos;
         p.rowexp[pos] = -127;
     }
     if (p.has_shared) {
-        const int base = p.expert_off[E];
+        const int base = p.expert_off[p.E];
         for (int tl = threadIdx.x; tl < TK_TOK && t0 + tl < p.T; tl += TK_THREADS) {
             int t = t0 + tl;
             p.row_tok[base + t] = t;
@@ -336,20 +383,39 @@ __global__ void __launch_bounds__(TK_THREADS) scatter_rows_kernel(RouteParams p)
             p.rowexp[base + t] = -127;
         }
     }
-    if (p.xs) {
-        // expert-sorted fp16 copy of x: each (token, slot) row (and the shared expert's row)
-        // goes to its sorted position, 16 B per lane, one warp per row
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-        const int per = k + (p.has_shared ? 1 : 0);
-        const int nrow = min(TK_TOK, p.T - t0) * per;
-        const int base = p.has_shared ? p.expert_off[E] : 0;
-        for (int i = warp; i < nrow; i += TK_THREADS / 32) {
-            const int tl = i / per, j = i - tl * per, t = t0 + tl;
-            const int pos = (j < k) ? off[p.topk_id[(size_t)t * k + j]] + p.local_rank[(size_t)t * k + j] : base + t;
-            const uint4* src = reinterpret_cast<const uint4*>(p.xb + (size_t)t * p.H);
-            uint4* dst = reinterpret_cast<uint4*>(p.xs + (size_t)pos * p.H);
-            for (int c = lane; c < p.H / 8; c += 32) dst[c] = src[c];
+}
+
+// Expert-sorted fp16 copy of x for the tensor-core path: one warp per token reads its fp16 row
+// once (4 KB column chunks) and writes it to each of its rows (k picks + the shared expert);
+// the same warp zeroes the token's output row for the atomic combine.
+static constexpr int GX_CHUNK = 8;  // 16-B units per lane per chunk
+__global__ void __launch_bounds__(256) gather_x_kernel(RouteParams p) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (t >= p.T) return;
+    const int k = p.k, per = k + (p.has_shared ? 1 : 0), units = p.H / 8;
+    const int dst_row = lane < k ? p.slot_row[(size_t)t * k + lane] : 0;  // lane j < k: row of pick j
+    const int shared_row = p.has_shared ? p.expert_off[p.E] + t : 0;
+    const uint4* src = reinterpret_cast<const uint4*>(p.xb + (size_t)t * p.H);
+    for (int u0 = 0; u0 < units; u0 += 32 * GX_CHUNK) {
+        uint4 v[GX_CHUNK];
+#pragma unroll
+        for (int c = 0; c < GX_CHUNK; c++) {
+            const int u = u0 + 32 * c + lane;
+            if (u < units) v[c] = src[u];
         }
+        for (int j = 0; j < per; j++) {
+            const int pos = j < k ? __shfl_sync(0xffffffffu, dst_row, j) : shared_row;
+            uint4* dst = reinterpret_cast<uint4*>(p.xs + (size_t)pos * p.H);
+#pragma unroll
+            for (int c = 0; c < GX_CHUNK; c++) {
+                const int u = u0 + 32 * c + lane;
+                if (u < units) dst[u] = v[c];
+            }
+        }
+    }
+    if (p.out_zero) {
+        float4* o = reinterpret_cast<float4*>(p.out_zero + (size_t)t * p.H);
+        for (int u = lane; u < p.H / 4; u += 32) o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 }
 
@@ -370,6 +436,8 @@ cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
     topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess || !p.xs) return e;
+    gather_x_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p);
     return cudaGetLastError();
 }
 
