@@ -375,6 +375,20 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     const uint32_t bring = sbase, rawring = sbase + NST * G::B_STAGE;
     uint8_t* raw_g = gbase + NST * G::B_STAGE;
 
+    // TMA of raw stage j (all planes of all matrices) into ring slot j % TC_RST
+    auto issue_raw = [&](int j) {
+        const int s = j % TC_RST;
+        const uint32_t bar = smem_u32(&bar_raw_full[s]);
+        mbar_arrive_expect_tx(bar, (uint32_t)G::RAW_STAGE);
+#pragma unroll
+        for (int m = 0; m < NMAT; m++) {
+            const WMaps& wm = maps.w[sh][m];
+            const uint32_t dst = rawring + (uint32_t)(s * NMAT + m) * RS::BYTES;
+            tma_2d(dst, &wm.main, j * (Raw<TYPE>::MB / 2), grow0, bar);
+            if (Raw<TYPE>::DBLK) tma_2d(dst + RS::DOFF, &wm.d, grow0, j * Raw<TYPE>::DBLK, bar);
+            if (Raw<TYPE>::AUX) tma_2d(dst + RS::AOFF, &wm.aux, grow0, j * Raw<TYPE>::AUX, bar);
+        }
+    };
     if (tid == 0) {
         for (int i = 0; i < TC_RST; i++) {
             mbar_init(smem_u32(&bar_raw_full[i]), 1);
@@ -388,6 +402,8 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         mbar_init(smem_u32(&bar_acc), 1);
         s_abort = 0;
         fence_mbar_init();
+        // the first raw stages need no free-slot wait: start them before the prologue's loads
+        for (int j = 0; j < TC_RST && j < nraw; j++) issue_raw(j);
     }
     for (int n = tid; n < TC_BN; n += G::THREADS) {
         int tok = 0, rexp = 0;
@@ -417,23 +433,13 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     if (warp == 0) {
         // ---------------- TMA producer: raw weight superblocks ----------------
         if (lane == 0) {
-            for (int j = 0; j < nraw; j++) {
-                const int s = j % TC_RST;
+            for (int j = TC_RST; j < nraw; j++) {
                 if (s_abort) break;
-                if (j >= TC_RST && !mbar_wait(smem_u32(&bar_raw_empty[s]), ((j / TC_RST) + 1) & 1)) {
+                if (!mbar_wait(smem_u32(&bar_raw_empty[j % TC_RST]), ((j / TC_RST) + 1) & 1)) {
                     fail();
                     break;
                 }
-                const uint32_t bar = smem_u32(&bar_raw_full[s]);
-                mbar_arrive_expect_tx(bar, (uint32_t)G::RAW_STAGE);
-#pragma unroll
-                for (int m = 0; m < NMAT; m++) {
-                    const WMaps& wm = maps.w[sh][m];
-                    const uint32_t dst = rawring + (uint32_t)(s * NMAT + m) * RS::BYTES;
-                    tma_2d(dst, &wm.main, j * (Raw<TYPE>::MB / 2), grow0, bar);
-                    if (Raw<TYPE>::DBLK) tma_2d(dst + RS::DOFF, &wm.d, grow0, j * Raw<TYPE>::DBLK, bar);
-                    if (Raw<TYPE>::AUX) tma_2d(dst + RS::AOFF, &wm.aux, grow0, j * Raw<TYPE>::AUX, bar);
-                }
+                issue_raw(j);
             }
         }
         __syncwarp();
@@ -479,47 +485,54 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         }
     } else {
         // ---------------- converters: one thread per weight row ----------------
-        // warp (4 + cw) writes TMEM lanes 32 * (warp & 3) (a warp may only reach its quarter)
+        // warp (4 + cw) writes TMEM lanes 32 * (warp & 3) (a warp may only reach its quarter).
+        // Software-pipelined by one stage: the tensor-memory store of slice kt completes while
+        // slice kt + 1 is decoded, and only then is stage kt reported full (two register sets).
         constexpr int CW = G::CW;
-        const int cw = warp - 4, m = cw / CW, q = warp & 3, part = (cw % CW) >> 2;  // part: slice half (CW 8)
+        static_assert(CW == 4, "one converter warp per lane quarter and matrix");
+        const int cw = warp - 4, m = cw / CW, q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
         bool ok = true;
-        for (int kt = 0; kt < nk && ok; kt++) {
+        int pend = -1;  // stage whose store is in flight
+        auto report = [&](uint32_t* vp) {  // the pending store (of vp) has landed: stage full
+            tmem_st_wait_hold(vp);
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[pend % NST]));
+            pend = -1;
+        };
+        auto stage = [&](int kt, uint32_t* v, uint32_t* vp) {
             const int j = kt / SUBS, sub = kt % SUBS, s = kt % NST;
-            if (s_abort) { ok = false; break; }
+            if (s_abort) { ok = false; return; }
             if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % TC_RST]), (j / TC_RST) & 1)) {
                 fail();
                 ok = false;
-                break;
+                return;
             }
             if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
                 fail();
                 ok = false;
-                break;
+                return;
             }
             const uint8_t* mat = raw_g + (size_t)((j % TC_RST) * NMAT + m) * RS::BYTES;
             const uint8_t *rp = mat + r * PITCH, *rd = mat + RS::DOFF + r * 2, *ra = mat + RS::AOFF + r * 4;
-            const uint32_t acol = tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32);
-            if (CW == 8) {
-                uint32_t v[16];
-                slice32<TYPE>(rp, rd, ra, sub, part, v);
-                tmem_st16(acol + 16 * part, v);
-            } else {
-                uint32_t v[32];
-                slice32<TYPE>(rp, rd, ra, sub, 0, v);
-                slice32<TYPE>(rp, rd, ra, sub, 1, v + 16);
-                tmem_st32(acol, v);
-            }
-            tmem_st_wait();
-            fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[s]));
-            if (sub == SUBS - 1) {
+            slice32<TYPE>(rp, rd, ra, sub, 0, v);
+            slice32<TYPE>(rp, rd, ra, sub, 1, v + 16);
+            if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % TC_RST]));
             }
+            if (pend >= 0) report(vp);
+            tmem_st32(tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32), v);
+            pend = kt;
+        };
+        uint32_t v0[32], v1[32];
+        for (int kt = 0; kt < nk && ok; kt += 2) {  // nk is a multiple of 4
+            stage(kt, v0, v1);
+            if (ok) stage(kt + 1, v1, v0);
         }
+        if (pend >= 0) report((pend & 1) ? v1 : v0);
         // ---------------- epilogue ----------------
         const bool acc_ok = mbar_wait(smem_u32(&bar_acc), 0);
         if (!acc_ok) fail();
@@ -528,7 +541,7 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         if (NMAT == 2) {
             // SwiGLU in f32 into a shared staging tile hs[n][f] (the rings are free now)
             float* hs = reinterpret_cast<float*>(gbase);
-            constexpr int HLD = TC_M + 1;
+            constexpr int HLD = TC_M + 4;  // 16-B aligned rows; lanes of one read hit distinct banks
             // token chunk c (32 columns) of the accumulators: warps of a lane quarter share them out
             for (int c = cw >> 2; c * 32 < n_eff; c += G::CONV / 128) {
                 uint32_t g[32], u[32];
@@ -551,11 +564,15 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
                 const int nblk = p.I / HBLK;
                 const int ct = tid - 128;
                 for (int pi = ct; pi < nrows * 2; pi += G::CONV) {
-                    const int n = pi >> 1, blk = pi & 1;
+                    const int blk = pi >= nrows ? 1 : 0, n = pi - blk * nrows;  // consecutive lanes: rows
                     const float* src = hs + n * HLD + blk * 64;
+                    const float4* s4 = reinterpret_cast<const float4*>(src);
                     float amax = 0.0f;
-#pragma unroll 8
-                    for (int i = 0; i < 64; i++) amax = fmaxf(amax, fabsf(src[i]));
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const float4 t = s4[i];
+                        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w))));
+                    }
                     int ex = -127;
                     if (amax > 0.0f) {
                         int e2;
@@ -567,11 +584,11 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
                     uint4* dst = reinterpret_cast<uint4*>(p.h + rr * p.I + fb * TC_M + blk * 64);
 #pragma unroll
                     for (int j2 = 0; j2 < 8; j2++) {
-                        const float* s8 = src + 8 * j2;
-                        dst[j2] = make_uint4(pack_f16x2(__fmul_rn(s8[0], sc), __fmul_rn(s8[1], sc)),
-                                             pack_f16x2(__fmul_rn(s8[2], sc), __fmul_rn(s8[3], sc)),
-                                             pack_f16x2(__fmul_rn(s8[4], sc), __fmul_rn(s8[5], sc)),
-                                             pack_f16x2(__fmul_rn(s8[6], sc), __fmul_rn(s8[7], sc)));
+                        const float4 a = s4[2 * j2], b = s4[2 * j2 + 1];
+                        dst[j2] = make_uint4(pack_f16x2(__fmul_rn(a.x, sc), __fmul_rn(a.y, sc)),
+                                             pack_f16x2(__fmul_rn(a.z, sc), __fmul_rn(a.w, sc)),
+                                             pack_f16x2(__fmul_rn(b.x, sc), __fmul_rn(b.y, sc)),
+                                             pack_f16x2(__fmul_rn(b.z, sc), __fmul_rn(b.w, sc)));
                     }
                     p.hexp[rr * nblk + fb * 2 + blk] = (int8_t)ex;
                     atomicMax(p.rowexp + rr, ex);

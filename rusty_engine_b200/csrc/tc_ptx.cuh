@@ -123,6 +123,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
         : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
+// The same wait, naming the 32 source registers of the store it completes as operands so that
+// the compiler keeps them untouched until the store has landed.
+__device__ __forceinline__ void tmem_st_wait_hold(uint32_t* v) {
+    asm volatile("tcgen05.wait::st.sync.aligned;\n"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                   "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]),
+                   "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]),
+                   "+r"(v[29]), "+r"(v[30]), "+r"(v[31])
+                 :
+                 : "memory");
+}
 
 // Each thread of the warp reads 32 consecutive 32-bit columns of its TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
