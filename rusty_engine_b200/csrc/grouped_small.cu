@@ -1,53 +1,155 @@
 // grouped_small.cu -- grouped expert products for small per-expert row counts (decode).
 //
-// One CTA = one (tile of <= NT expert-sorted rows, block of 64 weight rows).  Weights are
-// read straight from the device planes, decoded to fp16 (chunk8<TYPE>) into an XOR-swizzled
-// shared tile, activations are gathered by token into a second swizzled tile, and four warps
-// run mma.sync m16n8k16 (fp16 in, f32 accumulate).  The weight stream is the only HBM
-// traffic that grows with the layer, so this path is bandwidth-bound at decode batch sizes.
+// One CTA = one (tile of <= NT expert-sorted rows, block of 64 weight rows).  At decode sizes
+// the layer is a weight stream: every touched expert's GGUF bytes are read once, so the kernel
+// is built to keep that stream moving.  A ring of SB_RSTG raw stages (one 256-element
+// superblock column of the CTA's 64 rows, all planes, plus the tile's token rows) is filled
+// with cp.async while earlier stages are decoded; each landed stage is decoded to fp16 (the
+// same half-slice decoders as the tensor-core kernels) into a 128-B-swizzled shared tile and
+// four warps run mma.sync m16n8k16 (fp16 in, f32 accumulate) over it.  NT, the MMA width in
+// tokens, is 8 or 16: a decode step touches a handful of rows per expert.
 //
 //   gate/up kernel: h[row, f] = silu(gate_f . x) * (up_f . x)      (src/moe.rs:280-299)
 //                   stored as fp16 * 2^e with e per (row, 64-feature block), and the row's
 //                   largest e folded into rowexp[row] (atomicMax)
 //   down kernel:    y = down . h[row] with every h block brought to the row's common scale
-//                   while it is staged; out[tok] += w_slot * y * 2^rowexp  (src/moe.rs:373-380)
+//                   once it has landed; out[tok] += w_slot * y * 2^rowexp  (src/moe.rs:373-380)
 #include "common.cuh"
+#include "decode.cuh"
 #include "kernels.h"
 
 namespace rmoe {
 
-static constexpr int SM_BM = 64;       // weight rows per CTA (per matrix)
-static constexpr int SM_KC = 128;      // K elements per stage
-static constexpr int SM_THREADS = 128; // 4 warps x 16 rows
-static constexpr int SM_CPR = SM_KC / 8;
-static constexpr int SM_NT = 64;       // rows (tokens) per tile
+static constexpr int SB_M = 64;          // weight rows per CTA (per matrix)
+static constexpr int SB_THREADS = 256;   // 8 warps: all decode; warp w multiplies rows 16 (w & 3).., tokens 8 (w >> 2)..
+static constexpr int SB_KS = 64;         // K elements per decoded sub-slice
+static constexpr int SB_SMEM_MAX = 110 * 1024;  // two CTAs per SM
 
-int small_tile_rows() { return SM_NT; }
+int small_tile_rows(int T) { return T <= 8 ? 8 : 16; }
+int small_tile_rows_min() { return 8; }
 
-__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * SM_KC * 2 + ((c ^ (r & 7)) << 4)); }
+__device__ __forceinline__ void cpa16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+// 16-B copy reading `bytes` (0 or 16) from src; the rest of the 16 B is zero-filled
+__device__ __forceinline__ void cpa16_zfill(uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+template <int TYPE, int NT, int NMAT>
+struct SmallGeom {
+    using R = Raw<TYPE>;
+    using RS = RawStage<TYPE, SB_M>;
+    static constexpr int SK = R::RK;                  // K elements per stage
+    static constexpr int SUBS = SK / SB_KS;           // decoded sub-slices per stage
+    static constexpr int A_BYTES = SB_M * SB_KS * 2;  // one decoded sub-slice per matrix
+    static constexpr int B_BYTES = NT * SK * 2;       // token tile per stage
+    static constexpr int STAGE = NMAT * RS::BYTES + B_BYTES;
+    static constexpr int FIXED = 2 * NMAT * A_BYTES;  // double-buffered sub-slice tiles
+    // deepest ring (<= 4 stages) that keeps two CTAs per SM
+    static constexpr int RSTG = FIXED + 4 * STAGE <= SB_SMEM_MAX ? 4 : FIXED + 3 * STAGE <= SB_SMEM_MAX ? 3 : 2;
+    static constexpr int RAW_OFF = 0;
+    static constexpr int B_OFF = RSTG * NMAT * RS::BYTES;
+    static constexpr int A_OFF = B_OFF + RSTG * B_BYTES;
+    static constexpr int SMEM = A_OFF + 2 * NMAT * A_BYTES;
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+    static_assert(NT * (HBLK + 1) * 4 <= SMEM, "epilogue staging");
+    static_assert(B_OFF % 128 == 0 && A_OFF % 128 == 0, "alignment");
+};
+
+// byte offset of 16-B chunk c of row r in a [rows][SK] fp16 tile with the 128-B XOR swizzle
+template <int SK>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+    return (uint32_t)(r * SK * 2 + ((c ^ (r & 7)) << 4));
+}
+
+// cp.async one raw stage j (256- or 128-element column) of the CTA's 64 rows of matrix M
 template <int TYPE>
-__device__ __forceinline__ void load_weights(const DevMat& M, uint64_t row0, int k0, uint8_t* As, int tid) {
-    for (int q = tid; q < SM_BM * SM_CPR; q += SM_THREADS) {
-        int r = q / SM_CPR, c = q % SM_CPR;
-        uint4 v = chunk8<TYPE>(M, row0 + r, (uint32_t)(k0 / 8 + c));
-        *reinterpret_cast<uint4*>(As + swz(r, c)) = v;
+__device__ __forceinline__ void stage_raw(const DevMat& M, uint64_t grow0, int j, uint32_t dst, int tid) {
+    using R = Raw<TYPE>;
+    using RS = RawStage<TYPE, SB_M>;
+    constexpr int PPR = R::MB / 16;  // 16-B pieces per row
+    for (int q = tid; q < SB_M * PPR; q += SB_THREADS) {
+        const int r = q / PPR, c = q - r * PPR;
+        cpa16(dst + r * R::PITCH + c * 16, M.main + (grow0 + r) * M.main_stride + (uint64_t)j * R::MB + c * 16);
+    }
+    if (R::DBLK)
+        for (int q = tid; q < R::DBLK * SB_M * 2 / 16; q += SB_THREADS) {
+            const int b = q / (SB_M * 2 / 16), c = q % (SB_M * 2 / 16);
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(M.dpl + ((uint64_t)j * R::DBLK + b) * M.trows + grow0);
+            cpa16(dst + RS::DOFF + b * SB_M * 2 + c * 16, src + c * 16);
+        }
+    if (R::AUX)
+        for (int q = tid; q < R::AUX * SB_M * 4 / 16; q += SB_THREADS) {
+            const int b = q / (SB_M * 4 / 16), c = q % (SB_M * 4 / 16);
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(M.aux + ((uint64_t)j * R::AUX + b) * M.trows + grow0);
+            cpa16(dst + RS::AOFF + b * SB_M * 4 + c * 16, src + c * 16);
+        }
+}
+
+// cp.async the stage-j columns of the tile's token rows (x by token for gate/up, h by row for
+// down) into a swizzled [NT][SK] tile; rows past nrows are zero-filled.
+template <int NT, int SK>
+__device__ __forceinline__ void stage_b(const __half* base, const int* s_src, int width, int nrows, int j, uint32_t dst,
+                                        int tid) {
+    constexpr int CPR = SK / 8;
+    for (int q = tid; q < NT * CPR; q += SB_THREADS) {
+        const int n = q / CPR, c = q - n * CPR;
+        const bool live = n < nrows;
+        const __half* src = base + (live ? (size_t)s_src[n] * width + (size_t)j * SK + c * 8 : 0);
+        cpa16_zfill(dst + swz<SK>(n, c), src, live ? 16u : 0u);
     }
 }
 
-// x rows gathered by token (fp16, [T, H]); rows >= nrows are zero.
-template <int NT>
-__device__ __forceinline__ void load_x(const __half* xb, const int* row_tok, int row0, int nrows, int H, int k0,
-                                       uint8_t* Bs, int tid) {
-    for (int q = tid; q < NT * SM_CPR; q += SM_THREADS) {
-        int n = q / SM_CPR, c = q % SM_CPR;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (n < nrows) {
-            size_t r = (size_t)__ldg(row_tok + row0 + n);
-            v = __ldg(reinterpret_cast<const uint4*>(xb + r * H + k0 + c * 8));
-        }
-        *reinterpret_cast<uint4*>(Bs + swz(n, c)) = v;
+// Decode sub-slice `sub` (64 K-elements) of the raw stage at `raw` for NMAT matrices into the
+// fp16 tiles at `at` ([NMAT][64][64], 128-B swizzle): one thread per (matrix, row, 32-element half).
+template <int TYPE, int NMAT>
+__device__ __forceinline__ void decode_sub(const uint8_t* raw, int sub, uint8_t* at, int tid) {
+    using R = Raw<TYPE>;
+    using RS = RawStage<TYPE, SB_M>;
+    for (int t = tid; t < NMAT * SB_M * 2; t += SB_THREADS) {
+        const int m = t / (SB_M * 2), rem = t % (SB_M * 2), r = rem % SB_M, half = rem / SB_M;
+        const uint8_t* rm = raw + m * RS::BYTES;
+        uint32_t v[16];
+        slice32<TYPE, SB_M>(rm + r * R::PITCH, rm + RS::DOFF + r * 2, rm + RS::AOFF + r * 4, sub, half, v);
+        uint8_t* am = at + m * (SB_M * SB_KS * 2);
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            *reinterpret_cast<uint4*>(am + swz<SB_KS>(r, half * 4 + c)) =
+                make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
     }
+}
+
+// MMAs of one sub-slice for one matrix and one warp: acc[4] += A(rows 16 (warp & 3)..) x
+// B(tokens 8 (warp >> 2).., K columns 64 sub.. of the stage's token tile)
+template <int SK>
+__device__ __forceinline__ void mma_sub(uint32_t a_base, uint32_t b_base, int sub, int warp, int lane, float* acc) {
+#pragma unroll
+    for (int ks = 0; ks < SB_KS / 16; ks++) {
+        uint32_t a[4], b0, b1;
+        {
+            const int mi = lane >> 3, r = (warp & 3) * 16 + (lane & 7) + (mi & 1) * 8, c = ks * 2 + (mi >> 1);
+            ldmatrix_x4(a_base + swz<SB_KS>(r, c), a[0], a[1], a[2], a[3]);
+        }
+        {
+            const int n = (warp >> 2) * 8 + (lane & 7), c = sub * (SB_KS / 8) + ks * 2 + ((lane >> 3) & 1);
+            ldmatrix_x2(b_base + swz<SK>(n, c), b0, b1);
+        }
+        mma_f16_16816(acc, a, b0, b1);
+    }
+}
+
+// Exponent e with max|v| * 2^-e in [2^13, 2^14): a zero block gets -127 (never the row max
+// unless the whole row is zero).
+__device__ __forceinline__ int block_exp(float amax) {
+    if (!(amax > 0.0f)) return -127;
+    int e;
+    frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
+    e -= 14;
+    return max(-100, min(100, e));
 }
 
 // Multiply 8 packed fp16 values by 2^d (d <= 0), in f32, rounding back to fp16.
@@ -64,65 +166,14 @@ __device__ __forceinline__ uint4 scale_h8(uint4 v, int d) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// h rows (fp16 * 2^hexp per block) staged at the row's common scale 2^rowexp.
+// SwiGLU values hs[NT][64] (f32, smem) -> fp16 blocks with per-(row, block) exponent; rowexp
+// gets the row maximum.
 template <int NT>
-__device__ __forceinline__ void load_h(const __half* h, const int8_t* hexp, const int* rexp_s, int row0, int nrows,
-                                       int I, int k0, uint8_t* Bs, int tid) {
-    const int nblk = I / HBLK;
-    for (int q = tid; q < NT * SM_CPR; q += SM_THREADS) {
-        int n = q / SM_CPR, c = q % SM_CPR;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (n < nrows) {
-            size_t r = (size_t)(row0 + n);
-            int k = k0 + c * 8;
-            v = __ldg(reinterpret_cast<const uint4*>(h + r * I + k));
-            v = scale_h8(v, (int)__ldg(hexp + r * nblk + k / HBLK) - rexp_s[n]);
-        }
-        *reinterpret_cast<uint4*>(Bs + swz(n, c)) = v;
-    }
-}
-
-// One K stage of MMAs for one weight tile: acc[NT/8][4] += A(16 rows of warp) x B(NT)
-template <int NT>
-__device__ __forceinline__ void mma_stage(const uint8_t* As, const uint8_t* Bs, int warp, int lane,
-                                          float (*acc)[4]) {
-    const uint32_t a_base = smem_u32(As), b_base = smem_u32(Bs);
-#pragma unroll
-    for (int ks = 0; ks < SM_KC / 16; ks++) {
-        uint32_t a[4];
-        {
-            int mi = lane >> 3, r = warp * 16 + (lane & 7) + (mi & 1) * 8, c = ks * 2 + (mi >> 1);
-            ldmatrix_x4(a_base + swz(r, c), a[0], a[1], a[2], a[3]);
-        }
-#pragma unroll
-        for (int nt = 0; nt < NT / 16; nt++) {
-            uint32_t b0, b1, b2, b3;
-            int mi = lane >> 3, n = nt * 16 + (lane & 7) + (mi >> 1) * 8, c = ks * 2 + (mi & 1);
-            ldmatrix_x4(b_base + swz(n, c), b0, b1, b2, b3);
-            mma_f16_16816(acc[nt * 2 + 0], a, b0, b1);
-            mma_f16_16816(acc[nt * 2 + 1], a, b2, b3);
-        }
-    }
-}
-
-// Exponent e with max|v| * 2^-e in [2^13, 2^14): a zero block gets -127 (never the row max
-// unless the whole row is zero).
-__device__ __forceinline__ int block_exp(float amax) {
-    if (!(amax > 0.0f)) return -127;
-    int e;
-    frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
-    e -= 14;
-    return max(-100, min(100, e));
-}
-
-// Epilogue shared by the gate/up kernels: SwiGLU values hs[NT][64] (f32, smem) -> fp16
-// blocks with per-(row, block) exponent; rowexp gets the row maximum.
-template <int NT, int THREADS>
 __device__ __forceinline__ void store_h_block(const float* hs, int row0, int nrows, int fblk, const GroupedParams& p,
                                               int tid) {
     const int nblk = p.I / HBLK;
     // two threads per row, 32 features each
-    for (int q = tid; q < NT * 2; q += THREADS) {
+    for (int q = tid; q < NT * 2; q += SB_THREADS) {
         int n = q >> 1, half = q & 1;
         const float* src = hs + n * (HBLK + 1) + half * 32;
         float amax = 0.0f;
@@ -150,96 +201,115 @@ __device__ __forceinline__ void store_h_block(const float* hs, int row0, int nro
     }
 }
 
-template <int TYPE, int NT>
-__global__ void __launch_bounds__(SM_THREADS) small_gateup_kernel(GroupedParams p) {
+template <int TYPE, int NT, int NMAT>
+__global__ void __launch_bounds__(SB_THREADS, 2) small_kernel(GroupedParams p) {
+    using G = SmallGeom<TYPE, NT, NMAT>;
+    using RS = RawStage<TYPE, SB_M>;
+    constexpr int SK = G::SK, RSTG = G::RSTG, SUBS = G::SUBS;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* Ag = smem;
-    uint8_t* Au = smem + SM_BM * SM_KC * 2;
-    uint8_t* Bs = smem + 2 * SM_BM * SM_KC * 2;
+    __shared__ int s_src[NT], s_rexp[NT];
     const int tile = blockIdx.y;
     if (tile >= *p.n_tiles) return;
     const int4 ti = p.tiles[tile];
     const int e = ti.x, row0 = ti.y, nrows = ti.z;
-    const DevMat& G = (e < p.E) ? p.gate : p.sgate;
-    const DevMat& U = (e < p.E) ? p.up : p.sup;
-    const uint64_t wrow0 = (uint64_t)(e < p.E ? e : 0) * G.rows + (uint64_t)blockIdx.x * SM_BM;
+    const bool sh = e >= p.E;
+    const DevMat& M0 = NMAT == 2 ? (sh ? p.sgate : p.gate) : (sh ? p.sdown : p.down);
+    const DevMat& M1 = NMAT == 2 ? (sh ? p.sup : p.up) : M0;
+    const uint64_t grow0 = (uint64_t)(sh ? 0 : e) * M0.rows + (uint64_t)blockIdx.x * SB_M;
+    const int K = NMAT == 2 ? p.H : p.I;
+    const int nst = K / SK;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool mma_warp = (warp >> 2) < NT / 8;  // NT 8: warps 4-7 only decode
+    const uint32_t sbase = smem_u32(smem);
 
-    float accg[NT / 8][4], accu[NT / 8][4];
-#pragma unroll
-    for (int i = 0; i < NT / 8; i++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) accg[i][j] = accu[i][j] = 0.0f;
-
-    for (int k0 = 0; k0 < p.H; k0 += SM_KC) {
-        load_weights<TYPE>(G, wrow0, k0, Ag, tid);
-        load_weights<TYPE>(U, wrow0, k0, Au, tid);
-        load_x<NT>(p.xb, p.row_tok, row0, nrows, p.H, k0, Bs, tid);
-        __syncthreads();
-        mma_stage<NT>(Ag, Bs, warp, lane, accg);
-        mma_stage<NT>(Au, Bs, warp, lane, accu);
-        __syncthreads();
+    for (int n = tid; n < NT; n += SB_THREADS) {
+        const bool live = n < nrows;
+        s_src[n] = NMAT == 2 ? (live ? __ldg(p.row_tok + row0 + n) : 0) : row0 + n;
+        s_rexp[n] = (NMAT == 1 && live) ? __ldg(p.rowexp + row0 + n) : 0;
     }
-    // SwiGLU in f32 (silu(g) * u, src/moe.rs:280-283) into smem hs[n][f]
-    float* hs = reinterpret_cast<float*>(smem);
-    const int g = lane >> 2, tq = lane & 3;
-#pragma unroll
-    for (int nt = 0; nt < NT / 8; nt++)
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            int n = nt * 8 + tq * 2 + (j & 1);
-            int f = warp * 16 + g + (j >> 1) * 8;
-            hs[n * (HBLK + 1) + f] = silu_ref(accg[nt][j]) * accu[nt][j];
+    __syncthreads();
+    const __half* bsrc = NMAT == 2 ? p.xb : p.h;
+    const int bwidth = NMAT == 2 ? p.H : p.I;
+
+    auto issue = [&](int j) {
+        if (j < nst) {
+            const int slot = j % RSTG;
+            const uint32_t raw = sbase + G::RAW_OFF + slot * NMAT * RS::BYTES;
+            stage_raw<TYPE>(M0, grow0, j, raw, tid);
+            if (NMAT == 2) stage_raw<TYPE>(M1, grow0, j, raw + RS::BYTES, tid);
+            stage_b<NT, SK>(bsrc, s_src, bwidth, nrows, j, sbase + G::B_OFF + slot * G::B_BYTES, tid);
         }
-    __syncthreads();
-    store_h_block<NT, SM_THREADS>(hs, row0, nrows, blockIdx.x, p, tid);
-}
+        cpa_commit();  // one group per stage (possibly empty), so the wait count stays fixed
+    };
 
-template <int TYPE, int NT>
-__global__ void __launch_bounds__(SM_THREADS) small_down_kernel(GroupedParams p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* Ad = smem;
-    uint8_t* Bs = smem + SM_BM * SM_KC * 2;
-    __shared__ int rexp_s[NT];
-    const int tile = blockIdx.y;
-    if (tile >= *p.n_tiles) return;
-    const int4 ti = p.tiles[tile];
-    const int e = ti.x, row0 = ti.y, nrows = ti.z;
-    const DevMat& D = (e < p.E) ? p.down : p.sdown;
-    const uint64_t wrow0 = (uint64_t)(e < p.E ? e : 0) * D.rows + (uint64_t)blockIdx.x * SM_BM;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int n = tid; n < NT; n += SM_THREADS) rexp_s[n] = (n < nrows) ? __ldg(p.rowexp + row0 + n) : 0;
-    __syncthreads();
-
-    float acc[NT / 8][4];
+    float acc[NMAT][4];
 #pragma unroll
-    for (int i = 0; i < NT / 8; i++)
+    for (int m = 0; m < NMAT; m++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+        for (int q = 0; q < 4; q++) acc[m][q] = 0.0f;
 
-    for (int k0 = 0; k0 < p.I; k0 += SM_KC) {
-        load_weights<TYPE>(D, wrow0, k0, Ad, tid);
-        load_h<NT>(p.h, p.hexp, rexp_s, row0, nrows, p.I, k0, Bs, tid);
-        __syncthreads();
-        mma_stage<NT>(Ad, Bs, warp, lane, acc);
-        __syncthreads();
+    for (int j = 0; j < RSTG - 1; j++) issue(j);
+    for (int j = 0; j < nst; j++) {
+        cpa_wait<RSTG - 2>();  // this thread's copies of stage j have landed
+        __syncthreads();       // ... everyone's; and every warp is done with stage j - 1
+        issue(j + RSTG - 1);   // into the slot stage j - 1 used
+        const int slot = j % RSTG;
+        const uint8_t* raw = smem + G::RAW_OFF + slot * NMAT * RS::BYTES;
+        uint8_t* bt = smem + G::B_OFF + slot * G::B_BYTES;
+        if (NMAT == 1) {
+            // h blocks to the row's common scale (exact power-of-two multiplies); the first
+            // sub-slice's barrier below publishes them
+            const int nblk = p.I / HBLK;
+            for (int q = tid; q < nrows * (SK / 8); q += SB_THREADS) {
+                const int n = q / (SK / 8), c = q - n * (SK / 8);
+                const int blk = (j * SK + c * 8) / HBLK;
+                const int d = (int)__ldg(p.hexp + (size_t)(row0 + n) * nblk + blk) - s_rexp[n];
+                uint4* ptr = reinterpret_cast<uint4*>(bt + swz<SK>(n, c));
+                *ptr = scale_h8(*ptr, d);
+            }
+        }
+#pragma unroll 1
+        for (int sub = 0; sub < SUBS; sub++) {
+            const int buf = (j * SUBS + sub) & 1;
+            decode_sub<TYPE, NMAT>(raw, sub, smem + G::A_OFF + buf * NMAT * G::A_BYTES, tid);
+            __syncthreads();  // tile `buf` complete; every MMA of the tile decoded before it is done
+            if (mma_warp)
+#pragma unroll
+                for (int m = 0; m < NMAT; m++)
+                    mma_sub<SK>(sbase + G::A_OFF + (buf * NMAT + m) * G::A_BYTES, sbase + G::B_OFF + slot * G::B_BYTES,
+                                sub, warp, lane, acc[m]);
+        }
     }
+    cpa_wait<0>();
+    __syncthreads();  // the rings are free for the epilogue staging
+
     const int g = lane >> 2, tq = lane & 3;
-    const int f0 = blockIdx.x * SM_BM + warp * 16 + g;
+    if (NMAT == 2) {
+        // SwiGLU in f32 (silu(g) * u, src/moe.rs:280-283) into smem hs[n][f]
+        float* hs = reinterpret_cast<float*>(smem);
+        if (mma_warp)
 #pragma unroll
-    for (int nt = 0; nt < NT / 8; nt++) {
+            for (int q = 0; q < 4; q++) {
+                const int n = (warp >> 2) * 8 + tq * 2 + (q & 1);
+                const int f = (warp & 3) * 16 + g + (q >> 1) * 8;
+                hs[n * (HBLK + 1) + f] = silu_ref(acc[0][q]) * acc[NMAT - 1][q];
+            }
+        __syncthreads();
+        store_h_block<NT>(hs, row0, nrows, blockIdx.x, p, tid);
+    } else if (mma_warp) {
+        const int f0 = blockIdx.x * SB_M + (warp & 3) * 16 + g;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            int n = nt * 8 + tq * 2 + (j & 1);
-            int f = f0 + (j >> 1) * 8;
+        for (int q = 0; q < 4; q++) {
+            const int n = (warp >> 2) * 8 + tq * 2 + (q & 1);
+            const int f = f0 + (q >> 1) * 8;
             if (n < nrows) {
-                int r = row0 + n;
-                float yv = __fmul_rn(acc[nt][j], exp2i(rexp_s[n]));
+                const int r = row0 + n;
+                const float yv = __fmul_rn(acc[0][q], exp2i(s_rexp[n]));
                 if (p.y) {
                     p.y[(size_t)r * p.H + f] = yv;
                 } else {
-                    int tok = __ldg(p.row_tok + r), slot = __ldg(p.row_slot + r);
-                    float w = (slot < p.k) ? __ldg(p.topk_w + (size_t)tok * p.k + slot) : 1.0f;
+                    const int tok = __ldg(p.row_tok + r), slot = __ldg(p.row_slot + r);
+                    const float w = (slot < p.k) ? __ldg(p.topk_w + (size_t)tok * p.k + slot) : 1.0f;
                     atomicAdd(p.out + (size_t)tok * p.H + f, __fmul_rn(w, yv));
                 }
             }
@@ -247,52 +317,44 @@ __global__ void __launch_bounds__(SM_THREADS) small_down_kernel(GroupedParams p)
     }
 }
 
-template <int NT>
-static size_t smem_gateup() {
-    size_t mma = (size_t)(2 * SM_BM + NT) * SM_KC * 2, epi = (size_t)NT * (HBLK + 1) * 4;
-    return mma > epi ? mma : epi;
-}
-template <int NT>
-static size_t smem_down() { return (size_t)(SM_BM + NT) * SM_KC * 2; }
-
-template <int TYPE, int NT>
-static cudaError_t go_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s) {
-    auto k = small_gateup_kernel<TYPE, NT>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_gateup<NT>());
-    dim3 grid(p.I / SM_BM, max_tiles);
-    k<<<grid, SM_THREADS, smem_gateup<NT>(), s>>>(p);
+template <int TYPE, int NT, int NMAT>
+static cudaError_t go_small(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+    using G = SmallGeom<TYPE, NT, NMAT>;
+    auto k = small_kernel<TYPE, NT, NMAT>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
+    if (e != cudaSuccess) return e;
+    dim3 grid((NMAT == 2 ? p.I : p.H) / SB_M, max_tiles);
+    k<<<grid, SB_THREADS, G::SMEM, s>>>(p);
     return cudaGetLastError();
 }
 
-template <int TYPE, int NT>
-static cudaError_t go_down(const GroupedParams& p, int max_tiles, cudaStream_t s) {
-    auto k = small_down_kernel<TYPE, NT>;
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_down<NT>());
-    dim3 grid(p.H / SM_BM, max_tiles);
-    k<<<grid, SM_THREADS, smem_down<NT>(), s>>>(p);
-    return cudaGetLastError();
-}
-
-#define RMOE_TYPE_SWITCH(T, ...)                                   \
-    switch (T) {                                                   \
-        case T_Q4_0: { constexpr int TT = T_Q4_0; __VA_ARGS__; }   \
-        case T_Q5_0: { constexpr int TT = T_Q5_0; __VA_ARGS__; }   \
-        case T_Q8_0: { constexpr int TT = T_Q8_0; __VA_ARGS__; }   \
-        case T_Q4_K: { constexpr int TT = T_Q4_K; __VA_ARGS__; }   \
-        case T_Q5_K: { constexpr int TT = T_Q5_K; __VA_ARGS__; }   \
-        case T_Q6_K: { constexpr int TT = T_Q6_K; __VA_ARGS__; }   \
-        case T_DENSE: { constexpr int TT = T_DENSE; __VA_ARGS__; } \
-        default: return cudaErrorInvalidValue;                     \
+template <int NMAT>
+static cudaError_t go_small_nt(int type, const GroupedParams& p, int max_tiles, int nt, cudaStream_t s) {
+#define RMOE_SMALL_NT(TT)                                                      \
+    return nt == 8 ? go_small<TT, 8, NMAT>(p, max_tiles, s) : go_small<TT, 16, NMAT>(p, max_tiles, s)
+    switch (type) {
+        case T_Q4_0: RMOE_SMALL_NT(T_Q4_0);
+        case T_Q5_0: RMOE_SMALL_NT(T_Q5_0);
+        case T_Q8_0: RMOE_SMALL_NT(T_Q8_0);
+        case T_Q4_K: RMOE_SMALL_NT(T_Q4_K);
+        case T_Q5_K: RMOE_SMALL_NT(T_Q5_K);
+        case T_Q6_K: RMOE_SMALL_NT(T_Q6_K);
+        case T_DENSE: RMOE_SMALL_NT(T_DENSE);
+        default: return cudaErrorInvalidValue;
     }
-
-cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s) {
-    if (max_tiles <= 0) return cudaSuccess;
-    RMOE_TYPE_SWITCH(p.gate.type, return go_gateup<TT, SM_NT>(p, max_tiles, s))
+#undef RMOE_SMALL_NT
 }
 
-cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, cudaStream_t s) {
+cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, int nt, cudaStream_t s) {
     if (max_tiles <= 0) return cudaSuccess;
-    RMOE_TYPE_SWITCH(p.down.type, return go_down<TT, SM_NT>(p, max_tiles, s))
+    if (nt != 8 && nt != 16) return cudaErrorInvalidValue;
+    return go_small_nt<2>(p.gate.type, p, max_tiles, nt, s);
+}
+
+cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, int nt, cudaStream_t s) {
+    if (max_tiles <= 0) return cudaSuccess;
+    if (nt != 8 && nt != 16) return cudaErrorInvalidValue;
+    return go_small_nt<1>(p.down.type, p, max_tiles, nt, s);
 }
 
 }  // namespace rmoe

@@ -23,6 +23,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "decode.cuh"
 #include "kernels.h"
 #include "tc_ptx.cuh"
 
@@ -30,35 +31,12 @@ namespace rmoe {
 using namespace tc;
 
 static constexpr int TC_M = 128;   // weight rows per matrix per CTA (= TMEM lanes, = TMA box rows)
-static constexpr int TC_BN = 128;  // expert-sorted rows per tile (MMA N, rounded to 16 per tile)
+static constexpr int TC_BN = 256;  // expert-sorted rows per tile at most (MMA N, rounded to 16 per tile)
 static constexpr int TC_KS = 64;   // K elements per MMA stage (one 128-B swizzle row of fp16)
 static constexpr int TC_NST = 4;   // MMA stages in flight
 static constexpr int TC_RST = 2;   // raw weight stages in flight
 
 int tc_tile_rows() { return TC_BN; }
-
-// Raw-stage geometry per type: RK K-elements per stage; PITCH = bytes per row of the main-plane
-// box (what each row needs, plus 16 B where that keeps the pitch an odd number of 16-B units so
-// 16-B loads of 8 consecutive rows hit distinct banks); DBLK = block scales per row per stage
-// ([block][row] plane); AUX = Q5_0 high-bit words ([block][row] plane).
-template <int TYPE> struct Raw;
-template <> struct Raw<T_Q4_K> { static constexpr int RK = 256, PITCH = 144, MB = 144, DBLK = 0, AUX = 0; };
-template <> struct Raw<T_Q5_K> { static constexpr int RK = 256, PITCH = 176, MB = 176, DBLK = 0, AUX = 0; };
-template <> struct Raw<T_Q6_K> { static constexpr int RK = 256, PITCH = 208, MB = 208, DBLK = 1, AUX = 0; };
-template <> struct Raw<T_Q4_0> { static constexpr int RK = 256, PITCH = 144, MB = 128, DBLK = 8, AUX = 0; };
-template <> struct Raw<T_Q5_0> { static constexpr int RK = 256, PITCH = 144, MB = 128, DBLK = 8, AUX = 8; };
-template <> struct Raw<T_Q8_0> { static constexpr int RK = 256, PITCH = 272, MB = 256, DBLK = 8, AUX = 0; };
-template <> struct Raw<T_DENSE> { static constexpr int RK = 128, PITCH = 272, MB = 256, DBLK = 0, AUX = 0; };
-
-template <int TYPE>
-struct RawStage {
-    using R = Raw<TYPE>;
-    static constexpr int MAIN = TC_M * R::PITCH;  // bytes per matrix: main box
-    static constexpr int DOFF = MAIN, DBYTES = R::DBLK * TC_M * 2;
-    static constexpr int AOFF = DOFF + DBYTES, ABYTES = R::AUX * TC_M * 4;
-    static constexpr int BYTES = AOFF + ABYTES;   // per matrix; every region 128-B aligned
-    static_assert(MAIN % 128 == 0 && DBYTES % 128 == 0 && ABYTES % 128 == 0, "TMA regions must be 128-B aligned");
-};
 
 // ---------------------------------------------------------------------------------------------
 // host: tensor maps
@@ -140,216 +118,44 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
         : "memory");
 }
 
-// Decode K-elements [64*sub + 32*half, +32) of one weight row into 16 packed fp16 pairs (k, k+1).
-// p = the row's main-plane bytes for the stage; dq / aq = its block-scale / high-bit entries
-// (block b of the stage at dq + 256 b / aq + 512 b).  half is warp-uniform.
-template <int TYPE>
-__device__ __forceinline__ void slice32(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub, int half,
-                                        uint32_t* v);
-
-// Packed-half helpers: a 4- or 6-bit code c placed in the low mantissa bits of 0x6400 is the
-// exact fp16 value 1024 + c, so code -> fp16 costs one byte permute and one logic op per pair.
-__device__ __forceinline__ __half2 as_h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
-__device__ __forceinline__ uint32_t as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-__device__ __forceinline__ uint32_t lop_or3(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t r;
-    asm("lop3.b32 %0, %1, %2, %3, 0xFE;\n" : "=r"(r) : "r"(a), "r"(b), "r"(c));  // a | b | c
-    return r;
-}
-
-// Q4_K: y = d*sc*q - dmin*m over sub-block 2*sub + half (the low nibbles of the slice's 32 qs
-// bytes for half 0, the high nibbles for half 1).  Per pair: the two codes land in 1024 + q
-// (exact), 1024 is subtracted exactly, and one fused multiply-add by the fp16-rounded sub-block
-// scale and min gives the value (the scale, the min and the result each round once to fp16;
-// the f32 path rounds the result only, and the difference is well inside the layer tolerance).
-template <>
-__device__ __forceinline__ void slice32<T_Q4_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub, int half,
-                                                uint32_t* v) {
-    const uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
-    const float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
-    int sc, mn;
-    scale_min_k4(2 * sub + half, p + 4, sc, mn);
-    const __half2 D = __float2half2_rn(__fmul_rn(d, (float)sc)), M = __float2half2_rn(-__fmul_rn(dmin, (float)mn));
-    const __half2 K = __float2half2_rn(1024.0f);
-    const uint4* q = reinterpret_cast<const uint4*>(p + 16 + sub * 32);
-    const uint4 a = q[0], b = q[1];
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const int sh = 4 * half;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const uint32_t p01 = __byte_perm(w[i], 0, 0x4140), p23 = __byte_perm(w[i], 0, 0x4342);
-        v[2 * i] = as_u32(__hfma2(__hsub2(as_h2(((p01 >> sh) & 0x000F000Fu) | 0x64006400u), K), D, M));
-        v[2 * i + 1] = as_u32(__hfma2(__hsub2(as_h2(((p23 >> sh) & 0x000F000Fu) | 0x64006400u), K), D, M));
-    }
-}
-
-template <>
-__device__ __forceinline__ void slice32<T_Q5_K>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub, int half,
-                                                uint32_t* v) {
-    const uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
-    const float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
-    int sc, mn;
-    scale_min_k4(2 * sub + half, p + 4, sc, mn);
-    const float d1 = __fmul_rn(d, (float)sc), dm1 = __fmul_rn(dmin, (float)mn);
-    const uint4* q = reinterpret_cast<const uint4*>(p + 48 + sub * 32);
-    const uint4* hq = reinterpret_cast<const uint4*>(p + 16);
-    const uint4 a = q[0], b = q[1], ha = hq[0], hb = hq[1];
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    const uint32_t hw[8] = {ha.x, ha.y, ha.z, ha.w, hb.x, hb.y, hb.z, hb.w};
-    const int sh = 4 * half, ub = 2 * sub + half;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        auto val = [&](int byte) {
-            float qv = (float)(((w[i] >> (8 * byte + sh)) & 0xFu) + (((hw[i] >> (8 * byte + ub)) & 1u) << 4));
-            return __fsub_rn(__fmul_rn(d1, qv), dm1);
-        };
-        v[2 * i] = pack_f16x2(val(0), val(1));
-        v[2 * i + 1] = pack_f16x2(val(2), val(3));
-    }
-}
-
-// Q6_K main plane row: ql[128] | qh[64] | scales[16]; d from the block-scale plane.  Slice
-// `sub` covers quadrants 2*(sub&1) and 2*(sub&1)+1 of the 128-element half sub>>1; `half`
-// picks one: its low bits are the low (sub even) or high (sub odd) nibbles of ql[0..31]
-// (half 0) or ql[32..63] (half 1) of that half, its two high bits sit at bits 2*quadrant of qh.
-template <>
-__device__ __forceinline__ void slice32<T_Q6_K>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub, int half,
-                                                uint32_t* v) {
-    const float q6d = h2f(*reinterpret_cast<const uint16_t*>(dq));
-    const int h = sub >> 1, odd = sub & 1, qd = 2 * odd + half;
-    const uint4* ql = reinterpret_cast<const uint4*>(p + h * 64 + half * 32);
-    const uint4* qh = reinterpret_cast<const uint4*>(p + 128 + h * 32);
-    const uint4 l0 = ql[0], l1 = ql[1], h0 = qh[0], h1 = qh[1];
-    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-    const int8_t* sc = reinterpret_cast<const int8_t*>(p + 192 + h * 8);
-    const int nsh = 4 * odd;
-    // scales rounded once to fp16; (q6 - 32) is exact in fp16 (1024 + q6 - 1056)
-    const __half2 s0 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qd * 2]));
-    const __half2 s1 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qd * 2 + 1]));
-    const __half2 K = __float2half2_rn(1056.0f);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {  // l = 4i .. 4i+3
-        const __half2 s = (i < 4) ? s0 : s1;
-#pragma unroll
-        for (int pr = 0; pr < 2; pr++) {  // byte pairs (0,1) and (2,3)
-            const uint32_t sel = pr ? 0x4342 : 0x4140;
-            const uint32_t pl = __byte_perm(lw[i], 0, sel), ph = __byte_perm(hw[i], 0, sel);
-            // the quadrant's two high bits (2*qd, 2*qd+1) moved to bits 4..5
-            const uint32_t hb = qd <= 2 ? (ph << (4 - 2 * qd)) : (ph >> 2);
-            const uint32_t c = lop_or3((pl >> nsh) & 0x000F000Fu, hb & 0x00300030u, 0x64006400u);
-            v[2 * i + pr] = as_u32(__hmul2(__hsub2(as_h2(c), K), s));
-        }
-    }
-}
-
-// Q4_0 main plane row: qs[8 x 16]; half = block 2*sub + half (low nibbles -> elements 0..15,
-// high nibbles -> 16..31).
-template <>
-__device__ __forceinline__ void slice32<T_Q4_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub, int half,
-                                                uint32_t* v) {
-    const int b = 2 * sub + half;
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
-    const uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        auto lo = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte)) & 0xFu) - 8), d); };
-        auto hi = [&](int byte) { return __fmul_rn((float)((int)((w[i] >> (8 * byte + 4)) & 0xFu) - 8), d); };
-        v[2 * i] = pack_f16x2(lo(0), lo(1));
-        v[2 * i + 1] = pack_f16x2(lo(2), lo(3));
-        v[8 + 2 * i] = pack_f16x2(hi(0), hi(1));
-        v[8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
-    }
-}
-
-// Q5_0 main plane row: qs[8 x 16]; high bits and scales from their planes.
-template <>
-__device__ __forceinline__ void slice32<T_Q5_0>(const uint8_t* p, const uint8_t* dq, const uint8_t* aq, int sub,
-                                                int half, uint32_t* v) {
-    const int b = 2 * sub + half;
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
-    const uint32_t qh = *reinterpret_cast<const uint32_t*>(aq + 512 * b);
-    const uint4 q = *reinterpret_cast<const uint4*>(p + 16 * b);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        auto lo = [&](int byte) {
-            int j = 4 * i + byte;
-            int x = (int)(((w[i] >> (8 * byte)) & 0xFu) | (((qh >> j) & 1u) << 4)) - 16;
-            return __fmul_rn((float)x, d);
-        };
-        auto hi = [&](int byte) {
-            int j = 4 * i + byte;
-            int x = (int)(((w[i] >> (8 * byte + 4)) & 0xFu) | (((qh >> (j + 16)) & 1u) << 4)) - 16;
-            return __fmul_rn((float)x, d);
-        };
-        v[2 * i] = pack_f16x2(lo(0), lo(1));
-        v[2 * i + 1] = pack_f16x2(lo(2), lo(3));
-        v[8 + 2 * i] = pack_f16x2(hi(0), hi(1));
-        v[8 + 2 * i + 1] = pack_f16x2(hi(2), hi(3));
-    }
-}
-
-// Q8_0 main plane row: qs[8 x 32]; half = block 2*sub + half.
-template <>
-__device__ __forceinline__ void slice32<T_Q8_0>(const uint8_t* p, const uint8_t* dq, const uint8_t*, int sub, int half,
-                                                uint32_t* v) {
-    const int b = 2 * sub + half;
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(dq + 256 * b));
-    const uint4* q = reinterpret_cast<const uint4*>(p + 32 * b);
-    const uint4 a = q[0], c = q[1];
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-    for (int i = 0; i < 8; i++) {  // word i holds elements 4i..4i+3 of the block
-        auto val = [&](int byte) { return __fmul_rn((float)(int8_t)((w[i] >> (8 * byte)) & 0xFFu), d); };
-        v[2 * i] = pack_f16x2(val(0), val(1));
-        v[2 * i + 1] = pack_f16x2(val(2), val(3));
-    }
-}
-
-template <>
-__device__ __forceinline__ void slice32<T_DENSE>(const uint8_t* p, const uint8_t*, const uint8_t*, int sub, int half,
-                                                 uint32_t* v) {
-    const uint4* q = reinterpret_cast<const uint4*>(p + 128 * sub + 64 * half);
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint4 a = q[i];
-        v[4 * i] = a.x;
-        v[4 * i + 1] = a.y;
-        v[4 * i + 2] = a.z;
-        v[4 * i + 3] = a.w;
-    }
-}
-
 template <int TYPE, int NMAT>
 struct TcGeom {
     static constexpr int B_STAGE = TC_BN * 128;  // bytes per token tile stage
-    static constexpr int RAW_STAGE = NMAT * RawStage<TYPE>::BYTES;
-    // down keeps one stage less so that two of its CTAs fit on an SM (one drains while the other
-    // computes); gate/up fills the tensor memory with its two accumulators and runs alone
-    static constexpr int NST = NMAT == 2 ? TC_NST : TC_NST - 1;
-    static constexpr int SMEM = NST * B_STAGE + TC_RST * RAW_STAGE + 1024;
+    static constexpr int RAW_STAGE = NMAT * RawStage<TYPE, TC_M>::BYTES;
+    // gate/up: its two accumulators (2 x 256 columns) fill the tensor memory, so the dequantized
+    // weight tiles go to shared memory (A_SMEM, 128-B-swizzled like the token tiles) and two
+    // stages fit; down keeps its weight tiles in tensor memory after the one accumulator.
+    static constexpr bool A_SMEM = NMAT == 2;
+    static constexpr int A_STAGE = A_SMEM ? NMAT * TC_M * 128 : 0;  // bytes per stage
+    static constexpr int NST = A_SMEM ? 2 : TC_NST;
+    static constexpr int SMEM_MAX = 232448;  // opt-in shared memory per block
+    static constexpr int RING = NST * (B_STAGE + A_STAGE) + 1024;
+    // raw ring depth: two superblocks where they fit (all down types, the 4/5-bit gate/up types)
+    static constexpr int RST = RING + 2 * RAW_STAGE <= SMEM_MAX - 4096 ? 2 : 1;
+    static constexpr int SMEM = RING + RST * RAW_STAGE;
     // converter warps per matrix: 4 decode whole 64-element slices; 8 would split each slice
     // into two 32-element halves (measured slower on B200: the per-slice waits and arrivals
     // double while the decode itself does not shrink)
     static constexpr int CW = 4;
     static constexpr int CONV = 32 * CW * NMAT;  // converter / epilogue threads
     static constexpr int THREADS = 128 + CONV;
-    static constexpr int MIN_BLOCKS = NMAT == 2 ? 1 : 2;
-    static constexpr uint32_t TMEM_COLS = NMAT == 2 ? 512 : 256;
-    static constexpr int A_COL0 = NMAT * TC_BN;  // A ring after the accumulators
+    static constexpr int MIN_BLOCKS = 1;
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr int A_COL0 = NMAT * TC_BN;  // down: A ring after the accumulator
+    static_assert(A_SMEM || A_COL0 + NST * 32 <= 512, "tensor memory budget");
+    static_assert(SMEM <= SMEM_MAX - 4096, "shared memory budget (static part included)");
+    static_assert(SMEM - 1024 >= TC_BN * (TC_M + 4) * 4, "epilogue staging tile fits in the rings");
 };
 
 template <int TYPE, int NMAT>
 __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT>::MIN_BLOCKS)
     tc_grouped_kernel(const __grid_constant__ GroupedParams p, const __grid_constant__ TcMaps maps) {
     using G = TcGeom<TYPE, NMAT>;
-    using RS = RawStage<TYPE>;
+    using RS = RawStage<TYPE, TC_M>;
     constexpr int RK = Raw<TYPE>::RK, PITCH = Raw<TYPE>::PITCH, SUBS = RK / TC_KS;
-    constexpr int NST = G::NST;
+    constexpr int NST = G::NST, RST = G::RST;
     extern __shared__ uint8_t dsmem[];
-    __shared__ __align__(8) uint64_t bar_raw_full[TC_RST], bar_raw_empty[TC_RST];
+    __shared__ __align__(8) uint64_t bar_raw_full[RST], bar_raw_empty[RST];
     __shared__ __align__(8) uint64_t bar_a_full[NST], bar_b_full[NST], bar_empty[NST];
     __shared__ __align__(8) uint64_t bar_acc;
     __shared__ uint32_t tmem_holder;
@@ -372,12 +178,14 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
 
     const uint32_t sbase = (smem_u32(dsmem) + 1023u) & ~1023u;  // 1024-B aligned (SW128 atoms)
     uint8_t* gbase = dsmem + (sbase - smem_u32(dsmem));
-    const uint32_t bring = sbase, rawring = sbase + NST * G::B_STAGE;
-    uint8_t* raw_g = gbase + NST * G::B_STAGE;
+    // [B ring | A ring (gate/up) | raw ring], every tile 1024-B aligned
+    const uint32_t bring = sbase, aring = sbase + NST * G::B_STAGE, rawring = aring + NST * G::A_STAGE;
+    uint8_t* a_g = gbase + NST * G::B_STAGE;
+    uint8_t* raw_g = a_g + NST * G::A_STAGE;
 
-    // TMA of raw stage j (all planes of all matrices) into ring slot j % TC_RST
+    // TMA of raw stage j (all planes of all matrices) into ring slot j % RST
     auto issue_raw = [&](int j) {
-        const int s = j % TC_RST;
+        const int s = j % RST;
         const uint32_t bar = smem_u32(&bar_raw_full[s]);
         mbar_arrive_expect_tx(bar, (uint32_t)G::RAW_STAGE);
 #pragma unroll
@@ -390,7 +198,7 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         }
     };
     if (tid == 0) {
-        for (int i = 0; i < TC_RST; i++) {
+        for (int i = 0; i < RST; i++) {
             mbar_init(smem_u32(&bar_raw_full[i]), 1);
             mbar_init(smem_u32(&bar_raw_empty[i]), G::CW * NMAT);
         }
@@ -403,7 +211,7 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         s_abort = 0;
         fence_mbar_init();
         // the first raw stages need no free-slot wait: start them before the prologue's loads
-        for (int j = 0; j < TC_RST && j < nraw; j++) issue_raw(j);
+        for (int j = 0; j < RST && j < nraw; j++) issue_raw(j);
     }
     for (int n = tid; n < TC_BN; n += G::THREADS) {
         int tok = 0, rexp = 0;
@@ -433,9 +241,9 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     if (warp == 0) {
         // ---------------- TMA producer: raw weight superblocks ----------------
         if (lane == 0) {
-            for (int j = TC_RST; j < nraw; j++) {
+            for (int j = RST; j < nraw; j++) {
                 if (s_abort) break;
-                if (!mbar_wait(smem_u32(&bar_raw_empty[j % TC_RST]), ((j / TC_RST) + 1) & 1)) {
+                if (!mbar_wait(smem_u32(&bar_raw_empty[j % RST]), ((j / RST) + 1) & 1)) {
                     fail();
                     break;
                 }
@@ -460,9 +268,16 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
 #pragma unroll
                 for (int m = 0; m < NMAT; m++)
 #pragma unroll
-                    for (int ks = 0; ks < TC_KS / 16; ks++)
-                        mma_ts(tbase + (uint32_t)(m * TC_BN), tbase + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32 + ks * 8),
-                               smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
+                    for (int ks = 0; ks < TC_KS / 16; ks++) {
+                        if (G::A_SMEM)
+                            mma_ss(tbase + (uint32_t)(m * TC_BN),
+                                   smem_desc_sw128(aring + (uint32_t)(s * NMAT + m) * (TC_M * 128) + ks * 32),
+                                   smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
+                        else
+                            mma_ts(tbase + (uint32_t)(m * TC_BN),
+                                   tbase + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32 + ks * 8),
+                                   smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
+                    }
                 mma_commit(smem_u32(&bar_empty[s]));
             }
             mma_commit(smem_u32(&bar_acc));  // also fires when aborted: every issued MMA has finished
@@ -505,7 +320,7 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         auto stage = [&](int kt, uint32_t* v, uint32_t* vp) {
             const int j = kt / SUBS, sub = kt % SUBS, s = kt % NST;
             if (s_abort) { ok = false; return; }
-            if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % TC_RST]), (j / TC_RST) & 1)) {
+            if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % RST]), (j / RST) & 1)) {
                 fail();
                 ok = false;
                 return;
@@ -515,17 +330,29 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
                 ok = false;
                 return;
             }
-            const uint8_t* mat = raw_g + (size_t)((j % TC_RST) * NMAT + m) * RS::BYTES;
+            const uint8_t* mat = raw_g + (size_t)((j % RST) * NMAT + m) * RS::BYTES;
             const uint8_t *rp = mat + r * PITCH, *rd = mat + RS::DOFF + r * 2, *ra = mat + RS::AOFF + r * 4;
-            slice32<TYPE>(rp, rd, ra, sub, 0, v);
-            slice32<TYPE>(rp, rd, ra, sub, 1, v + 16);
+            slice32<TYPE, TC_M>(rp, rd, ra, sub, 0, v);
+            slice32<TYPE, TC_M>(rp, rd, ra, sub, 1, v + 16);
             if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % TC_RST]));
+                if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % RST]));
             }
-            if (pend >= 0) report(vp);
-            tmem_st32(tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32), v);
-            pend = kt;
+            if (G::A_SMEM) {
+                // row r of the 128-B-swizzled K-major tile: 16-B chunk c at (c ^ (r & 7)) * 16
+                uint8_t* at = a_g + (size_t)(s * NMAT + m) * (TC_M * 128) + r * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++)
+                    *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
+                        make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[s]));
+            } else {
+                if (pend >= 0) report(vp);
+                tmem_st32(tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32), v);
+                pend = kt;
+            }
         };
         uint32_t v0[32], v1[32];
         for (int kt = 0; kt < nk && ok; kt += 2) {  // nk is a multiple of 4

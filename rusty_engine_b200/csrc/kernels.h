@@ -72,10 +72,12 @@ int route_grid(int T);
 __host__ __device__ inline int route_cnt_stride(int ncta) { return (ncta + 15) & ~15; }
 cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s);
 
-// small-batch (mma.sync) grouped kernels; tile_rows = tokens per tile
-int small_tile_rows();
-cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, cudaStream_t s);
-cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, cudaStream_t s);
+// small-batch (mma.sync) grouped kernels; nt = rows per tile (8 or 16, small_tile_rows(T) for
+// a batch of T tokens; the dispatch must use the same value)
+int small_tile_rows(int T);
+int small_tile_rows_min();
+cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, int nt, cudaStream_t s);
+cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, int nt, cudaStream_t s);
 
 // TMA descriptors of one weight-matrix stack: main plane (viewed as u16, 128-row boxes), the
 // block-scale plane and the Q5_0 high-bit plane (both [block][row], 128-row boxes).

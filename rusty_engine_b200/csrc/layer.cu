@@ -263,6 +263,9 @@ static rmoe_status check_dims(const rmoe_tensor& t, uint64_t d0, uint64_t d1, ui
     return RMOE_OK;
 }
 
+// Device type a GGUF type is held as (unquantized experts become one fp16 plane).
+static int canon_type(uint32_t t) { return (t == T_F32 || t == T_F16 || t == T_BF16) ? T_DENSE : (int)t; }
+
 rmoe_status validate_desc(const rmoe_layer_desc* d) {
     if (!d) return fail(RMOE_ERR_INVALID, "null layer description");
     if (d->hidden == 0 || d->inter == 0 || d->n_experts == 0)
@@ -279,6 +282,11 @@ rmoe_status validate_desc(const rmoe_layer_desc* d) {
     if ((s = check_dims(d->up_exps, d->hidden, d->inter, d->n_experts, "ffn_up_exps"))) return s;
     if ((s = check_dims(d->down_exps, d->inter, d->hidden, d->n_experts, "ffn_down_exps"))) return s;
     if (d->has_shared) {
+        // the grouped kernels decode a launch's tiles with one type per projection
+        if (canon_type(d->gate_shexp.ggml_type) != canon_type(d->gate_exps.ggml_type) ||
+            canon_type(d->up_shexp.ggml_type) != canon_type(d->up_exps.ggml_type) ||
+            canon_type(d->down_shexp.ggml_type) != canon_type(d->down_exps.ggml_type))
+            return fail(RMOE_ERR_UNSUPPORTED, "shared expert tensors must have the routed experts' ggml types");
         if ((s = check_dims(d->gate_shexp, d->hidden, d->inter, 1, "ffn_gate_shexp"))) return s;
         if ((s = check_dims(d->up_shexp, d->hidden, d->inter, 1, "ffn_up_shexp"))) return s;
         if ((s = check_dims(d->down_shexp, d->inter, d->hidden, 1, "ffn_down_shexp"))) return s;
@@ -286,8 +294,6 @@ rmoe_status validate_desc(const rmoe_layer_desc* d) {
     return RMOE_OK;
 }
 
-// Device type a GGUF type is held as (unquantized experts become one fp16 plane).
-static int canon_type(uint32_t t) { return (t == T_F32 || t == T_F16 || t == T_BF16) ? T_DENSE : (int)t; }
 
 rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_count, rmoe_layer* L) {
     const uint32_t H = d->hidden, I = d->inter;
@@ -343,7 +349,7 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     Owned& o = L->ws_own;
     const uint32_t H = L->H, I = L->I, E = L->E, k = L->k;
     const uint64_t rows = (uint64_t)cap * k + (L->has_shared ? cap : 0);
-    const int NT = small_tile_rows();
+    const int NT = small_tile_rows_min();
     L->max_tiles = (int)(rows / NT + E + 2);
     Workspace& w = L->ws;
     bool ok = true;
@@ -406,7 +412,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     if (flags & RMOE_FLAG_FORCE_SMALL) use_tc = false;
     if (flags & RMOE_FLAG_FORCE_LARGE) use_tc = true;
     rp.xs = use_tc ? w.xs : nullptr;
-    const int tile_rows = use_tc ? tc_tile_rows() : small_tile_rows();
+    const int tile_rows = use_tc ? tc_tile_rows() : small_tile_rows((int)T);
     const uint64_t rows_T = (uint64_t)T * L->k + (L->has_shared ? T : 0);
     const int max_tiles = (int)std::min<uint64_t>((uint64_t)L->max_tiles, rows_T / tile_rows + L->E + 2);
     rp.max_tiles = max_tiles; rp.tile_rows = tile_rows; rp.status = w.status;
@@ -437,7 +443,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         maps.w[1][1] = L->smu;
         maps.b = L->xsmap;
     }
-    e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : launch_small_gateup(gp, max_tiles, s);
+    e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : launch_small_gateup(gp, max_tiles, tile_rows, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
     mark(2);
     if (use_tc && (e = launch_rescale_h(gp, (int)rows_T, s)) != cudaSuccess) return cuda_fail(e, "h rescale launch");
@@ -446,7 +452,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         maps.w[1][0] = L->smd;
         maps.b = L->hmap;
     }
-    e = use_tc ? launch_tc_down(gp, maps, max_tiles, s) : launch_small_down(gp, max_tiles, s);
+    e = use_tc ? launch_tc_down(gp, maps, max_tiles, s) : launch_small_down(gp, max_tiles, tile_rows, s);
     if (e != cudaSuccess) return cuda_fail(e, "down launch");
     L->last_tc = use_tc;
     mark(3);
@@ -597,7 +603,7 @@ rmoe_status rmoe_qmat_matmul(uint32_t t, const void* w_host, uint64_t w_nbytes, 
     if (s) return s;
     if (rows == 0) return RMOE_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int NT = small_tile_rows();
+    const int NT = 16;
     const int ntiles = (int)((rows + NT - 1) / NT);
     __half* xb = (__half*)own.alloc((size_t)rows * n * 2);
     int* rowtok = (int*)own.alloc((size_t)rows * 4);
@@ -622,7 +628,7 @@ rmoe_status rmoe_qmat_matmul(uint32_t t, const void* w_host, uint64_t w_nbytes, 
     gp.sdown.type = -1;
     gp.H = (int)m; gp.I = (int)n; gp.E = 1; gp.k = 1;
     gp.h = xb; gp.hexp = hexp; gp.rowexp = rexp; gp.row_tok = rowtok; gp.tiles = tiles; gp.n_tiles = nt; gp.y = out;
-    if ((e = launch_small_down(gp, ntiles, st)) != cudaSuccess) return cuda_fail(e, "qmat launch");
+    if ((e = launch_small_down(gp, ntiles, NT, st)) != cudaSuccess) return cuda_fail(e, "qmat launch");
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "qmat");
     return RMOE_OK;
 }

@@ -94,7 +94,8 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
         return fail(RMOE_ERR_INVALID, "device x / out must be 16-byte aligned");
     if (L->E_local != L->E) return fail(RMOE_ERR_UNSUPPORTED, "noalloc forward: expert-parallel layers are not supported");
     const uint64_t rows = (uint64_t)T * L->k + (L->has_shared ? T : 0);
-    const int max_tiles = (int)(rows / small_tile_rows() + L->E + 2);
+    const int nt = small_tile_rows((int)T);
+    const int max_tiles = (int)(rows / nt + L->E + 2);
     Workspace w{};
     Carver measure{nullptr};
     carve(measure, L, T, rows, max_tiles, w);
@@ -123,7 +124,7 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;
     rp.ticket = w.ticket; rp.expert_off = w.expert_off; rp.row_tok = w.row_tok; rp.row_slot = w.row_slot;
     rp.slot_row = w.slot_row; rp.n_rows = w.n_rows; rp.tiles = w.tiles; rp.n_tiles = w.n_tiles;
-    rp.max_tiles = max_tiles; rp.tile_rows = small_tile_rows(); rp.status = w.status;
+    rp.max_tiles = max_tiles; rp.tile_rows = nt; rp.status = w.status;
     if ((e = launch_route_dispatch(rp, s)) != cudaSuccess) return cuda_fail(e, "noalloc route_dispatch launch");
 
     GroupedParams gp{};
@@ -133,8 +134,8 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
     gp.topk_w = w.topk_w; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp;
     gp.y = nullptr; gp.out = out; gp.status = w.status;
-    if ((e = launch_small_gateup(gp, max_tiles, s)) != cudaSuccess) return cuda_fail(e, "noalloc gate/up launch");
-    if ((e = launch_small_down(gp, max_tiles, s)) != cudaSuccess) return cuda_fail(e, "noalloc down launch");
+    if ((e = launch_small_gateup(gp, max_tiles, nt, s)) != cudaSuccess) return cuda_fail(e, "noalloc gate/up launch");
+    if ((e = launch_small_down(gp, max_tiles, nt, s)) != cudaSuccess) return cuda_fail(e, "noalloc down launch");
     return RMOE_OK;
 }
 

@@ -3,8 +3,8 @@
 // Router logits are bit-identical to rusty-engine's moe::matvec (src/moe.rs:271-277): each
 // logit is a sequential f32 sum over H of w*x with separate multiply and add roundings (Rust
 // never contracts), accumulated in ascending k.  Two kernels compute them:
-//   * small batches: one lane per (token, expert), streaming the expert's weight row with
-//     128-bit loads while the token's activations are broadcast across the warp;
+//   * small batches: one thread per (token, expert) chain, fed by a cp.async ring of 16 weight
+//     rows and 8 token rows per CTA;
 //   * large batches: a register-tiled product (64 tokens x 64 experts per CTA, 4 x 4 outputs
 //     per thread, cp.async double-buffered k-tiles), every output keeping the same order.
 // Top-k is rusty-engine's stable descending argsort (src/moe.rs:75-93): larger score first,
@@ -24,37 +24,77 @@ static constexpr int TK_TOK = 32;  // tokens per top-k CTA
 static constexpr int TK_THREADS = 256;
 
 // ---------------------------------------------------------------------------------------
-// logits, small batches: warp = (token t, 32 experts), lane = expert
+// logits, small batches (T <= 64): CTA = 16 experts x 8 tokens, one thread per logit.  Each
+// logit is one sequential chain of H dependent adds, so the router's latency is that chain;
+// everything else is kept off it: all 128 threads stream 256-element chunks of the 16 weight
+// rows and 8 token rows into a 4-deep cp.async ring, and the chains read them from shared
+// memory (rows padded to 1040 B, so the 16 rows a warp reads land in distinct banks).
 // ---------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) logits_small_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                                           int T, int H, int E, float* __restrict__ logits,
-                                                           __half* __restrict__ xb, unsigned* status) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    const int groups = (E + 31) / 32;
-    const int t = warp / groups, g = warp % groups;
-    if (t >= T) return;
-    const int e = g * 32 + lane;
-    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)t * H);
-    const float4* wr = reinterpret_cast<const float4*>(w + (size_t)min(e, E - 1) * H);
+static constexpr int LC_EB = 16, LC_TB = 8, LC_KC = 256, LC_ST = 4, LC_LD = LC_KC + 4, LC_THREADS = 128;
+static constexpr int LC_SMEM = LC_ST * (LC_EB + LC_TB) * LC_LD * 4;
+
+__device__ __forceinline__ void lc_cpa16(uint32_t dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+__global__ void __launch_bounds__(LC_THREADS) logits_chain_kernel(const float* __restrict__ x,
+                                                                   const float* __restrict__ w, int T, int H, int E,
+                                                                   float* __restrict__ logits, __half* __restrict__ xb,
+                                                                   unsigned* status) {
+    extern __shared__ __align__(16) float lsm[];  // [LC_ST][LC_EB weight rows + LC_TB token rows][LC_LD]
+    const int e0 = blockIdx.x * LC_EB, t0 = blockIdx.y * LC_TB;
+    const int ne = min(LC_EB, E - e0), nt = min(LC_TB, T - t0);
+    const int tid = threadIdx.x;
+    const int nchunk = H / LC_KC;
+    auto issue = [&](int c) {
+        if (c < nchunk) {
+            float* buf = lsm + (c % LC_ST) * (LC_EB + LC_TB) * LC_LD;
+            for (int q = tid; q < (LC_EB + LC_TB) * (LC_KC / 4); q += LC_THREADS) {
+                const int row = q / (LC_KC / 4), pc = q % (LC_KC / 4);
+                const bool wrow = row < LC_EB;
+                const int idx = wrow ? row : row - LC_EB;
+                const bool live = idx < (wrow ? ne : nt);
+                const float* src = wrow ? w + (size_t)(e0 + (live ? idx : 0)) * H : x + (size_t)(t0 + (live ? idx : 0)) * H;
+                lc_cpa16(smem_u32(buf + row * LC_LD + pc * 4), src + (size_t)c * LC_KC + pc * 4, live ? 16u : 0u);
+            }
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    for (int c = 0; c < LC_ST - 1; c++) issue(c);
+    const int ce = tid % LC_EB, ct = tid / LC_EB;
+    const bool chain = ce < ne && ct < nt;
     float s = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < H / 4; i++) {
-        float4 xv = __ldg(xr + i);
-        float4 wv = __ldg(wr + i);
-        s = __fadd_rn(s, __fmul_rn(wv.x, xv.x));
-        s = __fadd_rn(s, __fmul_rn(wv.y, xv.y));
-        s = __fadd_rn(s, __fmul_rn(wv.z, xv.z));
-        s = __fadd_rn(s, __fmul_rn(wv.w, xv.w));
-        if (g == 0 && xb && (i & 31) == lane) {
+    for (int c = 0; c < nchunk; c++) {
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(LC_ST - 2) : "memory");
+        __syncthreads();  // chunk c landed for everyone; chunk c - 1 fully read
+        issue(c + LC_ST - 1);
+        const float* buf = lsm + (c % LC_ST) * (LC_EB + LC_TB) * LC_LD;
+        if (chain) {
+            const float4* wr = reinterpret_cast<const float4*>(buf + ce * LC_LD);
+            const float4* xr = reinterpret_cast<const float4*>(buf + (LC_EB + ct) * LC_LD);
+#pragma unroll 16
+            for (int i = 0; i < LC_KC / 4; i++) {
+                const float4 a = wr[i], b = xr[i];
+                s = __fadd_rn(s, __fmul_rn(a.x, b.x));
+                s = __fadd_rn(s, __fmul_rn(a.y, b.y));
+                s = __fadd_rn(s, __fmul_rn(a.z, b.z));
+                s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+            }
+        }
+        if (xb && blockIdx.x == 0) {
             // fp16 MMA operand; |x| beyond the fp16 range is reported, never silently inf
-            if (!(fabsf(xv.x) <= 65504.f && fabsf(xv.y) <= 65504.f && fabsf(xv.z) <= 65504.f &&
-                  fabsf(xv.w) <= 65504.f))
-                atomicOr(status, (unsigned)DERR_FP16_RANGE);
-            uint2 pk = make_uint2(pack_f16x2(xv.x, xv.y), pack_f16x2(xv.z, xv.w));
-            *reinterpret_cast<uint2*>(xb + (size_t)t * H + i * 4) = pk;
+            for (int q = tid; q < nt * (LC_KC / 4); q += LC_THREADS) {
+                const int t = q / (LC_KC / 4), pc = q % (LC_KC / 4);
+                const float4 v = *reinterpret_cast<const float4*>(buf + (LC_EB + t) * LC_LD + pc * 4);
+                if (!(fabsf(v.x) <= 65504.f && fabsf(v.y) <= 65504.f && fabsf(v.z) <= 65504.f && fabsf(v.w) <= 65504.f))
+                    atomicOr(status, (unsigned)DERR_FP16_RANGE);
+                *reinterpret_cast<uint2*>(xb + (size_t)(t0 + t) * H + (size_t)c * LC_KC + pc * 4) =
+                    make_uint2(pack_f16x2(v.x, v.y), pack_f16x2(v.z, v.w));
+            }
         }
     }
-    if (e < E) logits[(size_t)t * E + e] = s;
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    if (chain) logits[(size_t)(t0 + ct) * E + e0 + ce] = s;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -233,6 +273,42 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
     return v;
 }
 
+// One warp: expert offsets and the tile list (expert, first row, rows) from the per-expert
+// row counts cnt_s[0..NE) (NE = E + the shared expert).  An expert's rows are split into the
+// fewest tiles of <= tile_rows rows, of equal size rounded up to 16 (the MMA N granularity)
+// except the last, so no tile is nearly empty.  Offsets also go to off_s when given.
+__device__ void build_tiles(const RouteParams& p, const int* cnt_s, int* off_s, int lane) {
+    const int NE = p.E + (p.has_shared ? 1 : 0);
+    int run = 0, tiles = 0;
+    for (int e0 = 0; e0 < NE; e0 += 32) {
+        const int e = e0 + lane;
+        const int c = e < NE ? cnt_s[e] : 0;
+        const int n0 = (c + p.tile_rows - 1) / p.tile_rows;
+        const int tr = c ? min(p.tile_rows, ((c + n0 - 1) / n0 + 15) & ~15) : 1;
+        const int nt = (c + tr - 1) / tr;
+        const int ic = warp_incl_scan(c, lane), itl = warp_incl_scan(nt, lane);
+        const int off = run + ic - c, tb = tiles + itl - nt;
+        if (e < NE) {
+            p.expert_off[e] = off;
+            if (off_s) off_s[e] = off;
+            for (int j = 0; j < nt; j++)
+                if (tb + j < p.max_tiles) p.tiles[tb + j] = make_int4(e, off + j * tr, min(tr, c - j * tr), 0);
+        }
+        run += __shfl_sync(0xffffffffu, ic, 31);
+        tiles += __shfl_sync(0xffffffffu, itl, 31);
+    }
+    if (lane == 0) {
+        p.expert_off[NE] = run;
+        if (off_s) off_s[NE] = run;
+        *p.n_rows = run;
+        if (tiles > p.max_tiles) {
+            atomicOr(p.status, (unsigned)DERR_TILES_OVERFLOW);
+            tiles = p.max_tiles;
+        }
+        *p.n_tiles = tiles;
+    }
+}
+
 __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     __shared__ int ids_s[TK_TOK * MAX_K];
     __shared__ int cnt_s[MAX_E + 2];
@@ -328,35 +404,9 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     }
     if (tid == 0 && p.has_shared) cnt_s[E] = p.T;
     __syncthreads();
-    // warp 0: expert offsets and the tile list (expert, first row, rows), <= tile_rows rows each
     if (warp == 0) {
-        const int NE = E + (p.has_shared ? 1 : 0);
-        int run = 0, tiles = 0;
-        for (int e0 = 0; e0 < NE; e0 += 32) {
-            const int e = e0 + lane;
-            const int c = e < NE ? cnt_s[e] : 0;
-            const int nt = (c + p.tile_rows - 1) / p.tile_rows;
-            const int ic = warp_incl_scan(c, lane), itl = warp_incl_scan(nt, lane);
-            const int off = run + ic - c, tb = tiles + itl - nt;
-            if (e < NE) {
-                p.expert_off[e] = off;
-                for (int j = 0; j < nt; j++)
-                    if (tb + j < p.max_tiles)
-                        p.tiles[tb + j] = make_int4(e, off + j * p.tile_rows, min(p.tile_rows, c - j * p.tile_rows), 0);
-            }
-            run += __shfl_sync(0xffffffffu, ic, 31);
-            tiles += __shfl_sync(0xffffffffu, itl, 31);
-        }
-        if (lane == 0) {
-            p.expert_off[NE] = run;
-            *p.n_rows = run;
-            if (tiles > p.max_tiles) {
-                atomicOr(p.status, (unsigned)DERR_TILES_OVERFLOW);
-                tiles = p.max_tiles;
-            }
-            *p.n_tiles = tiles;
-            *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
-        }
+        build_tiles(p, cnt_s, nullptr, lane);
+        if (lane == 0) *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
     }
 }
 
@@ -419,23 +469,75 @@ __global__ void __launch_bounds__(256) gather_x_kernel(RouteParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------------------
+// Whole dispatch for a small batch (T <= 64) in one CTA: top-k of every token, per-expert
+// counts and token-order ranks, offsets and tiles, row placement -- all through shared memory.
+// ---------------------------------------------------------------------------------------
+static constexpr int RS_MAX_T = 64;
+
+__global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) {
+    __shared__ int ids_s[RS_MAX_T * MAX_K], rank_s[RS_MAX_T * MAX_K];
+    __shared__ int cnt_s[MAX_E + 2], off_s[MAX_E + 2];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = p.T, E = p.E, k = p.k, H = p.H;
+    for (int t = warp; t < T; t += TK_THREADS / 32) {
+        const int id = warp_topk(p.logits + (size_t)t * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+        if (lane < k) {
+            p.topk_id[(size_t)t * k + lane] = id;
+            ids_s[t * k + lane] = id;
+        }
+    }
+    if (p.out_zero && !p.xs)
+        for (int i = tid * 4; i < T * H; i += TK_THREADS * 4)
+            *reinterpret_cast<float4*>(p.out_zero + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    for (int e = tid; e < E; e += TK_THREADS) {  // ranks in token order
+        int c = 0;
+        for (int i = 0; i < T * k; i++)
+            if (ids_s[i] == e) rank_s[i] = c++;
+        cnt_s[e] = c;
+    }
+    if (tid == 0 && p.has_shared) cnt_s[E] = T;
+    __syncthreads();
+    if (warp == 0) build_tiles(p, cnt_s, off_s, lane);
+    __syncthreads();
+    for (int i = tid; i < T * k; i += TK_THREADS) {
+        const int t = i / k, pos = off_s[ids_s[i]] + rank_s[i];
+        p.row_tok[pos] = t;
+        p.row_slot[pos] = i - t * k;
+        p.slot_row[i] = pos;
+        p.rowexp[pos] = -127;
+    }
+    if (p.has_shared)
+        for (int t = tid; t < T; t += TK_THREADS) {
+            const int pos = off_s[E] + t;
+            p.row_tok[pos] = t;
+            p.row_slot[pos] = k;
+            p.rowexp[pos] = -127;
+        }
+}
+
 int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
 
-static constexpr int SMALL_T = 64;  // lane-per-logit path up to this batch
-
 cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
-    if (p.T <= SMALL_T) {
-        int warps = p.T * ((p.E + 31) / 32);
-        logits_small_kernel<<<(warps + 3) / 4, 128, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+    cudaError_t e;
+    if (p.T <= RS_MAX_T) {
+        // small batches: chained logits, then the whole dispatch in one CTA
+        if ((e = cudaFuncSetAttribute(logits_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LC_SMEM)) !=
+            cudaSuccess)
+            return e;
+        dim3 grid((p.E + LC_EB - 1) / LC_EB, (p.T + LC_TB - 1) / LC_TB);
+        logits_chain_kernel<<<grid, LC_THREADS, LC_SMEM, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        route_small_kernel<<<1, TK_THREADS, 0, s>>>(p);
     } else {
         dim3 grid((p.T + LT_TOK - 1) / LT_TOK, (p.E + LT_EXP - 1) / LT_EXP);
         logits_tiled_kernel<<<grid, LT_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
     }
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-    topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess || !p.xs) return e;
     gather_x_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p);
     return cudaGetLastError();
