@@ -10,7 +10,8 @@ L2 is flushed (a 256 MiB write) between steps outside the events.  ``e2e`` is th
 through the public host-buffer entry point (pinned host x in, host out, copies inside).
 ``--impl reference`` times the CPU restatement of rusty-engine's pooled path (oracle/, all
 host threads) on the same config.  N > 1 runs one rank per GPU (torchrun); each rank serves
-its own batch (weak scaling).
+its own batch (weak scaling) through an expert-parallel layer: experts split evenly over the
+ranks, tokens exchanged with NCCL (rmoe_ep_layer_create).
 """
 from __future__ import annotations
 
@@ -35,15 +36,23 @@ CONFIGS = {
     "c3b8": ("config_c2", 8, "c3 Qwen3-30B-A3B MoE layer decode batch 8"),
     "c3b32": ("config_c2", 32, "c3 Qwen3-30B-A3B MoE layer decode batch 32"),
     "c3b64": ("config_c2", 64, "c3 Qwen3-30B-A3B MoE layer decode batch 64"),
-    "c5": ("config_c5", 8192, "c5 Qwen3-235B-A22B MoE layer H4096 E128 k8 I1536 Q4_K/Q6_K, 8192 tokens"),
+    "c5": ("config_c5", 8192, "c5 Qwen3-235B-A22B MoE layer H4096 E128 k8 I1536 Q4_K/Q6_K, 8192 tokens, "
+                              "Zipf(1.1) expert load"),
 }
 
 
-def kernels_per_forward(lw, T):
-    """Kernels of this library one forward launches: router logits, top-k + dispatch scan, row
-    scatter, gate/up (+SwiGLU), down (+atomic weighted combine); the tensor-core path (T*k >=
-    32*E) adds the expert-sorted x gather and the h rescale between gate/up and down."""
-    return 7 if T * lw.k >= 32 * lw.E else 5
+def kernels_per_forward(lw, T, world=1, rows_local=None):
+    """Kernels of this library one forward launches.  Whole layer: router logits, dispatch (one
+    kernel up to 64 tokens, else top-k scan + row scatter), gate/up (+SwiGLU), down (+atomic
+    weighted combine); the tensor-core path (T*k >= 32*E) adds the expert-sorted x gather and
+    the h rescale.  Expert-parallel: logits + top-k, plan, pack, unpack, the local layer over
+    the received rows (given routing: no logits) and the combine."""
+    def local(rows, E):
+        tc = rows * lw.k >= 32 * E
+        return (1 if rows <= 64 else 2) + (2 if tc else 0) + 2
+    if world == 1:
+        return 1 + local(T, lw.E)
+    return 2 + 3 + local(rows_local, lw.E // world) + 1
 
 
 def load_peaks():
@@ -217,8 +226,18 @@ def main():
     from rusty_engine_b200.moe import MoELayer
 
     lw = getattr(synth, builder)()
-    x_np = synth.activations(T, lw.H, seed=1 + rank)
-    layer = MoELayer(lw, device=local)
+    if args.config == "c5":
+        lw, x_np = synth.zipf_workload(lw, T, seed=1 + rank)
+    else:
+        x_np = synth.activations(T, lw.H, seed=1 + rank)
+    if world > 1:
+        from rusty_engine_b200.moe import ep_unique_id
+
+        box = [ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        layer = MoELayer.expert_parallel(lw, rank, world, box[0], device=local)
+    else:
+        layer = MoELayer(lw, device=local)
     x = torch.from_numpy(x_np).cuda()
     out = torch.empty_like(x)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
@@ -241,12 +260,14 @@ def main():
     stage = np.zeros(4)
     barrier()
     sampler.start()
+    tflags = _lib.FLAG_STAGE_TIMING if world == 1 else 0
     for i in range(args.steps):
         flush.fill_(float(i))
         starts[i].record(stream)
-        layer.forward(x, out, flags=_lib.FLAG_STAGE_TIMING)
+        layer.forward(x, out, flags=tflags)
         ends[i].record(stream)
-        stage += np.array(layer.stage_ms())
+        if world == 1:
+            stage += np.array(layer.stage_ms())
     barrier()
     clocks = sampler.stop()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
@@ -288,7 +309,14 @@ def main():
         # dominant kernel by measured time share
         names = ["route_dispatch", "gateup", "down", "combine"]
         dom = int(np.argmax(stage))
-        if T >= 256:
+        if world > 1:
+            # per rank: its share of the expert products over the whole step (exchanges included)
+            ach = (fg + fd) / (ms / 1e3) / 1e12
+            roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                    "frac": ach / peaks["bf16_tflops_sustained"], "traffic": None,
+                    "kernel": "whole expert-parallel step per rank (router, exchanges, experts, combine)",
+                    "peak_src": peaks["src"] + " sustained bf16"}
+        elif T >= 256:
             work = {1: fg, 2: fd}.get(dom, fg)
             ach = work / (stage[dom] / 1e3) / 1e12
             roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -305,12 +333,12 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16-mma/f32-acc/f32-router", "data": "synthetic",
             "config": {"workload": label, "tokens_per_gpu": T, "experts_touched": int(touched),
                        "l2": "flushed between steps (256 MiB write outside the events)",
-                       "parallelism": f"replicas{world}" if world > 1 else "single"},
+                       "parallelism": f"ep{world}" if world > 1 else "single"},
             "stage_ms": {n: float(v) for n, v in zip(names, stage)},
             "roofline": roof,
             "e2e": {"value": T * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * lw.H * 4,
                     "d2h_bytes_per_step": T * lw.H * 4},
-            "gpu_launches": kernels_per_forward(lw, T) * args.steps,
+            "gpu_launches": kernels_per_forward(lw, T, world, T) * args.steps,
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -37,6 +37,8 @@ struct RouteParams {
     int max_tiles;
     int tile_rows;          // rows per tile
     unsigned int* status;   // device status word (DevErr bits)
+    int given;              // 1: topk_id / topk_w are filled in already (x and logits unused);
+                            // ids >= E are empty picks and get no row
 };
 
 // Grouped expert products over the expert-sorted rows.
@@ -71,6 +73,8 @@ int route_grid(int T);
 // row stride of the per-(expert, top-k CTA) count table: CTAs rounded up to 16
 __host__ __device__ inline int route_cnt_stride(int ncta) { return (ncta + 15) & ~15; }
 cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s);
+// router logits and top-k only (topk_id, topk_w, xb): no dispatch tables
+cudaError_t launch_router_topk(const RouteParams& p, cudaStream_t s);
 
 // small-batch (mma.sync) grouped kernels; nt = rows per tile (8 or 16, small_tile_rows(T) for
 // a batch of T tokens; the dispatch must use the same value)

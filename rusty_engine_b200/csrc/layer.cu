@@ -264,7 +264,7 @@ static rmoe_status check_dims(const rmoe_tensor& t, uint64_t d0, uint64_t d1, ui
 }
 
 // Device type a GGUF type is held as (unquantized experts become one fp16 plane).
-static int canon_type(uint32_t t) { return (t == T_F32 || t == T_F16 || t == T_BF16) ? T_DENSE : (int)t; }
+int canon_type(uint32_t t) { return (t == T_F32 || t == T_F16 || t == T_BF16) ? T_DENSE : (int)t; }
 
 rmoe_status validate_desc(const rmoe_layer_desc* d) {
     if (!d) return fail(RMOE_ERR_INVALID, "null layer description");
@@ -389,19 +389,24 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
 }
 
 rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s,
-                                 uint32_t flags) {
+                                 uint32_t flags, bool given) {
     const bool det = flags & RMOE_FLAG_DETERMINISTIC;
-    rmoe_status st = ensure_workspace(L, T, det);
-    if (st) return st;
+    if (given) {
+        if (T > L->ws_T || (det && !L->ws.y)) return fail(RMOE_ERR_INVALID, "given routing without its workspace");
+    } else {
+        rmoe_status st = ensure_workspace(L, T, det);
+        if (st) return st;
+    }
     Workspace& w = L->ws;
     RouteParams rp{};
-    rp.x = x;
+    rp.x = given ? nullptr : x;
     rp.router_w = L->router_w;
     rp.T = (int)T; rp.H = (int)L->H; rp.E = (int)L->E; rp.k = (int)L->k; rp.gate = (int)L->gate_kind;
     rp.has_shared = L->has_shared;
+    rp.given = given ? 1 : 0;
     rp.xb = w.xb;
     rp.rowexp = w.rowexp;
-    rp.logits = w.logits;
+    rp.logits = given ? nullptr : w.logits;
     rp.out_zero = det ? nullptr : out;
     rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;
     rp.ticket = w.ticket; rp.expert_off = w.expert_off; rp.row_tok = w.row_tok; rp.row_slot = w.row_slot;
@@ -497,6 +502,7 @@ rmoe_status rmoe_layer_create(const rmoe_layer_desc* d, rmoe_layer** out) {
     L->gate_kind = d->gate;
     L->has_shared = d->has_shared ? 1 : 0;
     L->E_local = L->E;
+    L->E_router = L->E;
     if ((s = layer_upload(d, 0, d->n_experts, L))) { delete L; return s; }
     *out = L;
     return RMOE_OK;
@@ -508,6 +514,12 @@ rmoe_status rmoe_layer_forward(rmoe_layer* L, const float* x, uint32_t T, float*
     if (!x || !out) return fail(RMOE_ERR_INVALID, "null x / out");
     DeviceGuard g(L->device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (L->ep && (flags & RMOE_FLAG_HOST_IO)) return ep_forward_host(L, x, T, out, s, flags);
+    if (L->ep) {
+        if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
+            return fail(RMOE_ERR_INVALID, "device x / out must be 16-byte aligned");
+        return ep_forward(L, x, T, out, s, flags);
+    }
     if (flags & RMOE_FLAG_HOST_IO) {
         rmoe_status st = ensure_workspace(L, T, flags & RMOE_FLAG_DETERMINISTIC);
         if (st) return st;
@@ -531,6 +543,10 @@ rmoe_status rmoe_layer_forward(rmoe_layer* L, const float* x, uint32_t T, float*
 
 rmoe_status rmoe_layer_routing(rmoe_layer* L, uint32_t T, uint32_t* ids, float* weights) {
     if (!L) return fail(RMOE_ERR_INVALID, "null layer");
+    if (L->ep) {
+        DeviceGuard g(L->device);
+        return ep_routing(L, T, ids, weights, nullptr);
+    }
     if (T > L->last_T) return fail(RMOE_ERR_INVALID, "routing of %u tokens requested, last forward had %u", T, L->last_T);
     DeviceGuard g(L->device);
     cudaError_t e = cudaDeviceSynchronize();
@@ -544,6 +560,10 @@ rmoe_status rmoe_layer_routing(rmoe_layer* L, uint32_t T, uint32_t* ids, float* 
 
 rmoe_status rmoe_layer_logits(rmoe_layer* L, uint32_t T, float* logits) {
     if (!L || !logits) return fail(RMOE_ERR_INVALID, "null layer / buffer");
+    if (L->ep) {
+        DeviceGuard g(L->device);
+        return ep_routing(L, T, nullptr, nullptr, logits);
+    }
     if (T > L->last_T) return fail(RMOE_ERR_INVALID, "logits of %u tokens requested, last forward had %u", T, L->last_T);
     DeviceGuard g(L->device);
     cudaError_t e = cudaDeviceSynchronize();
@@ -571,6 +591,16 @@ void rmoe_layer_destroy(rmoe_layer* L) {
     cudaDeviceSynchronize();
     delete L;
 }
+
+}  // extern "C"
+
+rmoe_layer::~rmoe_layer() {
+    for (auto& e : ev)
+        if (e) cudaEventDestroy(e);
+    if (ep) rmoe::ep_free(this);
+}
+
+extern "C" {
 
 rmoe_status rmoe_dequant(uint32_t t, const void* src, uint64_t nbytes, float* dst, void* stream) {
     uint32_t el, by;

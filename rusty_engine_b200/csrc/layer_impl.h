@@ -53,6 +53,8 @@ struct Workspace {
     float* logits = nullptr;
 };
 
+struct EpState;  // expert-parallel state (ep.cu)
+
 }  // namespace rmoe
 
 struct rmoe_layer {
@@ -60,6 +62,9 @@ struct rmoe_layer {
     uint32_t H = 0, I = 0, E = 0, k = 0, gate_kind = 0;
     int has_shared = 0;
     uint32_t E_local = 0;
+    uint32_t E_router = 0;      // experts the router scores (E, or all experts of an EP layer)
+    uint32_t e_begin = 0;       // first global expert id held here (EP)
+    rmoe::EpState* ep = nullptr;  // expert-parallel state (null for a whole layer)
     rmoe::DevMat wg{}, wu{}, wd{}, swg{}, swu{}, swd{};
     rmoe::WMaps mg{}, mu{}, md{}, smg{}, smu{}, smd{};  // TMA maps of the stacks above
     CUtensorMap hmap{}, xsmap{};                          // TMA maps of the workspace h and xs
@@ -74,10 +79,7 @@ struct rmoe_layer {
     bool last_tc = false;  // the last forward ran the tcgen05 kernels
     cudaEvent_t ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     bool ev_valid = false, ev_combine = false;
-    ~rmoe_layer() {
-        for (auto& e : ev)
-            if (e) cudaEventDestroy(e);
-    }
+    ~rmoe_layer();
 };
 
 namespace rmoe {
@@ -89,5 +91,13 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
 rmoe_status validate_desc(const rmoe_layer_desc* d);
 rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_count, rmoe_layer* L);
 rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y);
-rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags);
+// given: the workspace's xb / topk_id / topk_w already hold T rows' routing (x unused; ids >= E
+// are empty picks) -- the expert-parallel local step
+rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags,
+                                 bool given = false);
+rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags);
+rmoe_status ep_forward_host(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags);
+rmoe_status ep_routing(rmoe_layer* L, uint32_t T, uint32_t* ids, float* weights, float* logits);
+void ep_free(rmoe_layer* L);
+int canon_type(uint32_t t);
 }  // namespace rmoe

@@ -12,7 +12,8 @@ __global__ void combine_kernel(CombineParams p) {
     const float* wt = p.topk_w + (size_t)t * p.k;
     for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
         float o = 0.0f;
-        for (int j = 0; j < p.k; j++) o = __fadd_rn(o, __fmul_rn(wt[j], p.y[(size_t)sr[j] * p.H + i]));
+        for (int j = 0; j < p.k; j++)
+            if (sr[j] >= 0) o = __fadd_rn(o, __fmul_rn(wt[j], p.y[(size_t)sr[j] * p.H + i]));  // < 0: empty pick
         if (p.has_shared) o = __fadd_rn(o, p.y[(size_t)(p.shared_row0 + t) * p.H + i]);
         p.out[(size_t)t * p.H + i] = o;
     }

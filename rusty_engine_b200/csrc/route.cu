@@ -321,6 +321,10 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
 
     for (int tl = warp; tl < ntok; tl += TK_THREADS / 32) {
         int t = t0 + tl;
+        if (p.given) {
+            if (lane < k) ids_s[tl * k + lane] = p.topk_id[(size_t)t * k + lane];
+            continue;
+        }
         int id = warp_topk(p.logits + (size_t)t * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
         if (lane < k) {
             p.topk_id[(size_t)t * k + lane] = id;
@@ -418,6 +422,10 @@ __global__ void __launch_bounds__(TK_THREADS) scatter_rows_kernel(RouteParams p)
         int gi = t0 * k + i;
         int t = gi / k;
         const int e = p.topk_id[gi];
+        if (e >= p.E) {  // empty pick (given routing)
+            p.slot_row[gi] = -1;
+            continue;
+        }
         int pos = p.expert_off[e] + p.cta_cnt[(size_t)e * ncp + blockIdx.x] + p.local_rank[gi];
         p.row_tok[pos] = t;
         p.row_slot[pos] = gi - t * k;
@@ -455,6 +463,7 @@ __global__ void __launch_bounds__(256) gather_x_kernel(RouteParams p) {
         }
         for (int j = 0; j < per; j++) {
             const int pos = j < k ? __shfl_sync(0xffffffffu, dst_row, j) : shared_row;
+            if (pos < 0) continue;  // empty pick
             uint4* dst = reinterpret_cast<uint4*>(p.xs + (size_t)pos * p.H);
 #pragma unroll
             for (int c = 0; c < GX_CHUNK; c++) {
@@ -481,6 +490,10 @@ __global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = p.T, E = p.E, k = p.k, H = p.H;
     for (int t = warp; t < T; t += TK_THREADS / 32) {
+        if (p.given) {
+            if (lane < k) ids_s[t * k + lane] = p.topk_id[(size_t)t * k + lane];
+            continue;
+        }
         const int id = warp_topk(p.logits + (size_t)t * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
         if (lane < k) {
             p.topk_id[(size_t)t * k + lane] = id;
@@ -502,6 +515,10 @@ __global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) 
     if (warp == 0) build_tiles(p, cnt_s, off_s, lane);
     __syncthreads();
     for (int i = tid; i < T * k; i += TK_THREADS) {
+        if (ids_s[i] >= E) {  // empty pick (given routing)
+            p.slot_row[i] = -1;
+            continue;
+        }
         const int t = i / k, pos = off_s[ids_s[i]] + rank_s[i];
         p.row_tok[pos] = t;
         p.row_slot[pos] = i - t * k;
@@ -519,21 +536,36 @@ __global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) 
 
 int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
 
-cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
-    cudaError_t e;
+// Router logits (and the fp16 copy of x): chained per-logit kernel for small batches,
+// register-tiled kernel otherwise.
+static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
     if (p.T <= RS_MAX_T) {
-        // small batches: chained logits, then the whole dispatch in one CTA
-        if ((e = cudaFuncSetAttribute(logits_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LC_SMEM)) !=
-            cudaSuccess)
-            return e;
+        cudaError_t e = cudaFuncSetAttribute(logits_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LC_SMEM);
+        if (e != cudaSuccess) return e;
         dim3 grid((p.E + LC_EB - 1) / LC_EB, (p.T + LC_TB - 1) / LC_TB);
         logits_chain_kernel<<<grid, LC_THREADS, LC_SMEM, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        route_small_kernel<<<1, TK_THREADS, 0, s>>>(p);
     } else {
         dim3 grid((p.T + LT_TOK - 1) / LT_TOK, (p.E + LT_EXP - 1) / LT_EXP);
         logits_tiled_kernel<<<grid, LT_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    return cudaGetLastError();
+}
+
+__global__ void route_only_kernel(const float* logits, int T, int E, int k, int gate, int* ids, float* w);
+
+cudaError_t launch_router_topk(const RouteParams& p, cudaStream_t s) {
+    cudaError_t e = launch_logits(p, s);
+    if (e != cudaSuccess || p.T <= 0) return e;
+    route_only_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p.logits, p.T, p.E, p.k, p.gate, p.topk_id, p.topk_w);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
+    cudaError_t e;
+    if (!p.given && (e = launch_logits(p, s)) != cudaSuccess) return e;
+    if (p.T <= RS_MAX_T) {
+        route_small_kernel<<<1, TK_THREADS, 0, s>>>(p);  // the whole dispatch in one CTA
+    } else {
         topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
         scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);

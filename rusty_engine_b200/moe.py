@@ -195,8 +195,22 @@ def _tensor(q: Optional[QTensor]) -> _lib.Tensor:
     return t
 
 
+def ep_unique_id() -> bytes:
+    """A fresh NCCL unique id (rmoe_ep_unique_id) for the ranks of one expert-parallel layer."""
+    buf = (C.c_uint8 * 128)()
+    _call(_lib.load().rmoe_ep_unique_id(buf))
+    return bytes(buf)
+
+
 class MoELayer:
     """A resident MoE layer on one GPU (rmoe_layer_create / rmoe_layer_forward)."""
+
+    @classmethod
+    def expert_parallel(cls, lw: LayerWeights, rank: int, world: int, uid: bytes, device: Optional[int] = None):
+        """This rank's shard of an expert-parallel layer (rmoe_ep_layer_create): experts
+        [rank E/world, (rank + 1) E/world) on `device`; every rank calls it with the same uid.
+        forward() then takes this rank's tokens and returns their full layer outputs."""
+        return cls(lw, device, _ep=(rank, world, uid))
 
     def __init__(self, lw: LayerWeights, device: Optional[int] = None, *, _ep=None):
         _require_cuda()
@@ -219,7 +233,8 @@ class MoELayer:
             _call(L.rmoe_layer_create(C.byref(d), C.byref(h)))
         else:
             rank, world, uid = _ep
-            _call(L.rmoe_ep_layer_create(C.byref(d), rank, world, uid, C.byref(h)))
+            idbuf = (C.c_uint8 * 128).from_buffer_copy(bytes(uid))
+            _call(L.rmoe_ep_layer_create(C.byref(d), rank, world, idbuf, C.byref(h)))
         self._h = h
 
     def forward(self, x, out=None, *, flags: int = 0, stream=None):

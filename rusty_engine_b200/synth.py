@@ -165,3 +165,17 @@ def zipf_router_bias(layer: LayerWeights, x: np.ndarray, s: float = 1.1, iters: 
         load = np.bincount(top.ravel(), minlength=E) / top.size
         b += 0.5 * (np.log(target + 1e-9) - np.log(load + 1e-9))
     return b.astype(np.float32)
+
+
+def zipf_workload(layer: LayerWeights, T: int, s: float = 1.1, seed: int = 1, mean: float = 1.0):
+    """Activations with a common mean mu (every element `mean`) and the layer with the Zipf(s)
+    per-expert bias folded into its router: row e gains b_e * mu / |mu|^2, so W.x = W.x_0 +
+    b_e (1 + mu.z / |mu|^2) ~ W.x_0 + b_e.  Returns (layer with the folded router, x)."""
+    x = activations(T, layer.H, seed=seed) + np.float32(mean)
+    b = zipf_router_bias(layer, x, s=s)
+    mu = np.full(layer.H, mean, dtype=np.float64)
+    rw = (layer.router_w.astype(np.float64) + np.outer(b, mu / (mu @ mu))).astype(np.float32)
+    lw = LayerWeights(layer.H, layer.I, layer.E, layer.k, layer.gate, rw, layer.gate_exps, layer.up_exps,
+                      layer.down_exps, layer.shared, name=layer.name + f"-zipf{s}")
+    return lw, x
+

@@ -1,0 +1,66 @@
+"""Expert-parallel layer over NCCL on two GPUs: each rank's outputs for its own tokens match the
+oracle's whole layer within the layer tolerance (relative L2 <= 5e-3; max-abs <= 2e-2, or
+2e-2 x RMS for outputs whose RMS is >= 50), on the small-batch and the tensor-core local
+paths.  Skipped where fewer than two GPUs are visible."""
+import time
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from rusty_engine_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+REL_L2, MAX_ABS = 5e-3, 2e-2
+
+
+def _check(got, want, what):
+    rel = float(np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want))
+    rms = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    bound = MAX_ABS if rms < 1.0 / MAX_ABS else MAX_ABS * rms
+    assert rel <= REL_L2, f"{what}: rel-L2 {rel:.3e}"
+    assert np.abs(got - want).max() <= bound, f"{what}: max-abs {np.abs(got - want).max():.3e}"
+
+
+def _rank(rank, world, uid, tokens):
+    import torch
+
+    from oracle import oracle as O
+    from rusty_engine_b200.moe import MoELayer
+
+    torch.cuda.set_device(rank)
+    lw = synth.config_c1()
+    layer = MoELayer.expert_parallel(lw, rank, world, uid, device=rank)
+    for T in tokens:
+        x = synth.activations(T, lw.H, seed=10 * rank + T)
+        out = layer.forward(torch.from_numpy(x).cuda())
+        torch.cuda.synchronize()
+        want, ids, _, _ = O.moe_layer_q_exact(x, lw)
+        got_ids, _ = layer.routing(T)
+        assert (got_ids == ids).all(), f"rank {rank} T {T}: routing differs"
+        _check(out.cpu().numpy(), want, f"rank {rank} T {T}")
+    layer.close()
+
+
+def _run(world, tokens, timeout_s=300):
+    from rusty_engine_b200.moe import ep_unique_id
+
+    uid = ep_unique_id()
+    ctx = mp.start_processes(_rank, args=(world, uid, tokens), nprocs=world, start_method="spawn", join=False)
+    deadline = time.time() + timeout_s
+    while not ctx.join(timeout=5):
+        if time.time() > deadline:
+            for p in ctx.processes:
+                if p.is_alive():
+                    p.kill()
+            pytest.fail(f"expert-parallel ranks did not finish in {timeout_s} s")
+
+
+def test_ep_two_gpus_matches_oracle(gpu):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    # 3 and 16 tokens: small-batch local path; 512: tensor-core local path
+    _run(2, (3, 16, 512))

@@ -1,0 +1,61 @@
+"""Expert-parallel exchange on CPU: two gloo ranks run the host restatement of ep.cu's plan /
+pack / local experts / return / combine (tests/ep_sim.py) and must reproduce the whole-layer
+oracle on their own tokens (only the f32 summation order over a token's experts differs).
+Ragged shards, a rank without tokens and picks that all land on one rank are covered."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from rusty_engine_b200 import synth
+from rusty_engine_b200.synth import GGML_Q4_K, GGML_Q6_K, row_bytes
+
+REL = 2e-6
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _experts_f32(lw):
+    from oracle import oracle as O
+
+    out = []
+    for e in range(lw.E):
+        def part(qt, rows, K):
+            nb = rows * row_bytes(qt.ggml_type, K)
+            return O.dequant(qt.ggml_type, qt.data[e * nb:(e + 1) * nb]).reshape(rows, K)
+        out.append((part(lw.gate_exps, lw.I, lw.H), part(lw.up_exps, lw.I, lw.H), part(lw.down_exps, lw.H, lw.I)))
+    return out
+
+
+def _rank(rank, world, port, tokens, seed, bias_to):
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from tests import ep_sim
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        lw = synth.make_layer(256, 256, 8, 3, gate_t=GGML_Q4_K, up_t=GGML_Q4_K, down_t=GGML_Q6_K, dlo=0.001,
+                              dhi=0.01, seed=seed, name="ep-sim")
+        if bias_to is not None:  # every token's picks on one rank's experts
+            lw.router_w[bias_to * 4:(bias_to + 1) * 4] += np.float32(0.5)
+        ex = _experts_f32(lw)
+        x = synth.activations(tokens[rank], lw.H, seed=100 + rank) if tokens[rank] else np.zeros((0, lw.H), np.float32)
+        got = ep_sim.ep_forward(x, lw, ex, rank, world)
+        if tokens[rank]:
+            want = O.moe_layer_q_exact(x, lw)[0]
+            rel = np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want)
+            assert rel <= REL, f"rank {rank}: rel-L2 {rel:.3e}"
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tokens,bias_to", [((5, 3), None), ((4, 0), None), ((3, 6), 1)])
+def test_ep_exchange_matches_whole_layer(tokens, bias_to):
+    mp.start_processes(_rank, args=(2, _free_port(), tokens, 7, bias_to), nprocs=2, start_method="spawn", join=True)
