@@ -170,9 +170,14 @@ RMOE_API rmoe_status rmoe_route(const float* logits, uint32_t T, uint32_t E, uin
 /* 128-byte NCCL unique id, made on one rank and shared with all ranks out of band. */
 RMOE_API rmoe_status rmoe_ep_unique_id(uint8_t id[128]);
 
-/* Create this rank's shard of an expert-parallel layer: experts are placed contiguously,
- * E / world_size per rank (rank r holds [r*E/W, (r+1)*E/W)); the router is replicated.
- * desc carries the FULL tensors (each rank uploads only its slice). */
+/* Create this rank's shard of an expert-parallel layer (a collective: every rank calls it with
+ * the same id): experts are dealt round-robin, E / world_size per rank (rank r holds experts
+ * r, r + W, r + 2W, ...), so a skewed load spreads over the ranks; the router is replicated.
+ * desc carries the FULL tensors (each rank uploads only its experts).  E must divide by W,
+ * W <= 16, no shared expert.  rmoe_layer_forward on the handle takes this rank's T tokens
+ * (device or RMOE_FLAG_HOST_IO buffers) and returns their complete layer outputs; it exchanges
+ * rows with the other ranks over NCCL and reads the per-rank row counts back to the host
+ * once (the call synchronises the stream there). */
 RMOE_API rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* desc, int32_t rank, int32_t world_size,
                                  const uint8_t id[128], rmoe_layer** out);
 

@@ -1,8 +1,9 @@
 // ep.cu -- expert-parallel layers: the experts split over G ranks (one GPU each), NCCL
 // send/recv exchanges between them.
 //
-// Rank r holds experts [r * E/G, (r + 1) * E/G) and the whole router.  A forward on rank r
-// takes r's own T tokens:
+// Rank r holds experts r, r + G, r + 2G, ... (dealt round-robin, so the most popular experts
+// of a skewed load land on different ranks; local id = e / G) and the whole router.  A forward
+// on rank r takes r's own T tokens:
 //   1. router logits + top-k over all E experts (the same kernels as a whole layer);
 //   2. plan: for every destination rank d, which tokens have at least one pick on d (each such
 //      token is sent to d once, however many of its picks d holds) and their order (token
@@ -10,7 +11,7 @@
 //   3. counts exchange (one int per peer) and one device-to-host read of the counts, which
 //      size the payload calls;
 //   4. pack + exchange: a row per (token, destination): the token's fp16 activations followed
-//      by its k picks as seen by d (d's local expert id, or the empty id E/G, and the weight);
+//      by its k picks as seen by d (d's local expert id e / G, or the empty id E/G, and the weight);
 //   5. d runs its local experts over the rows it received with the given routing (the grouped
 //      tensor-core or small-batch kernels), producing per received row the weighted sum of its
 //      local picks' outputs (f32);
@@ -69,7 +70,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int* topk_id, int T
         const int t = t0 + tid;
         int f = 0;
         if (t < T)
-            for (int j = 0; j < k; j++) f |= (topk_id[(size_t)t * k + j] / E_local) == d;
+            for (int j = 0; j < k; j++) f |= (topk_id[(size_t)t * k + j] % G) == d;
         int inc = f;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
@@ -114,8 +115,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __half* xb, const in
     for (int u = lane; u < H / 8; u += 32) dst[u] = src[u];
     if (lane < k) {
         const int id = topk_id[(size_t)t * k + lane];
-        const bool mine = id / E_local == d;
-        reinterpret_cast<int*>(row + (size_t)H * 2)[lane] = mine ? id - d * E_local : E_local;
+        const bool mine = id % G == d;
+        reinterpret_cast<int*>(row + (size_t)H * 2)[lane] = mine ? id / G : E_local;
         reinterpret_cast<float*>(row + (size_t)H * 2 + k * 4)[lane] = mine ? topk_w[(size_t)t * k + lane] : 0.0f;
     }
 }
@@ -337,11 +338,11 @@ rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* d, int32_t rank, int32_t
     L->H = d->hidden; L->I = d->inter;
     L->E_router = d->n_experts;
     L->E = L->E_local = d->n_experts / (uint32_t)world_size;
-    L->e_begin = (uint32_t)rank * L->E;
+    L->e_begin = (uint32_t)rank;
     L->k = d->top_k < d->n_experts ? d->top_k : d->n_experts;
     L->gate_kind = d->gate;
     L->has_shared = 0;
-    if ((s = layer_upload(d, L->e_begin, L->E, L))) { delete L; return s; }
+    if ((s = layer_upload(d, L->e_begin, L->E, L, (uint32_t)world_size))) { delete L; return s; }
     L->ep = new EpState();
     L->ep->rank = rank;
     L->ep->world = world_size;

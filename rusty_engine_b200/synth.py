@@ -146,24 +146,27 @@ def config_c5(seed: int = 0) -> LayerWeights:
                       dlo=0.001, dhi=0.01, seed=seed, name="c5-qwen3-235b-a22b-h4096-e128-k8-i1536-q4k-q6k")
 
 
-def zipf_router_bias(layer: LayerWeights, x: np.ndarray, s: float = 1.1, iters: int = 30,
+def zipf_router_bias(layer: LayerWeights, x: np.ndarray, s: float = 1.1, iters: int = 200,
                      sample: int = 2048, seed: int = 3) -> np.ndarray:
     """Per-expert logit bias so that top-k load over ``x`` follows Zipf(s) by expert rank.
 
-    Returned bias b_e is realised inside the router itself (the layer signature has no bias
-    input): ``fold_bias`` adds b_e * mu / |mu|^2 to router row e for an activation mean mu.
+    Damped log-ratio updates on a sample (loads floored at a quarter pick so unloaded experts
+    do not blow the step up, mean removed each round).  A token picks an expert at most once,
+    so no expert can carry more than 1/k of the picks: the head of the distribution saturates
+    there.  The bias is realised inside the router by ``zipf_workload``.
     """
     rng = np.random.default_rng(seed)
     xs = x[rng.choice(x.shape[0], min(sample, x.shape[0]), replace=False)]
-    logits = xs @ layer.router_w.T
+    logits = xs.astype(np.float64) @ layer.router_w.T.astype(np.float64)
     E, k = layer.E, layer.k
     target = 1.0 / np.arange(1, E + 1) ** s
     target = target / target.sum()
     b = np.zeros(E)
     for _ in range(iters):
-        top = np.argsort(-(logits + b), axis=1, kind="stable")[:, :k]
+        top = np.argpartition(-(logits + b), k, axis=1)[:, :k]
         load = np.bincount(top.ravel(), minlength=E) / top.size
-        b += 0.5 * (np.log(target + 1e-9) - np.log(load + 1e-9))
+        b += 0.2 * (np.log(target) - np.log(np.maximum(load, 0.25 / top.size)))
+        b -= b.mean()
     return b.astype(np.float32)
 
 

@@ -1,6 +1,6 @@
 """Host restatement of the expert-parallel exchange (rusty_engine_b200/csrc/ep.cu) for the CPU
-tests: the same plan (each token sent once to every rank holding one of its picks, in token
-order), the same row contents (the token and its picks as seen by the destination: local
+tests: the same placement (expert e on rank e % G, local id e // G), the same plan (each
+token sent once to every rank holding one of its picks, in token order), the same row contents (the token and its picks as seen by the destination: local
 expert id or the empty id E/G, and the weight), the same per-row partial sums and the same
 combine order (ascending rank), with torch.distributed all-to-all standing in for NCCL.
 Expert math is the oracle's exact f32 path.  Test infrastructure only."""
@@ -11,13 +11,14 @@ import torch.distributed as dist
 from oracle import oracle as O
 
 
-def plan(ids: np.ndarray, E_local: int, G: int):
-    """pos[t, d] = row of token t in d's block (-1 when not sent), counts[d]."""
+def plan(ids: np.ndarray, G: int):
+    """pos[t, d] = row of token t in d's block (-1 when not sent), counts[d]; expert e lives
+    on rank e % G."""
     T = ids.shape[0]
     flags = np.zeros((T, G), dtype=bool)
     for t in range(T):
         for e in ids[t]:
-            flags[t, int(e) // E_local] = True
+            flags[t, int(e) % G] = True
     pos = np.full((T, G), -1, dtype=np.int64)
     counts = np.zeros(G, dtype=np.int64)
     for d in range(G):
@@ -43,7 +44,7 @@ def ep_forward(x: np.ndarray, layer, experts_f32, rank: int, G: int) -> np.ndarr
     El = E // G
     logits = O.router_logits(x, layer.router_w, E)
     ids, w = O.route_batch(logits, layer.gate, k)
-    pos, send_counts = plan(ids, El, G)
+    pos, send_counts = plan(ids, G)
     recv_counts = torch.empty(G, dtype=torch.int64)
     dist.all_to_all_single(recv_counts, torch.from_numpy(send_counts))
     recv_counts = recv_counts.numpy()
@@ -58,8 +59,8 @@ def ep_forward(x: np.ndarray, layer, experts_f32, rank: int, G: int) -> np.ndarr
             r = soff[d] + pos[t, d]
             rows[r, :H] = x[t]
             for j in range(k):
-                mine = int(ids[t, j]) // El == d
-                rows[r, H + j] = int(ids[t, j]) - d * El if mine else El
+                mine = int(ids[t, j]) % G == d
+                rows[r, H + j] = int(ids[t, j]) // G if mine else El
                 rows[r, H + k + j] = w[t, j] if mine else 0.0
     got = a2a(rows, send_counts, recv_counts, width)
     # local experts: per received row, the weighted sum of its picks held here
@@ -70,7 +71,7 @@ def ep_forward(x: np.ndarray, layer, experts_f32, rank: int, G: int) -> np.ndarr
             le = int(got[r, H + j])
             if le >= El:
                 continue
-            g, u, dn = experts_f32[rank * El + le]
+            g, u, dn = experts_f32[le * G + rank]
             part[r] += got[r, H + k + j] * O.expert_ffn(xr, g, u, dn, H, I).astype(np.float64)
     back = a2a(part, recv_counts, send_counts, H)
     out = np.zeros((T, H))

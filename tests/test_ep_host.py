@@ -43,8 +43,8 @@ def _rank(rank, world, port, tokens, seed, bias_to):
     try:
         lw = synth.make_layer(256, 256, 8, 3, gate_t=GGML_Q4_K, up_t=GGML_Q4_K, down_t=GGML_Q6_K, dlo=0.001,
                               dhi=0.01, seed=seed, name="ep-sim")
-        if bias_to is not None:  # every token's picks on one rank's experts
-            lw.router_w[bias_to * 4:(bias_to + 1) * 4] += np.float32(0.5)
+        if bias_to is not None:  # every token's picks on one rank's experts (e % 2 == bias_to)
+            lw.router_w[bias_to::2] += np.float32(0.5)
         ex = _experts_f32(lw)
         x = synth.activations(tokens[rank], lw.H, seed=100 + rank) if tokens[rank] else np.zeros((0, lw.H), np.float32)
         got = ep_sim.ep_forward(x, lw, ex, rank, world)
