@@ -55,6 +55,15 @@ def kernels_per_forward(lw, T, world=1, rows_local=None):
     return 2 + 3 + local(rows_local, lw.E // world) + 1
 
 
+# DRAM bytes (read + write) per launch of the dominant kernels, from one ncu capture each of the
+# same command on a B200 (profiles/tc_kernels_c2_prefill.md, profiles/small_kernels_c3_decode_b64.md)
+NCU_TRAFFIC = {
+    ("c2", "gateup"): 360.961e6 + 41.065e6,
+    ("c2", "down"): 267.533e6 + 30.683e6,
+    ("c3b64", "down"): 162.655e6 + 3.513e6,
+}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -320,12 +329,14 @@ def main():
             work = {1: fg, 2: fd}.get(dom, fg)
             ach = work / (stage[dom] / 1e3) / 1e12
             roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                    "frac": ach / peaks["bf16_tflops"], "traffic": None, "kernel": names[dom],
+                    "frac": ach / peaks["bf16_tflops"], "traffic": NCU_TRAFFIC.get((args.config, names[dom])),
+                    "traffic_unit": "bytes per launch (ncu)", "kernel": names[dom],
                     "peak_src": peaks["src"] + " burst bf16"}
         else:
             gb = (gu_bytes if dom == 1 else nbytes - gu_bytes) / (stage[dom] / 1e3) / 1e9
             roof = {"bound": "hbm", "achieved": gb, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": gb / peaks["hbm_gbs"], "traffic": None, "kernel": names[dom],
+                    "frac": gb / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC.get((args.config, names[dom])),
+                    "traffic_unit": "bytes per launch (ncu)", "kernel": names[dom],
                     "peak_src": peaks["src"] + " copy"}
         line = {
             "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,

@@ -1,0 +1,58 @@
+"""Layer golden fixtures (tests/golden/*.npz, made by tests/golden/make_golden.py from the
+oracle's exact-f32 layer on seeded inputs).  CPU: the oracle still reproduces them bit for bit
+(a change to the oracle or to the synthetic generator shows up here first).  GPU: the CUDA
+path matches them -- routing ids and logits exactly, outputs within the layer tolerance
+(relative L2 <= 5e-3; max-abs <= 2e-2, or 2e-2 x RMS for outputs whose RMS is >= 50)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+sys.path.insert(0, HERE)
+import make_golden as G  # noqa: E402
+
+CASES = sorted(G.CASES)
+
+
+def _load(name):
+    return np.load(os.path.join(HERE, name + ".npz"))
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_oracle_reproduces_golden(name):
+    f = _load(name)
+    _, _, out, ids, w, logits = G.compute(name)
+    assert np.array_equal(out, f["out"]) and np.array_equal(ids, f["ids"])
+    assert np.array_equal(w, f["w"]) and np.array_equal(logits, f["logits"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", CASES)
+def test_gpu_matches_golden(name, gpu):
+    import torch
+
+    from rusty_engine_b200 import _lib
+    from rusty_engine_b200.moe import MoELayer
+
+    build, T, seed = G.CASES[name]
+    lw = build()
+    from rusty_engine_b200 import synth
+
+    x = synth.activations(T, lw.H, seed=seed)
+    f = _load(name)
+    layer = MoELayer(lw, device=0)
+    out = layer.forward(torch.from_numpy(x).cuda(), flags=_lib.FLAG_ROUTING_OUT).cpu().numpy()
+    ids, w = layer.routing(T)
+    logits = layer.logits(T)
+    layer.close()
+    assert np.array_equal(logits, f["logits"]), "router logits differ"
+    assert np.array_equal(ids, f["ids"]), "top-k ids differ"
+    np.testing.assert_allclose(w, f["w"], rtol=3e-7, atol=0)
+    want = f["out"].astype(np.float64)
+    rel = np.linalg.norm(out - want) / np.linalg.norm(want)
+    assert rel <= 5e-3, f"rel-L2 {rel:.3e}"
+    rms = float(np.sqrt(np.mean(want ** 2)))
+    bound = 2e-2 if rms < 50.0 else 2e-2 * rms  # K-quant layers have outputs ~1e5-1e6
+    assert np.abs(out - want).max() <= bound, f"max-abs {np.abs(out - want).max():.3e} (rms {rms:.3e})"
