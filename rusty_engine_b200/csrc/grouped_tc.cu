@@ -22,6 +22,8 @@
 // status word, skips the remaining work, waits for its own MMAs and frees its tensor memory.
 #include <string.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "decode.cuh"
 #include "kernels.h"
@@ -505,6 +507,305 @@ static cudaError_t go_tc(const GroupedParams& p, const TcMaps& maps, int max_til
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------------
+// down, persistent.  One CTA per SM walks the (tile, 128-feature block) items of the launch
+// (item = tile * H/128 + block, strided by the grid, so the CTAs working on one tile at a time
+// share its h rows in L2).  Two 256-column TMEM accumulators let the epilogue of item i run on
+// its own four warps while item i + 1 is decoded and multiplied; the dequantized weight tiles
+// therefore go to shared memory (the SS form of the MMA).  Warps:
+//   0 raw TMA producer, 1 MMA issuer, 2 h-tile TMA, 4-7 converters (one weight row per thread),
+//   8-11 epilogue: TMEM -> 32-token shared chunks -> scaled 16-B stores or vector reductions.
+// ---------------------------------------------------------------------------------------------
+template <int TYPE>
+struct DownGeom {
+    using RS = RawStage<TYPE, TC_M>;
+    static constexpr int NA = 2, RST = 2;  // weight-tile and raw stages
+    static constexpr int B_STAGE = TC_BN * 128, A_STAGE = TC_M * 128;
+    static constexpr int YLD = TC_M + 4, YCH = 32, Y_STAGE = YCH * YLD * 4;
+    static constexpr int FIXED = NA * A_STAGE + RST * RS::BYTES + 2 * Y_STAGE + 1024;
+    // h-tile stages: three where they fit (the 4-6-bit types), else two
+    static constexpr int NB = FIXED + 3 * B_STAGE <= 232448 - 4096 ? 3 : 2;
+    static constexpr int A_OFF = NB * B_STAGE, RAW_OFF = A_OFF + NA * A_STAGE, Y_OFF = RAW_OFF + RST * RS::BYTES;
+    static constexpr int SMEM = Y_OFF + 2 * Y_STAGE + 1024;
+    static constexpr int THREADS = 384;
+    static_assert(SMEM <= 232448 - 4096, "shared memory budget");
+    static_assert(A_OFF % 1024 == 0 && RAW_OFF % 128 == 0 && Y_OFF % 16 == 0, "alignment");
+};
+
+template <int TYPE>
+__global__ void __launch_bounds__(384, 1)
+    tc_down_kernel(const __grid_constant__ GroupedParams p, const __grid_constant__ TcMaps maps) {
+    using D = DownGeom<TYPE>;
+    using RS = RawStage<TYPE, TC_M>;
+    constexpr int RK = Raw<TYPE>::RK, PITCH = Raw<TYPE>::PITCH, SUBS = RK / TC_KS, NA = D::NA, NB = D::NB, RST = D::RST;
+    extern __shared__ uint8_t dsmem[];
+    __shared__ __align__(8) uint64_t bar_raw_full[RST], bar_raw_empty[RST];
+    __shared__ __align__(8) uint64_t bar_a_full[NA], bar_a_empty[NA], bar_b_full[NB], bar_b_empty[NB];
+    __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2], bar_fin;
+    __shared__ uint32_t tmem_holder;
+    __shared__ volatile int s_abort, s_epi_stop;
+
+    const int nfb = p.H / TC_M;
+    const int n_items = *p.n_tiles * nfb;
+    if ((int)blockIdx.x >= n_items) return;  // uniform exit before any barrier or TMEM use
+    const int K = p.I, nk = K / TC_KS, nraw = K / RK;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t sbase = (smem_u32(dsmem) + 1023u) & ~1023u;
+    uint8_t* gbase = dsmem + (sbase - smem_u32(dsmem));
+    const uint32_t bring = sbase, aring = sbase + D::A_OFF, rawring = sbase + D::RAW_OFF;
+    uint8_t* a_g = gbase + D::A_OFF;
+    uint8_t* raw_g = gbase + D::RAW_OFF;
+    float* ys_g = reinterpret_cast<float*>(gbase + D::Y_OFF);
+
+    if (tid == 0) {
+        for (int i = 0; i < RST; i++) {
+            mbar_init(smem_u32(&bar_raw_full[i]), 1);
+            mbar_init(smem_u32(&bar_raw_empty[i]), 4);
+        }
+        for (int i = 0; i < NA; i++) {
+            mbar_init(smem_u32(&bar_a_full[i]), 4);
+            mbar_init(smem_u32(&bar_a_empty[i]), 1);
+        }
+        for (int i = 0; i < NB; i++) {
+            mbar_init(smem_u32(&bar_b_full[i]), 1);
+            mbar_init(smem_u32(&bar_b_empty[i]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(smem_u32(&bar_acc_full[i]), 1);
+            mbar_init(smem_u32(&bar_acc_empty[i]), 4);
+        }
+        mbar_init(smem_u32(&bar_fin), 1);
+        s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(smem_u32(&tmem_holder), 512);
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tbase = tmem_holder;
+    auto fail = [&]() {
+        s_abort = 1;
+        atomicOr(p.status, (unsigned)DERR_TIMEOUT);
+    };
+    // the (expert, first row, rows, feature block) of an item
+    auto info = [&](int item, int& e, int& row0, int& nrows, int& fb) {
+        const int4 ti = p.tiles[item / nfb];
+        e = ti.x; row0 = ti.y; nrows = ti.z; fb = item % nfb;
+    };
+
+    if (warp == 0) {
+        // ---------------- raw weight producer ----------------
+        if (lane == 0) {
+            int gj = 0;
+            for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+                int e, row0, nrows, fb;
+                info(item, e, row0, nrows, fb);
+                const int sh = e >= p.E ? 1 : 0;
+                const DevMat& M = sh ? p.sdown : p.down;
+                const int grow0 = (sh ? 0 : e) * (int)M.rows + fb * TC_M;
+                const WMaps& wm = maps.w[sh][0];
+                for (int j = 0; j < nraw; j++, gj++) {
+                    const int s = gj % RST;
+                    if (gj >= RST && !mbar_wait(smem_u32(&bar_raw_empty[s]), ((gj / RST) + 1) & 1)) {
+                        fail();
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&bar_raw_full[s]), dst = rawring + (uint32_t)s * RS::BYTES;
+                    mbar_arrive_expect_tx(bar, (uint32_t)RS::BYTES);
+                    tma_2d(dst, &wm.main, j * (Raw<TYPE>::MB / 2), grow0, bar);
+                    if (Raw<TYPE>::DBLK) tma_2d(dst + RS::DOFF, &wm.d, grow0, j * Raw<TYPE>::DBLK, bar);
+                    if (Raw<TYPE>::AUX) tma_2d(dst + RS::AOFF, &wm.aux, grow0, j * Raw<TYPE>::AUX, bar);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int gk = 0, it = 0;
+            for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x, it++) {
+                int e, row0, nrows, fb;
+                info(item, e, row0, nrows, fb);
+                const int acc = it & 1;
+                if (it >= 2 && !mbar_wait(smem_u32(&bar_acc_empty[acc]), ((it / 2) + 1) & 1)) {
+                    fail();
+                    break;
+                }
+                fence_after_sync();
+                const uint32_t idesc = idesc_f16(TC_M, (nrows + 15) & ~15);
+                bool ok = true;
+                for (int kt = 0; kt < nk; kt++, gk++) {
+                    const int sa = gk % NA, sb = gk % NB;
+                    if (s_abort || !mbar_wait(smem_u32(&bar_a_full[sa]), (gk / NA) & 1) ||
+                        !mbar_wait(smem_u32(&bar_b_full[sb]), (gk / NB) & 1)) {
+                        if (!s_abort) fail();
+                        ok = false;
+                        break;
+                    }
+                    fence_after_sync();
+#pragma unroll
+                    for (int ks = 0; ks < TC_KS / 16; ks++)
+                        mma_ss(tbase + (uint32_t)(acc * TC_BN), smem_desc_sw128(aring + (uint32_t)sa * D::A_STAGE + ks * 32),
+                               smem_desc_sw128(bring + (uint32_t)sb * D::B_STAGE + ks * 32), idesc, (kt | ks) != 0);
+                    mma_commit(smem_u32(&bar_a_empty[sa]));
+                    mma_commit(smem_u32(&bar_b_empty[sb]));
+                }
+                if (!ok) break;
+                mma_commit(smem_u32(&bar_acc_full[acc]));
+            }
+            mma_commit(smem_u32(&bar_fin));  // every MMA this thread issued has finished when it fires
+            if (!mbar_wait(smem_u32(&bar_fin), 0)) fail();
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        // ---------------- h tiles ----------------
+        if (lane == 0) {
+            int gk = 0;
+            for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+                int e, row0, nrows, fb;
+                info(item, e, row0, nrows, fb);
+                for (int kt = 0; kt < nk; kt++, gk++) {
+                    const int s = gk % NB;
+                    if (gk >= NB && !mbar_wait(smem_u32(&bar_b_empty[s]), ((gk / NB) + 1) & 1)) {
+                        fail();
+                        break;
+                    }
+                    const uint32_t bar = smem_u32(&bar_b_full[s]);
+                    mbar_arrive_expect_tx(bar, (uint32_t)D::B_STAGE);
+                    tma_2d(bring + (uint32_t)s * D::B_STAGE, &maps.b, kt * TC_KS, row0, bar);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- converters: one weight row per thread ----------------
+        const int q = warp & 3, r = q * 32 + lane;
+        int gk = 0, gj = 0;
+        for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
+            bool ok = true;
+            for (int kt = 0; kt < nk; kt++, gk++) {
+                const int sub = kt % SUBS, s = gk % NA, rs = gj % RST;
+                if (s_abort) { ok = false; break; }
+                if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[rs]), (gj / RST) & 1)) { fail(); ok = false; break; }
+                if (gk >= NA && !mbar_wait(smem_u32(&bar_a_empty[s]), ((gk / NA) + 1) & 1)) { fail(); ok = false; break; }
+                const uint8_t* mat = raw_g + (size_t)rs * RS::BYTES;
+                uint32_t v[32];
+                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 0, v);
+                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 1, v + 16);
+                if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[rs]));
+                    gj++;
+                }
+                uint8_t* at = a_g + (size_t)s * D::A_STAGE + r * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++)
+                    *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
+                        make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[s]));
+            }
+            if (!ok) break;
+        }
+    } else if (warp >= 8) {
+        // ---------------- epilogue ----------------
+        const int q = warp & 3;
+        const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
+        int it = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, it++) {
+            // the four warps share named barrier 2, so they stop together: one thread samples the
+            // abort flag between two barriers (the first also ends every read of the previous
+            // item's staging chunks)
+            if (warp == 8 && lane == 0) s_epi_stop = s_abort;
+            asm volatile("bar.sync 2, 128;\n" ::: "memory");
+            const bool stop = s_epi_stop;
+            asm volatile("bar.sync 2, 128;\n" ::: "memory");
+            if (stop) break;
+            int e, row0, nrows, fb;
+            info(item, e, row0, nrows, fb);
+            const int acc = it & 1;
+            // this warp writes tokens c * 32 + q * 8 + t (t < 8) of every chunk c; lane l holds
+            // (token, scale) for chunk l / 8 (first) and l / 8 + 4 (second), t = l % 8
+            int tok[2];
+            float sc[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int n = ((lane >> 3) + 4 * h) * 32 + q * 8 + (lane & 7);
+                tok[h] = 0;
+                sc[h] = 0.0f;
+                if (n < nrows) {
+                    const int rr = row0 + n;
+                    tok[h] = __ldg(p.row_tok + rr);
+                    const int slot = __ldg(p.row_slot + rr);
+                    const float w = p.y ? 1.0f : ((slot < p.k) ? __ldg(p.topk_w + (size_t)tok[h] * p.k + slot) : 1.0f);
+                    sc[h] = __fmul_rn(w, exp2i(__ldg(p.rowexp + rr)));  // exact: 2^e
+                }
+            }
+            const bool ok = mbar_wait(smem_u32(&bar_acc_full[acc]), (it / 2) & 1);
+            if (!ok) fail();
+            fence_after_sync();
+            const int n_eff = (nrows + 15) & ~15;
+            for (int c = 0; c * 32 < n_eff; c++) {
+                uint32_t a[32];
+                tmem_ld32(tlane + (uint32_t)(acc * TC_BN + c * 32), a);
+                tmem_ld_wait();
+                float* ys = ys_g + (c & 1) * (D::YCH * D::YLD);
+#pragma unroll
+                for (int i = 0; i < 32; i++) ys[i * D::YLD + q * 32 + lane] = __uint_as_float(a[i]);
+                asm volatile("bar.sync 2, 128;\n" ::: "memory");
+                if (ok && !s_abort) {
+#pragma unroll
+                    for (int t = 0; t < 8; t++) {
+                        const int n = c * 32 + q * 8 + t;
+                        const int src = (c & 3) * 8 + t;
+                        const int tk = __shfl_sync(0xffffffffu, c < 4 ? tok[0] : tok[1], src);
+                        const float scl = __shfl_sync(0xffffffffu, c < 4 ? sc[0] : sc[1], src);
+                        if (n < nrows) {
+                            float4 v = *reinterpret_cast<const float4*>(ys + (q * 8 + t) * D::YLD + 4 * lane);
+                            v.x = __fmul_rn(v.x, scl); v.y = __fmul_rn(v.y, scl);
+                            v.z = __fmul_rn(v.z, scl); v.w = __fmul_rn(v.w, scl);
+                            const int f = fb * TC_M + 4 * lane;
+                            if (p.y) *reinterpret_cast<float4*>(p.y + (size_t)(row0 + n) * p.H + f) = v;
+                            else atomicAdd(reinterpret_cast<float4*>(p.out + (size_t)tk * p.H + f), v);
+                        }
+                    }
+                }
+            }
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
+        }
+    }
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after_sync();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+static int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int TYPE>
+static cudaError_t go_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s) {
+    using D = DownGeom<TYPE>;
+    auto k = tc_down_kernel<TYPE>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, D::SMEM);
+    if (e != cudaSuccess) return e;
+    const int items = max_tiles * (p.H / TC_M);
+    k<<<std::min(items, sm_count()), D::THREADS, D::SMEM, s>>>(p, maps);
+    return cudaGetLastError();
+}
+
 #define RMOE_TC_SWITCH(T, ...)                                     \
     switch (T) {                                                   \
         case T_Q4_0: { constexpr int TT = T_Q4_0; __VA_ARGS__; }   \
@@ -524,7 +825,7 @@ cudaError_t launch_tc_gateup(const GroupedParams& p, const TcMaps& maps, int max
 
 cudaError_t launch_tc_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s) {
     if (max_tiles <= 0) return cudaSuccess;
-    RMOE_TC_SWITCH(p.down.type, return go_tc<TT, 1>(p, maps, max_tiles, s))
+    RMOE_TC_SWITCH(p.down.type, return go_down<TT>(p, maps, max_tiles, s))
 }
 
 }  // namespace rmoe

@@ -5,8 +5,8 @@
 // never contracts), accumulated in ascending k.  Two kernels compute them:
 //   * small batches: one thread per (token, expert) chain, fed by a cp.async ring of 16 weight
 //     rows and 8 token rows per CTA;
-//   * large batches: a register-tiled product (64 tokens x 64 experts per CTA, 4 x 4 outputs
-//     per thread, cp.async double-buffered k-tiles), every output keeping the same order.
+//   * large batches: a register-tiled product (32 tokens x 64 experts per CTA, 4 x 4 outputs
+//     per thread, a 3-deep cp.async ring of k-tiles), every output keeping the same order.
 // Top-k is rusty-engine's stable descending argsort (src/moe.rs:75-93): larger score first,
 // equal scores by lower expert index; softmax over the chosen k (src/moe.rs:61-72) or the
 // sigmoid renormalisation (src/moe.rs:97-117).
@@ -20,7 +20,7 @@
 
 namespace rmoe {
 
-static constexpr int TK_TOK = 32;  // tokens per top-k CTA
+static constexpr int TK_TOK = 16;  // tokens per top-k CTA
 static constexpr int TK_THREADS = 256;
 
 // ---------------------------------------------------------------------------------------
@@ -98,11 +98,13 @@ __global__ void __launch_bounds__(LC_THREADS) logits_chain_kernel(const float* _
 }
 
 // ---------------------------------------------------------------------------------------
-// logits, large batches: CTA = 64 tokens x 64 experts, 256 threads, 4 x 4 outputs each
-// (thread (tx, ty) owns experts e0 + tx + 16j and tokens t0 + ty + 16i, so the 16-B shared
-// loads of one warp touch distinct banks up to a 2-way conflict)
+// logits, large batches: CTA = 32 tokens x 64 experts, 128 threads, 4 x 4 outputs each
+// (thread (tx, ty) owns experts e0 + tx + 16j and tokens t0 + ty + 8i; the 16 weight rows a
+// quarter-warp reads sit 144 B apart, so 16-B shared loads hit distinct banks), K tiles of 32
+// in a 3-deep cp.async ring.  Small CTAs so that several share an SM: the sequential chains
+// are latency-bound and want many warps.
 // ---------------------------------------------------------------------------------------
-static constexpr int LT_TOK = 64, LT_EXP = 64, LT_K = 32, LT_THREADS = 256, LT_LD = LT_K + 4;
+static constexpr int LT_TOK = 32, LT_EXP = 64, LT_K = 32, LT_THREADS = 128, LT_LD = LT_K + 4, LT_ST = 3;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem));
@@ -115,8 +117,8 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
                                                                   const float* __restrict__ w, int T, int H, int E,
                                                                   float* __restrict__ logits, __half* __restrict__ xb,
                                                                   unsigned* status) {
-    __shared__ __align__(16) float xs[2][LT_TOK][LT_LD];
-    __shared__ __align__(16) float ws[2][LT_EXP][LT_LD];
+    __shared__ __align__(16) float xs[LT_ST][LT_TOK][LT_LD];
+    __shared__ __align__(16) float ws[LT_ST][LT_EXP][LT_LD];
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * LT_TOK, e0 = blockIdx.y * LT_EXP;
     const int tx = tid & 15, ty = tid >> 4;
@@ -126,32 +128,37 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
 
-    auto issue = [&](int buf, int k0) {
-        for (int q = tid; q < LT_TOK * LT_K / 4; q += LT_THREADS) {
-            int r = q / (LT_K / 4), c = (q % (LT_K / 4)) * 4;
-            cp_async16(&xs[buf][r][c], x + (size_t)min(t0 + r, T - 1) * H + k0 + c);
-            cp_async16(&ws[buf][r][c], w + (size_t)min(e0 + r, E - 1) * H + k0 + c);
+    const int nk = H / LT_K;
+    auto issue = [&](int kt) {
+        if (kt < nk) {
+            const int buf = kt % LT_ST, k0 = kt * LT_K;
+            for (int q = tid; q < LT_TOK * LT_K / 4; q += LT_THREADS) {
+                const int r = q / (LT_K / 4), c = (q % (LT_K / 4)) * 4;
+                cp_async16(&xs[buf][r][c], x + (size_t)min(t0 + r, T - 1) * H + k0 + c);
+            }
+            for (int q = tid; q < LT_EXP * LT_K / 4; q += LT_THREADS) {
+                const int r = q / (LT_K / 4), c = (q % (LT_K / 4)) * 4;
+                cp_async16(&ws[buf][r][c], w + (size_t)min(e0 + r, E - 1) * H + k0 + c);
+            }
         }
         cp_async_commit();
     };
-    const int nk = H / LT_K;
-    issue(0, 0);
+    for (int kt = 0; kt < LT_ST - 1; kt++) issue(kt);
     for (int kt = 0; kt < nk; kt++) {
-        const int buf = kt & 1;
-        if (kt + 1 < nk) {
-            issue(buf ^ 1, (kt + 1) * LT_K);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
+        const int buf = kt % LT_ST;
+        cp_async_wait<LT_ST - 2>();
+        __syncthreads();  // tile kt landed for everyone; tile kt - 1 fully read
+        issue(kt + LT_ST - 1);
         if (blockIdx.y == 0 && xb) {  // the fp16 copy of x (GEMM operand), once per token tile
-            for (int q = tid; q < LT_TOK * LT_K; q += LT_THREADS) {
-                int r = q / LT_K, c = q % LT_K;
+            for (int q = tid; q < LT_TOK * LT_K / 4; q += LT_THREADS) {
+                const int r = q / (LT_K / 4), c = (q % (LT_K / 4)) * 4;
                 if (t0 + r < T) {
-                    float xv = xs[buf][r][c];
-                    if (!(fabsf(xv) <= 65504.0f)) atomicOr(status, (unsigned)DERR_FP16_RANGE);
-                    xb[(size_t)(t0 + r) * H + kt * LT_K + c] = __float2half_rn(xv);
+                    const float4 v = *reinterpret_cast<const float4*>(&xs[buf][r][c]);
+                    if (!(fabsf(v.x) <= 65504.f && fabsf(v.y) <= 65504.f && fabsf(v.z) <= 65504.f &&
+                          fabsf(v.w) <= 65504.f))
+                        atomicOr(status, (unsigned)DERR_FP16_RANGE);
+                    *reinterpret_cast<uint2*>(xb + (size_t)(t0 + r) * H + kt * LT_K + c) =
+                        make_uint2(pack_f16x2(v.x, v.y), pack_f16x2(v.z, v.w));
                 }
             }
         }
@@ -159,7 +166,7 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
         for (int kq = 0; kq < LT_K; kq += 4) {
             float4 xv[4], wv[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) xv[i] = *reinterpret_cast<const float4*>(&xs[buf][ty + 16 * i][kq]);
+            for (int i = 0; i < 4; i++) xv[i] = *reinterpret_cast<const float4*>(&xs[buf][ty + 8 * i][kq]);
 #pragma unroll
             for (int j = 0; j < 4; j++) wv[j] = *reinterpret_cast<const float4*>(&ws[buf][tx + 16 * j][kq]);
 #pragma unroll
@@ -174,11 +181,11 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
                     acc[i][j] = a;
                 }
         }
-        __syncthreads();
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        int t = t0 + ty + 16 * i;
+        int t = t0 + ty + 8 * i;
         if (t >= T) continue;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -482,14 +489,14 @@ __global__ void __launch_bounds__(256) gather_x_kernel(RouteParams p) {
 // Whole dispatch for a small batch (T <= 64) in one CTA: top-k of every token, per-expert
 // counts and token-order ranks, offsets and tiles, row placement -- all through shared memory.
 // ---------------------------------------------------------------------------------------
-static constexpr int RS_MAX_T = 64;
+static constexpr int RS_MAX_T = 64, RS_THREADS = 1024;
 
-__global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) {
+__global__ void __launch_bounds__(RS_THREADS) route_small_kernel(RouteParams p) {
     __shared__ int ids_s[RS_MAX_T * MAX_K], rank_s[RS_MAX_T * MAX_K];
     __shared__ int cnt_s[MAX_E + 2], off_s[MAX_E + 2];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = p.T, E = p.E, k = p.k, H = p.H;
-    for (int t = warp; t < T; t += TK_THREADS / 32) {
+    for (int t = warp; t < T; t += RS_THREADS / 32) {
         if (p.given) {
             if (lane < k) ids_s[t * k + lane] = p.topk_id[(size_t)t * k + lane];
             continue;
@@ -501,10 +508,10 @@ __global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) 
         }
     }
     if (p.out_zero && !p.xs)
-        for (int i = tid * 4; i < T * H; i += TK_THREADS * 4)
+        for (int i = tid * 4; i < T * H; i += RS_THREADS * 4)
             *reinterpret_cast<float4*>(p.out_zero + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     __syncthreads();
-    for (int e = tid; e < E; e += TK_THREADS) {  // ranks in token order
+    for (int e = tid; e < E; e += RS_THREADS) {  // ranks in token order
         int c = 0;
         for (int i = 0; i < T * k; i++)
             if (ids_s[i] == e) rank_s[i] = c++;
@@ -514,7 +521,7 @@ __global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) 
     __syncthreads();
     if (warp == 0) build_tiles(p, cnt_s, off_s, lane);
     __syncthreads();
-    for (int i = tid; i < T * k; i += TK_THREADS) {
+    for (int i = tid; i < T * k; i += RS_THREADS) {
         if (ids_s[i] >= E) {  // empty pick (given routing)
             p.slot_row[i] = -1;
             continue;
@@ -526,7 +533,7 @@ __global__ void __launch_bounds__(TK_THREADS) route_small_kernel(RouteParams p) 
         p.rowexp[pos] = -127;
     }
     if (p.has_shared)
-        for (int t = tid; t < T; t += TK_THREADS) {
+        for (int t = tid; t < T; t += RS_THREADS) {
             const int pos = off_s[E] + t;
             p.row_tok[pos] = t;
             p.row_slot[pos] = k;
@@ -564,7 +571,7 @@ cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
     cudaError_t e;
     if (!p.given && (e = launch_logits(p, s)) != cudaSuccess) return e;
     if (p.T <= RS_MAX_T) {
-        route_small_kernel<<<1, TK_THREADS, 0, s>>>(p);  // the whole dispatch in one CTA
+        route_small_kernel<<<1, RS_THREADS, 0, s>>>(p);  // the whole dispatch in one CTA
     } else {
         topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
