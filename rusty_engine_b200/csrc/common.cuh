@@ -80,152 +80,6 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, i
 }
 
 // --------------------------------------------------------------------------------------
-// chunk8: decode 8 consecutive elements [8*c8, 8*c8+8) of row `row` (global row index in
-// the stack) into 4 packed fp16x2 words.  The f32 value of each element is computed with
-// the same operation order as quant::dequant, then rounded to fp16 (round-to-nearest-even).
-// --------------------------------------------------------------------------------------
-template <int TYPE>
-__device__ __forceinline__ uint4 chunk8(const DevMat& M, uint64_t row, uint32_t c8);
-
-// Q4_K: y = d*sc*q - dmin*m (src/quant.rs:263-289), 4 groups of 64 per 144-B superblock.
-template <>
-__device__ __forceinline__ uint4 chunk8<T_Q4_K>(const DevMat& M, uint64_t row, uint32_t c8) {
-    const uint8_t* sb = M.main + row * M.main_stride + (uint64_t)(c8 >> 5) * 144u;
-    uint32_t w = c8 & 31u, grp = w >> 3, hi = (w >> 2) & 1u, q8 = w & 3u;
-    uint2 qs = __ldg(reinterpret_cast<const uint2*>(sb + 16 + grp * 32 + q8 * 8));
-    uint32_t dd = __ldg(reinterpret_cast<const uint32_t*>(sb));
-    float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
-    int sc, m;
-    scale_min_k4((int)(grp * 2 + hi), sb + 4, sc, m);
-    float d1 = __fmul_rn(d, (float)sc), dm1 = __fmul_rn(dmin, (float)m);
-    uint32_t sh = hi * 4;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        v[i] = __fsub_rn(__fmul_rn(d1, (float)((qs.x >> (8 * i + sh)) & 0xF)), dm1);
-        v[4 + i] = __fsub_rn(__fmul_rn(d1, (float)((qs.y >> (8 * i + sh)) & 0xF)), dm1);
-    }
-    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-                      pack_f16x2(v[6], v[7]));
-}
-
-// Q5_K: Q4_K plus a 5th bit from qh (src/quant.rs:294-323), 176-B superblocks.
-template <>
-__device__ __forceinline__ uint4 chunk8<T_Q5_K>(const DevMat& M, uint64_t row, uint32_t c8) {
-    const uint8_t* sb = M.main + row * M.main_stride + (uint64_t)(c8 >> 5) * 176u;
-    uint32_t w = c8 & 31u, grp = w >> 3, hi = (w >> 2) & 1u, q8 = w & 3u;
-    uint2 qs = __ldg(reinterpret_cast<const uint2*>(sb + 48 + grp * 32 + q8 * 8));
-    uint2 qh = __ldg(reinterpret_cast<const uint2*>(sb + 16 + q8 * 8));
-    uint32_t dd = __ldg(reinterpret_cast<const uint32_t*>(sb));
-    float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
-    int sc, m;
-    scale_min_k4((int)(grp * 2 + hi), sb + 4, sc, m);
-    float d1 = __fmul_rn(d, (float)sc), dm1 = __fmul_rn(dmin, (float)m);
-    uint32_t sh = hi * 4, ub = grp * 2 + hi;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int q0 = (int)((qs.x >> (8 * i + sh)) & 0xF) + (((qh.x >> (8 * i + ub)) & 1u) ? 16 : 0);
-        int q1 = (int)((qs.y >> (8 * i + sh)) & 0xF) + (((qh.y >> (8 * i + ub)) & 1u) ? 16 : 0);
-        v[i] = __fsub_rn(__fmul_rn(d1, (float)q0), dm1);
-        v[4 + i] = __fsub_rn(__fmul_rn(d1, (float)q1), dm1);
-    }
-    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-                      pack_f16x2(v[6], v[7]));
-}
-
-// Q6_K: y = d*sc*(q6 - 32) (src/quant.rs:328-357); main plane 208 B/superblock, d plane.
-template <>
-__device__ __forceinline__ uint4 chunk8<T_Q6_K>(const DevMat& M, uint64_t row, uint32_t c8) {
-    uint32_t sbi = c8 >> 5;
-    const uint8_t* sb = M.main + row * M.main_stride + (uint64_t)sbi * 208u;
-    uint32_t e0 = (c8 & 31u) * 8u;        // element within the superblock
-    uint32_t h = e0 >> 7, r = e0 & 127u;  // half, offset in half
-    uint32_t qd = r >> 5, l0 = r & 31u;   // quadrant (which ql/qh bits), l
-    const uint8_t* ql = sb + h * 64 + (qd & 1u) * 32 + l0;
-    uint2 lo = __ldg(reinterpret_cast<const uint2*>(ql));
-    uint2 hb = __ldg(reinterpret_cast<const uint2*>(sb + 128 + h * 32 + l0));
-    int sc = (int)(int8_t)__ldg(sb + 192 + h * 8 + qd * 2 + (l0 >> 4));
-    float d = __half2float(M.dpl[(uint64_t)sbi * M.trows + row]);
-    float ds = __fmul_rn(d, (float)sc);
-    uint32_t nsh = (qd >> 1) * 4, hsh = qd * 2;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int q0 = (int)(((lo.x >> (8 * i + nsh)) & 0xF) | (((hb.x >> (8 * i + hsh)) & 3u) << 4)) - 32;
-        int q1 = (int)(((lo.y >> (8 * i + nsh)) & 0xF) | (((hb.y >> (8 * i + hsh)) & 3u) << 4)) - 32;
-        v[i] = __fmul_rn(ds, (float)q0);
-        v[4 + i] = __fmul_rn(ds, (float)q1);
-    }
-    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-                      pack_f16x2(v[6], v[7]));
-}
-
-// Q4_0: y = (nibble - 8) * d, split-half (src/quant.rs:106-119); 16-B qs plane + d plane.
-template <>
-__device__ __forceinline__ uint4 chunk8<T_Q4_0>(const DevMat& M, uint64_t row, uint32_t c8) {
-    uint32_t blk = c8 >> 2, q = c8 & 3u;
-    uint2 qs = __ldg(reinterpret_cast<const uint2*>(M.main + row * M.main_stride + blk * 16u + (q & 1u) * 8u));
-    float d = __half2float(M.dpl[(uint64_t)blk * M.trows + row]);
-    uint32_t sh = (q >> 1) * 4;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        v[i] = __fmul_rn((float)((int)((qs.x >> (8 * i + sh)) & 0xF) - 8), d);
-        v[4 + i] = __fmul_rn((float)((int)((qs.y >> (8 * i + sh)) & 0xF) - 8), d);
-    }
-    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-                      pack_f16x2(v[6], v[7]));
-}
-
-// Q5_0: y = ((nibble | bit<<4) - 16) * d (src/quant.rs:126-144); qs, qh and d planes.
-template <>
-__device__ __forceinline__ uint4 chunk8<T_Q5_0>(const DevMat& M, uint64_t row, uint32_t c8) {
-    uint32_t blk = c8 >> 2, q = c8 & 3u;
-    uint2 qs = __ldg(reinterpret_cast<const uint2*>(M.main + row * M.main_stride + blk * 16u + (q & 1u) * 8u));
-    uint32_t qh = __ldg(M.aux + (uint64_t)blk * M.trows + row);
-    float d = __half2float(M.dpl[(uint64_t)blk * M.trows + row]);
-    uint32_t sh = (q >> 1) * 4;
-    uint32_t e0 = (q & 1u) * 8u + (q >> 1) * 16u;  // first element index in the block
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        int x0 = (int)(((qs.x >> (8 * i + sh)) & 0xF) | (((qh >> (e0 + i)) & 1u) << 4)) - 16;
-        int x1 = (int)(((qs.y >> (8 * i + sh)) & 0xF) | (((qh >> (e0 + 4 + i)) & 1u) << 4)) - 16;
-        v[i] = __fmul_rn((float)x0, d);
-        v[4 + i] = __fmul_rn((float)x1, d);
-    }
-    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-                      pack_f16x2(v[6], v[7]));
-}
-
-// Q8_0: y = (int8) * d (src/quant.rs:147-158); 32-B qs plane + d plane.
-template <>
-__device__ __forceinline__ uint4 chunk8<T_Q8_0>(const DevMat& M, uint64_t row, uint32_t c8) {
-    uint32_t blk = c8 >> 2, q = c8 & 3u;
-    uint2 qs = __ldg(reinterpret_cast<const uint2*>(M.main + row * M.main_stride + blk * 32u + q * 8u));
-    float d = __half2float(M.dpl[(uint64_t)blk * M.trows + row]);
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        v[i] = __fmul_rn((float)(int8_t)((qs.x >> (8 * i)) & 0xFF), d);
-        v[4 + i] = __fmul_rn((float)(int8_t)((qs.y >> (8 * i)) & 0xFF), d);
-    }
-    return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-                      pack_f16x2(v[6], v[7]));
-}
-
-// Unquantized experts (F32/F16/BF16 in GGUF) are held as an fp16 plane.
-template <>
-__device__ __forceinline__ uint4 chunk8<T_DENSE>(const DevMat& M, uint64_t row, uint32_t c8) {
-    return __ldg(reinterpret_cast<const uint4*>(M.main + row * M.main_stride + (uint64_t)c8 * 16u));
-}
-
-// f32 value of one element, for the stand-alone dequant operator.
-template <int TYPE>
-__device__ __forceinline__ void chunk8_f32(const DevMat& M, uint64_t row, uint32_t c8, float* out);
-
-// --------------------------------------------------------------------------------------
 // small PTX helpers
 // --------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -10,7 +10,7 @@ namespace rmoe {
 // 16-B loads of 8 consecutive rows hit distinct banks); DBLK = block scales per row per stage
 // ([block][row] plane); AUX = Q5_0 high-bit words ([block][row] plane).
 template <int TYPE> struct Raw;
-template <> struct Raw<T_Q4_K> { static constexpr int RK = 256, PITCH = 144, MB = 144, DBLK = 0, AUX = 0; };
+template <> struct Raw<T_Q4_K> { static constexpr int RK = 128, PITCH = 80, MB = 80, DBLK = 0, AUX = 0; };
 template <> struct Raw<T_Q5_K> { static constexpr int RK = 256, PITCH = 176, MB = 176, DBLK = 0, AUX = 0; };
 template <> struct Raw<T_Q6_K> { static constexpr int RK = 256, PITCH = 208, MB = 208, DBLK = 1, AUX = 0; };
 template <> struct Raw<T_Q4_0> { static constexpr int RK = 256, PITCH = 144, MB = 128, DBLK = 8, AUX = 0; };
@@ -52,20 +52,18 @@ __device__ __forceinline__ uint32_t lop_or3(uint32_t a, uint32_t b, uint32_t c) 
     return r;
 }
 
-// Q4_K: y = d*sc*q - dmin*m over sub-block 2*sub + half (the low nibbles of the slice's 32 qs
-// bytes for half 0, the high nibbles for half 1).  Per pair: the two codes land in 1024 + q
-// (exact), 1024 is subtracted exactly, and one fused multiply-add by the fp16-rounded sub-block
-// scale and min gives the value (the scale, the min and the result each round once to fp16;
-// the f32 path rounds the result only, and the difference is well inside the layer tolerance).
+// Q4_K, device layout: a stage row is one half-superblock (128 elements): four (fp16 d*sc,
+// fp16 -(dmin*m)) pairs, then 64 quant bytes (the low nibbles of bytes 32 g .. 32 g + 31 are
+// sub-block 2 g, the high nibbles 2 g + 1).  y = d*sc*q - dmin*m for sub-block 2*sub + half:
+// the two codes of a pair land in 1024 + q (exact), 1024 is subtracted exactly and one fused
+// multiply-add by the fp16 scale and min gives the value (scale, min and result each round once
+// to fp16; the f32 path rounds the result only, well inside the layer tolerance).
 template <int ROWS>
 struct Slice<T_Q4_K, ROWS> {
     static __device__ __forceinline__ void run(const uint8_t* p, const uint8_t*, const uint8_t*, int sub, int half,
-                                                uint32_t* v) {
-        const uint32_t dd = *reinterpret_cast<const uint32_t*>(p);
-        const float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
-        int sc, mn;
-        scale_min_k4(2 * sub + half, p + 4, sc, mn);
-        const __half2 D = __float2half2_rn(__fmul_rn(d, (float)sc)), M = __float2half2_rn(-__fmul_rn(dmin, (float)mn));
+                                               uint32_t* v) {
+        const uint32_t dm = *reinterpret_cast<const uint32_t*>(p + 4 * (2 * sub + half));
+        const __half2 D = as_h2(__byte_perm(dm, 0, 0x1010)), M = as_h2(__byte_perm(dm, 0, 0x3232));
         const __half2 K = __float2half2_rn(1024.0f);
         const uint4* q = reinterpret_cast<const uint4*>(p + 16 + sub * 32);
         const uint4 a = q[0], b = q[1];

@@ -1,25 +1,29 @@
 // grouped_tc.cu -- tensor-core (tcgen05) grouped expert products for large batches (prefill).
 //
-// One CTA computes a 128-feature block of one expert for a tile of <= 128 expert-sorted rows:
 //   gate/up: h[row, f] = silu(gate_f . x_row) * (up_f . x_row)   (src/moe.rs:280-299)
 //   down:    out[tok] += w_slot * (down . h_row)                  (src/moe.rs:373-380)
 //
-// Warp roles (gate/up runs one CTA per SM, down two; everything is ordered through mbarriers):
+// Both work on tiles of <= 256 expert-sorted rows (one expert each) and 128-feature blocks of
+// the expert's weights, with MMA M = 128 (weight rows), N = the tile's rows (rounded to 16),
+// K = 64 per stage, fp16 operands and f32 accumulators in tensor memory.
+//
+// gate/up (tc_grouped_kernel<TYPE, 2>, one CTA per (tile, block), one CTA per SM):
 //   warp 0      TMA producer: one 2-D tensor copy per matrix and plane brings the raw GGUF
-//               bytes of the CTA's 128 weight rows for one 256-element superblock (or 8 blocks
-//               of 32) into a shared ring;
-//   warp 1      allocates tensor memory and issues tcgen05.mma (one elected thread): A is the
-//               dequantized weight tile held in TMEM, B the token tile in shared memory;
-//   warps 2-3   token tiles: one thread loads each 64-column tile of the expert-sorted x rows
-//               (gate/up) or of the SwiGLU activations h (down) with a 128-B-swizzled 2-D TMA;
-//               for down, warp 3 then brings each h row of the tile to its row's common scale;
-//   warps 4..   one thread per weight row decodes 64 K-elements of its row per stage from the
-//               raw ring (bit-identical f32 values to quant::dequant, rounded to fp16) and
-//               stores them into its TMEM lane with tcgen05.st; after the last stage the same
-//               warps drain the f32 accumulators from TMEM and run the epilogue.
-// The fp16 weights never touch shared memory; shared memory carries the raw bytes and the
-// token tiles only.  Every wait is bounded: on a timeout the kernel records DERR_TIMEOUT in the
-// status word, skips the remaining work, waits for its own MMAs and frees its tensor memory.
+//               bytes of the CTA's 128 gate and 128 up rows for one raw stage into a ring;
+//   warp 1      allocates tensor memory and issues tcgen05.mma (one elected thread), A (the
+//               dequantized weights) and B (the token tile) both from shared memory, into the
+//               gate and up accumulators (2 x 256 columns);
+//   warp 2      one thread streams the expert-sorted x tiles with a 128-B-swizzled 2-D TMA;
+//   warps 4-11  one thread per weight row decodes 64 K-elements of its row per stage from the
+//               raw ring and writes them, 128-B-swizzled and K-major, as the MMA's A tile; after
+//               the last stage the same warps run SwiGLU and store h as fp16 x 2^e per (row,
+//               64-feature block).
+// down (tc_down_kernel<TYPE>, persistent, one CTA per SM walking (tile, block) items): the same
+//   producer / MMA / h-tile / converter roles, two accumulators so that four epilogue warps
+//   drain item i (y scaled by the routing weight, 16-B vector reductions into out) while item
+//   i + 1 is decoded and multiplied.
+// Every wait is bounded: on a timeout a kernel records DERR_TIMEOUT in the status word, skips
+// the remaining work, waits for its own MMAs and frees its tensor memory.
 #include <string.h>
 
 #include <algorithm>

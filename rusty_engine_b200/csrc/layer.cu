@@ -164,7 +164,43 @@ rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t
                         wmax);
     }
     switch (t.ggml_type) {
-        case T_Q4_K: case T_Q5_K:
+        case T_Q4_K: {
+            // half-superblocks of 80 B: the four sub-blocks' fp16 scale d*sc and negated min
+            // -(dmin*m) (the products exact in f32, rounded once, as the kernels used them),
+            // then the 64 quant bytes of those 128 elements
+            out.type = T_Q4_K;
+            out.main_stride = nblk * 160;
+            mainp.resize(total_rows * nblk * 160);
+            for (uint64_t r = 0; r < total_rows; r++)
+                for (uint64_t b = 0; b < nblk; b++) {
+                    const uint8_t* sb = src + r * rb + b * 144;
+                    const float d = f16_to_f32_host((uint16_t)(sb[0] | (sb[1] << 8)));
+                    const float dmin = f16_to_f32_host((uint16_t)(sb[2] | (sb[3] << 8)));
+                    for (int h = 0; h < 2; h++) {
+                        uint8_t* o = &mainp[(r * nblk + b) * 160 + h * 80];
+                        for (int i = 0; i < 4; i++) {
+                            const int j = 4 * h + i;
+                            const uint8_t* q = sb + 4;
+                            int sc, mn;
+                            if (j < 4) {
+                                sc = q[j] & 63;
+                                mn = q[j + 4] & 63;
+                            } else {
+                                sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+                                mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+                            }
+                            uint16_t hd, hm;
+                            f32_to_f16_rne(d * (float)sc, hd);
+                            f32_to_f16_rne(-(dmin * (float)mn), hm);
+                            memcpy(o + 4 * i, &hd, 2);
+                            memcpy(o + 4 * i + 2, &hm, 2);
+                        }
+                        memcpy(o + 16, sb + 16 + 64 * h, 64);
+                    }
+                }
+            break;
+        }
+        case T_Q5_K:
             out.type = (int)t.ggml_type;
             out.main_stride = rb;
             mainp.assign(src, src + t.nbytes);
