@@ -39,7 +39,6 @@ using namespace tc;
 static constexpr int TC_M = 128;   // weight rows per matrix per CTA (= TMEM lanes, = TMA box rows)
 static constexpr int TC_BN = 256;  // expert-sorted rows per tile at most (MMA N, rounded to 16 per tile)
 static constexpr int TC_KS = 64;   // K elements per MMA stage (one 128-B swizzle row of fp16)
-static constexpr int TC_NST = 4;   // MMA stages in flight
 static constexpr int TC_RST = 2;   // raw weight stages in flight
 
 int tc_tile_rows() { return TC_BN; }
@@ -126,14 +125,13 @@ __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int
 
 template <int TYPE, int NMAT>
 struct TcGeom {
+    static_assert(NMAT == 2, "the gate and up matrices");
     static constexpr int B_STAGE = TC_BN * 128;  // bytes per token tile stage
     static constexpr int RAW_STAGE = NMAT * RawStage<TYPE, TC_M>::BYTES;
-    // gate/up: its two accumulators (2 x 256 columns) fill the tensor memory, so the dequantized
-    // weight tiles go to shared memory (A_SMEM, 128-B-swizzled like the token tiles) and two
-    // stages fit; down keeps its weight tiles in tensor memory after the one accumulator.
-    static constexpr bool A_SMEM = NMAT == 2;
-    static constexpr int A_STAGE = A_SMEM ? NMAT * TC_M * 128 : 0;  // bytes per stage
-    static constexpr int NST = A_SMEM ? 2 : TC_NST;
+    // the two accumulators (2 x 256 columns) fill the tensor memory, so the dequantized weight
+    // tiles go to shared memory (128-B-swizzled like the token tiles) and two stages fit
+    static constexpr int A_STAGE = NMAT * TC_M * 128;  // bytes per stage
+    static constexpr int NST = 2;
     static constexpr int SMEM_MAX = 232448;  // opt-in shared memory per block
     static constexpr int RING = NST * (B_STAGE + A_STAGE) + 1024;
     // raw ring depth: two superblocks where they fit (all down types, the 4/5-bit gate/up types)
@@ -147,8 +145,6 @@ struct TcGeom {
     static constexpr int THREADS = 128 + CONV;
     static constexpr int MIN_BLOCKS = 1;
     static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr int A_COL0 = NMAT * TC_BN;  // down: A ring after the accumulator
-    static_assert(A_SMEM || A_COL0 + NST * 32 <= 512, "tensor memory budget");
     static_assert(SMEM <= SMEM_MAX - 4096, "shared memory budget (static part included)");
     static_assert(SMEM - 1024 >= TC_BN * (TC_M + 4) * 4, "epilogue staging tile fits in the rings");
 };
@@ -165,8 +161,6 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     __shared__ __align__(8) uint64_t bar_a_full[NST], bar_b_full[NST], bar_empty[NST];
     __shared__ __align__(8) uint64_t bar_acc;
     __shared__ uint32_t tmem_holder;
-    __shared__ int s_tok[TC_BN], s_rexp[TC_BN];
-    __shared__ float s_w[TC_BN];
     __shared__ volatile int s_abort;
 
     const int tile = blockIdx.y;
@@ -176,15 +170,15 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     const int n_eff = (nrows + 15) & ~15;
     const int fb = blockIdx.x;
     const int sh = e >= p.E ? 1 : 0;  // shared expert: its own single-expert stacks
-    const DevMat& M0 = NMAT == 2 ? (sh ? p.sgate : p.gate) : (sh ? p.sdown : p.down);
+    const DevMat& M0 = sh ? p.sgate : p.gate;
     const int grow0 = (sh ? 0 : e) * (int)M0.rows + fb * TC_M;  // first weight row of the CTA
-    const int K = NMAT == 2 ? p.H : p.I;
+    const int K = p.H;
     const int nk = K / TC_KS, nraw = K / RK;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     const uint32_t sbase = (smem_u32(dsmem) + 1023u) & ~1023u;  // 1024-B aligned (SW128 atoms)
     uint8_t* gbase = dsmem + (sbase - smem_u32(dsmem));
-    // [B ring | A ring (gate/up) | raw ring], every tile 1024-B aligned
+    // [B ring | A ring | raw ring], every tile 1024-B aligned
     const uint32_t bring = sbase, aring = sbase + NST * G::B_STAGE, rawring = aring + NST * G::A_STAGE;
     uint8_t* a_g = gbase + NST * G::B_STAGE;
     uint8_t* raw_g = a_g + NST * G::A_STAGE;
@@ -218,20 +212,6 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         fence_mbar_init();
         // the first raw stages need no free-slot wait: start them before the prologue's loads
         for (int j = 0; j < RST && j < nraw; j++) issue_raw(j);
-    }
-    for (int n = tid; n < TC_BN; n += G::THREADS) {
-        int tok = 0, rexp = 0;
-        float w = 0.0f;
-        if (n < nrows) {
-            const int r = row0 + n;
-            tok = __ldg(p.row_tok + r);
-            const int slot = __ldg(p.row_slot + r);
-            w = (slot < p.k) ? __ldg(p.topk_w + (size_t)tok * p.k + slot) : 1.0f;
-            if (NMAT == 1) rexp = __ldg(p.rowexp + r);
-        }
-        s_tok[n] = tok;
-        s_w[n] = w;
-        s_rexp[n] = rexp;
     }
     if (warp == 1) tmem_alloc(smem_u32(&tmem_holder), G::TMEM_COLS);
     fence_before_sync();
@@ -274,16 +254,10 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
 #pragma unroll
                 for (int m = 0; m < NMAT; m++)
 #pragma unroll
-                    for (int ks = 0; ks < TC_KS / 16; ks++) {
-                        if (G::A_SMEM)
-                            mma_ss(tbase + (uint32_t)(m * TC_BN),
-                                   smem_desc_sw128(aring + (uint32_t)(s * NMAT + m) * (TC_M * 128) + ks * 32),
-                                   smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
-                        else
-                            mma_ts(tbase + (uint32_t)(m * TC_BN),
-                                   tbase + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32 + ks * 8),
-                                   smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
-                    }
+                    for (int ks = 0; ks < TC_KS / 16; ks++)
+                        mma_ss(tbase + (uint32_t)(m * TC_BN),
+                               smem_desc_sw128(aring + (uint32_t)(s * NMAT + m) * (TC_M * 128) + ks * 32),
+                               smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
                 mma_commit(smem_u32(&bar_empty[s]));
             }
             mma_commit(smem_u32(&bar_acc));  // also fires when aborted: every issued MMA has finished
@@ -306,72 +280,49 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         }
     } else {
         // ---------------- converters: one thread per weight row ----------------
-        // warp (4 + cw) writes TMEM lanes 32 * (warp & 3) (a warp may only reach its quarter).
-        // Software-pipelined by one stage: the tensor-memory store of slice kt completes while
-        // slice kt + 1 is decoded, and only then is stage kt reported full (two register sets).
+        // warp (4 + cw): matrix cw / 4, rows 32 (warp & 3) .. +31 (the epilogue reads the
+        // accumulators of those TMEM lanes, which a warp may only reach in its own quarter)
         constexpr int CW = G::CW;
         static_assert(CW == 4, "one converter warp per lane quarter and matrix");
         const int cw = warp - 4, m = cw / CW, q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
-        bool ok = true;
-        int pend = -1;  // stage whose store is in flight
-        auto report = [&](uint32_t* vp) {  // the pending store (of vp) has landed: stage full
-            tmem_st_wait_hold(vp);
-            fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[pend % NST]));
-            pend = -1;
-        };
-        auto stage = [&](int kt, uint32_t* v, uint32_t* vp) {
+        for (int kt = 0; kt < nk; kt++) {
             const int j = kt / SUBS, sub = kt % SUBS, s = kt % NST;
-            if (s_abort) { ok = false; return; }
+            if (s_abort) break;
             if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % RST]), (j / RST) & 1)) {
                 fail();
-                ok = false;
-                return;
+                break;
             }
             if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
                 fail();
-                ok = false;
-                return;
+                break;
             }
             const uint8_t* mat = raw_g + (size_t)((j % RST) * NMAT + m) * RS::BYTES;
             const uint8_t *rp = mat + r * PITCH, *rd = mat + RS::DOFF + r * 2, *ra = mat + RS::AOFF + r * 4;
+            uint32_t v[32];
             slice32<TYPE, TC_M>(rp, rd, ra, sub, 0, v);
             slice32<TYPE, TC_M>(rp, rd, ra, sub, 1, v + 16);
             if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % RST]));
             }
-            if (G::A_SMEM) {
-                // row r of the 128-B-swizzled K-major tile: 16-B chunk c at (c ^ (r & 7)) * 16
-                uint8_t* at = a_g + (size_t)(s * NMAT + m) * (TC_M * 128) + r * 128;
+            // row r of the 128-B-swizzled K-major tile: 16-B chunk c at (c ^ (r & 7)) * 16
+            uint8_t* at = a_g + (size_t)(s * NMAT + m) * (TC_M * 128) + r * 128;
 #pragma unroll
-                for (int c = 0; c < 8; c++)
-                    *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
-                        make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-                fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[s]));
-            } else {
-                if (pend >= 0) report(vp);
-                tmem_st32(tlane + (uint32_t)(G::A_COL0 + (s * NMAT + m) * 32), v);
-                pend = kt;
-            }
-        };
-        uint32_t v0[32], v1[32];
-        for (int kt = 0; kt < nk && ok; kt += 2) {  // nk is a multiple of 4
-            stage(kt, v0, v1);
-            if (ok) stage(kt + 1, v1, v0);
+            for (int c = 0; c < 8; c++)
+                *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
+                    make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+            fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[s]));
         }
-        if (pend >= 0) report((pend & 1) ? v1 : v0);
         // ---------------- epilogue ----------------
         const bool acc_ok = mbar_wait(smem_u32(&bar_acc), 0);
         if (!acc_ok) fail();
         fence_after_sync();
         const bool work = acc_ok && !s_abort;
-        if (NMAT == 2) {
+        {
             // SwiGLU in f32 into a shared staging tile hs[n][f] (the rings are free now)
             float* hs = reinterpret_cast<float*>(gbase);
             constexpr int HLD = TC_M + 4;  // 16-B aligned rows; lanes of one read hit distinct banks
@@ -425,33 +376,6 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
                     }
                     p.hexp[rr * nblk + fb * 2 + blk] = (int8_t)ex;
                     atomicMax(p.rowexp + rr, ex);
-                }
-            }
-        } else {
-            // y tile through shared memory, ys[n][f] (the rings are idle once bar_acc has fired),
-            // so that each warp then writes whole 512-B token rows with 16-B stores or vector
-            // reductions. Scaling by 2^rowexp is exact, so w * (acc * 2^e) == acc * (w * 2^e).
-            float* ys = reinterpret_cast<float*>(gbase);
-            constexpr int YLD = TC_M + 4;
-            for (int c = cw >> 2; c * 32 < n_eff; c += G::CONV / 128) {
-                uint32_t a[32];
-                tmem_ld32(tlane + (uint32_t)(c * 32), a);
-                tmem_ld_wait();
-                if (!work) continue;
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int n = c * 32 + i;
-                    const float sc = p.y ? exp2i(s_rexp[n]) : __fmul_rn(s_w[n], exp2i(s_rexp[n]));
-                    ys[n * YLD + r] = __fmul_rn(__uint_as_float(a[i]), sc);
-                }
-            }
-            asm volatile("bar.sync 1, %0;\n" ::"n"(G::CONV) : "memory");
-            if (work) {
-                const int f = fb * TC_M + 4 * lane;
-                for (int n = cw; n < nrows; n += G::CONV / 32) {  // one token row per epilogue warp
-                    const float4 v = *reinterpret_cast<const float4*>(ys + n * YLD + 4 * lane);
-                    if (p.y) *reinterpret_cast<float4*>(p.y + (size_t)(row0 + n) * p.H + f) = v;
-                    else atomicAdd(reinterpret_cast<float4*>(p.out + (size_t)s_tok[n] * p.H + f), v);
                 }
             }
         }
