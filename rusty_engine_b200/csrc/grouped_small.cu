@@ -43,20 +43,21 @@ template <int TYPE, int NT, int NMAT>
 struct SmallGeom {
     using R = Raw<TYPE>;
     using RS = RawStage<TYPE, SB_M>;
-    static constexpr int SK = R::RK;                  // K elements per stage
-    static constexpr int SUBS = SK / SB_KS;           // decoded sub-slices per stage
-    static constexpr int A_BYTES = SB_M * SB_KS * 2;  // one decoded sub-slice per matrix
-    static constexpr int B_BYTES = NT * SK * 2;       // token tile per stage
+    static constexpr int SK = R::RK;                       // K elements per stage
+    static constexpr int SUBS = SK / SB_KS;                // decoded sub-slices per stage
+    static constexpr int A_WARP = NMAT * 16 * SB_KS * 2;   // a warp's decoded sub-slice (its 16 rows)
+    static constexpr int B_BYTES = NT * SK * 2;            // token tile per stage
     static constexpr int STAGE = NMAT * RS::BYTES + B_BYTES;
-    static constexpr int FIXED = 2 * NMAT * A_BYTES;  // double-buffered sub-slice tiles
-    // deepest ring (<= 4 stages) that keeps two CTAs per SM
-    static constexpr int RSTG = FIXED + 4 * STAGE <= SB_SMEM_MAX ? 4 : FIXED + 3 * STAGE <= SB_SMEM_MAX ? 3 : 2;
+    static constexpr int FIXED = 8 * A_WARP;
+    // ring depth (even: the two K halves take a stage each): the deepest of 6 / 4 / 2 that keeps
+    // two CTAs per SM
+    static constexpr int RSTG = FIXED + 6 * STAGE <= SB_SMEM_MAX ? 6 : FIXED + 4 * STAGE <= SB_SMEM_MAX ? 4 : 2;
     static constexpr int RAW_OFF = 0;
     static constexpr int B_OFF = RSTG * NMAT * RS::BYTES;
     static constexpr int A_OFF = B_OFF + RSTG * B_BYTES;
-    static constexpr int SMEM = A_OFF + 2 * NMAT * A_BYTES;
+    static constexpr int SMEM = A_OFF + FIXED;
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
-    static_assert(NT * (HBLK + 1) * 4 <= SMEM, "epilogue staging");
+    static_assert(NT * (HBLK + 1) * 4 <= SMEM && 4 * 32 * NMAT * (NT / 2) * 4 <= SMEM, "epilogue staging");
     static_assert(B_OFF % 128 == 0 && A_OFF % 128 == 0, "alignment");
 };
 
@@ -104,41 +105,54 @@ __device__ __forceinline__ void stage_b(const __half* base, const int* s_src, in
     }
 }
 
-// Decode sub-slice `sub` (64 K-elements) of the raw stage at `raw` for NMAT matrices into the
-// fp16 tiles at `at` ([NMAT][64][64], 128-B swizzle): one thread per (matrix, row, 32-element half).
+// A warp decodes sub-slice `sub` (64 K-elements) of its 16 weight rows (rows 16 rg .. of the
+// raw stage at `raw`) for NMAT matrices into its own fp16 tile at `at` ([NMAT][16][64], 128-B
+// swizzle): lane l takes row l & 15, half l >> 4.
 template <int TYPE, int NMAT>
-__device__ __forceinline__ void decode_sub(const uint8_t* raw, int sub, uint8_t* at, int tid) {
+__device__ __forceinline__ void decode_warp(const uint8_t* raw, int rg, int sub, uint8_t* at, int lane) {
     using R = Raw<TYPE>;
     using RS = RawStage<TYPE, SB_M>;
-    for (int t = tid; t < NMAT * SB_M * 2; t += SB_THREADS) {
-        const int m = t / (SB_M * 2), rem = t % (SB_M * 2), r = rem % SB_M, half = rem / SB_M;
+    const int row = lane & 15, half = lane >> 4, r = rg * 16 + row;
+#pragma unroll
+    for (int m = 0; m < NMAT; m++) {
         const uint8_t* rm = raw + m * RS::BYTES;
         uint32_t v[16];
         slice32<TYPE, SB_M>(rm + r * R::PITCH, rm + RS::DOFF + r * 2, rm + RS::AOFF + r * 4, sub, half, v);
-        uint8_t* am = at + m * (SB_M * SB_KS * 2);
+        uint8_t* am = at + m * (16 * SB_KS * 2);
 #pragma unroll
         for (int c = 0; c < 4; c++)
-            *reinterpret_cast<uint4*>(am + swz<SB_KS>(r, half * 4 + c)) =
+            *reinterpret_cast<uint4*>(am + swz<SB_KS>(row, half * 4 + c)) =
                 make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
     }
 }
 
-// MMAs of one sub-slice for one matrix and one warp: acc[4] += A(rows 16 (warp & 3)..) x
-// B(tokens 8 (warp >> 2).., K columns 64 sub.. of the stage's token tile)
-template <int SK>
-__device__ __forceinline__ void mma_sub(uint32_t a_base, uint32_t b_base, int sub, int warp, int lane, float* acc) {
+// A warp's MMAs over one decoded sub-slice for one matrix: acc[NT/8][4] += A(its 16 rows) x
+// B(all NT tokens, K columns 64 sub.. of the stage's token tile)
+template <int NT, int SK>
+__device__ __forceinline__ void mma_warp(uint32_t a_base, uint32_t b_base, int sub, int lane, float (*acc)[4]) {
 #pragma unroll
     for (int ks = 0; ks < SB_KS / 16; ks++) {
-        uint32_t a[4], b0, b1;
+        uint32_t a[4];
         {
-            const int mi = lane >> 3, r = (warp & 3) * 16 + (lane & 7) + (mi & 1) * 8, c = ks * 2 + (mi >> 1);
+            const int mi = lane >> 3, r = (lane & 7) + (mi & 1) * 8, c = ks * 2 + (mi >> 1);
             ldmatrix_x4(a_base + swz<SB_KS>(r, c), a[0], a[1], a[2], a[3]);
         }
-        {
-            const int n = (warp >> 2) * 8 + (lane & 7), c = sub * (SB_KS / 8) + ks * 2 + ((lane >> 3) & 1);
+        if (NT == 8) {
+            uint32_t b0, b1;
+            const int n = lane & 7, c = sub * (SB_KS / 8) + ks * 2 + ((lane >> 3) & 1);
             ldmatrix_x2(b_base + swz<SK>(n, c), b0, b1);
+            mma_f16_16816(acc[0], a, b0, b1);
+        } else {
+#pragma unroll
+            for (int nt = 0; nt < NT / 16; nt++) {
+                uint32_t b0, b1, b2, b3;
+                const int mi = lane >> 3, n = nt * 16 + (lane & 7) + (mi >> 1) * 8;
+                const int c = sub * (SB_KS / 8) + ks * 2 + (mi & 1);
+                ldmatrix_x4(b_base + swz<SK>(n, c), b0, b1, b2, b3);
+                mma_f16_16816(acc[nt * 2 + 0], a, b0, b1);
+                mma_f16_16816(acc[nt * 2 + 1], a, b2, b3);
+            }
         }
-        mma_f16_16816(acc, a, b0, b1);
     }
 }
 
@@ -219,8 +233,9 @@ __global__ void __launch_bounds__(SB_THREADS, 2) small_kernel(GroupedParams p) {
     const int K = NMAT == 2 ? p.H : p.I;
     const int nst = K / SK;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const bool mma_warp = (warp >> 2) < NT / 8;  // NT 8: warps 4-7 only decode
+    const int rg = warp & 3, kh = warp >> 2;  // rows 16 rg .. 16 rg + 15; stages of parity kh
     const uint32_t sbase = smem_u32(smem);
+    uint8_t* a_mine = smem + G::A_OFF + warp * G::A_WARP;
 
     for (int n = tid; n < NT; n += SB_THREADS) {
         const bool live = n < nrows;
@@ -242,78 +257,114 @@ __global__ void __launch_bounds__(SB_THREADS, 2) small_kernel(GroupedParams p) {
         cpa_commit();  // one group per stage (possibly empty), so the wait count stays fixed
     };
 
-    float acc[NMAT][4];
+    float acc[NMAT][NT / 8][4];
 #pragma unroll
     for (int m = 0; m < NMAT; m++)
 #pragma unroll
-        for (int q = 0; q < 4; q++) acc[m][q] = 0.0f;
+        for (int i = 0; i < NT / 8; i++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) acc[m][i][q] = 0.0f;
 
-    for (int j = 0; j < RSTG - 1; j++) issue(j);
-    for (int j = 0; j < nst; j++) {
-        cpa_wait<RSTG - 2>();  // this thread's copies of stage j have landed
-        __syncthreads();       // ... everyone's; and every warp is done with stage j - 1
-        issue(j + RSTG - 1);   // into the slot stage j - 1 used
-        const int slot = j % RSTG;
-        const uint8_t* raw = smem + G::RAW_OFF + slot * NMAT * RS::BYTES;
-        uint8_t* bt = smem + G::B_OFF + slot * G::B_BYTES;
+    // stages are taken in pairs, the even one by warps 0-3, the odd one by warps 4-7; inside a
+    // stage every warp decodes and multiplies its own 16 rows (no CTA barrier)
+    for (int j = 0; j < RSTG; j++) issue(j);
+    for (int j0 = 0; j0 < nst; j0 += 2) {
+        cpa_wait<RSTG - 2>();  // this thread's copies of stages j0, j0 + 1 have landed
+        __syncthreads();       // ... everyone's
         if (NMAT == 1) {
-            // h blocks to the row's common scale (exact power-of-two multiplies); the first
-            // sub-slice's barrier below publishes them
+            // h blocks to the row's common scale (exact power-of-two multiplies)
             const int nblk = p.I / HBLK;
-            for (int q = tid; q < nrows * (SK / 8); q += SB_THREADS) {
-                const int n = q / (SK / 8), c = q - n * (SK / 8);
-                const int blk = (j * SK + c * 8) / HBLK;
+            for (int q = tid; q < 2 * nrows * (SK / 8); q += SB_THREADS) {
+                const int jj = j0 + q / (nrows * (SK / 8)), rem = q % (nrows * (SK / 8));
+                const int n = rem / (SK / 8), c = rem - n * (SK / 8);
+                if (jj >= nst) continue;
+                const int blk = (jj * SK + c * 8) / HBLK;
                 const int d = (int)__ldg(p.hexp + (size_t)(row0 + n) * nblk + blk) - s_rexp[n];
-                uint4* ptr = reinterpret_cast<uint4*>(bt + swz<SK>(n, c));
+                uint4* ptr = reinterpret_cast<uint4*>(smem + G::B_OFF + (jj % RSTG) * G::B_BYTES + swz<SK>(n, c));
                 *ptr = scale_h8(*ptr, d);
             }
+            __syncthreads();
         }
+        const int j = j0 + kh;
+        if (j < nst) {
+            const int slot = j % RSTG;
+            const uint8_t* raw = smem + G::RAW_OFF + slot * NMAT * RS::BYTES;
+            const uint32_t bt = sbase + G::B_OFF + slot * G::B_BYTES;
 #pragma unroll 1
-        for (int sub = 0; sub < SUBS; sub++) {
-            const int buf = (j * SUBS + sub) & 1;
-            decode_sub<TYPE, NMAT>(raw, sub, smem + G::A_OFF + buf * NMAT * G::A_BYTES, tid);
-            __syncthreads();  // tile `buf` complete; every MMA of the tile decoded before it is done
-            if (mma_warp)
+            for (int sub = 0; sub < SUBS; sub++) {
+                decode_warp<TYPE, NMAT>(raw, rg, sub, a_mine, lane);
+                __syncwarp();
 #pragma unroll
                 for (int m = 0; m < NMAT; m++)
-                    mma_sub<SK>(sbase + G::A_OFF + (buf * NMAT + m) * G::A_BYTES, sbase + G::B_OFF + slot * G::B_BYTES,
-                                sub, warp, lane, acc[m]);
+                    mma_warp<NT, SK>(smem_u32(a_mine) + m * (16 * SB_KS * 2), bt, sub, lane, acc[m]);
+                __syncwarp();  // the tile is read before the next sub-slice overwrites it
+            }
         }
+        __syncthreads();  // both stages consumed: their slots take the next pair
+        issue(j0 + RSTG);
+        issue(j0 + RSTG + 1);
     }
     cpa_wait<0>();
-    __syncthreads();  // the rings are free for the epilogue staging
+    __syncthreads();
+
+    // the two K halves: warps 4-7 hand their sums to warps 0-3 (added in that fixed order)
+    float* red = reinterpret_cast<float*>(smem);
+    constexpr int PER = NMAT * (NT / 8) * 4;
+    if (kh == 1) {
+#pragma unroll
+        for (int m = 0; m < NMAT; m++)
+#pragma unroll
+            for (int i = 0; i < NT / 8; i++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) red[((rg * 32 + lane) * PER) + (m * (NT / 8) + i) * 4 + q] = acc[m][i][q];
+    }
+    __syncthreads();
+    if (kh == 0) {
+#pragma unroll
+        for (int m = 0; m < NMAT; m++)
+#pragma unroll
+            for (int i = 0; i < NT / 8; i++)
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    acc[m][i][q] = __fadd_rn(acc[m][i][q], red[((rg * 32 + lane) * PER) + (m * (NT / 8) + i) * 4 + q]);
+    }
+    __syncthreads();  // the reduction buffer is free for the epilogue staging
 
     const int g = lane >> 2, tq = lane & 3;
     if (NMAT == 2) {
         // SwiGLU in f32 (silu(g) * u, src/moe.rs:280-283) into smem hs[n][f]
         float* hs = reinterpret_cast<float*>(smem);
-        if (mma_warp)
+        if (kh == 0)
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int n = (warp >> 2) * 8 + tq * 2 + (q & 1);
-                const int f = (warp & 3) * 16 + g + (q >> 1) * 8;
-                hs[n * (HBLK + 1) + f] = silu_ref(acc[0][q]) * acc[NMAT - 1][q];
-            }
+            for (int i = 0; i < NT / 8; i++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int n = i * 8 + tq * 2 + (q & 1);
+                    const int f = rg * 16 + g + (q >> 1) * 8;
+                    hs[n * (HBLK + 1) + f] = silu_ref(acc[0][i][q]) * acc[NMAT - 1][i][q];
+                }
         __syncthreads();
         store_h_block<NT>(hs, row0, nrows, blockIdx.x, p, tid);
-    } else if (mma_warp) {
-        const int f0 = blockIdx.x * SB_M + (warp & 3) * 16 + g;
+    } else if (kh == 0) {
+        const int f0 = blockIdx.x * SB_M + rg * 16 + g;
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int n = (warp >> 2) * 8 + tq * 2 + (q & 1);
-            const int f = f0 + (q >> 1) * 8;
-            if (n < nrows) {
-                const int r = row0 + n;
-                const float yv = __fmul_rn(acc[0][q], exp2i(s_rexp[n]));
-                if (p.y) {
-                    p.y[(size_t)r * p.H + f] = yv;
-                } else {
-                    const int tok = __ldg(p.row_tok + r), slot = __ldg(p.row_slot + r);
-                    const float w = (slot < p.k) ? __ldg(p.topk_w + (size_t)tok * p.k + slot) : 1.0f;
-                    atomicAdd(p.out + (size_t)tok * p.H + f, __fmul_rn(w, yv));
+        for (int i = 0; i < NT / 8; i++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int n = i * 8 + tq * 2 + (q & 1);
+                const int f = f0 + (q >> 1) * 8;
+                if (n < nrows) {
+                    const int r = row0 + n;
+                    const float yv = __fmul_rn(acc[0][i][q], exp2i(s_rexp[n]));
+                    if (p.y) {
+                        p.y[(size_t)r * p.H + f] = yv;
+                    } else {
+                        const int tok = __ldg(p.row_tok + r), slot = __ldg(p.row_slot + r);
+                        const float w = (slot < p.k) ? __ldg(p.topk_w + (size_t)tok * p.k + slot) : 1.0f;
+                        atomicAdd(p.out + (size_t)tok * p.H + f, __fmul_rn(w, yv));
+                    }
                 }
             }
-        }
     }
 }
 

@@ -131,12 +131,16 @@ struct TcGeom {
     // the two accumulators (2 x 256 columns) fill the tensor memory, so the dequantized weight
     // tiles go to shared memory (128-B-swizzled like the token tiles) and two stages fit
     static constexpr int A_STAGE = NMAT * TC_M * 128;  // bytes per stage
-    static constexpr int NST = 2;
-    static constexpr int SMEM_MAX = 232448;  // opt-in shared memory per block
-    static constexpr int RING = NST * (B_STAGE + A_STAGE) + 1024;
-    // raw ring depth: two superblocks where they fit (all down types, the 4/5-bit gate/up types)
-    static constexpr int RST = RING + 2 * RAW_STAGE <= SMEM_MAX - 4096 ? 2 : 1;
-    static constexpr int SMEM = RING + RST * RAW_STAGE;
+    static constexpr int NA = 2;                       // weight-tile stages
+    static constexpr int SMEM_MAX = 232448;            // opt-in shared memory per block
+    static constexpr int LIM = SMEM_MAX - 4096, BASE = NA * A_STAGE + 1024;
+    // token-tile and raw stages: (3, 2) where they fit (the TMA latency of a token tile from L2
+    // spans about two MMA stages), then (2, 2), (2, 1)
+    static constexpr bool F32 = BASE + 3 * B_STAGE + 2 * RAW_STAGE <= LIM;
+    static constexpr bool F22 = BASE + 2 * B_STAGE + 2 * RAW_STAGE <= LIM;
+    static constexpr int NB = F32 ? 3 : 2;
+    static constexpr int RST = (F32 || F22) ? 2 : 1;
+    static constexpr int SMEM = BASE + NB * B_STAGE + RST * RAW_STAGE;
     // converter warps per matrix: 4 decode whole 64-element slices; 8 would split each slice
     // into two 32-element halves (measured slower on B200: the per-slice waits and arrivals
     // double while the decode itself does not shrink)
@@ -155,10 +159,10 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     using G = TcGeom<TYPE, NMAT>;
     using RS = RawStage<TYPE, TC_M>;
     constexpr int RK = Raw<TYPE>::RK, PITCH = Raw<TYPE>::PITCH, SUBS = RK / TC_KS;
-    constexpr int NST = G::NST, RST = G::RST;
+    constexpr int NA = G::NA, NB = G::NB, RST = G::RST;
     extern __shared__ uint8_t dsmem[];
     __shared__ __align__(8) uint64_t bar_raw_full[RST], bar_raw_empty[RST];
-    __shared__ __align__(8) uint64_t bar_a_full[NST], bar_b_full[NST], bar_empty[NST];
+    __shared__ __align__(8) uint64_t bar_a_full[NA], bar_a_empty[NA], bar_b_full[NB], bar_b_empty[NB];
     __shared__ __align__(8) uint64_t bar_acc;
     __shared__ uint32_t tmem_holder;
     __shared__ volatile int s_abort;
@@ -179,9 +183,9 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     const uint32_t sbase = (smem_u32(dsmem) + 1023u) & ~1023u;  // 1024-B aligned (SW128 atoms)
     uint8_t* gbase = dsmem + (sbase - smem_u32(dsmem));
     // [B ring | A ring | raw ring], every tile 1024-B aligned
-    const uint32_t bring = sbase, aring = sbase + NST * G::B_STAGE, rawring = aring + NST * G::A_STAGE;
-    uint8_t* a_g = gbase + NST * G::B_STAGE;
-    uint8_t* raw_g = a_g + NST * G::A_STAGE;
+    const uint32_t bring = sbase, aring = sbase + NB * G::B_STAGE, rawring = aring + NA * G::A_STAGE;
+    uint8_t* a_g = gbase + NB * G::B_STAGE;
+    uint8_t* raw_g = a_g + NA * G::A_STAGE;
 
     // TMA of raw stage j (all planes of all matrices) into ring slot j % RST
     auto issue_raw = [&](int j) {
@@ -202,10 +206,13 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
             mbar_init(smem_u32(&bar_raw_full[i]), 1);
             mbar_init(smem_u32(&bar_raw_empty[i]), G::CW * NMAT);
         }
-        for (int i = 0; i < NST; i++) {
+        for (int i = 0; i < NA; i++) {
             mbar_init(smem_u32(&bar_a_full[i]), G::CW * NMAT);
+            mbar_init(smem_u32(&bar_a_empty[i]), 1);
+        }
+        for (int i = 0; i < NB; i++) {
             mbar_init(smem_u32(&bar_b_full[i]), 1);
-            mbar_init(smem_u32(&bar_empty[i]), 1);
+            mbar_init(smem_u32(&bar_b_empty[i]), 1);
         }
         mbar_init(smem_u32(&bar_acc), 1);
         s_abort = 0;
@@ -242,23 +249,24 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         if (lane == 0) {
             const uint32_t idesc = idesc_f16(TC_M, n_eff);
             for (int kt = 0; kt < nk; kt++) {
-                const int s = kt % NST;
-                const uint32_t ph = (kt / NST) & 1;
+                const int sa = kt % NA, sb = kt % NB;
                 if (s_abort) break;
-                if (!mbar_wait(smem_u32(&bar_a_full[s]), ph) || !mbar_wait(smem_u32(&bar_b_full[s]), ph)) {
+                if (!mbar_wait(smem_u32(&bar_a_full[sa]), (kt / NA) & 1) ||
+                    !mbar_wait(smem_u32(&bar_b_full[sb]), (kt / NB) & 1)) {
                     fail();
                     break;
                 }
                 fence_after_sync();
-                const uint32_t bst = bring + (uint32_t)s * G::B_STAGE;
+                const uint32_t bst = bring + (uint32_t)sb * G::B_STAGE;
 #pragma unroll
                 for (int m = 0; m < NMAT; m++)
 #pragma unroll
                     for (int ks = 0; ks < TC_KS / 16; ks++)
                         mma_ss(tbase + (uint32_t)(m * TC_BN),
-                               smem_desc_sw128(aring + (uint32_t)(s * NMAT + m) * (TC_M * 128) + ks * 32),
+                               smem_desc_sw128(aring + (uint32_t)(sa * NMAT + m) * (TC_M * 128) + ks * 32),
                                smem_desc_sw128(bst + ks * 32), idesc, (kt | ks) != 0);
-                mma_commit(smem_u32(&bar_empty[s]));
+                mma_commit(smem_u32(&bar_a_empty[sa]));
+                mma_commit(smem_u32(&bar_b_empty[sb]));
             }
             mma_commit(smem_u32(&bar_acc));  // also fires when aborted: every issued MMA has finished
         }
@@ -267,9 +275,9 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         // ---------------- token tiles: one thread streams them with TMA onto b_full ----------------
         if (tid == 64) {
             for (int kt = 0; kt < nk; kt++) {
-                const int s = kt % NST;
+                const int s = kt % NB;
                 if (s_abort) break;
-                if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
+                if (kt >= NB && !mbar_wait(smem_u32(&bar_b_empty[s]), ((kt / NB) + 1) & 1)) {
                     fail();
                     break;
                 }
@@ -282,36 +290,44 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         // ---------------- converters: one thread per weight row ----------------
         // warp (4 + cw): matrix cw / 4, rows 32 (warp & 3) .. +31 (the epilogue reads the
         // accumulators of those TMEM lanes, which a warp may only reach in its own quarter)
+        // With 8 warps per matrix, the two warps of a lane quarter take the two 32-element
+        // halves of each slice.
         constexpr int CW = G::CW;
-        static_assert(CW == 4, "one converter warp per lane quarter and matrix");
-        const int cw = warp - 4, m = cw / CW, q = warp & 3;
+        static_assert(CW == 4 || CW == 8, "one or two converter warps per lane quarter and matrix");
+        const int cw = warp - 4, m = cw / CW, q = warp & 3, part = (cw % CW) >> 2;
         const int r = q * 32 + lane;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
         for (int kt = 0; kt < nk; kt++) {
-            const int j = kt / SUBS, sub = kt % SUBS, s = kt % NST;
+            const int j = kt / SUBS, sub = kt % SUBS, s = kt % NA;
             if (s_abort) break;
             if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % RST]), (j / RST) & 1)) {
                 fail();
                 break;
             }
-            if (kt >= NST && !mbar_wait(smem_u32(&bar_empty[s]), ((kt / NST) + 1) & 1)) {
+            if (kt >= NA && !mbar_wait(smem_u32(&bar_a_empty[s]), ((kt / NA) + 1) & 1)) {
                 fail();
                 break;
             }
             const uint8_t* mat = raw_g + (size_t)((j % RST) * NMAT + m) * RS::BYTES;
             const uint8_t *rp = mat + r * PITCH, *rd = mat + RS::DOFF + r * 2, *ra = mat + RS::AOFF + r * 4;
-            uint32_t v[32];
-            slice32<TYPE, TC_M>(rp, rd, ra, sub, 0, v);
-            slice32<TYPE, TC_M>(rp, rd, ra, sub, 1, v + 16);
+            constexpr int NV = CW == 4 ? 32 : 16;
+            uint32_t v[NV];
+            if (CW == 4) {
+                slice32<TYPE, TC_M>(rp, rd, ra, sub, 0, v);
+                slice32<TYPE, TC_M>(rp, rd, ra, sub, 1, v + 16);
+            } else {
+                slice32<TYPE, TC_M>(rp, rd, ra, sub, part, v);
+            }
             if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % RST]));
             }
             // row r of the 128-B-swizzled K-major tile: 16-B chunk c at (c ^ (r & 7)) * 16
             uint8_t* at = a_g + (size_t)(s * NMAT + m) * (TC_M * 128) + r * 128;
+            const int c0 = CW == 4 ? 0 : part * 4;
 #pragma unroll
-            for (int c = 0; c < 8; c++)
-                *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
+            for (int c = 0; c < NV / 4; c++)
+                *reinterpret_cast<uint4*>(at + (((c0 + c) ^ (r & 7)) << 4)) =
                     make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
             fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
             __syncwarp();
