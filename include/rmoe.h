@@ -86,8 +86,12 @@ enum {
     RMOE_FLAG_FORCE_SMALL = 1u << 2,   /* always use the small-batch (decode) kernels */
     RMOE_FLAG_FORCE_LARGE = 1u << 3,   /* always use the large-batch (prefill) kernels */
     RMOE_FLAG_ROUTING_OUT = 1u << 4,   /* also fill the routing buffers (rmoe_layer_routing) */
-    RMOE_FLAG_STAGE_TIMING = 1u << 5   /* record CUDA events between the pipeline stages
+    RMOE_FLAG_STAGE_TIMING = 1u << 5,  /* record CUDA events between the pipeline stages
                                           (read back with rmoe_layer_stage_ms) */
+    RMOE_FLAG_EXACT_ROUTER = 1u << 6   /* router logits bit-identical to moe::matvec (sequential
+                                          f32 sums, src/moe.rs:271-277); without it the logits
+                                          are FFMA sums a few ulp away, so top-k can differ from
+                                          the reference only at near-ties of that size */
 };
 
 /* Create a layer handle: validates the description on the host, copies router and expert
@@ -126,8 +130,8 @@ RMOE_API rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* layer, const float* 
  * and weights (T x k), copied to host buffers.  Mirrors route() (src/moe.rs:120-125). */
 RMOE_API rmoe_status rmoe_layer_routing(rmoe_layer* layer, uint32_t T, uint32_t* ids, float* weights);
 
-/* Router logits (T x E f32, the exact moe::matvec values) of the last forward that had
- * RMOE_FLAG_ROUTING_OUT, copied to a host buffer.  A debugging aid with no counterpart in
+/* Router logits (T x E f32: the exact moe::matvec values under RMOE_FLAG_EXACT_ROUTER) of the
+ * last forward that had RMOE_FLAG_ROUTING_OUT, copied to a host buffer.  A debugging aid with no counterpart in
  * the reference (its logits never leave moe_layer_forward). */
 RMOE_API rmoe_status rmoe_layer_logits(rmoe_layer* layer, uint32_t T, float* logits);
 

@@ -21,6 +21,7 @@ FLAG_FORCE_SMALL = 1 << 2
 FLAG_FORCE_LARGE = 1 << 3
 FLAG_ROUTING_OUT = 1 << 4
 FLAG_STAGE_TIMING = 1 << 5
+FLAG_EXACT_ROUTER = 1 << 6
 
 
 class RmoeError(RuntimeError):

@@ -2,11 +2,13 @@
 //
 // Device weight layout ("planes"): GGUF expert tensors are re-strided once at layer creation
 // so that every load a kernel issues is naturally aligned, without changing the byte count.
-//   Q4_K (12), Q5_K (13): unchanged GGUF superblocks (144 / 176 B, 16-B multiples).
+//   Q4_K (12): main plane [row][half-superblock] of 80 B = four (fp16 d*sc, fp16 -dmin*m)
+//              pairs (sub-blocks 0..3 of those 128 elements), then their 64 quant bytes.
+//   Q5_K (13): unchanged GGUF superblocks (176 B).
 //   Q6_K (14): main plane [row][sb] of 208 B = ql[128] | qh[64] | scales[16] (the GGUF
-//              superblock minus its trailing f16 d), d plane [row][sb] f16.
-//   Q4_0 (2):  main plane [row][blk] of 16 B qs, d plane [row][blk] f16.
-//   Q5_0 (6):  main plane [row][blk] of 16 B qs, aux plane [row][blk] u32 qh, d plane.
+//              superblock minus its trailing f16 d), d plane [sb][row] f16.
+//   Q4_0 (2):  main plane [row][blk] of 16 B qs, d plane [blk][row] f16.
+//   Q5_0 (6):  main plane [row][blk] of 16 B qs, aux plane [blk][row] u32 qh, d plane.
 //   Q8_0 (8):  main plane [row][blk] of 32 B int8, d plane.
 //   F32/F16/BF16 (0/1/30): main plane [row][K] fp16 (the MMA operand type), internal code T_DENSE.
 // Element values decoded from these planes are bit-identical (in f32) to quant::dequant
@@ -32,8 +34,10 @@ enum GgmlType : int {
 enum DevErr : uint32_t { DERR_NONE = 0, DERR_BAD_EXPERT = 1, DERR_ROWS_OVERFLOW = 2, DERR_TILES_OVERFLOW = 4,
                          DERR_TIMEOUT = 8, DERR_FP16_RANGE = 16 };
 
-// Rows of SwiGLU activations are stored as fp16 * 2^e per 64-feature block.
+// Rows of SwiGLU activations are stored as fp16 * 2^e per 64-feature block (tensor-core and
+// small-batch kernels) or per 16-feature block (the decode GEMV kernels).
 static constexpr int HBLK = 64;
+static constexpr int GV_EBLK = 16;
 
 // One stack of expert matrices (E experts x rows x K) in the device layout above.
 struct DevMat {
@@ -67,6 +71,16 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
 
 // 2^e as an exact float for e in [-126, 127].
 __device__ __forceinline__ float exp2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// Exponent e with max|v| * 2^-e in [2^13, 2^14): a zero block gets -127 (never the row max
+// unless the whole row is zero).
+__device__ __forceinline__ int block_exp(float amax) {
+    if (!(amax > 0.0f)) return -127;
+    int e;
+    frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
+    e -= 14;
+    return max(-100, min(100, e));
+}
 
 // get_scale_min_k4 (src/quant.rs:250-258) on the 12-byte scale array.
 __device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int& sc, int& m) {
@@ -104,6 +118,13 @@ __device__ __forceinline__ void mma_f16_16816(float* d, const uint32_t* a, uint3
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+
+// Programmatic dependent launch.  pdl_wait: block until the preceding kernel of the stream has
+// completed and its writes are visible (returns at once when this launch did not allow the
+// overlap).  pdl_trigger: the next kernel of the stream, if launched with the overlap allowed,
+// may start its CTAs once every CTA of this grid has triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
 // SiLU as rusty-engine computes it (src/moe.rs:44-51): x * (1 / (1 + exp(-x))).
 __device__ __forceinline__ float silu_ref(float x) { return x * (1.0f / (1.0f + expf(-x))); }

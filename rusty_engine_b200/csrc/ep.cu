@@ -43,6 +43,7 @@ struct EpState {
     int* pos = nullptr;      // [T][G]: row of the token in d's block, -1 when not sent to d
     int* cnt = nullptr;      // [2G]: send counts, then receive counts
     unsigned* status = nullptr;
+    unsigned* ticket = nullptr;  // router last-CTA counters (0 between launches)
     int* h_cnt = nullptr;    // pinned copy of cnt
     Owned send_own, recv_own;
     uint64_t cap_send = 0, cap_recv = 0;  // rows
@@ -183,8 +184,10 @@ static rmoe_status ep_token_buffers(rmoe_layer* L, uint32_t T) {
     P.pos = (int*)A((size_t)cap * G * 4);
     P.cnt = (int*)A((size_t)2 * G * 4);
     P.status = (unsigned*)A(16);
+    P.ticket = (unsigned*)A(64);
     if (!ok) return fail(RMOE_ERR_OOM, "expert-parallel token buffers for %u tokens", cap);
     cudaMemset(P.status, 0, 16);
+    cudaMemset(P.ticket, 0, 64);
     P.capT = cap;
     return RMOE_OK;
 }
@@ -215,8 +218,9 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     // 1. router + top-k over all experts
     RouteParams rp{};
     rp.x = x; rp.router_w = L->router_w; rp.T = (int)T; rp.H = H; rp.E = (int)L->E_router; rp.k = k;
+    rp.exact = (flags & RMOE_FLAG_EXACT_ROUTER) ? 1 : 0;
     rp.gate = (int)L->gate_kind; rp.xb = P.xb; rp.logits = P.logits; rp.topk_id = P.topk_id; rp.topk_w = P.topk_w;
-    rp.status = P.status;
+    rp.status = P.status; rp.ticket = P.ticket;
     if (T && (e = launch_router_topk(rp, s)) != cudaSuccess) return cuda_fail(e, "ep router launch");
     // 2. plan
     ep_plan_kernel<<<G, 1024, 0, s>>>(P.topk_id, (int)T, k, El, G, P.pos, P.cnt);

@@ -156,16 +156,6 @@ __device__ __forceinline__ void mma_warp(uint32_t a_base, uint32_t b_base, int s
     }
 }
 
-// Exponent e with max|v| * 2^-e in [2^13, 2^14): a zero block gets -127 (never the row max
-// unless the whole row is zero).
-__device__ __forceinline__ int block_exp(float amax) {
-    if (!(amax > 0.0f)) return -127;
-    int e;
-    frexpf(amax, &e);  // amax = m * 2^e, m in [0.5, 1)
-    e -= 14;
-    return max(-100, min(100, e));
-}
-
 // Multiply 8 packed fp16 values by 2^d (d <= 0), in f32, rounding back to fp16.
 __device__ __forceinline__ uint4 scale_h8(uint4 v, int d) {
     if (d == 0) return v;

@@ -20,13 +20,14 @@ struct RouteParams {
     __half* xb;             // [T, H] fp16 copy of x (GEMM B operand)
     int* rowexp;            // [rows] SwiGLU row exponents, set to -127 by the dispatch
     __half* xs;             // optional [rows, H]: x rows in expert-sorted order (tensor-core path)
-    float* logits;          // [T, E] router logits (the exact moe::matvec values)
+    float* logits;          // [T, E] router logits
     float* out_zero;        // optional: rows of `out` to zero (atomic combine)
     int* topk_id;           // [T, k]
     float* topk_w;          // [T, k]
     int* local_rank;        // [T, k] scratch
     int* cta_cnt;           // [E, route_cnt_stride(route_grid(T))] scratch: counts, then prefixes
-    unsigned int* ticket;   // last-CTA counter (0 between launches)
+    unsigned int* ticket;   // last-CTA counters, 0 between launches: [0] per launch, [1 + g] per
+                            // 8-token group (16 words)
     int* expert_off;        // [E + 2]
     int* row_tok;           // [rows] token of each expert-sorted row
     int* row_slot;          // [rows] slot (k for the shared expert)
@@ -39,6 +40,7 @@ struct RouteParams {
     unsigned int* status;   // device status word (DevErr bits)
     int given;              // 1: topk_id / topk_w are filled in already (x and logits unused);
                             // ids >= E are empty picks and get no row
+    int exact;              // 1: logits bit-identical to moe::matvec (sequential sums)
 };
 
 // Grouped expert products over the expert-sorted rows.
@@ -54,7 +56,7 @@ struct GroupedParams {
     const int* n_rows;            // expert-sorted rows in use
     const float* topk_w;          // [T, k]
     __half* h;                    // [rows, I] SwiGLU activations, fp16 * 2^hexp
-    int8_t* hexp;                 // [rows, I / 64] block exponents
+    int8_t* hexp;                 // [rows, I / 16] block exponents (I / 64 used by the tensor-core path)
     int* rowexp;                  // [rows] max block exponent per row
     float* y;                     // [rows, H] expert outputs (deterministic combine) or null
     float* out;                   // [T, H] atomic combine target (when y is null)
@@ -82,6 +84,13 @@ int small_tile_rows(int T);
 int small_tile_rows_min();
 cudaError_t launch_small_gateup(const GroupedParams& p, int max_tiles, int nt, cudaStream_t s);
 cudaError_t launch_small_down(const GroupedParams& p, int max_tiles, int nt, cudaStream_t s);
+
+// decode GEMV kernels (Q4_K / Q6_K experts, dequant in the mma.sync operand registers), same
+// tiles as the small-batch kernels; h blocks of GV_EBLK features
+bool gv_supported(int gate_type, int down_type);
+int gv_tile_rows(int T);
+cudaError_t launch_gv_gateup(const GroupedParams& p, int max_tiles, int nt, int T, cudaStream_t s);
+cudaError_t launch_gv_down(const GroupedParams& p, int max_tiles, int nt, int T, cudaStream_t s);
 
 // TMA descriptors of one weight-matrix stack: main plane (viewed as u16, 128-row boxes), the
 // block-scale plane and the Q5_0 high-bit plane (both [block][row], 128-row boxes).

@@ -408,7 +408,7 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.topk_w = (float*)A((size_t)cap * k * 4);
     w.local_rank = (int*)A((size_t)cap * k * 4);
     w.cta_cnt = (int*)A((size_t)route_cnt_stride(route_grid((int)cap)) * E * 4);
-    w.ticket = (unsigned*)A(16);
+    w.ticket = (unsigned*)A(64);  // dispatch tickets: one per launch, plus one per 8-token group
     w.status = (unsigned*)A(16);
     w.expert_off = (int*)A((size_t)(E + 2) * 4);
     w.row_tok = (int*)A(rows * 4);
@@ -419,14 +419,14 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.tiles = (int4*)A((size_t)L->max_tiles * 16);
     w.h = (__half*)A(rows * I * 2);
     w.xs = (__half*)A(rows * H * 2);
-    w.hexp = (int8_t*)A(rows * (I / HBLK));
+    w.hexp = (int8_t*)A(rows * (I / GV_EBLK));
     w.rowexp = (int*)A(rows * 4);
     w.logits = (float*)A((size_t)cap * E * 4);
     if (need_y || L->ws_had_y) w.y = (float*)A(rows * H * 4);
     if (!ok) return fail(RMOE_ERR_OOM, "workspace cudaMalloc failed for %u tokens", cap);
     if (!make_rows_map(w.h, rows, I, L->hmap) || !make_rows_map(w.xs, rows, H, L->xsmap))
         return fail(RMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the token operands");
-    cudaMemset(w.ticket, 0, 16);
+    cudaMemset(w.ticket, 0, 64);
     cudaMemset(w.status, 0, 16);
     L->ws_T = cap;
     L->ws_had_y = w.y != nullptr;
@@ -451,6 +451,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.T = (int)T; rp.H = (int)L->H; rp.E = (int)L->E; rp.k = (int)L->k; rp.gate = (int)L->gate_kind;
     rp.has_shared = L->has_shared;
     rp.given = given ? 1 : 0;
+    rp.exact = (flags & RMOE_FLAG_EXACT_ROUTER) ? 1 : 0;
     rp.xb = w.xb;
     rp.rowexp = w.rowexp;
     rp.logits = given ? nullptr : w.logits;
@@ -464,9 +465,14 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     if (flags & RMOE_FLAG_FORCE_SMALL) use_tc = false;
     if (flags & RMOE_FLAG_FORCE_LARGE) use_tc = true;
     rp.xs = use_tc ? w.xs : nullptr;
-    const int tile_rows = use_tc ? tc_tile_rows() : small_tile_rows((int)T);
+    // decode GEMV kernels where both expert types have register-fragment decoders
+    const bool gv = !use_tc && gv_supported(L->wg.type, L->wd.type);
+    const int tile_rows = use_tc ? tc_tile_rows() : gv ? gv_tile_rows((int)T) : small_tile_rows((int)T);
     const uint64_t rows_T = (uint64_t)T * L->k + (L->has_shared ? T : 0);
-    const int max_tiles = (int)std::min<uint64_t>((uint64_t)L->max_tiles, rows_T / tile_rows + L->E + 2);
+    // an expert with c rows takes at most c / tile_rows + 1 tiles, and at most rows_T experts
+    // are touched: the grids launch no more tile slots than that
+    const int max_tiles = (int)std::min<uint64_t>((uint64_t)L->max_tiles,
+                                                  rows_T / tile_rows + std::min<uint64_t>(L->E + 2, rows_T));
     rp.max_tiles = max_tiles; rp.tile_rows = tile_rows; rp.status = w.status;
     const bool timing = flags & RMOE_FLAG_STAGE_TIMING;
     if (timing && !L->ev[0])
@@ -495,7 +501,9 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         maps.w[1][1] = L->smu;
         maps.b = L->xsmap;
     }
-    e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : launch_small_gateup(gp, max_tiles, tile_rows, s);
+    e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s)
+        : gv   ? launch_gv_gateup(gp, max_tiles, tile_rows, (int)T, s)
+               : launch_small_gateup(gp, max_tiles, tile_rows, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
     mark(2);
     if (use_tc && (e = launch_rescale_h(gp, (int)rows_T, s)) != cudaSuccess) return cuda_fail(e, "h rescale launch");
@@ -504,7 +512,9 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         maps.w[1][0] = L->smd;
         maps.b = L->hmap;
     }
-    e = use_tc ? launch_tc_down(gp, maps, max_tiles, s) : launch_small_down(gp, max_tiles, tile_rows, s);
+    e = use_tc ? launch_tc_down(gp, maps, max_tiles, s)
+        : gv   ? launch_gv_down(gp, max_tiles, tile_rows, (int)T, s)
+               : launch_small_down(gp, max_tiles, tile_rows, s);
     if (e != cudaSuccess) return cuda_fail(e, "down launch");
     L->last_tc = use_tc;
     mark(3);

@@ -18,6 +18,8 @@
 // streams, or different layers on concurrent streams) race on it.
 #include <mutex>
 
+#include <algorithm>
+
 #include "layer_impl.h"
 
 namespace rmoe {
@@ -60,7 +62,7 @@ struct Carver {
 // The small-batch path's workspace for T tokens (the subset of Workspace those kernels read).
 static void carve(Carver& c, const rmoe_layer* L, uint32_t T, uint64_t rows, int max_tiles, Workspace& w) {
     const size_t H = L->H, I = L->I, E = L->E, k = L->k;
-    w.ticket = c.take<unsigned>(16);
+    w.ticket = c.take<unsigned>(64);
     w.status = c.take<unsigned>(16);
     w.n_rows = c.take<int>(16);
     w.n_tiles = c.take<int>(16);
@@ -76,7 +78,7 @@ static void carve(Carver& c, const rmoe_layer* L, uint32_t T, uint64_t rows, int
     w.row_slot = c.take<int>(rows * 4);
     w.tiles = c.take<int4>((size_t)max_tiles * 16);
     w.h = c.take<__half>(rows * I * 2);
-    w.hexp = c.take<int8_t>(rows * (I / HBLK));
+    w.hexp = c.take<int8_t>(rows * (I / GV_EBLK));
     w.rowexp = c.take<int>(rows * 4);
 }
 
@@ -94,8 +96,9 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
         return fail(RMOE_ERR_INVALID, "device x / out must be 16-byte aligned");
     if (L->E_local != L->E) return fail(RMOE_ERR_UNSUPPORTED, "noalloc forward: expert-parallel layers are not supported");
     const uint64_t rows = (uint64_t)T * L->k + (L->has_shared ? T : 0);
-    const int nt = small_tile_rows((int)T);
-    const int max_tiles = (int)(rows / nt + L->E + 2);
+    const bool gv = gv_supported(L->wg.type, L->wd.type);
+    const int nt = gv ? gv_tile_rows((int)T) : small_tile_rows((int)T);
+    const int max_tiles = (int)(rows / nt + std::min<uint64_t>(L->E + 2, rows));
     Workspace w{};
     Carver measure{nullptr};
     carve(measure, L, T, rows, max_tiles, w);
@@ -134,8 +137,10 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
     gp.topk_w = w.topk_w; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp;
     gp.y = nullptr; gp.out = out; gp.status = w.status;
-    if ((e = launch_small_gateup(gp, max_tiles, nt, s)) != cudaSuccess) return cuda_fail(e, "noalloc gate/up launch");
-    if ((e = launch_small_down(gp, max_tiles, nt, s)) != cudaSuccess) return cuda_fail(e, "noalloc down launch");
+    e = gv ? launch_gv_gateup(gp, max_tiles, nt, (int)T, s) : launch_small_gateup(gp, max_tiles, nt, s);
+    if (e != cudaSuccess) return cuda_fail(e, "noalloc gate/up launch");
+    e = gv ? launch_gv_down(gp, max_tiles, nt, (int)T, s) : launch_small_down(gp, max_tiles, nt, s);
+    if (e != cudaSuccess) return cuda_fail(e, "noalloc down launch");
     return RMOE_OK;
 }
 

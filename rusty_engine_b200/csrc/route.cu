@@ -1,12 +1,17 @@
 // route.cu -- router logits, top-k and dispatch (expert-sorted rows + GEMM tile list).
 //
-// Router logits are bit-identical to rusty-engine's moe::matvec (src/moe.rs:271-277): each
-// logit is a sequential f32 sum over H of w*x with separate multiply and add roundings (Rust
-// never contracts), accumulated in ascending k.  Two kernels compute them:
-//   * small batches: one thread per (token, expert) chain, fed by a cp.async ring of 16 weight
-//     rows and 8 token rows per CTA;
-//   * large batches: a register-tiled product (32 tokens x 64 experts per CTA, 4 x 4 outputs
-//     per thread, a 3-deep cp.async ring of k-tiles), every output keeping the same order.
+// Router logits, two modes.
+//   * exact (RMOE_FLAG_EXACT_ROUTER): bit-identical to rusty-engine's moe::matvec
+//     (src/moe.rs:271-277): each logit is a sequential f32 sum over H of w*x with separate
+//     multiply and add roundings (Rust never contracts), accumulated in ascending k -- small
+//     batches with one thread per (token, expert) chain fed by a cp.async ring, large batches
+//     with a register-tiled product (32 tokens x 64 experts per CTA, 4 x 4 outputs per thread)
+//     keeping that order for every output;
+//   * fast (default): the same products summed with fused multiply-adds (small batches: a
+//     warp per expert, K split over the lanes and folded by a shuffle tree; large batches: the
+//     tiled product with FFMA).  Logits differ from the sequential sums by a few ulp, so a
+//     top-k choice can differ only where two logits lie within that distance (the near-tie
+//     exception of the parity contract).
 // Top-k is rusty-engine's stable descending argsort (src/moe.rs:75-93): larger score first,
 // equal scores by lower expert index; softmax over the chosen k (src/moe.rs:61-72) or the
 // sigmoid renormalisation (src/moe.rs:97-117).
@@ -15,6 +20,8 @@
 // pick in token order; the last CTA to finish (atomic ticket, no spin-wait) scans the counts
 // into per-(CTA, expert) offsets and writes the tile list; a scatter kernel then places every
 // (token, slot) at offset + rank, so rows are in ascending token order inside each expert.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -113,6 +120,7 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+template <bool EXACT>
 __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* __restrict__ x,
                                                                   const float* __restrict__ w, int T, int H, int E,
                                                                   float* __restrict__ logits, __half* __restrict__ xb,
@@ -174,10 +182,17 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     float a = acc[i][j];
-                    a = __fadd_rn(a, __fmul_rn(wv[j].x, xv[i].x));
-                    a = __fadd_rn(a, __fmul_rn(wv[j].y, xv[i].y));
-                    a = __fadd_rn(a, __fmul_rn(wv[j].z, xv[i].z));
-                    a = __fadd_rn(a, __fmul_rn(wv[j].w, xv[i].w));
+                    if (EXACT) {
+                        a = __fadd_rn(a, __fmul_rn(wv[j].x, xv[i].x));
+                        a = __fadd_rn(a, __fmul_rn(wv[j].y, xv[i].y));
+                        a = __fadd_rn(a, __fmul_rn(wv[j].z, xv[i].z));
+                        a = __fadd_rn(a, __fmul_rn(wv[j].w, xv[i].w));
+                    } else {
+                        a = fmaf(wv[j].x, xv[i].x, a);
+                        a = fmaf(wv[j].y, xv[i].y, a);
+                        a = fmaf(wv[j].z, xv[i].z, a);
+                        a = fmaf(wv[j].w, xv[i].w, a);
+                    }
                     acc[i][j] = a;
                 }
         }
@@ -198,47 +213,10 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
 // ---------------------------------------------------------------------------------------
 // top-k of one token's E logits (one warp)
 // ---------------------------------------------------------------------------------------
-// Order = stable descending argsort (larger first, ties to the lower index), the rusty-engine
-// top_k / top_k_sigmoid contract (src/moe.rs:75-117).  Lane j < k returns the j-th expert id;
-// lane j < k writes pick j's weight to w_out[j].
-template <int NS>  // NS >= ceil(E / 32) logits per lane
-__device__ int warp_topk_n(const float* lg, int E, int k, int gate, int lane, float* w_out) {
-    float v[NS];
-    unsigned taken = 0;
-#pragma unroll
-    for (int s = 0; s < NS; s++) {
-        int e = lane + 32 * s;
-        float xv = (e < E) ? lg[e] : 0.0f;
-        if (gate == 1 && e < E) xv = 1.0f / (1.0f + expf(-xv));  // sigmoid (src/moe.rs:44-46)
-        v[s] = xv;
-        if (e >= E) taken |= 1u << s;
-    }
-    const int NONE = 0x7fffffff;
-    float chosen_score = 0.0f;
-    int chosen_id = 0;
-    for (int j = 0; j < k; j++) {
-        float best = 0.0f;
-        int bid = NONE;
-#pragma unroll
-        for (int s = 0; s < NS; s++) {
-            // s ascending = index ascending, so a strict '>' keeps the lowest index on ties
-            if (!((taken >> s) & 1u) && (bid == NONE || v[s] > best)) {
-                best = v[s];
-                bid = lane + 32 * s;
-            }
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            float ob = __shfl_xor_sync(0xffffffffu, best, off);
-            int oi = __shfl_xor_sync(0xffffffffu, bid, off);
-            bool better = (oi != NONE) && (bid == NONE || ob > best || (ob == best && oi < bid));
-            if (better) { best = ob; bid = oi; }
-        }
-        if ((bid & 31) == lane) taken |= 1u << (bid >> 5);
-        if (lane == j) { chosen_score = best; chosen_id = bid; }
-    }
-    // lane j < k holds pick j's score; the sums run in pick order on every lane (the same
-    // sequential f32 additions as the reference), each lane then forms its own weight
+// Routing weights of one token's k picks (one warp; lane j < k holds pick j's score and writes
+// w_out[j]).  The sums run in pick order on every lane (the same sequential f32 additions as
+// the reference), each lane then forms its own weight.
+__device__ __forceinline__ void pick_weights(float chosen_score, int k, int gate, int lane, float* w_out) {
     if (gate == 1) {
         float wsum = 0.0f;
         for (int j = 0; j < k; j++) wsum = __fadd_rn(wsum, __shfl_sync(0xffffffffu, chosen_score, j));
@@ -252,6 +230,58 @@ __device__ int warp_topk_n(const float* lg, int E, int k, int gate, int lane, fl
         for (int j = 0; j < k; j++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, j));
         if (lane < k) w_out[lane] = (sum != 0.0f) ? __fdiv_rn(ex, sum) : ex;
     }
+}
+
+// The score top-k ranks: the logit, or its sigmoid (src/moe.rs:44-46) for the sigmoid gate.
+__device__ __forceinline__ float gate_score(float x, int gate) { return gate == 1 ? 1.0f / (1.0f + expf(-x)) : x; }
+
+// Scores as unsigned keys in the same order (-0 and +0 equal, as the float compare has them);
+// 0 is left free to mark a taken or absent entry.
+__device__ __forceinline__ unsigned score_key(float v) {
+    const unsigned u = __float_as_uint(v + 0.0f);
+    const unsigned k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return k ? k : 1u;
+}
+__device__ __forceinline__ float key_score(unsigned k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// One token's top-k (one warp).  Order = stable descending argsort (larger first, ties to the
+// lower index), the rusty-engine top_k / top_k_sigmoid contract (src/moe.rs:75-117).  Lane
+// j < k returns the j-th expert id and writes pick j's weight to w_out[j].
+template <int NS>  // NS >= ceil(E / 32) logits per lane
+__device__ int warp_topk_n(const float* lg, int E, int k, int gate, int lane, float* w_out) {
+    unsigned key[NS];
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+        const int e = lane + 32 * s;
+        key[s] = e < E ? score_key(gate_score(lg[e], gate)) : 0u;
+    }
+    float chosen_score = 0.0f;
+    int chosen_id = 0;
+    for (int j = 0; j < k; j++) {
+        // this lane's best (s ascending = index ascending, so a strict '>' keeps the lower
+        // index), then the warp's largest key and, among the lanes holding it, the lowest index
+        unsigned bk = 0u;
+        int bs = 0;
+#pragma unroll
+        for (int s = 0; s < NS; s++)
+            if (key[s] > bk) {
+                bk = key[s];
+                bs = s;
+            }
+        const unsigned m = __reduce_max_sync(0xffffffffu, bk);
+        const int win = (int)__reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bs) : 0xffffffffu);
+        if ((win & 31) == lane)
+#pragma unroll
+            for (int s = 0; s < NS; s++)
+                if (s == (win >> 5)) key[s] = 0u;
+        if (lane == j) {
+            chosen_score = key_score(m);
+            chosen_id = win;
+        }
+    }
+    pick_weights(chosen_score, k, gate, lane, w_out);
     return chosen_id;
 }
 
@@ -280,31 +310,56 @@ __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
     return v;
 }
 
-// One warp: expert offsets and the tile list (expert, first row, rows) from the per-expert
-// row counts cnt_s[0..NE) (NE = E + the shared expert).  An expert's rows are split into the
-// fewest tiles of <= tile_rows rows, of equal size rounded up to 16 (the MMA N granularity)
-// except the last, so no tile is nearly empty.  Offsets also go to off_s when given.
-__device__ void build_tiles(const RouteParams& p, const int* cnt_s, int* off_s, int lane) {
+// Expert offsets and the tile list (expert, first row, rows) from the per-expert row counts
+// cnt_s[0..NE) (NE = E + the shared expert), by every thread of the CTA (one per expert, a
+// block-wide scan).  An expert's rows are split into the fewest tiles of <= tile_rows rows, of
+// equal size rounded up to 16 (the MMA N granularity) except the last, so no tile is nearly
+// empty.  Offsets also go to off_s when given.
+__device__ void build_tiles(const RouteParams& p, const int* cnt_s, int* off_s) {
+    __shared__ int s_w[2][32];  // per-warp totals, then exclusive offsets, of rows and tiles
+    __shared__ int s_run[2];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nw = nthr >> 5;
     const int NE = p.E + (p.has_shared ? 1 : 0);
-    int run = 0, tiles = 0;
-    for (int e0 = 0; e0 < NE; e0 += 32) {
-        const int e = e0 + lane;
+    if (tid == 0) s_run[0] = s_run[1] = 0;
+    __syncthreads();
+    for (int e0 = 0; e0 < NE; e0 += nthr) {
+        const int e = e0 + tid;
         const int c = e < NE ? cnt_s[e] : 0;
         const int n0 = (c + p.tile_rows - 1) / p.tile_rows;
         const int tr = c ? min(p.tile_rows, ((c + n0 - 1) / n0 + 15) & ~15) : 1;
         const int nt = (c + tr - 1) / tr;
         const int ic = warp_incl_scan(c, lane), itl = warp_incl_scan(nt, lane);
-        const int off = run + ic - c, tb = tiles + itl - nt;
+        if (lane == 31) {
+            s_w[0][warp] = ic;
+            s_w[1][warp] = itl;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const int a = lane < nw ? s_w[0][lane] : 0, b = lane < nw ? s_w[1][lane] : 0;
+            const int ia = warp_incl_scan(a, lane), ib = warp_incl_scan(b, lane);
+            if (lane < nw) {
+                s_w[0][lane] = ia - a;
+                s_w[1][lane] = ib - b;
+            }
+        }
+        __syncthreads();
+        const int off = s_run[0] + s_w[0][warp] + ic - c, tb = s_run[1] + s_w[1][warp] + itl - nt;
         if (e < NE) {
             p.expert_off[e] = off;
             if (off_s) off_s[e] = off;
             for (int j = 0; j < nt; j++)
                 if (tb + j < p.max_tiles) p.tiles[tb + j] = make_int4(e, off + j * tr, min(tr, c - j * tr), 0);
         }
-        run += __shfl_sync(0xffffffffu, ic, 31);
-        tiles += __shfl_sync(0xffffffffu, itl, 31);
+        __syncthreads();  // s_run and s_w read by everyone
+        if (tid == nthr - 1) {  // the running totals after this chunk
+            s_run[0] = off + c;
+            s_run[1] = tb + nt;
+        }
+        __syncthreads();
     }
-    if (lane == 0) {
+    if (tid == 0) {
+        const int run = s_run[0];
+        int tiles = s_run[1];
         p.expert_off[NE] = run;
         if (off_s) off_s[NE] = run;
         *p.n_rows = run;
@@ -415,10 +470,8 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     }
     if (tid == 0 && p.has_shared) cnt_s[E] = p.T;
     __syncthreads();
-    if (warp == 0) {
-        build_tiles(p, cnt_s, nullptr, lane);
-        if (lane == 0) *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
-    }
+    build_tiles(p, cnt_s, nullptr);
+    if (tid == 0) *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
 }
 
 // Place every (token, slot) at its expert-sorted row; CTA b handles the picks top-k CTA b made.
@@ -491,9 +544,72 @@ __global__ void __launch_bounds__(256) gather_x_kernel(RouteParams p) {
 // ---------------------------------------------------------------------------------------
 static constexpr int RS_MAX_T = 64, RS_THREADS = 1024;
 
+// Dispatch of a small batch inside one CTA, from the token-order picks ids_s[0 .. T k): per
+// expert counts and the token-order rank of every pick (warps match the expert ids of 32-pick
+// chunks; per-chunk counts are scanned over the chunks per expert), offsets and tiles, row
+// placement.  scratch: [ceil(T k / 32)][E] chunk counts, then T k ranks.
+__device__ void dispatch_small(const RouteParams& p, const int* ids_s, int* cnt_s, int* off_s, int* scratch) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nwarp = nthr >> 5;
+    const int T = p.T, E = p.E, k = p.k, np = T * k, nch = (np + 31) / 32;
+    int* ccnt = scratch;
+    int* rank_s = scratch + nch * E;
+    for (int q = tid; q < nch * E; q += nthr) ccnt[q] = 0;
+    __syncthreads();
+    for (int q = warp; q < nch; q += nwarp) {
+        const int i = q * 32 + lane;
+        const int id = i < np ? ids_s[i] : -1;
+        const unsigned m = __match_any_sync(0xffffffffu, id);
+        const int r = __popc(m & ((1u << lane) - 1u));
+        if (i < np) {
+            rank_s[i] = r;
+            if (id < E && r == 0) ccnt[q * E + id] = __popc(m);  // ids >= E: empty picks (given routing)
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += nthr) {  // exclusive prefix over the chunks, in token order
+        int run = 0;
+        for (int q = 0; q < nch; q++) {
+            const int c = ccnt[q * E + e];
+            ccnt[q * E + e] = run;
+            run += c;
+        }
+        cnt_s[e] = run;
+    }
+    if (tid == 0 && p.has_shared) cnt_s[E] = T;
+    __syncthreads();
+    build_tiles(p, cnt_s, off_s);
+    __syncthreads();
+    for (int i = tid; i < np; i += nthr) {
+        const int id = ids_s[i];
+        if (id >= E) {  // empty pick (given routing)
+            p.slot_row[i] = -1;
+            continue;
+        }
+        const int t = i / k, pos = off_s[id] + ccnt[(i >> 5) * E + id] + rank_s[i];
+        p.row_tok[pos] = t;
+        p.row_slot[pos] = i - t * k;
+        p.slot_row[i] = pos;
+        p.rowexp[pos] = -127;
+    }
+    if (p.has_shared)
+        for (int t = tid; t < T; t += nthr) {
+            const int pos = off_s[E] + t;
+            p.row_tok[pos] = t;
+            p.row_slot[pos] = k;
+            p.rowexp[pos] = -127;
+        }
+}
+
+static size_t dispatch_small_scratch(int T, int E, int k) {
+    const int np = T * k, nch = (np + 31) / 32;
+    return ((size_t)nch * E + np) * 4;
+}
+
 __global__ void __launch_bounds__(RS_THREADS) route_small_kernel(RouteParams p) {
-    __shared__ int ids_s[RS_MAX_T * MAX_K], rank_s[RS_MAX_T * MAX_K];
+    extern __shared__ int rs_scratch[];
+    __shared__ int ids_s[RS_MAX_T * MAX_K];
     __shared__ int cnt_s[MAX_E + 2], off_s[MAX_E + 2];
+    pdl_trigger();  // the expert kernels may take their SM slots now; they wait for this grid
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = p.T, E = p.E, k = p.k, H = p.H;
     for (int t = warp; t < T; t += RS_THREADS / 32) {
@@ -511,34 +627,152 @@ __global__ void __launch_bounds__(RS_THREADS) route_small_kernel(RouteParams p) 
         for (int i = tid * 4; i < T * H; i += RS_THREADS * 4)
             *reinterpret_cast<float4*>(p.out_zero + i) = make_float4(0.f, 0.f, 0.f, 0.f);
     __syncthreads();
-    for (int e = tid; e < E; e += RS_THREADS) {  // ranks in token order
-        int c = 0;
-        for (int i = 0; i < T * k; i++)
-            if (ids_s[i] == e) rank_s[i] = c++;
-        cnt_s[e] = c;
+    dispatch_small(p, ids_s, cnt_s, off_s, rs_scratch);
+}
+
+// ---------------------------------------------------------------------------------------
+// Whole routing of a small batch in fast mode, one launch.  CTA (expert group, token group) =
+// 8 experts (a warp each) x 8 tokens: the token rows are staged in shared memory (the first
+// expert group also writes their fp16 copy and zeroes their output rows) and every warp forms
+// its expert's logits from FFMA partial sums over K folded by shuffles.  The last CTA of each
+// token group to finish (atomic ticket, no waiting) runs top-k for those tokens; the last of
+// those runs dispatch_small for the whole batch and resets the tickets.
+// ---------------------------------------------------------------------------------------
+static constexpr int RF_EXP = 8, RF_TOK = 8, RF_THREADS = 256;
+static constexpr int RF_WCH = 16;  // float4 of the expert row each lane holds at a time
+
+static size_t route_fused_smem(int T, int H, int E, int k) {
+    return std::max(std::max((size_t)RF_TOK * H * 4, (size_t)RF_TOK * E * 4), dispatch_small_scratch(T, E, k));
+}
+
+template <bool DISPATCH>
+__global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RouteParams p) {
+    extern __shared__ __align__(16) float fsm[];
+    __shared__ int ids_s[RS_MAX_T * MAX_K];
+    __shared__ int cnt_s[MAX_E + 2], off_s[MAX_E + 2];
+    __shared__ unsigned ticket_s;
+    pdl_trigger();  // the expert kernels may take their SM slots now; they wait for this grid
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = p.T, H = p.H, E = p.E, k = p.k;
+    const int t0 = blockIdx.y * RF_TOK, nt = min(RF_TOK, T - t0);
+    const int n4 = H / 4;
+
+    // 0. this warp's expert row: its first 16 float4 per lane in flight before anything waits
+    const int e = blockIdx.x * RF_EXP + warp;
+    const float4* wr = reinterpret_cast<const float4*>(p.router_w + (size_t)min(e, E - 1) * H);
+    float4 wv[RF_WCH];
+#pragma unroll
+    for (int u = 0; u < RF_WCH; u++) {
+        const int j = lane + 32 * u;
+        wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (tid == 0 && p.has_shared) cnt_s[E] = T;
-    __syncthreads();
-    if (warp == 0) build_tiles(p, cnt_s, off_s, lane);
-    __syncthreads();
-    for (int i = tid; i < T * k; i += RS_THREADS) {
-        if (ids_s[i] >= E) {  // empty pick (given routing)
-            p.slot_row[i] = -1;
-            continue;
+
+    // 1. the token group's rows -> shared memory (+ fp16 copy and zeroed output rows)
+    float4* xs4 = reinterpret_cast<float4*>(fsm);
+    const float4* xg = reinterpret_cast<const float4*>(p.x + (size_t)t0 * H);
+    for (int q0 = 0; q0 < nt * n4; q0 += 4 * RF_THREADS) {  // four loads in flight per thread
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int q = q0 + u * RF_THREADS + tid;
+            v[u] = q < nt * n4 ? __ldg(xg + q) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        const int t = i / k, pos = off_s[ids_s[i]] + rank_s[i];
-        p.row_tok[pos] = t;
-        p.row_slot[pos] = i - t * k;
-        p.slot_row[i] = pos;
-        p.rowexp[pos] = -127;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int q = q0 + u * RF_THREADS + tid;
+            if (q >= nt * n4) continue;
+            xs4[q] = v[u];
+            if (blockIdx.x == 0) {
+                // fp16 MMA operand; |x| beyond the fp16 range is reported, never silently inf
+                if (!(fabsf(v[u].x) <= 65504.f && fabsf(v[u].y) <= 65504.f && fabsf(v[u].z) <= 65504.f &&
+                      fabsf(v[u].w) <= 65504.f))
+                    atomicOr(p.status, (unsigned)DERR_FP16_RANGE);
+                *reinterpret_cast<uint2*>(p.xb + (size_t)t0 * H + 4 * q) =
+                    make_uint2(pack_f16x2(v[u].x, v[u].y), pack_f16x2(v[u].z, v[u].w));
+                if (p.out_zero)
+                    *reinterpret_cast<float4*>(p.out_zero + (size_t)t0 * H + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
     }
-    if (p.has_shared)
-        for (int t = tid; t < T; t += RS_THREADS) {
-            const int pos = off_s[E] + t;
-            p.row_tok[pos] = t;
-            p.row_slot[pos] = k;
-            p.rowexp[pos] = -127;
+    __syncthreads();
+
+    // 2. logits: lane l sums K elements 4 l + 128 j of its expert for every token of the group
+    if (e < E) {
+        float acc[RF_TOK];
+#pragma unroll
+        for (int t = 0; t < RF_TOK; t++) acc[t] = 0.0f;
+        for (int j0 = 0; j0 < n4; j0 += 32 * RF_WCH) {
+            if (j0 > 0)
+#pragma unroll
+                for (int u = 0; u < RF_WCH; u++) {
+                    const int j = j0 + lane + 32 * u;
+                    wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+            for (int u = 0; u < RF_WCH; u++) {
+                const int j = j0 + lane + 32 * u;
+                if (j < n4)
+#pragma unroll
+                    for (int t = 0; t < RF_TOK; t++)
+                        if (t < nt) {
+                            const float4 a = wv[u], b = xs4[t * n4 + j];
+                            acc[t] = fmaf(a.x, b.x, acc[t]);
+                            acc[t] = fmaf(a.y, b.y, acc[t]);
+                            acc[t] = fmaf(a.z, b.z, acc[t]);
+                            acc[t] = fmaf(a.w, b.w, acc[t]);
+                        }
+            }
         }
+        float mine = 0.0f;
+#pragma unroll
+        for (int t = 0; t < RF_TOK; t++)
+            if (t < nt) {
+                float v = acc[t];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                if (lane == t) mine = v;
+            }
+        if (lane < nt) p.logits[(size_t)(t0 + lane) * E + e] = mine;
+    }
+
+    // 3. the token group's last CTA: top-k of its tokens
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket_s = atomicAdd(p.ticket + 1 + blockIdx.y, 1u);
+    __syncthreads();
+    if (ticket_s != gridDim.x - 1) return;
+    __threadfence();
+    if (tid == 0) p.ticket[1 + blockIdx.y] = 0u;  // every CTA of the group has taken its ticket
+    float* lg = fsm;  // the group's logits, read past L1 (other CTAs wrote them)
+    for (int q = tid; q < nt * E; q += RF_THREADS) lg[q] = __ldcg(p.logits + (size_t)t0 * E + q);
+    __syncthreads();
+    if (warp < nt) {
+        const int t = t0 + warp;
+        const int id = warp_topk(lg + warp * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+        if (lane < k) p.topk_id[(size_t)t * k + lane] = id;
+    }
+
+    // 4. the last token group: dispatch of the whole batch
+    if (!DISPATCH) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) ticket_s = atomicAdd(p.ticket, 1u);
+    __syncthreads();
+    if (ticket_s != gridDim.y - 1) return;
+    __threadfence();
+    for (int i = tid; i < T * k; i += RF_THREADS) ids_s[i] = __ldcg(p.topk_id + i);
+    __syncthreads();
+    if (tid == 0) p.ticket[0] = 0u;  // every token group has taken its ticket
+    dispatch_small(p, ids_s, cnt_s, off_s, reinterpret_cast<int*>(fsm));
+}
+
+static cudaError_t launch_route_fused(const RouteParams& p, bool dispatch, cudaStream_t s) {
+    const size_t sm = route_fused_smem(p.T, p.H, p.E, p.k);
+    auto k = dispatch ? route_fused_small_kernel<true> : route_fused_small_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+    k<<<dim3((p.E + RF_EXP - 1) / RF_EXP, (p.T + RF_TOK - 1) / RF_TOK), RF_THREADS, sm, s>>>(p);
+    return cudaGetLastError();
 }
 
 int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
@@ -553,7 +787,10 @@ static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
         logits_chain_kernel<<<grid, LC_THREADS, LC_SMEM, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
     } else {
         dim3 grid((p.T + LT_TOK - 1) / LT_TOK, (p.E + LT_EXP - 1) / LT_EXP);
-        logits_tiled_kernel<<<grid, LT_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+        if (p.exact)
+            logits_tiled_kernel<true><<<grid, LT_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+        else
+            logits_tiled_kernel<false><<<grid, LT_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
     }
     return cudaGetLastError();
 }
@@ -561,6 +798,7 @@ static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
 __global__ void route_only_kernel(const float* logits, int T, int E, int k, int gate, int* ids, float* w);
 
 cudaError_t launch_router_topk(const RouteParams& p, cudaStream_t s) {
+    if (p.T > 0 && p.T <= RS_MAX_T && !p.exact) return launch_route_fused(p, false, s);
     cudaError_t e = launch_logits(p, s);
     if (e != cudaSuccess || p.T <= 0) return e;
     route_only_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p.logits, p.T, p.E, p.k, p.gate, p.topk_id, p.topk_w);
@@ -569,13 +807,23 @@ cudaError_t launch_router_topk(const RouteParams& p, cudaStream_t s) {
 
 cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
     cudaError_t e;
-    if (!p.given && (e = launch_logits(p, s)) != cudaSuccess) return e;
-    if (p.T <= RS_MAX_T) {
-        route_small_kernel<<<1, RS_THREADS, 0, s>>>(p);  // the whole dispatch in one CTA
+    if (p.T <= RS_MAX_T && !p.given && !p.exact) {
+        // logits, top-k and dispatch in one launch
+        if ((e = launch_route_fused(p, true, s)) != cudaSuccess) return e;
     } else {
-        topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+        if (!p.given && (e = launch_logits(p, s)) != cudaSuccess) return e;
+        if (p.T <= RS_MAX_T) {
+            const size_t sm = dispatch_small_scratch(p.T, p.E, p.k);
+            if (sm > 48 * 1024 &&
+                (e = cudaFuncSetAttribute(route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)) !=
+                    cudaSuccess)
+                return e;
+            route_small_kernel<<<1, RS_THREADS, sm, s>>>(p);  // the whole dispatch in one CTA
+        } else {
+            topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+        }
     }
     if ((e = cudaGetLastError()) != cudaSuccess || !p.xs) return e;
     gather_x_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p);

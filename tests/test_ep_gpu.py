@@ -1,5 +1,5 @@
 """Expert-parallel layer over NCCL on two GPUs: each rank's outputs for its own tokens match the
-oracle's whole layer within the layer tolerance (relative L2 <= 5e-3; max-abs <= 2e-2, or
+oracle's whole layer (routing ids up to reported near-ties) within the layer tolerance (relative L2 <= 5e-3; max-abs <= 2e-2, or
 2e-2 x RMS for outputs whose RMS is >= 50), on the small-batch and the tensor-core local
 paths.  Skipped where fewer than two GPUs are visible."""
 import time
@@ -27,6 +27,7 @@ def _rank(rank, world, uid, tokens):
     import torch
 
     from oracle import oracle as O
+    from routing_check import check_routing
     from rusty_engine_b200.moe import MoELayer
 
     torch.cuda.set_device(rank)
@@ -36,10 +37,10 @@ def _rank(rank, world, uid, tokens):
         x = synth.activations(T, lw.H, seed=10 * rank + T)
         out = layer.forward(torch.from_numpy(x).cuda())
         torch.cuda.synchronize()
-        want, ids, _, _ = O.moe_layer_q_exact(x, lw)
-        got_ids, _ = layer.routing(T)
-        assert (got_ids == ids).all(), f"rank {rank} T {T}: routing differs"
-        _check(out.cpu().numpy(), want, f"rank {rank} T {T}")
+        want, ids, w, _ = O.moe_layer_q_exact(x, lw)
+        got_ids, got_w = layer.routing(T)
+        same = check_routing(got_ids, got_w, ids, w, x, lw.router_w, lw.E, f"rank {rank} T {T}")
+        _check(out.cpu().numpy()[same], want[same], f"rank {rank} T {T}")
     layer.close()
 
 
