@@ -471,17 +471,22 @@ struct DownGeom {
     static constexpr int NB = FIXED + 3 * B_STAGE <= 232448 - 4096 ? 3 : 2;
     static constexpr int A_OFF = NB * B_STAGE, RAW_OFF = A_OFF + NA * A_STAGE, Y_OFF = RAW_OFF + RST * RS::BYTES;
     static constexpr int SMEM = Y_OFF + 2 * Y_STAGE + 1024;
-    static constexpr int THREADS = 384;
+    // warps 0-3: producer / MMA / h tiles / idle; CW converter warps (two per weight row, half
+    // a stage each: the decode, not the MMA, is the long pole of a K = 64 stage); 4 epilogue warps
+    static constexpr int CW = 8;
+    static constexpr int THREADS = (4 + CW + 4) * 32;
     static_assert(SMEM <= 232448 - 4096, "shared memory budget");
     static_assert(A_OFF % 1024 == 0 && RAW_OFF % 128 == 0 && Y_OFF % 16 == 0, "alignment");
 };
 
 template <int TYPE>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     tc_down_kernel(const __grid_constant__ GroupedParams p, const __grid_constant__ TcMaps maps) {
     using D = DownGeom<TYPE>;
     using RS = RawStage<TYPE, TC_M>;
     constexpr int RK = Raw<TYPE>::RK, PITCH = Raw<TYPE>::PITCH, SUBS = RK / TC_KS, NA = D::NA, NB = D::NB, RST = D::RST;
+    constexpr int CW = D::CW, EPI0 = 4 + CW;  // converter warps 4 .. EPI0 - 1, epilogue warps EPI0 ..
+    static_assert(D::THREADS == 512 && (CW == 4 || CW == 8), "warp roles");
     extern __shared__ uint8_t dsmem[];
     __shared__ __align__(8) uint64_t bar_raw_full[RST], bar_raw_empty[RST];
     __shared__ __align__(8) uint64_t bar_a_full[NA], bar_a_empty[NA], bar_b_full[NB], bar_b_empty[NB];
@@ -504,10 +509,10 @@ __global__ void __launch_bounds__(384, 1)
     if (tid == 0) {
         for (int i = 0; i < RST; i++) {
             mbar_init(smem_u32(&bar_raw_full[i]), 1);
-            mbar_init(smem_u32(&bar_raw_empty[i]), 4);
+            mbar_init(smem_u32(&bar_raw_empty[i]), CW);
         }
         for (int i = 0; i < NA; i++) {
-            mbar_init(smem_u32(&bar_a_full[i]), 4);
+            mbar_init(smem_u32(&bar_a_full[i]), CW);
             mbar_init(smem_u32(&bar_a_empty[i]), 1);
         }
         for (int i = 0; i < NB; i++) {
@@ -621,9 +626,9 @@ __global__ void __launch_bounds__(384, 1)
             }
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {
-        // ---------------- converters: one weight row per thread ----------------
-        const int q = warp & 3, r = q * 32 + lane;
+    } else if (warp >= 4 && warp < EPI0) {
+        // ---------------- converters: one weight row per thread (per half stage when CW = 8) --------
+        const int cq = warp - 4, r = (cq & 3) * 32 + lane, part = cq >> 2;
         int gk = 0, gj = 0;
         for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
             bool ok = true;
@@ -633,18 +638,25 @@ __global__ void __launch_bounds__(384, 1)
                 if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[rs]), (gj / RST) & 1)) { fail(); ok = false; break; }
                 if (gk >= NA && !mbar_wait(smem_u32(&bar_a_empty[s]), ((gk / NA) + 1) & 1)) { fail(); ok = false; break; }
                 const uint8_t* mat = raw_g + (size_t)rs * RS::BYTES;
-                uint32_t v[32];
-                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 0, v);
-                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 1, v + 16);
+                constexpr int NV = CW == 8 ? 16 : 32, C0 = 0;
+                uint32_t v[NV];
+                if (CW == 8) {
+                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, part, v);
+                } else {
+                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 0, v);
+                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 1,
+                                        v + (NV - 16));
+                }
                 if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[rs]));
                     gj++;
                 }
                 uint8_t* at = a_g + (size_t)s * D::A_STAGE + r * 128;
+                const int c0 = C0 + (CW == 8 ? 4 * part : 0);
 #pragma unroll
-                for (int c = 0; c < 8; c++)
-                    *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
+                for (int c = 0; c < NV / 4; c++)
+                    *reinterpret_cast<uint4*>(at + (((c0 + c) ^ (r & 7)) << 4)) =
                         make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -652,7 +664,7 @@ __global__ void __launch_bounds__(384, 1)
             }
             if (!ok) break;
         }
-    } else if (warp >= 8) {
+    } else if (warp >= EPI0) {
         // ---------------- epilogue ----------------
         const int q = warp & 3;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
@@ -661,7 +673,7 @@ __global__ void __launch_bounds__(384, 1)
             // the four warps share named barrier 2, so they stop together: one thread samples the
             // abort flag between two barriers (the first also ends every read of the previous
             // item's staging chunks)
-            if (warp == 8 && lane == 0) s_epi_stop = s_abort;
+            if (warp == EPI0 && lane == 0) s_epi_stop = s_abort;
             asm volatile("bar.sync 2, 128;\n" ::: "memory");
             const bool stop = s_epi_stop;
             asm volatile("bar.sync 2, 128;\n" ::: "memory");

@@ -21,6 +21,9 @@ struct RouteParams {
     int* rowexp;            // [rows] SwiGLU row exponents, set to -127 by the dispatch
     __half* xs;             // optional [rows, H]: x rows in expert-sorted order (tensor-core path)
     float* logits;          // [T, E] router logits
+    float* logits_part;     // optional [8, T, E]: K-split partial logits of the fast large-batch
+                            // router (the top-k kernel sums them into logits); null (always in
+                            // exact mode): the logits kernel writes logits directly
     float* out_zero;        // optional: rows of `out` to zero (atomic combine)
     int* topk_id;           // [T, k]
     float* topk_w;          // [T, k]

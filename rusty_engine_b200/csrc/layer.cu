@@ -422,6 +422,7 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.hexp = (int8_t*)A(rows * (I / GV_EBLK));
     w.rowexp = (int*)A(rows * 4);
     w.logits = (float*)A((size_t)cap * E * 4);
+    w.logits_part = (float*)A((size_t)8 * cap * E * 4);
     if (need_y || L->ws_had_y) w.y = (float*)A(rows * H * 4);
     if (!ok) return fail(RMOE_ERR_OOM, "workspace cudaMalloc failed for %u tokens", cap);
     if (!make_rows_map(w.h, rows, I, L->hmap) || !make_rows_map(w.xs, rows, H, L->xsmap))
@@ -455,6 +456,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.xb = w.xb;
     rp.rowexp = w.rowexp;
     rp.logits = given ? nullptr : w.logits;
+    rp.logits_part = (given || (flags & RMOE_FLAG_EXACT_ROUTER)) ? nullptr : w.logits_part;
     rp.out_zero = det ? nullptr : out;
     rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;
     rp.ticket = w.ticket; rp.expert_off = w.expert_off; rp.row_tok = w.row_tok; rp.row_slot = w.row_slot;

@@ -51,6 +51,7 @@ struct Workspace {
     __half* xs = nullptr;   // expert-sorted x (tensor-core path)
     float* y = nullptr;
     float* logits = nullptr;
+    float* logits_part = nullptr;  // K-split partial router logits (large batches, fast router)
 };
 
 struct EpState;  // expert-parallel state (ep.cu)

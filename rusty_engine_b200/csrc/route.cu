@@ -17,9 +17,11 @@
 // sigmoid renormalisation (src/moe.rs:97-117).
 //
 // Dispatch: the top-k kernel counts each CTA's picks per expert and the in-CTA rank of every
-// pick in token order; the last CTA to finish (atomic ticket, no spin-wait) scans the counts
-// into per-(CTA, expert) offsets and writes the tile list; a scatter kernel then places every
-// (token, slot) at offset + rank, so rows are in ascending token order inside each expert.
+// pick in token order; a scan kernel (a CTA per expert) turns the counts into per-(CTA, expert)
+// offsets, and its last CTA to finish (atomic ticket, no spin-wait) writes the expert offsets
+// and the tile list; a scatter kernel then places every (token, slot) at offset + rank, so rows
+// are in ascending token order inside each expert.  Batches of at most 64 tokens take a single
+// launch for all of it (route_fused_small_kernel).
 #include <algorithm>
 
 #include "common.cuh"
@@ -211,6 +213,149 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
 }
 
 // ---------------------------------------------------------------------------------------
+// logits, large batches, fast mode: an FFMA register-tiled product, CTA = 128 tokens x 128
+// experts x one of LG_S K-splits (the batch's 4096 tokens give 32 token tiles, so splitting K
+// fills the GPU), 256 threads with 8 x 8 outputs each (token rows ty*4 + {0..3} and 64 + ty*4 +
+// {0..3}, experts tx*4 + {0..3} and 64 + tx*4 + {0..3}).  k-tiles of 16 are staged transposed in
+// shared memory, the next tile's loads held in registers while the current one is multiplied.
+// Each split writes its partial sums; the top-k kernel adds the splits in order.  The first
+// expert tile also writes the fp16 copy of its tokens' K range.
+// ---------------------------------------------------------------------------------------
+static constexpr int LG_M = 128, LG_N = 128, LG_K = 16, LG_S = 8, LG_THREADS = 256, LG_LD = LG_M + 4;
+
+__global__ void __launch_bounds__(LG_THREADS, 2) logits_ffma_kernel(const float* __restrict__ x,
+                                                                 const float* __restrict__ w, int T, int H, int E,
+                                                                 float* __restrict__ part, __half* __restrict__ xb,
+                                                                 unsigned* status) {
+    __shared__ __align__(16) float xs[2][LG_K][LG_LD];
+    __shared__ __align__(16) float wsm[2][LG_K][LG_LD];
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    const int t0 = blockIdx.x * LG_M, e0 = blockIdx.y * LG_N, sp = blockIdx.z;
+    const int klen = H / LG_S, kbeg = sp * klen;
+    // loader: rows lr and lr + 64 of the x and w tiles, k-quad lq of the 16-wide k-tile
+    const int lr = tid >> 2, lq = tid & 3;
+    const float* xr0 = x + (size_t)min(t0 + lr, T - 1) * H + kbeg + 4 * lq;
+    const float* xr1 = x + (size_t)min(t0 + lr + 64, T - 1) * H + kbeg + 4 * lq;
+    const float* wr0 = w + (size_t)min(e0 + lr, E - 1) * H + kbeg + 4 * lq;
+    const float* wr1 = w + (size_t)min(e0 + lr + 64, E - 1) * H + kbeg + 4 * lq;
+    const bool write_xb = xb && blockIdx.y == 0;
+    float4 ra[4];
+    auto load = [&](int kt) {
+        const int ko = kt * LG_K;
+        ra[0] = __ldg(reinterpret_cast<const float4*>(xr0 + ko));
+        ra[1] = __ldg(reinterpret_cast<const float4*>(xr1 + ko));
+        ra[2] = __ldg(reinterpret_cast<const float4*>(wr0 + ko));
+        ra[3] = __ldg(reinterpret_cast<const float4*>(wr1 + ko));
+    };
+    auto store = [&](int buf, int kt) {
+        const float* a0 = &ra[0].x;
+        const float* a1 = &ra[1].x;
+        const float* b0 = &ra[2].x;
+        const float* b1 = &ra[3].x;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            xs[buf][4 * lq + i][lr] = a0[i];
+            xs[buf][4 * lq + i][lr + 64] = a1[i];
+            wsm[buf][4 * lq + i][lr] = b0[i];
+            wsm[buf][4 * lq + i][lr + 64] = b1[i];
+        }
+        if (write_xb) {  // fp16 MMA operand; |x| beyond the fp16 range is reported, never silently inf
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const float4 v = ra[h];
+                const int t = t0 + lr + 64 * h;
+                if (t < T) {
+                    if (!(fabsf(v.x) <= 65504.f && fabsf(v.y) <= 65504.f && fabsf(v.z) <= 65504.f &&
+                          fabsf(v.w) <= 65504.f))
+                        atomicOr(status, (unsigned)DERR_FP16_RANGE);
+                    *reinterpret_cast<uint2*>(xb + (size_t)t * H + kbeg + kt * LG_K + 4 * lq) =
+                        make_uint2(pack_f16x2(v.x, v.y), pack_f16x2(v.z, v.w));
+                }
+            }
+        }
+    };
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+    const int nk = klen / LG_K;
+    load(0);
+    store(0, 0);
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) load(kt + 1);
+#pragma unroll
+        for (int k = 0; k < LG_K; k++) {
+            const float4 a0 = *reinterpret_cast<const float4*>(&xs[buf][k][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&xs[buf][k][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&wsm[buf][k][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&wsm[buf][k][64 + tx * 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        if (kt + 1 < nk) store(buf ^ 1, kt + 1);
+        __syncthreads();
+    }
+    float* out = part + (size_t)sp * T * E;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int t = t0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+        if (t >= T) continue;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int e = e0 + h * 64 + tx * 4;
+            float* o = out + (size_t)t * E + e;
+            if (e + 3 < E && (E & 3) == 0) {
+                *reinterpret_cast<float4*>(o) = make_float4(acc[i][4 * h], acc[i][4 * h + 1], acc[i][4 * h + 2], acc[i][4 * h + 3]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    if (e + j < E) o[j] = acc[i][4 * h + j];
+            }
+        }
+    }
+}
+
+// The router logits of token t into row[0 .. E) (shared memory), one warp: the logits as
+// written, or the LG_S split partial sums added in split order (written back as the logits).
+__device__ __forceinline__ void logit_row(const RouteParams& p, int t, int lane, float* row) {
+    const int E = p.E;
+    if (p.logits_part) {
+        const size_t stride = (size_t)p.T * E;
+        for (int e0 = 0; e0 < E; e0 += 128) {  // all loads of four columns in flight, then the sums
+            float v[4][LG_S];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int e = e0 + 32 * u + lane;
+#pragma unroll
+                for (int sp = 0; sp < LG_S; sp++)
+                    v[u][sp] = e < E ? __ldcg(p.logits_part + sp * stride + (size_t)t * E + e) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int e = e0 + 32 * u + lane;
+                float sum = v[u][0];
+#pragma unroll
+                for (int sp = 1; sp < LG_S; sp++) sum = __fadd_rn(sum, v[u][sp]);
+                if (e < E) {
+                    row[e] = sum;
+                    p.logits[(size_t)t * E + e] = sum;
+                }
+            }
+        }
+    } else {
+        for (int e = lane; e < E; e += 32) row[e] = p.logits[(size_t)t * E + e];
+    }
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------------------
 // top-k of one token's E logits (one warp)
 // ---------------------------------------------------------------------------------------
 // Routing weights of one token's k picks (one warp; lane j < k holds pick j's score and writes
@@ -298,8 +443,8 @@ __device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, floa
 // top-k + counts (+ last-CTA scan and tile list)
 // ---------------------------------------------------------------------------------------
 // cta_cnt is expert-major, [E][ncp] with ncp = ncta rounded up to 16 (zero padding): CTA b's
-// pick count for expert e at e * ncp + b; the last CTA turns every expert's run of counts into
-// exclusive prefixes (rows before CTA b's first row of that expert), so a pick's row =
+// pick count for expert e at e * ncp + b; scan_counts_kernel turns every expert's run of counts
+// into exclusive prefixes (rows before CTA b's first row of that expert), so a pick's row =
 // expert_off[e] + cta_cnt[e * ncp + b] + local rank.
 __device__ __forceinline__ int warp_incl_scan(int v, int lane) {
 #pragma unroll
@@ -373,8 +518,7 @@ __device__ void build_tiles(const RouteParams& p, const int* cnt_s, int* off_s) 
 
 __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     __shared__ int ids_s[TK_TOK * MAX_K];
-    __shared__ int cnt_s[MAX_E + 2];
-    __shared__ unsigned int ticket_s;
+    __shared__ float row_s[TK_THREADS / 32][MAX_E];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = blockIdx.x * TK_TOK;
     const int E = p.E, H = p.H, k = p.k;
@@ -387,11 +531,13 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
             if (lane < k) ids_s[tl * k + lane] = p.topk_id[(size_t)t * k + lane];
             continue;
         }
-        int id = warp_topk(p.logits + (size_t)t * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+        logit_row(p, t, lane, row_s[warp]);
+        int id = warp_topk(row_s[warp], E, k, p.gate, lane, p.topk_w + (size_t)t * k);
         if (lane < k) {
             p.topk_id[(size_t)t * k + lane] = id;
             ids_s[tl * k + lane] = id;
         }
+        __syncwarp();  // the row is read before the warp's next token overwrites it
     }
     // zero the output rows this CTA owns when the combine accumulates with atomics (the x
     // gather kernel does it instead when it runs)
@@ -412,63 +558,44 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
         if (blockIdx.x == 0)
             for (int b = ncta; b < ncp; b++) p.cta_cnt[(size_t)e * ncp + b] = 0;
     }
+}
 
-    // ---- last CTA: per-(expert, CTA) prefixes, expert offsets, tile list ----
+// Per-expert scan of the top-k CTAs' counts, one CTA per expert: cta_cnt[e][b] becomes the rows of
+// expert e that come before CTA b's (token order), the expert's total goes to expert_off[e];
+// the last CTA to finish (atomic ticket, no waiting) turns the totals into expert offsets and
+// the tile list.
+static constexpr int SC_THREADS = 256;
+__global__ void __launch_bounds__(SC_THREADS) scan_counts_kernel(RouteParams p, int ncta) {
+    __shared__ int warp_s[SC_THREADS / 32];
+    __shared__ int cnt_s[MAX_E + 2];
+    __shared__ unsigned ticket_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, e = blockIdx.x;
+    const int ncp = route_cnt_stride(ncta);
+    int* row = p.cta_cnt + (size_t)e * ncp;
+    int run = 0;
+    for (int b0 = 0; b0 < ncta; b0 += SC_THREADS) {
+        const int b = b0 + tid;
+        const int c = b < ncta ? __ldcg(row + b) : 0;
+        const int incl = warp_incl_scan(c, lane);
+        if (lane == 31) warp_s[warp] = incl;
+        __syncthreads();
+        int before = run;
+        for (int w = 0; w < warp; w++) before += warp_s[w];
+        if (b < ncta) row[b] = before + incl - c;
+        int total = 0;
+        for (int w = 0; w < SC_THREADS / 32; w++) total += warp_s[w];
+        run += total;
+        __syncthreads();
+    }
+    if (tid == 0) p.expert_off[e] = run;
     __threadfence();
     __syncthreads();
     if (tid == 0) ticket_s = atomicAdd(p.ticket, 1u);
     __syncthreads();
     if (ticket_s != gridDim.x - 1) return;
     __threadfence();
-
-    // TPE threads per expert (a power of two), each owning a run of consecutive CTAs (a multiple
-    // of 16): sum the run with 16-B loads (64 counts in flight), scan the runs' sums across the
-    // group, then rewrite the run as exclusive prefixes
-    int E2 = 1;
-    while (E2 < E) E2 <<= 1;
-    const int TPE = max(1, min(32, TK_THREADS / E2));
-    const int seg = (ncp / 16 + TPE - 1) / TPE * 16;
-    for (int e0 = 0; e0 < E; e0 += TK_THREADS / TPE) {
-        const int e = e0 + tid / TPE, part = tid % TPE;
-        const int b_lo = min(ncp, part * seg), b_hi = min(ncp, b_lo + seg);
-        int4* row = reinterpret_cast<int4*>(p.cta_cnt + (size_t)min(e, E - 1) * ncp);
-        int sum = 0;
-        int4 first[16];
-        for (int b = b_lo; b < b_hi; b += 64) {
-            int4 v[16];
-#pragma unroll
-            for (int u = 0; u < 16; u++) v[u] = (e < E && b + 4 * u < b_hi) ? __ldcg(row + b / 4 + u) : make_int4(0, 0, 0, 0);
-#pragma unroll
-            for (int u = 0; u < 16; u++) {
-                sum += v[u].x + v[u].y + v[u].z + v[u].w;
-                if (b == b_lo) first[u] = v[u];
-            }
-        }
-        int incl = sum;
-        for (int off = 1; off < TPE; off <<= 1) {
-            const int o = __shfl_up_sync(0xffffffffu, incl, off, TPE);
-            if (part >= off) incl += o;
-        }
-        if (e < E) {
-            int run = incl - sum;
-            for (int b = b_lo; b < b_hi; b += 64) {
-                int4 v[16];
-#pragma unroll
-                for (int u = 0; u < 16; u++)
-                    v[u] = (b == b_lo) ? first[u] : (b + 4 * u < b_hi) ? __ldcg(row + b / 4 + u) : make_int4(0, 0, 0, 0);
-#pragma unroll
-                for (int u = 0; u < 16; u++) {
-                    if (b + 4 * u < b_hi) {
-                        const int4 c = v[u];
-                        row[b / 4 + u] = make_int4(run, run + c.x, run + c.x + c.y, run + c.x + c.y + c.z);
-                        run += c.x + c.y + c.z + c.w;
-                    }
-                }
-            }
-            if (part == TPE - 1) cnt_s[e] = incl;
-        }
-    }
-    if (tid == 0 && p.has_shared) cnt_s[E] = p.T;
+    for (int i = tid; i < p.E; i += SC_THREADS) cnt_s[i] = __ldcg(p.expert_off + i);
+    if (tid == 0 && p.has_shared) cnt_s[p.E] = p.T;
     __syncthreads();
     build_tiles(p, cnt_s, nullptr);
     if (tid == 0) *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
@@ -645,7 +772,7 @@ static size_t route_fused_smem(int T, int H, int E, int k) {
     return std::max(std::max((size_t)RF_TOK * H * 4, (size_t)RF_TOK * E * 4), dispatch_small_scratch(T, E, k));
 }
 
-template <bool DISPATCH>
+template <int MODE>  // 0: logits (and the fp16 copy) only; 1: + top-k; 2: + the dispatch
 __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RouteParams p) {
     extern __shared__ __align__(16) float fsm[];
     __shared__ int ids_s[RS_MAX_T * MAX_K];
@@ -689,7 +816,7 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
                     atomicOr(p.status, (unsigned)DERR_FP16_RANGE);
                 *reinterpret_cast<uint2*>(p.xb + (size_t)t0 * H + 4 * q) =
                     make_uint2(pack_f16x2(v[u].x, v[u].y), pack_f16x2(v[u].z, v[u].w));
-                if (p.out_zero)
+                if (MODE == 2 && p.out_zero)
                     *reinterpret_cast<float4*>(p.out_zero + (size_t)t0 * H + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
@@ -736,6 +863,7 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     }
 
     // 3. the token group's last CTA: top-k of its tokens
+    if (MODE == 0) return;
     __threadfence();
     __syncthreads();
     if (tid == 0) ticket_s = atomicAdd(p.ticket + 1 + blockIdx.y, 1u);
@@ -753,7 +881,7 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     }
 
     // 4. the last token group: dispatch of the whole batch
-    if (!DISPATCH) return;
+    if (MODE == 1) return;
     __threadfence();
     __syncthreads();
     if (tid == 0) ticket_s = atomicAdd(p.ticket, 1u);
@@ -766,9 +894,9 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     dispatch_small(p, ids_s, cnt_s, off_s, reinterpret_cast<int*>(fsm));
 }
 
-static cudaError_t launch_route_fused(const RouteParams& p, bool dispatch, cudaStream_t s) {
-    const size_t sm = route_fused_smem(p.T, p.H, p.E, p.k);
-    auto k = dispatch ? route_fused_small_kernel<true> : route_fused_small_kernel<false>;
+static cudaError_t launch_route_fused(const RouteParams& p, int mode, cudaStream_t s) {
+    const size_t sm = mode == 0 ? (size_t)RF_TOK * p.H * 4 : route_fused_smem(p.T, p.H, p.E, p.k);
+    auto k = mode == 0 ? route_fused_small_kernel<0> : mode == 1 ? route_fused_small_kernel<1> : route_fused_small_kernel<2>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) return e;
     k<<<dim3((p.E + RF_EXP - 1) / RF_EXP, (p.T + RF_TOK - 1) / RF_TOK), RF_THREADS, sm, s>>>(p);
@@ -777,14 +905,24 @@ static cudaError_t launch_route_fused(const RouteParams& p, bool dispatch, cudaS
 
 int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
 
-// Router logits (and the fp16 copy of x): chained per-logit kernel for small batches,
-// register-tiled kernel otherwise.
+// Batches from which the fast router's logits come from the K-split FFMA product (with fewer
+// tokens its CTAs could not fill the GPU; the warp-per-expert kernel takes them).
+static constexpr int LG_MIN_T = 1024;
+static bool use_split(const RouteParams& p) { return !p.exact && p.logits_part && p.T >= LG_MIN_T; }
+
+// Router logits (and the fp16 copy of x).  Exact: the chained per-logit kernel for small
+// batches, the register-tiled one otherwise; fast: the warp-per-expert kernel, or the K-split
+// product for large batches.
 static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
+    if (!p.exact && !use_split(p)) return launch_route_fused(p, 0, s);
     if (p.T <= RS_MAX_T) {
         cudaError_t e = cudaFuncSetAttribute(logits_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LC_SMEM);
         if (e != cudaSuccess) return e;
         dim3 grid((p.E + LC_EB - 1) / LC_EB, (p.T + LC_TB - 1) / LC_TB);
         logits_chain_kernel<<<grid, LC_THREADS, LC_SMEM, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
+    } else if (use_split(p)) {
+        dim3 grid((p.T + LG_M - 1) / LG_M, (p.E + LG_N - 1) / LG_N, LG_S);
+        logits_ffma_kernel<<<grid, LG_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits_part, p.xb, p.status);
     } else {
         dim3 grid((p.T + LT_TOK - 1) / LT_TOK, (p.E + LT_EXP - 1) / LT_EXP);
         if (p.exact)
@@ -797,19 +935,23 @@ static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
 
 __global__ void route_only_kernel(const float* logits, int T, int E, int k, int gate, int* ids, float* w);
 
-cudaError_t launch_router_topk(const RouteParams& p, cudaStream_t s) {
-    if (p.T > 0 && p.T <= RS_MAX_T && !p.exact) return launch_route_fused(p, false, s);
+cudaError_t launch_router_topk(const RouteParams& p0, cudaStream_t s) {
+    if (p0.T > 0 && p0.T <= RS_MAX_T && !p0.exact) return launch_route_fused(p0, 1, s);
+    RouteParams p = p0;
+    p.logits_part = nullptr;  // route_only_kernel reads finished logits
     cudaError_t e = launch_logits(p, s);
     if (e != cudaSuccess || p.T <= 0) return e;
     route_only_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p.logits, p.T, p.E, p.k, p.gate, p.topk_id, p.topk_w);
     return cudaGetLastError();
 }
 
-cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
+cudaError_t launch_route_dispatch(const RouteParams& p0, cudaStream_t s) {
     cudaError_t e;
+    RouteParams p = p0;
+    if (!use_split(p)) p.logits_part = nullptr;  // the top-k kernel sums partials only after the K-split product
     if (p.T <= RS_MAX_T && !p.given && !p.exact) {
         // logits, top-k and dispatch in one launch
-        if ((e = launch_route_fused(p, true, s)) != cudaSuccess) return e;
+        if ((e = launch_route_fused(p, 2, s)) != cudaSuccess) return e;
     } else {
         if (!p.given && (e = launch_logits(p, s)) != cudaSuccess) return e;
         if (p.T <= RS_MAX_T) {
@@ -821,6 +963,8 @@ cudaError_t launch_route_dispatch(const RouteParams& p, cudaStream_t s) {
             route_small_kernel<<<1, RS_THREADS, sm, s>>>(p);  // the whole dispatch in one CTA
         } else {
             topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+            scan_counts_kernel<<<p.E, SC_THREADS, 0, s>>>(p, route_grid(p.T));
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
             scatter_rows_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
         }

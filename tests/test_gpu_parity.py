@@ -5,8 +5,9 @@ Contract:
 * with RMOE_FLAG_EXACT_ROUTER, router logits and top-k expert ids are bit-exact with
   moe::matvec / top_k (the GPU computes the same sequential f32 sums); routing weights within
   2 ulp-scale (expf differs between CUDA and glibc by <= 2 ulp);
-* by default (FFMA logits), ids are bit-exact except near-ties (float64 logits within 1e-6),
-  which are reported (routing_check.py);
+* by default (FFMA logits), ids are bit-exact except near-ties, which are reported with their
+  float64 logit gaps (routing_check.py: under 1e-6, or within the reference's own f32
+  summation error);
 * layer outputs: max-abs <= 2e-2 and relative L2 <= 5e-3 (bf16 MMA on dequantised values).
   Where the output scale makes an absolute 2e-2 meaningless (Qwen-shaped Q4_K layers have
   outputs ~1e5), max-abs is checked relative to the output RMS instead: <= 2e-2 * RMS.
@@ -140,7 +141,8 @@ def test_c1_layer_parity(torch_cuda):
     assert np.allclose(got["w"], w, rtol=2e-6, atol=1e-7)
     assert_layer_close(got["out"], out, "c1 exact router")
     got = run_layer(torch_cuda, lw, x)
-    np.testing.assert_allclose(got["logits"], logits, rtol=0, atol=2e-6)
+    # FFMA sums vs the sequential f32 sums: both within f32 summation error of the exact value
+    np.testing.assert_allclose(got["logits"], logits, rtol=0, atol=5e-6)
     check_layer(got, lw, x, out, ids, w, "c1")
 
 
