@@ -36,6 +36,7 @@ struct EpState {
     uint32_t capT = 0, lastT = 0;
     __half* xb = nullptr;
     float* logits = nullptr;
+    float* logits_part = nullptr;  // K-split partial router logits (large batches)
     int* topk_id = nullptr;
     float* topk_w = nullptr;
     float* xin = nullptr;    // host-IO staging
@@ -179,6 +180,7 @@ static rmoe_status ep_token_buffers(rmoe_layer* L, uint32_t T) {
     P.xin = (float*)A((size_t)cap * L->H * 4);
     P.xout = (float*)A((size_t)cap * L->H * 4);
     P.logits = (float*)A((size_t)cap * L->E_router * 4);
+    P.logits_part = (float*)A((size_t)8 * cap * L->E_router * 4);
     P.topk_id = (int*)A((size_t)cap * L->k * 4);
     P.topk_w = (float*)A((size_t)cap * L->k * 4);
     P.pos = (int*)A((size_t)cap * G * 4);
@@ -220,6 +222,7 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     rp.x = x; rp.router_w = L->router_w; rp.T = (int)T; rp.H = H; rp.E = (int)L->E_router; rp.k = k;
     rp.exact = (flags & RMOE_FLAG_EXACT_ROUTER) ? 1 : 0;
     rp.gate = (int)L->gate_kind; rp.xb = P.xb; rp.logits = P.logits; rp.topk_id = P.topk_id; rp.topk_w = P.topk_w;
+    rp.logits_part = rp.exact ? nullptr : P.logits_part;
     rp.status = P.status; rp.ticket = P.ticket;
     if (T && (e = launch_router_topk(rp, s)) != cudaSuccess) return cuda_fail(e, "ep router launch");
     // 2. plan

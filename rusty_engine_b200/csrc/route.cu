@@ -911,10 +911,11 @@ static constexpr int LG_MIN_T = 1024;
 static bool use_split(const RouteParams& p) { return !p.exact && p.logits_part && p.T >= LG_MIN_T; }
 
 // Router logits (and the fp16 copy of x).  Exact: the chained per-logit kernel for small
-// batches, the register-tiled one otherwise; fast: the warp-per-expert kernel, or the K-split
-// product for large batches.
+// batches, the register-tiled one otherwise; fast: the warp-per-expert kernel below LG_MIN_T
+// tokens, the K-split product above (the register-tiled one with FFMA when there is no
+// partial-sum buffer).
 static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
-    if (!p.exact && !use_split(p)) return launch_route_fused(p, 0, s);
+    if (!p.exact && p.T < LG_MIN_T) return launch_route_fused(p, 0, s);
     if (p.T <= RS_MAX_T) {
         cudaError_t e = cudaFuncSetAttribute(logits_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LC_SMEM);
         if (e != cudaSuccess) return e;
@@ -935,13 +936,24 @@ static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
 
 __global__ void route_only_kernel(const float* logits, int T, int E, int k, int gate, int* ids, float* w);
 
+// Top-k of every token's logits (one warp per token), summing the K-split partials first when
+// the split product made them.
+__global__ void __launch_bounds__(256) route_rows_kernel(RouteParams p) {
+    __shared__ float row_s[8][MAX_E];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = blockIdx.x * 8 + warp;
+    if (t >= p.T) return;
+    logit_row(p, t, lane, row_s[warp]);
+    const int id = warp_topk(row_s[warp], p.E, p.k, p.gate, lane, p.topk_w + (size_t)t * p.k);
+    if (lane < p.k) p.topk_id[(size_t)t * p.k + lane] = id;
+}
+
 cudaError_t launch_router_topk(const RouteParams& p0, cudaStream_t s) {
     if (p0.T > 0 && p0.T <= RS_MAX_T && !p0.exact) return launch_route_fused(p0, 1, s);
     RouteParams p = p0;
-    p.logits_part = nullptr;  // route_only_kernel reads finished logits
+    if (!use_split(p)) p.logits_part = nullptr;
     cudaError_t e = launch_logits(p, s);
     if (e != cudaSuccess || p.T <= 0) return e;
-    route_only_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p.logits, p.T, p.E, p.k, p.gate, p.topk_id, p.topk_w);
+    route_rows_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p);
     return cudaGetLastError();
 }
 
