@@ -465,12 +465,13 @@ struct DownGeom {
     using RS = RawStage<TYPE, TC_M>;
     static constexpr int NA = 2, RST = 2;  // weight-tile and raw stages
     static constexpr int B_STAGE = TC_BN * 128, A_STAGE = TC_M * 128;
-    static constexpr int YLD = TC_M + 4, YCH = 32, Y_STAGE = YCH * YLD * 4;
-    static constexpr int FIXED = NA * A_STAGE + RST * RS::BYTES + 2 * Y_STAGE + 1024;
+    // the epilogue's transpose buffers (YB of them): 32-token chunks
+    static constexpr int YLD = TC_M + 4, YCH = 32, Y_STAGE = YCH * YLD * 4, YB = 2;
+    static constexpr int FIXED = NA * A_STAGE + RST * RS::BYTES + YB * Y_STAGE + 1024;
     // h-tile stages: three where they fit (the 4-6-bit types), else two
     static constexpr int NB = FIXED + 3 * B_STAGE <= 232448 - 4096 ? 3 : 2;
     static constexpr int A_OFF = NB * B_STAGE, RAW_OFF = A_OFF + NA * A_STAGE, Y_OFF = RAW_OFF + RST * RS::BYTES;
-    static constexpr int SMEM = Y_OFF + 2 * Y_STAGE + 1024;
+    static constexpr int SMEM = Y_OFF + YB * Y_STAGE + 1024;
     // warps 0-3: producer / MMA / h tiles / idle; CW converter warps (two per weight row, half
     // a stage each: the decode, not the MMA, is the long pole of a K = 64 stage); 4 epilogue warps
     static constexpr int CW = 8;
@@ -706,7 +707,8 @@ __global__ void __launch_bounds__(512, 1)
                 uint32_t a[32];
                 tmem_ld32(tlane + (uint32_t)(acc * TC_BN + c * 32), a);
                 tmem_ld_wait();
-                float* ys = ys_g + (c & 1) * (D::YCH * D::YLD);
+                float* ys = ys_g + (D::YB == 2 ? (c & 1) * (D::YCH * D::YLD) : 0);
+                if (D::YB == 1 && c > 0) asm volatile("bar.sync 2, 128;\n" ::: "memory");  // chunk c - 1 read
 #pragma unroll
                 for (int i = 0; i < 32; i++) ys[i * D::YLD + q * 32 + lane] = __uint_as_float(a[i]);
                 asm volatile("bar.sync 2, 128;\n" ::: "memory");
