@@ -42,25 +42,29 @@ CONFIGS = {
 
 
 def kernels_per_forward(lw, T, world=1, rows_local=None):
-    """Kernels of this library one forward launches.  Whole layer: router logits, dispatch (one
-    kernel up to 64 tokens, else top-k scan + row scatter), gate/up (+SwiGLU), down (+atomic
+    """Kernels of this library one forward launches.  Whole layer: routing (one kernel up to 64
+    tokens; else logits, top-k, count scan, row scatter), gate/up (+SwiGLU), down (+atomic
     weighted combine); the tensor-core path (T*k >= 32*E) adds the expert-sorted x gather and
-    the h rescale.  Expert-parallel: logits + top-k, plan, pack, unpack, the local layer over
-    the received rows (given routing: no logits) and the combine."""
-    def local(rows, E):
-        tc = rows * lw.k >= 32 * E
-        return (1 if rows <= 64 else 2) + (2 if tc else 0) + 2
+    the h rescale.  Expert-parallel: logits + top-k (one kernel up to 64 tokens), plan, pack,
+    unpack, the local layer over the received rows (given routing: top-k-free dispatch, one
+    kernel up to 64 rows, else count, scan, scatter) and the combine."""
+    def experts(rows, E):
+        return (2 if rows * lw.k >= 32 * E else 0) + 2
     if world == 1:
-        return 1 + local(T, lw.E)
-    return 2 + 3 + local(rows_local, lw.E // world) + 1
+        return (1 if T <= 64 else 4) + experts(T, lw.E)
+    router = 1 if T <= 64 else 2
+    return router + 3 + (1 if rows_local <= 64 else 3) + experts(rows_local, lw.E // world) + 1
 
 
-# DRAM bytes (read + write) per launch of the dominant kernels, from one ncu capture each of the
-# same command on a B200 (profiles/tc_kernels_c2_prefill.md, profiles/small_kernels_c3_decode_b64.md)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernels,
+# from one ncu --set full capture each of the same bench command on a B200
 NCU_TRAFFIC = {
-    ("c2", "gateup"): 360.961e6 + 41.065e6,
-    ("c2", "down"): 267.533e6 + 30.683e6,
-    ("c3b64", "down"): 162.655e6 + 3.513e6,
+    ("c2", "gateup"): 386.122e6 + 43.173e6,
+    ("c2", "down"): 266.012e6 + 28.321e6,
+    ("c3b64", "gateup"): 246.148e6 + 4.643e6,
+    ("c3b64", "down"): 162.667e6 + 6.531e6,
+    ("c3b1", "gateup"): 15.762e6,
+    ("c3b1", "down"): 10.372e6,
 }
 
 
