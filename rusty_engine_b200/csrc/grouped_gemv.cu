@@ -506,7 +506,9 @@ int gv_tile_rows(int T) { return T <= 64 ? 8 : 16; }
 cudaError_t launch_gv_gateup(const GroupedParams& p, int max_tiles, int nt, int T, cudaStream_t s) {
     if (max_tiles <= 0) return cudaSuccess;
     if (nt != 8 && nt != 16) return cudaErrorInvalidValue;
-    return T <= 2 ? go_gv_type<2, 4>(p.gate.type, p, max_tiles, nt, s) : go_gv_type<2, 2>(p.gate.type, p, max_tiles, nt, s);
+    return T <= 2   ? go_gv_type<2, 4>(p.gate.type, p, max_tiles, nt, s)
+           : T <= 8 ? go_gv_type<2, 2>(p.gate.type, p, max_tiles, nt, s)
+                    : go_gv_type<2, 1>(p.gate.type, p, max_tiles, nt, s);
 }
 
 cudaError_t launch_gv_down(const GroupedParams& p, int max_tiles, int nt, int T, cudaStream_t s) {
