@@ -74,12 +74,10 @@ struct Gv<T_Q4_K> {
         c = ((kk >> 6) << 1) | ((kk >> 4) & 1);
         s = (((kk >> 2) & 3) << 1) | ((kk >> 5) & 1);
     }
-    __device__ static const uint8_t* src16(const DevMat& M, uint64_t grow, int u, int c, int) {
-        return M.main + grow * M.main_stride + (uint64_t)u * 80 + 16 + 16 * c;
-    }
-    __device__ static const uint8_t* src8(const DevMat& M, uint64_t grow, int u, int c, int) {
-        return M.main + grow * M.main_stride + (uint64_t)u * 80 + 8 * (c >> 1);
-    }
+    // byte offset of unit u in a main-plane row, and of lane c's pieces inside the unit
+    __device__ static int unit_base(int u) { return u * 80; }
+    __device__ static int off16(int, int c, int) { return 16 + 16 * c; }
+    __device__ static int off8(int, int c, int) { return 8 * (c >> 1); }
     // y = d*sc*q - dmin*m: q lands in 1024 + q (low nibble) or 1024 + 16 q (high nibble), both
     // exact; 1024 is taken off / the 16 divided out exactly, then one fma with the fp16 pair.
     __device__ static void decode(const uint4* q16, const uint2* q8, int, uint16_t, uint32_t (&a)[8][2]) {
@@ -119,11 +117,11 @@ struct Gv<T_Q6_K> {
         c = (kk >> 3) & 3;
         s = (kk >> 5) | (((kk >> 2) & 1) << 2);
     }
-    __device__ static const uint8_t* src16(const DevMat& M, uint64_t grow, int u, int c, int) { return nullptr; }
-    __device__ static const uint8_t* src8(const DevMat& M, uint64_t grow, int u, int c, int j) {
+    __device__ static int unit_base(int u) { return (u >> 1) * 208; }
+    __device__ static int off16(int, int, int) { return 0; }
+    __device__ static int off8(int u, int c, int j) {
         const int n = u & 1;
-        const uint8_t* b = M.main + grow * M.main_stride + (uint64_t)(u >> 1) * 208;
-        return b + (j == 0 ? 64 * n + 8 * c : j == 1 ? 64 * n + 32 + 8 * c : j == 2 ? 128 + 32 * n + 8 * c : 192 + 8 * n);
+        return j == 0 ? 64 * n + 8 * c : j == 1 ? 64 * n + 32 + 8 * c : j == 2 ? 128 + 32 * n + 8 * c : 192 + 8 * n;
     }
     // q6 lands in 1024 + q6 (low bits at mantissa 0..3, high at 4..5) or 1024 + 16 q6 (4..7 and
     // 8..9), whichever needs fewer shifts for that quadrant and byte pair; q6 - 32 is recovered
@@ -234,27 +232,37 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gv_kernel(GroupedParams p, int 
 
     const uint32_t ring = smem_u32(smem) + ring_off;
     const int nmine = (NU - kq + KS - 1) / KS;
+    // this lane's weight rows (matrix m, row g + 8 r of its group) and ring slot addresses
+    const uint8_t* rowp[NMAT][2];
+#pragma unroll
+    for (int m = 0; m < NMAT; m++)
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const DevMat& M = m ? M1 : M0;
+            rowp[m][r] = M.main + (grow0 + 16 * rg + g + 8 * r) * M.main_stride;
+        }
+    int slot_in = 0;  // ring slot the next issued unit goes to
     auto issue = [&](int i) {
         if (i < nmine) {
             const int u = kq + i * KS;
-            const uint32_t sl = ring + (uint32_t)((i % depth) * G::SLOT);
+            const uint32_t sl = ring + (uint32_t)(slot_in * G::SLOT) + tid * 16;
+            const uint32_t sl8 = ring + (uint32_t)(slot_in * G::SLOT + G::OFF8) + tid * 8;
+            const int ub = D::unit_base(u);
 #pragma unroll
-            for (int m = 0; m < NMAT; m++) {
-                const DevMat& M = m ? M1 : M0;
+            for (int m = 0; m < NMAT; m++)
 #pragma unroll
                 for (int r = 0; r < 2; r++) {
-                    const uint64_t grow = grow0 + 16 * rg + g + 8 * r;
+                    const uint8_t* b = rowp[m][r] + ub;
 #pragma unroll
                     for (int j = 0; j < D::N16; j++)
-                        gv_cp16(sl + ((m * 2 + r) * D::N16 + j) * (GV_THREADS * 16) + tid * 16, D::src16(M, grow, u, c, j));
+                        gv_cp16(sl + ((m * 2 + r) * D::N16 + j) * (GV_THREADS * 16), b + D::off16(u, c, j));
 #pragma unroll
                     for (int j = 0; j < D::N8; j++)
-                        gv_cp8(sl + G::OFF8 + ((m * 2 + r) * D::N8 + j) * (GV_THREADS * 8) + tid * 8,
-                               D::src8(M, grow, u, c, j));
+                        gv_cp8(sl8 + ((m * 2 + r) * D::N8 + j) * (GV_THREADS * 8), b + D::off8(u, c, j));
                 }
-            }
         }
         gv_commit();  // one group per unit (possibly empty), so the wait count stays fixed
+        if (++slot_in == depth) slot_in = 0;
     };
     // the down kernel streams its first units while gate/up finishes; gate/up first sends the
     // token-row loads of its operand (below), so they do not queue behind the weight stream
@@ -340,11 +348,13 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gv_kernel(GroupedParams p, int 
 
     const int nsb = K / 256;
     const int ntl = (nrows + 7) >> 3;  // n-tiles holding live token rows
+    int slot_out = 0;  // ring slot of unit i
     for (int i = 0; i < nmine; i++) {
         issue(i + depth - 1);
         gv_wait_dyn(depth - 1);  // this lane's unit i has landed (only this lane reads it)
         const int u = kq + i * KS;
-        const uint8_t* sl = smem + ring_off + (i % depth) * G::SLOT;
+        const uint8_t* sl = smem + ring_off + slot_out * G::SLOT;
+        if (++slot_out == depth) slot_out = 0;
         const uint2* bu = bsm + (size_t)u * 8 * NTT * 32 + lane;
 #pragma unroll
         for (int m = 0; m < NMAT; m++) {
