@@ -727,6 +727,39 @@ __device__ void dispatch_small(const RouteParams& p, const int* ids_s, int* cnt_
         }
 }
 
+// Dispatch of at most 32 picks (no shared expert, every expert's rows within one tile) by one
+// warp: a pick's expert-sorted row is its rank by (expert, pick index), each expert one tile.
+__device__ void dispatch_tiny(const RouteParams& p, const int* ids_s, int lane) {
+    const int np = p.T * p.k;
+    const bool live = lane < np;
+    const int id = live ? ids_s[lane] : 0x7fffffff;
+    int pos = 0, below = 0;  // picks before this one in expert order; experts below this one
+    bool first = true;       // this lane holds its expert's first pick
+    for (int j = 0; j < np; j++) {
+        const int o = __shfl_sync(0xffffffffu, id, j);
+        pos += (o < id) || (o == id && j < lane);
+        if (o == id && j < lane) first = false;
+    }
+    const unsigned heads = __ballot_sync(0xffffffffu, live && first);
+    for (int j = 0; j < np; j++) {
+        const int o = __shfl_sync(0xffffffffu, id, j);
+        below += ((heads >> j) & 1u) && o < id;
+    }
+    const int rows = __popc(__match_any_sync(0xffffffffu, id));
+    if (live) {
+        const int t = lane / p.k;
+        p.row_tok[pos] = t;
+        p.row_slot[pos] = lane - t * p.k;
+        p.slot_row[lane] = pos;
+        p.rowexp[pos] = -127;
+        if (first) p.tiles[below] = make_int4(id, pos, rows, 0);
+    }
+    if (lane == 0) {
+        *p.n_rows = np;
+        *p.n_tiles = __popc(heads);
+    }
+}
+
 static size_t dispatch_small_scratch(int T, int E, int k) {
     const int np = T * k, nch = (np + 31) / 32;
     return ((size_t)nch * E + np) * 4;
@@ -877,21 +910,30 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     if (warp < nt) {
         const int t = t0 + warp;
         const int id = warp_topk(lg + warp * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
-        if (lane < k) p.topk_id[(size_t)t * k + lane] = id;
+        if (lane < k) {
+            p.topk_id[(size_t)t * k + lane] = id;
+            ids_s[t * k + lane] = id;
+        }
     }
 
-    // 4. the last token group: dispatch of the whole batch
+    // 4. the last token group: dispatch of the whole batch (a single group is its own last)
     if (MODE == 1) return;
-    __threadfence();
+    if (gridDim.y > 1) {
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) ticket_s = atomicAdd(p.ticket, 1u);
+        __syncthreads();
+        if (ticket_s != gridDim.y - 1) return;
+        __threadfence();
+        for (int i = tid; i < T * k; i += RF_THREADS) ids_s[i] = __ldcg(p.topk_id + i);
+        if (tid == 0) p.ticket[0] = 0u;  // every token group has taken its ticket
+    }
     __syncthreads();
-    if (tid == 0) ticket_s = atomicAdd(p.ticket, 1u);
-    __syncthreads();
-    if (ticket_s != gridDim.y - 1) return;
-    __threadfence();
-    for (int i = tid; i < T * k; i += RF_THREADS) ids_s[i] = __ldcg(p.topk_id + i);
-    __syncthreads();
-    if (tid == 0) p.ticket[0] = 0u;  // every token group has taken its ticket
-    dispatch_small(p, ids_s, cnt_s, off_s, reinterpret_cast<int*>(fsm));
+    if (T * k <= 32 && !p.has_shared && T <= p.tile_rows) {
+        if (warp == 0) dispatch_tiny(p, ids_s, lane);
+    } else {
+        dispatch_small(p, ids_s, cnt_s, off_s, reinterpret_cast<int*>(fsm));
+    }
 }
 
 static cudaError_t launch_route_fused(const RouteParams& p, int mode, cudaStream_t s) {
