@@ -486,18 +486,7 @@ static cudaError_t go_gv(const GroupedParams& p, int max_tiles, cudaStream_t s) 
     auto k = gv_kernel<TYPE, NT, NMAT, KS>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    // programmatic dependent launch: the CTAs may start while the previous kernel finishes
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(rows / G::RB, max_tiles);
-    cfg.blockDim = dim3(GV_THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, k, p, depth, (int)ring_off);
+    return launch_pdl(k, dim3(rows / G::RB, max_tiles), dim3(GV_THREADS), smem, s, p, depth, (int)ring_off);
 }
 
 template <int NMAT, int KS>

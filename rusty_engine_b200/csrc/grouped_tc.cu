@@ -141,9 +141,8 @@ struct TcGeom {
     static constexpr int NB = F32 ? 3 : 2;
     static constexpr int RST = (F32 || F22) ? 2 : 1;
     static constexpr int SMEM = BASE + NB * B_STAGE + RST * RAW_STAGE;
-    // converter warps per matrix: 4 decode whole 64-element slices; 8 would split each slice
-    // into two 32-element halves (measured slower on B200: the per-slice waits and arrivals
-    // double while the decode itself does not shrink)
+    // converter warps per stage-parity group (two groups; a thread decodes one gate and one up
+    // row of every other stage)
     static constexpr int CW = 4;
     static constexpr int CONV = 32 * CW * NMAT;  // converter / epilogue threads
     static constexpr int THREADS = 128 + CONV;
@@ -167,6 +166,9 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     __shared__ uint32_t tmem_holder;
     __shared__ volatile int s_abort;
 
+    // launched with programmatic dependent launch after the x gather: the tile list and the
+    // weights may be read at once, the token tiles only after pdl_wait (token-tile producer)
+    pdl_trigger();
     const int tile = blockIdx.y;
     if (tile >= *p.n_tiles) return;  // uniform exit before any barrier or TMEM use
     const int4 ti = p.tiles[tile];
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
             mbar_init(smem_u32(&bar_raw_empty[i]), G::CW * NMAT);
         }
         for (int i = 0; i < NA; i++) {
-            mbar_init(smem_u32(&bar_a_full[i]), G::CW * NMAT);
+            mbar_init(smem_u32(&bar_a_full[i]), G::CW);  // the four warps of one stage-parity group
             mbar_init(smem_u32(&bar_a_empty[i]), 1);
         }
         for (int i = 0; i < NB; i++) {
@@ -274,6 +276,7 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
     } else if (warp < 4) {
         // ---------------- token tiles: one thread streams them with TMA onto b_full ----------------
         if (tid == 64) {
+            pdl_wait();  // the expert-sorted token rows are the previous kernel's output
             for (int kt = 0; kt < nk; kt++) {
                 const int s = kt % NB;
                 if (s_abort) break;
@@ -288,19 +291,21 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
         }
     } else {
         // ---------------- converters: one thread per weight row ----------------
-        // warp (4 + cw): matrix cw / 4, rows 32 (warp & 3) .. +31 (the epilogue reads the
-        // accumulators of those TMEM lanes, which a warp may only reach in its own quarter)
-        // With 8 warps per matrix, the two warps of a lane quarter take the two 32-element
-        // halves of each slice.
+        // Two groups of four warps take alternate stages (group g the stages kt = g mod 2, so it
+        // always fills A slot g): each thread decodes 64 K-elements of its gate row and of its up
+        // row per stage, and has two MMA stages of time for it, which hides the latency of the
+        // raw loads, the stores and the proxy fence of one stage behind the other group's.
+        // Warp (4 + cw): group cw / 4, rows 32 (warp & 3) .. +31 (the epilogue reads the
+        // accumulators of those TMEM lanes, which a warp may only reach in its own quarter).
         constexpr int CW = G::CW;
-        static_assert(CW == 4 || CW == 8, "one or two converter warps per lane quarter and matrix");
-        const int cw = warp - 4, m = cw / CW, q = warp & 3, part = (cw % CW) >> 2;
+        static_assert(CW == 4 && NA == 2 && SUBS % 2 == 0, "two stage-parity groups of four warps");
+        const int cw = warp - 4, g = cw >> 2, q = warp & 3;
         const int r = q * 32 + lane;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
-        for (int kt = 0; kt < nk; kt++) {
+        for (int kt = g; kt < nk; kt += 2) {
             const int j = kt / SUBS, sub = kt % SUBS, s = kt % NA;
             if (s_abort) break;
-            if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[j % RST]), (j / RST) & 1)) {
+            if (sub == g && !mbar_wait(smem_u32(&bar_raw_full[j % RST]), (j / RST) & 1)) {
                 fail();
                 break;
             }
@@ -308,27 +313,24 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
                 fail();
                 break;
             }
-            const uint8_t* mat = raw_g + (size_t)((j % RST) * NMAT + m) * RS::BYTES;
-            const uint8_t *rp = mat + r * PITCH, *rd = mat + RS::DOFF + r * 2, *ra = mat + RS::AOFF + r * 4;
-            constexpr int NV = CW == 4 ? 32 : 16;
-            uint32_t v[NV];
-            if (CW == 4) {
+#pragma unroll
+            for (int m = 0; m < NMAT; m++) {
+                const uint8_t* mat = raw_g + (size_t)((j % RST) * NMAT + m) * RS::BYTES;
+                const uint8_t *rp = mat + r * PITCH, *rd = mat + RS::DOFF + r * 2, *ra = mat + RS::AOFF + r * 4;
+                uint32_t v[32];
                 slice32<TYPE, TC_M>(rp, rd, ra, sub, 0, v);
                 slice32<TYPE, TC_M>(rp, rd, ra, sub, 1, v + 16);
-            } else {
-                slice32<TYPE, TC_M>(rp, rd, ra, sub, part, v);
-            }
-            if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % RST]));
-            }
-            // row r of the 128-B-swizzled K-major tile: 16-B chunk c at (c ^ (r & 7)) * 16
-            uint8_t* at = a_g + (size_t)(s * NMAT + m) * (TC_M * 128) + r * 128;
-            const int c0 = CW == 4 ? 0 : part * 4;
+                if (m == NMAT - 1 && sub == SUBS - 2 + g) {  // this group's last read of the raw slot
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[j % RST]));
+                }
+                // row r of the 128-B-swizzled K-major tile: 16-B chunk c at (c ^ (r & 7)) * 16
+                uint8_t* at = a_g + (size_t)(s * NMAT + m) * (TC_M * 128) + r * 128;
 #pragma unroll
-            for (int c = 0; c < NV / 4; c++)
-                *reinterpret_cast<uint4*>(at + (((c0 + c) ^ (r & 7)) << 4)) =
-                    make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                for (int c = 0; c < 8; c++)
+                    *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
+                        make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+            }
             fence_proxy_async_smem();  // generic-proxy writes -> the MMA's async-proxy reads
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&bar_a_full[s]));
@@ -415,12 +417,14 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
 __global__ void __launch_bounds__(256) rescale_h_kernel(__half* __restrict__ h, const int8_t* __restrict__ hexp,
                                                         const int* __restrict__ rowexp, const int* __restrict__ n_rows,
                                                         int I) {
+    pdl_trigger();
+    pdl_wait();  // h and its exponents are gate/up's output
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (r >= *n_rows) return;
-    const int re = __ldg(rowexp + r), nblk = I / HBLK;
+    const int re = rowexp[r], nblk = I / HBLK;
     uint4* row = reinterpret_cast<uint4*>(h + (size_t)r * I);
     for (int c = lane; c < I / 8; c += 32) {
-        const int dexp = (int)__ldg(hexp + (size_t)r * nblk + c / 8) - re;
+        const int dexp = (int)hexp[(size_t)r * nblk + c / 8] - re;
         if (dexp == 0) continue;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (dexp >= -24) {
@@ -436,8 +440,8 @@ __global__ void __launch_bounds__(256) rescale_h_kernel(__half* __restrict__ h, 
 
 cudaError_t launch_rescale_h(const GroupedParams& p, int max_rows, cudaStream_t s) {
     if (max_rows <= 0) return cudaSuccess;
-    rescale_h_kernel<<<(max_rows + 7) / 8, 256, 0, s>>>(p.h, p.hexp, p.rowexp, p.n_rows, p.I);
-    return cudaGetLastError();
+    return launch_pdl(rescale_h_kernel, dim3((max_rows + 7) / 8), dim3(256), 0, s, p.h, (const int8_t*)p.hexp,
+                      (const int*)p.rowexp, (const int*)p.n_rows, p.I);
 }
 
 template <int TYPE, int NMAT>
@@ -447,8 +451,7 @@ static cudaError_t go_tc(const GroupedParams& p, const TcMaps& maps, int max_til
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((NMAT == 2 ? p.I : p.H) / TC_M, max_tiles);
-    k<<<grid, G::THREADS, G::SMEM, s>>>(p, maps);
-    return cudaGetLastError();
+    return launch_pdl(k, grid, dim3(G::THREADS), G::SMEM, s, p, maps);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -472,8 +475,9 @@ struct DownGeom {
     static constexpr int NB = FIXED + 3 * B_STAGE <= 232448 - 4096 ? 3 : 2;
     static constexpr int A_OFF = NB * B_STAGE, RAW_OFF = A_OFF + NA * A_STAGE, Y_OFF = RAW_OFF + RST * RS::BYTES;
     static constexpr int SMEM = Y_OFF + YB * Y_STAGE + 1024;
-    // warps 0-3: producer / MMA / h tiles / idle; CW converter warps (two per weight row, half
-    // a stage each: the decode, not the MMA, is the long pole of a K = 64 stage); 4 epilogue warps
+    // warps 0-3: producer / MMA / h tiles / idle; CW converter warps (two groups taking
+    // alternate stages: the decode, not the MMA, is the long pole of a K = 64 stage); 4 epilogue
+    // warps
     static constexpr int CW = 8;
     static constexpr int THREADS = (4 + CW + 4) * 32;
     static_assert(SMEM <= 232448 - 4096, "shared memory budget");
@@ -487,7 +491,7 @@ __global__ void __launch_bounds__(512, 1)
     using RS = RawStage<TYPE, TC_M>;
     constexpr int RK = Raw<TYPE>::RK, PITCH = Raw<TYPE>::PITCH, SUBS = RK / TC_KS, NA = D::NA, NB = D::NB, RST = D::RST;
     constexpr int CW = D::CW, EPI0 = 4 + CW;  // converter warps 4 .. EPI0 - 1, epilogue warps EPI0 ..
-    static_assert(D::THREADS == 512 && (CW == 4 || CW == 8), "warp roles");
+    static_assert(D::THREADS == 512, "warp roles");
     extern __shared__ uint8_t dsmem[];
     __shared__ __align__(8) uint64_t bar_raw_full[RST], bar_raw_empty[RST];
     __shared__ __align__(8) uint64_t bar_a_full[NA], bar_a_empty[NA], bar_b_full[NB], bar_b_empty[NB];
@@ -495,6 +499,10 @@ __global__ void __launch_bounds__(512, 1)
     __shared__ uint32_t tmem_holder;
     __shared__ volatile int s_abort, s_epi_stop;
 
+    // launched with programmatic dependent launch after the h rescale: the tile list and the
+    // weights may be read at once (the weight stream and the decode start early), h and the row
+    // exponents only after pdl_wait (the h-tile producer and the epilogue warps wait)
+    pdl_trigger();
     const int nfb = p.H / TC_M;
     const int n_items = *p.n_tiles * nfb;
     if ((int)blockIdx.x >= n_items) return;  // uniform exit before any barrier or TMEM use
@@ -513,7 +521,7 @@ __global__ void __launch_bounds__(512, 1)
             mbar_init(smem_u32(&bar_raw_empty[i]), CW);
         }
         for (int i = 0; i < NA; i++) {
-            mbar_init(smem_u32(&bar_a_full[i]), CW);
+            mbar_init(smem_u32(&bar_a_full[i]), CW / 2);  // the warps of one stage-parity group
             mbar_init(smem_u32(&bar_a_empty[i]), 1);
         }
         for (int i = 0; i < NB; i++) {
@@ -610,6 +618,7 @@ __global__ void __launch_bounds__(512, 1)
     } else if (warp == 2) {
         // ---------------- h tiles ----------------
         if (lane == 0) {
+            pdl_wait();  // h (rescaled) is the previous kernels' output
             int gk = 0;
             for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
                 int e, row0, nrows, fb;
@@ -628,36 +637,34 @@ __global__ void __launch_bounds__(512, 1)
         }
         __syncwarp();
     } else if (warp >= 4 && warp < EPI0) {
-        // ---------------- converters: one weight row per thread (per half stage when CW = 8) --------
-        const int cq = warp - 4, r = (cq & 3) * 32 + lane, part = cq >> 2;
+        // ---------------- converters: one weight row per thread, alternate stages --------
+        // group g = (warp - 4) / 4 decodes the stages of parity g (every item has an even number
+        // of stages, so group g always fills A slot g); each thread decodes 64 K-elements of its
+        // row per stage with two MMA stages of time for it
+        static_assert(CW == 8 && NA == 2 && SUBS % 2 == 0, "two stage-parity groups of four warps");
+        const int cq = warp - 4, r = (cq & 3) * 32 + lane, g = cq >> 2;
         int gk = 0, gj = 0;
         for (int item = blockIdx.x; item < n_items && !s_abort; item += gridDim.x) {
             bool ok = true;
             for (int kt = 0; kt < nk; kt++, gk++) {
-                const int sub = kt % SUBS, s = gk % NA, rs = gj % RST;
+                const int sub = kt % SUBS, s = gk % NA, jj = gj, rs = jj % RST;
+                if (sub == SUBS - 1) gj++;  // both groups count every raw stage
+                if ((kt & 1) != g) continue;
                 if (s_abort) { ok = false; break; }
-                if (sub == 0 && !mbar_wait(smem_u32(&bar_raw_full[rs]), (gj / RST) & 1)) { fail(); ok = false; break; }
+                if (sub == g && !mbar_wait(smem_u32(&bar_raw_full[rs]), (jj / RST) & 1)) { fail(); ok = false; break; }
                 if (gk >= NA && !mbar_wait(smem_u32(&bar_a_empty[s]), ((gk / NA) + 1) & 1)) { fail(); ok = false; break; }
                 const uint8_t* mat = raw_g + (size_t)rs * RS::BYTES;
-                constexpr int NV = CW == 8 ? 16 : 32, C0 = 0;
-                uint32_t v[NV];
-                if (CW == 8) {
-                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, part, v);
-                } else {
-                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 0, v);
-                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 1,
-                                        v + (NV - 16));
-                }
-                if (sub == SUBS - 1) {  // every lane has read its last bytes of this raw slot
+                uint32_t v[32];
+                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 0, v);
+                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 1, v + 16);
+                if (sub == SUBS - 2 + g) {  // this group's last read of the raw slot
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[rs]));
-                    gj++;
                 }
                 uint8_t* at = a_g + (size_t)s * D::A_STAGE + r * 128;
-                const int c0 = C0 + (CW == 8 ? 4 * part : 0);
 #pragma unroll
-                for (int c = 0; c < NV / 4; c++)
-                    *reinterpret_cast<uint4*>(at + (((c0 + c) ^ (r & 7)) << 4)) =
+                for (int c = 0; c < 8; c++)
+                    *reinterpret_cast<uint4*>(at + ((c ^ (r & 7)) << 4)) =
                         make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -667,6 +674,7 @@ __global__ void __launch_bounds__(512, 1)
         }
     } else if (warp >= EPI0) {
         // ---------------- epilogue ----------------
+        pdl_wait();  // the row exponents below are gate/up's output
         const int q = warp & 3;
         const uint32_t tlane = tbase + ((uint32_t)(q * 32) << 16);
         int it = 0;
@@ -760,8 +768,7 @@ static cudaError_t go_down(const GroupedParams& p, const TcMaps& maps, int max_t
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, D::SMEM);
     if (e != cudaSuccess) return e;
     const int items = max_tiles * (p.H / TC_M);
-    k<<<std::min(items, sm_count()), D::THREADS, D::SMEM, s>>>(p, maps);
-    return cudaGetLastError();
+    return launch_pdl(k, dim3(std::min(items, sm_count())), dim3(D::THREADS), D::SMEM, s, p, maps);
 }
 
 #define RMOE_TC_SWITCH(T, ...)                                     \

@@ -6,9 +6,30 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace rmoe {
+
+// Launch with programmatic dependent launch allowed: the kernel's CTAs may start while the
+// previous kernel of the stream finishes; the kernel itself waits (pdl_wait) before it reads
+// anything that kernel writes.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 static constexpr int MAX_E = 512;  // experts per layer this build supports
 static constexpr int MAX_K = 32;   // top-k this build supports

@@ -635,6 +635,7 @@ __global__ void __launch_bounds__(TK_THREADS) scatter_rows_kernel(RouteParams p)
 // the same warp zeroes the token's output row for the atomic combine.
 static constexpr int GX_CHUNK = 8;  // 16-B units per lane per chunk
 __global__ void __launch_bounds__(256) gather_x_kernel(RouteParams p) {
+    pdl_trigger();  // the gate/up kernel may take its SM slots; it waits for this grid's rows
     const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (t >= p.T) return;
     const int k = p.k, per = k + (p.has_shared ? 1 : 0), units = p.H / 8;
