@@ -219,7 +219,7 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     cudaError_t e;
     // 1. router + top-k over all experts
     RouteParams rp{};
-    rp.x = x; rp.router_w = L->router_w; rp.T = (int)T; rp.H = H; rp.E = (int)L->E_router; rp.k = k;
+    rp.x = x; rp.router_w = L->router_w; rp.router_wh = L->router_wh; rp.router_wl = L->router_wl; rp.T = (int)T; rp.H = H; rp.E = (int)L->E_router; rp.k = k;
     rp.exact = (flags & RMOE_FLAG_EXACT_ROUTER) ? 1 : 0;
     rp.gate = (int)L->gate_kind; rp.xb = P.xb; rp.logits = P.logits; rp.topk_id = P.topk_id; rp.topk_w = P.topk_w;
     rp.logits_part = rp.exact ? nullptr : P.logits_part;

@@ -112,6 +112,12 @@ bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMa
                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+bool make_f32_rows_map(const float* base, uint64_t rows, uint32_t width, uint32_t box_w, uint32_t box_rows,
+                       CUtensorMap& out) {
+    return encode2d(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, base, width, rows, (uint64_t)width * 4, box_w, box_rows,
+                    CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 // ---------------------------------------------------------------------------------------------
 // device: TMA 2-D tile load (no multicast)
 // ---------------------------------------------------------------------------------------------

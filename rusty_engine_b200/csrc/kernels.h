@@ -32,11 +32,14 @@ static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 b
 }
 
 static constexpr int MAX_E = 512;  // experts per layer this build supports
+static constexpr int LOGIT_SPLITS = 8;  // K-splits of the large-batch fast router (logits_part planes)
 static constexpr int MAX_K = 32;   // top-k this build supports
 
 struct RouteParams {
     const float* x;         // [T, H] f32
     const float* router_w;  // [E, H] f32
+    const float* router_wh; // optional [E, H]: router_w with the 13 low mantissa bits cleared
+    const float* router_wl; // optional [E, H]: router_w - router_wh (the tensor-core logits)
     int T, H, E, k, gate, has_shared;
     __half* xb;             // [T, H] fp16 copy of x (GEMM B operand)
     int* rowexp;            // [rows] SwiGLU row exponents, set to -127 by the dispatch
@@ -133,6 +136,13 @@ struct alignas(64) TcMaps {
 // Build the maps of one stack (after upload_mat) / of the h workspace; false on a driver error.
 bool make_weight_maps(const DevMat& M, WMaps& out);
 bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMap& out);
+// fp32 [rows, width] row-major, 128-B-swizzled boxes of box_w (32) x box_rows
+bool make_f32_rows_map(const float* base, uint64_t rows, uint32_t width, uint32_t box_w, uint32_t box_rows,
+                       CUtensorMap& out);
+// large-batch fast-router logits on the tensor cores (split partial sums into logits_part);
+// cudaErrorNotSupported where the shapes or the pointers do not allow it
+bool logits_tc_supported(const RouteParams& p);
+cudaError_t launch_logits_tc(const RouteParams& p, cudaStream_t s);
 
 // large-batch (tcgen05) grouped kernels; tile_rows = rows per tile
 int tc_tile_rows();

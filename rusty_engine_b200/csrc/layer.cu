@@ -382,6 +382,25 @@ rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_
     cudaError_t e = cudaMemcpy(rw, d->router_w, (size_t)d->n_experts * H * 4, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_fail(e, "router upload");
     L->router_w = static_cast<float*>(rw);
+    // the router split for the tensor-core logits: hi = w with its 13 low mantissa bits
+    // cleared (a tf32 value), lo = w - hi (exact)
+    const size_t nw = (size_t)d->n_experts * H;
+    std::vector<float> hl(2 * nw);
+    for (size_t i = 0; i < nw; i++) {
+        uint32_t u;
+        memcpy(&u, d->router_w + i, 4);
+        u &= 0xffffe000u;
+        float h;
+        memcpy(&h, &u, 4);
+        hl[i] = h;
+        hl[nw + i] = d->router_w[i] - h;
+    }
+    void* rs = L->own.alloc(2 * nw * 4);
+    if (!rs) return fail(RMOE_ERR_OOM, "router split cudaMalloc failed");
+    if ((e = cudaMemcpy(rs, hl.data(), 2 * nw * 4, cudaMemcpyHostToDevice)) != cudaSuccess)
+        return cuda_fail(e, "router split upload");
+    L->router_wh = static_cast<float*>(rs);
+    L->router_wl = L->router_wh + nw;
     return RMOE_OK;
 }
 
@@ -448,7 +467,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     Workspace& w = L->ws;
     RouteParams rp{};
     rp.x = given ? nullptr : x;
-    rp.router_w = L->router_w;
+    rp.router_w = L->router_w; rp.router_wh = L->router_wh; rp.router_wl = L->router_wl;
     rp.T = (int)T; rp.H = (int)L->H; rp.E = (int)L->E; rp.k = (int)L->k; rp.gate = (int)L->gate_kind;
     rp.has_shared = L->has_shared;
     rp.given = given ? 1 : 0;

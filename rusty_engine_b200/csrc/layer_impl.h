@@ -70,6 +70,8 @@ struct rmoe_layer {
     rmoe::WMaps mg{}, mu{}, md{}, smg{}, smu{}, smd{};  // TMA maps of the stacks above
     CUtensorMap hmap{}, xsmap{};                          // TMA maps of the workspace h and xs
     float* router_w = nullptr;
+    float* router_wh = nullptr;  // router_w split for the tensor-core logits (hi | lo, [E, H] each)
+    float* router_wl = nullptr;
     rmoe::Owned own;       // weights
     rmoe::Owned ws_own;    // workspace
     rmoe::Workspace ws;

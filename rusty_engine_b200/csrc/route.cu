@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(LT_THREADS) logits_tiled_kernel(const float* _
 // Each split writes its partial sums; the top-k kernel adds the splits in order.  The first
 // expert tile also writes the fp16 copy of its tokens' K range.
 // ---------------------------------------------------------------------------------------
-static constexpr int LG_M = 128, LG_N = 128, LG_K = 16, LG_S = 8, LG_THREADS = 256, LG_LD = LG_M + 4;
+static constexpr int LG_M = 128, LG_N = 128, LG_K = 16, LG_S = LOGIT_SPLITS, LG_THREADS = 256, LG_LD = LG_M + 4;
 
 __global__ void __launch_bounds__(LG_THREADS, 2) logits_ffma_kernel(const float* __restrict__ x,
                                                                  const float* __restrict__ w, int T, int H, int E,
@@ -955,8 +955,8 @@ static bool use_split(const RouteParams& p) { return !p.exact && p.logits_part &
 
 // Router logits (and the fp16 copy of x).  Exact: the chained per-logit kernel for small
 // batches, the register-tiled one otherwise; fast: the warp-per-expert kernel below LG_MIN_T
-// tokens, the K-split product above (the register-tiled one with FFMA when there is no
-// partial-sum buffer).
+// tokens, the K-split product above (on the tensor cores with split-fp32 operands where the
+// shapes allow, else with FFMA; the register-tiled one when there is no partial-sum buffer).
 static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
     if (!p.exact && p.T < LG_MIN_T) return launch_route_fused(p, 0, s);
     if (p.T <= RS_MAX_T) {
@@ -965,6 +965,7 @@ static cudaError_t launch_logits(const RouteParams& p, cudaStream_t s) {
         dim3 grid((p.E + LC_EB - 1) / LC_EB, (p.T + LC_TB - 1) / LC_TB);
         logits_chain_kernel<<<grid, LC_THREADS, LC_SMEM, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits, p.xb, p.status);
     } else if (use_split(p)) {
+        if (logits_tc_supported(p)) return launch_logits_tc(p, s);
         dim3 grid((p.T + LG_M - 1) / LG_M, (p.E + LG_N - 1) / LG_N, LG_S);
         logits_ffma_kernel<<<grid, LG_THREADS, 0, s>>>(p.x, p.router_w, p.T, p.H, p.E, p.logits_part, p.xb, p.status);
     } else {

@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from routing_check import check_routing
+from routing_check import SUM_ERR, check_routing
 from rusty_engine_b200 import _lib, synth
 
 pytestmark = pytest.mark.gpu
@@ -172,8 +172,34 @@ def test_c2_layer_parity(torch_cuda):
     out = O.moe_layer_q_exact(x[sample], lw)[0]
     assert_layer_close(got["out"][sample], out, "c2 exact router")
     got = run_layer(torch_cuda, lw, x)
+    check_fast_logits(got["logits"], logits, x, lw, "c2")
     same = check_routing(got["ids"], got["w"], ids, w, x, lw.router_w, lw.E, "c2")
     assert_layer_close(got["out"][sample][same[sample]], out[same[sample]], "c2")
+
+
+@pytest.mark.parametrize("E,T", [(256, 1100), (96, 1100), (64, 1030), (16, 1024), (128, 2053)])
+def test_large_batch_router_logits(torch_cuda, E, T):
+    """The fast router at >= 1024 tokens (tensor-core product of split fp32 operands for up to
+    128 experts, the FFMA product above; K-split partial sums added in split order): logits
+    within the f32 summation error of the sequential sums, ids up to near-ties, for expert
+    counts 16..256 and token counts off the 128-token tile grid."""
+    lw = synth.make_layer(1024, 256, E, 8, gate_t=synth.GGML_Q4_0, up_t=synth.GGML_Q4_0,
+                          down_t=synth.GGML_Q4_0, dlo=0.005, dhi=0.02, seed=E)
+    x = synth.activations(T, lw.H, seed=T)
+    logits = O.router_logits(x, lw.router_w, lw.E)
+    ids, w = O.route_batch(logits, 0, lw.k)
+    got = run_layer(torch_cuda, lw, x)
+    check_fast_logits(got["logits"], logits, x, lw, f"E={E} T={T}")
+    check_routing(got["ids"], got["w"], ids, w, x, lw.router_w, lw.E, f"E={E} T={T}")
+
+
+def check_fast_logits(got, seq, x, lw, what):
+    """Fast-router logits: within SUM_ERR of the exact (float64) sums, the level of the
+    reference's own sequential f32 summation error at these sizes (both are printed)."""
+    l64 = O.router_logits_f64(x, lw.router_w, lw.E)
+    e_gpu, e_seq = float(np.abs(got - l64).max()), float(np.abs(seq - l64).max())
+    print(f"{what}: max |logit - float64| gpu {e_gpu:.2e}, sequential f32 {e_seq:.2e}")
+    assert e_gpu <= SUM_ERR, f"{what}: logits {e_gpu:.2e} from the float64 sums"
 
 
 @pytest.fixture(scope="module")
