@@ -59,8 +59,8 @@ def kernels_per_forward(lw, T, world=1, rows_local=None):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernels,
 # from one ncu --set full capture each of the same bench command on a B200
 NCU_TRAFFIC = {
-    ("c2", "gateup"): 386.122e6 + 43.173e6,
-    ("c2", "down"): 266.012e6 + 28.321e6,
+    ("c2", "gateup"): 386.080e6 + 42.816e6,
+    ("c2", "down"): 265.979e6 + 27.879e6,
     ("c3b64", "gateup"): 246.148e6 + 4.643e6,
     ("c3b64", "down"): 162.667e6 + 6.531e6,
     ("c3b1", "gateup"): 15.762e6,
