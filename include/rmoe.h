@@ -90,8 +90,11 @@ enum {
                                           (read back with rmoe_layer_stage_ms) */
     RMOE_FLAG_EXACT_ROUTER = 1u << 6   /* router logits bit-identical to moe::matvec (sequential
                                           f32 sums, src/moe.rs:271-277); without it the logits
-                                          are FFMA sums a few ulp away, so top-k can differ from
-                                          the reference only at near-ties of that size */
+                                          are sums in another order (FFMA, or from 1024 tokens
+                                          tensor-core products of hi/lo-split fp32 operands)
+                                          within the f32 summation error of the exact sums, so
+                                          top-k can differ from the reference only at near-ties
+                                          of that size */
 };
 
 /* Create a layer handle: validates the description on the host, copies router and expert
@@ -184,6 +187,32 @@ RMOE_API rmoe_status rmoe_ep_unique_id(uint8_t id[128]);
  * once (the call synchronises the stream there). */
 RMOE_API rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* desc, int32_t rank, int32_t world_size,
                                  const uint8_t id[128], rmoe_layer** out);
+
+/* ---- GGUF expert binding (MmapModel::open / tensor_bytes, src/loader.rs:33-102; the MoE
+ *      tensors of a block, src/model.rs:366-391) ---------------------------------------------- */
+
+/* A GGUF file mapped read-only with its parsed header (version 2 or 3).  Parse errors are
+ * RMOE_ERR_INVALID with "gguf parse error at <byte offset>: <what>" (src/gguf.rs:174-178). */
+typedef struct rmoe_gguf rmoe_gguf;
+RMOE_API rmoe_status rmoe_gguf_open(const char* path, rmoe_gguf** out);
+RMOE_API void rmoe_gguf_close(rmoe_gguf* g);
+
+/* A tensor's type, dims (up to 3; unused dims are 1) and bytes inside the mapping:
+ * [aligned data start + offset, + bytes_for_numel(type, numel)), bounds-checked
+ * (MmapModel::tensor_bytes, src/loader.rs:97-102).  Valid until rmoe_gguf_close. */
+RMOE_API rmoe_status rmoe_gguf_tensor(const rmoe_gguf* g, const char* name, rmoe_tensor* out);
+
+/* An integer metadata value by its full key (e.g. "qwen3moe.expert_count"). */
+RMOE_API rmoe_status rmoe_gguf_meta_uint(const rmoe_gguf* g, const char* key, uint64_t* out);
+
+/* The layer description of MoE block `block`: blk.N.ffn_gate_inp [H, E] (router; F32 used in
+ * place, F16 / BF16 widened to f32 in memory the rmoe_gguf handle owns), ffn_{gate,up}_exps
+ * [H, I, E], ffn_down_exps [I, H, E] and, when all three exist, ffn_{gate,up,down}_shexp
+ * ([H, I], [H, I], [I, H]).  top_k = {arch}.expert_used_count, the expert count is checked
+ * against {arch}.expert_count where present (then general.*, src/model.rs:131-147), gate =
+ * sigmoid when {arch}.expert_gating_func is 2, else softmax; device 0.  The description
+ * points into the mapping: pass it to rmoe_layer_create before rmoe_gguf_close. */
+RMOE_API rmoe_status rmoe_gguf_moe_layer_desc(rmoe_gguf* g, uint32_t block, rmoe_layer_desc* out);
 
 /* Build info: "sm_100a <git-describe> <kernels...>". */
 RMOE_API const char* rmoe_build_info(void);

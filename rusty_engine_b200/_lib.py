@@ -53,6 +53,7 @@ EXPORTS = [
     "rmoe_layer_create", "rmoe_layer_forward", "rmoe_layer_routing", "rmoe_layer_logits", "rmoe_layer_destroy",
     "rmoe_last_error", "rmoe_dequant", "rmoe_qmat_matmul", "rmoe_route", "rmoe_ep_unique_id",
     "rmoe_ep_layer_create", "rmoe_build_info", "rmoe_layer_stage_ms", "rmoe_layer_forward_noalloc",
+    "rmoe_gguf_open", "rmoe_gguf_close", "rmoe_gguf_tensor", "rmoe_gguf_meta_uint", "rmoe_gguf_moe_layer_desc",
 ]
 
 NOALLOC_SCRATCH_BYTES = 8 << 20  # RMOE_NOALLOC_SCRATCH_BYTES
@@ -86,6 +87,12 @@ def load():
         L.rmoe_ep_unique_id.argtypes = [vp]
         L.rmoe_ep_layer_create.argtypes = [C.POINTER(LayerDesc), i32, i32, vp, C.POINTER(vp)]
         L.rmoe_build_info.restype = C.c_char_p
+        L.rmoe_gguf_open.argtypes = [C.c_char_p, C.POINTER(vp)]
+        L.rmoe_gguf_close.argtypes = [vp]
+        L.rmoe_gguf_close.restype = None
+        L.rmoe_gguf_tensor.argtypes = [vp, C.c_char_p, C.POINTER(Tensor)]
+        L.rmoe_gguf_meta_uint.argtypes = [vp, C.c_char_p, C.POINTER(u64)]
+        L.rmoe_gguf_moe_layer_desc.argtypes = [vp, u32, C.POINTER(LayerDesc)]
         for name in EXPORTS:
             fn = getattr(L, name)
             if fn.restype is C.c_int or name in ("rmoe_layer_create",):

@@ -10,7 +10,8 @@ tests) read like the reference's own:
 * ``QMat.from_bytes(...).matvec/.matmul``                         -- src/qmat.rs:51-182
 * ``dequant(ggml_type, data)``                                    -- src/quant.rs:363-453
 * ``MoELayer``: a resident layer over GGUF expert tensors (the B200 handle that
-  ``moe_layer_forward`` drives when the experts come from ``ffn_*_exps``).
+  ``moe_layer_forward`` drives when the experts come from ``ffn_*_exps``); ``gguf.MmapModel``
+  binds a model file's ``blk.N.ffn_*_exps`` to it (src/loader.rs:97-102, src/model.rs:366-391).
 
 Shape errors raise ``ValueError`` where the Rust code asserts (panics); recoverable errors
 raise ``EngineError`` (src/core.rs:56-68).  Every computation runs on the GPU through the C
@@ -236,6 +237,22 @@ class MoELayer:
             idbuf = (C.c_uint8 * 128).from_buffer_copy(bytes(uid))
             _call(L.rmoe_ep_layer_create(C.byref(d), rank, world, idbuf, C.byref(h)))
         self._h = h
+
+    @classmethod
+    def from_desc(cls, d: _lib.LayerDesc, device: Optional[int] = None) -> "MoELayer":
+        """A layer from a filled rmoe_layer_desc (e.g. gguf.MmapModel.moe_layer_desc): the
+        bytes it points to are copied to HBM inside the call."""
+        _require_cuda()
+        self = cls.__new__(cls)
+        self.lw = None
+        self.H, self.I, self.E, self.k = d.hidden, d.inter, d.n_experts, min(d.top_k, d.n_experts)
+        self.device = torch.cuda.current_device() if device is None else device
+        self._router = None
+        d.device = self.device
+        h = C.c_void_p()
+        _call(_lib.load().rmoe_layer_create(C.byref(d), C.byref(h)))
+        self._h = h
+        return self
 
     def forward(self, x, out=None, *, flags: int = 0, stream=None):
         """x: [T, H] f32 cuda tensor -> out [T, H] f32 (stream-ordered, no sync)."""
