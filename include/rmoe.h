@@ -171,6 +171,18 @@ RMOE_API rmoe_status rmoe_qmat_matmul(uint32_t ggml_type, const void* w_host, ui
 RMOE_API rmoe_status rmoe_route(const float* logits, uint32_t T, uint32_t E, uint32_t k, uint32_t gate,
                        uint32_t* ids, float* weights, void* stream);
 
+/* route_noaux_tc (src/moe.rs:192-268; noaux != 0) or route_group (src/moe.rs:127-190;
+ * noaux == 0) over T rows of E logits, device pointers: scores sigmoid(logit + bias) (bias of
+ * length nbias, 0 past it, may be null when nbias is 0); experts in n_groups contiguous groups
+ * (expert i in group i * n_groups / E); a group scores the sum of its top-2 scores (noaux) or
+ * of all its scores; only the top_k_group best groups are eligible (every group when
+ * top_k_group < 0); the top k eligible experts by score, weights renormalised over the picks.
+ * ids / weights are T x k in chosen order; picks beyond the eligible experts get id
+ * 0xFFFFFFFF and weight 0 (the reference returns fewer picks).  n_groups <= 64, k <= 32. */
+RMOE_API rmoe_status rmoe_route_grouped(const float* logits, const float* bias, uint32_t nbias, uint32_t T,
+                               uint32_t E, uint32_t k, uint32_t n_groups, int32_t top_k_group, int32_t noaux,
+                               uint32_t* ids, float* weights, void* stream);
+
 /* ---- expert parallelism (no counterpart in the reference: its B9 dist-MoE is planned,
  *      docs/roadmap.md:235-246) ---------------------------------------------------------- */
 

@@ -34,6 +34,7 @@ static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 b
 static constexpr int MAX_E = 512;  // experts per layer this build supports
 static constexpr int LOGIT_SPLITS = 8;  // K-splits of the large-batch fast router (logits_part planes)
 static constexpr int MAX_K = 32;   // top-k this build supports
+static constexpr int RG_MAX_G = 64; // expert groups the group router supports
 
 struct RouteParams {
     const float* x;         // [T, H] f32
@@ -141,6 +142,9 @@ bool make_f32_rows_map(const float* base, uint64_t rows, uint32_t width, uint32_
                        CUtensorMap& out);
 // large-batch fast-router logits on the tensor cores (split partial sums into logits_part);
 // cudaErrorNotSupported where the shapes or the pointers do not allow it
+// route_noaux_tc / route_group over precomputed logits (one warp per token)
+cudaError_t launch_route_grouped(const float* logits, const float* bias, int nbias, int T, int E, int k, int ng,
+                                 int tkg, int noaux, unsigned* ids, float* w, cudaStream_t s);
 bool logits_tc_supported(const RouteParams& p);
 cudaError_t launch_logits_tc(const RouteParams& p, cudaStream_t s);
 

@@ -701,6 +701,22 @@ rmoe_status rmoe_route(const float* logits, uint32_t T, uint32_t E, uint32_t k, 
     return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "route launch");
 }
 
+rmoe_status rmoe_route_grouped(const float* logits, const float* bias, uint32_t nbias, uint32_t T, uint32_t E,
+                               uint32_t k, uint32_t n_groups, int32_t top_k_group, int32_t noaux, uint32_t* ids,
+                               float* weights, void* stream) {
+    if (E == 0 || T == 0) return RMOE_OK;
+    if (!logits || !ids || !weights || (nbias && !bias)) return fail(RMOE_ERR_INVALID, "null pointer");
+    if (E > (uint32_t)MAX_E) return fail(RMOE_ERR_UNSUPPORTED, "E %u > %d", E, MAX_E);
+    if (k == 0 || k > (uint32_t)MAX_K) return fail(RMOE_ERR_UNSUPPORTED, "k %u unsupported (1..%d)", k, MAX_K);
+    uint32_t ng = n_groups < 1 ? 1 : n_groups;  // n_groups.max(1).min(n), src/moe.rs:211
+    if (ng > E) ng = E;
+    if (ng > (uint32_t)RG_MAX_G) return fail(RMOE_ERR_UNSUPPORTED, "%u expert groups (at most %d)", ng, RG_MAX_G);
+    const int tkg = top_k_group < 0 ? -1 : (int)std::min<uint32_t>((uint32_t)top_k_group, ng);
+    cudaError_t e = launch_route_grouped(logits, bias, (int)std::min<uint32_t>(nbias, E), (int)T, (int)E, (int)k, (int)ng,
+                                         tkg, noaux ? 1 : 0, ids, weights, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "grouped route launch");
+}
+
 rmoe_status rmoe_qmat_matmul(uint32_t t, const void* w_host, uint64_t w_nbytes, uint32_t m, uint32_t n, const float* x,
                              uint32_t rows, float* out, void* stream) {
     if (m % 64) return fail(RMOE_ERR_UNSUPPORTED, "m %u must be a multiple of 64", m);

@@ -24,6 +24,8 @@
 // launch for all of it (route_fused_small_kernel).
 #include <algorithm>
 
+#include <float.h>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -1027,6 +1029,121 @@ cudaError_t launch_route_dispatch(const RouteParams& p0, cudaStream_t s) {
     }
     if ((e = cudaGetLastError()) != cudaSuccess || !p.xs) return e;
     gather_x_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------
+// Group routing over precomputed logits (one warp per token): route_noaux_tc
+// (src/moe.rs:192-268; noaux != 0) and route_group (src/moe.rs:127-190; noaux == 0).
+//   scores s_i = sigmoid(logits_i + bias_i) (bias_i = 0 past the bias length);
+//   contiguous groups, expert i in group i * ng / E; a group's score is the sum of its top-2
+//   scores (noaux: updated in ascending expert order with the reference's >= / > rule) or of
+//   all its scores (ascending f32 sum);
+//   the top_k_group groups by a stable descending sort (ties to the lower group) are eligible
+//   (all of them when top_k_group < 0);
+//   the top k eligible experts by a stable descending sort, weights s / (sum of the picked s
+//   in pick order); picks beyond the eligible experts get id 0xFFFFFFFF and weight 0.
+// ---------------------------------------------------------------------------------------
+static constexpr int RG_WARPS = 8;
+
+template <int NS>  // NS >= ceil(E / 32)
+__global__ void __launch_bounds__(RG_WARPS * 32) route_grouped_kernel(const float* __restrict__ logits,
+                                                                      const float* __restrict__ bias, int nbias,
+                                                                      int T, int E, int k, int ng, int tkg,
+                                                                      int noaux, unsigned* ids, float* w) {
+    __shared__ float s_sc[RG_WARPS][MAX_E];
+    __shared__ float s_gs[RG_WARPS][RG_MAX_G];
+    __shared__ unsigned char s_ok[RG_WARPS][RG_MAX_G];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = blockIdx.x * RG_WARPS + warp;
+    if (t >= T) return;  // warp-uniform
+    float* sc = s_sc[warp];
+    for (int e = lane; e < E; e += 32) {
+        const float x = logits[(size_t)t * E + e] + (e < nbias ? bias[e] : 0.0f);
+        sc[e] = 1.0f / (1.0f + expf(-x));  // sigmoid, src/moe.rs:44-51
+    }
+    __syncwarp();
+    for (int g = lane; g < ng; g += 32) {
+        const int b = (g * E + ng - 1) / ng, en = ((g + 1) * E + ng - 1) / ng;  // i * ng / E == g
+        float sum = 0.0f, t1 = -FLT_MAX, t2 = -FLT_MAX;
+        for (int i = b; i < en; i++) {
+            const float v = sc[i];
+            if (noaux) {
+                if (v >= t1) {
+                    t2 = t1;
+                    t1 = v;
+                } else if (v > t2) {
+                    t2 = v;
+                }
+            } else {
+                sum = __fadd_rn(sum, v);
+            }
+        }
+        s_gs[warp][g] = noaux ? __fadd_rn(t1, t2 == -FLT_MAX ? 0.0f : t2) : sum;
+    }
+    __syncwarp();
+    for (int g = lane; g < ng; g += 32) {
+        bool ok = true;
+        if (tkg >= 0) {
+            const float v = s_gs[warp][g];
+            int rank = 0;
+            for (int h = 0; h < ng; h++) {
+                const float u = s_gs[warp][h];
+                rank += (u > v || (u == v && h < g)) ? 1 : 0;
+            }
+            ok = rank < tkg;
+        }
+        s_ok[warp][g] = ok ? 1 : 0;
+    }
+    __syncwarp();
+    unsigned key[NS];
+#pragma unroll
+    for (int q = 0; q < NS; q++) {
+        const int e = lane + 32 * q;
+        key[q] = (e < E && s_ok[warp][e * ng / E]) ? score_key(sc[e]) : 0u;
+    }
+    float chosen = 0.0f;
+    int chosen_id = -1;
+    for (int j = 0; j < k; j++) {
+        unsigned bk = 0u;
+        int bq = 0;
+#pragma unroll
+        for (int q = 0; q < NS; q++)
+            if (key[q] > bk) {
+                bk = key[q];
+                bq = q;
+            }
+        const unsigned m = __reduce_max_sync(0xffffffffu, bk);
+        if (m == 0u) break;  // no eligible expert left (warp-uniform)
+        const int win = (int)__reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bq) : 0xffffffffu);
+        if ((win & 31) == lane)
+#pragma unroll
+            for (int q = 0; q < NS; q++)
+                if (q == (win >> 5)) key[q] = 0u;
+        if (lane == j) {
+            chosen = key_score(m);
+            chosen_id = win;
+        }
+    }
+    float wsum = 0.0f;  // the picked scores summed in pick order, as the reference's iterator sum
+    for (int j = 0; j < k; j++) {
+        const float v = __shfl_sync(0xffffffffu, chosen, j);
+        if (__shfl_sync(0xffffffffu, chosen_id, j) >= 0) wsum = __fadd_rn(wsum, v);
+    }
+    if (lane < k) {
+        ids[(size_t)t * k + lane] = chosen_id >= 0 ? (unsigned)chosen_id : 0xffffffffu;
+        w[(size_t)t * k + lane] = (chosen_id < 0 || wsum == 0.0f) ? 0.0f : __fdiv_rn(chosen, wsum);
+    }
+}
+
+cudaError_t launch_route_grouped(const float* logits, const float* bias, int nbias, int T, int E, int k, int ng,
+                                 int tkg, int noaux, unsigned* ids, float* w, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    const dim3 grid((T + RG_WARPS - 1) / RG_WARPS), block(RG_WARPS * 32);
+    const int ns = (E + 31) / 32;
+    if (ns <= 4)
+        route_grouped_kernel<4><<<grid, block, 0, s>>>(logits, bias, nbias, T, E, k, ng, tkg, noaux, ids, w);
+    else
+        route_grouped_kernel<MAX_E / 32><<<grid, block, 0, s>>>(logits, bias, nbias, T, E, k, ng, tkg, noaux, ids, w);
     return cudaGetLastError();
 }
 

@@ -5,6 +5,7 @@ tests) read like the reference's own:
 
 * ``Gate``, ``RouterConfig``, ``ExpertScore``, ``ExpertWeights``  -- src/moe.rs:11-41, 348-353
 * ``route(logits, cfg)``                                          -- src/moe.rs:120-125
+* ``route_noaux_tc`` / ``route_group`` (+ ``route_grouped_batch``) -- src/moe.rs:127-268
 * ``moe_layer_forward(hidden, router_w, n_experts, experts, shared, inter, cfg)``
                                                                    -- src/moe.rs:360-388
 * ``QMat.from_bytes(...).matvec/.matmul``                         -- src/qmat.rs:51-182
@@ -125,6 +126,46 @@ def top_k(scores: Sequence[float], k: int) -> List[ExpertScore]:
 
 def top_k_sigmoid(scores: Sequence[float], k: int) -> List[ExpertScore]:
     return route(scores, RouterConfig(Gate.Sigmoid, k))
+
+
+def route_grouped_batch(logits, bias, n_groups: int, top_k: int, top_k_group: Optional[int], noaux: bool = True):
+    """Group routing of a [T, E] batch on the GPU (rmoe_route_grouped) -> (ids [T, k] uint32,
+    weights [T, k]); picks beyond the eligible experts have id 0xFFFFFFFF and weight 0."""
+    _require_cuda()
+    lg = _dev_f32(logits)
+    if lg.dim() == 1:
+        lg = lg[None]
+    T, E = lg.shape
+    if T == 0 or E == 0 or top_k == 0:
+        return np.zeros((T, 0), np.uint32), np.zeros((T, 0), np.float32)
+    b = _dev_f32(bias) if bias is not None and len(bias) else None
+    ids = torch.empty((T, top_k), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, top_k), dtype=torch.float32, device="cuda")
+    _call(_lib.load().rmoe_route_grouped(lg.data_ptr(), b.data_ptr() if b is not None else None,
+                                         0 if b is None else b.numel(), T, E, top_k, n_groups,
+                                         -1 if top_k_group is None else top_k_group, 1 if noaux else 0,
+                                         ids.data_ptr(), w.data_ptr(), _stream()))
+    torch.cuda.synchronize()
+    return ids.cpu().numpy().view(np.uint32), w.cpu().numpy()
+
+
+def _grouped(logits, bias, n_groups, top_k, top_k_group, noaux) -> List[ExpertScore]:
+    if len(logits) == 0:
+        return []
+    ids, w = route_grouped_batch(np.asarray(logits, dtype=np.float32)[None], bias, n_groups, top_k, top_k_group,
+                                 noaux)
+    return [ExpertScore(int(i), float(x)) for i, x in zip(ids[0], w[0]) if i != 0xFFFFFFFF]
+
+
+def route_noaux_tc(logits, bias, n_groups: int, top_k: int, top_k_group: Optional[int]) -> List[ExpertScore]:
+    """route_noaux_tc (src/moe.rs:192-268): sigmoid(logit + bias) scores, groups ranked by the
+    sum of their top-2 scores, the top_k_group best eligible, top_k experts renormalised."""
+    return _grouped(logits, bias, n_groups, top_k, top_k_group, True)
+
+
+def route_group(logits, bias, n_groups: int, top_k: int, top_k_group: Optional[int]) -> List[ExpertScore]:
+    """route_group (src/moe.rs:127-190): as route_noaux_tc with groups ranked by their summed score."""
+    return _grouped(logits, bias, n_groups, top_k, top_k_group, False)
 
 
 # ---- dequant / QMat -------------------------------------------------------------------

@@ -93,6 +93,48 @@ def test_route_reference_kats(torch_cuda):
     assert route([], RouterConfig()) == []
 
 
+def test_route_grouped_reference_kats(torch_cuda):
+    """The reference's group-routing tests (src/moe.rs:666-710) through rmoe_route_grouped."""
+    from rusty_engine_b200.moe import route_group, route_noaux_tc
+
+    logits = [5.0, 2.0, -9.0, -9.0, 0.0, 0.0, 0.0, 0.0]
+    s = route_noaux_tc(logits, [], 2, 1, 1)  # the dominant pair's group wins
+    assert s[0].id == 0 and abs(s[0].weight - 1.0) < 1e-5
+    assert 4 <= route_group(logits, [], 2, 1, 1)[0].id <= 7  # the all-sum version: the other group
+    s = route_noaux_tc(logits, [], 2, 2, 1)
+    assert [e.id for e in s] == [0, 1] and abs(sum(e.weight for e in s) - 1.0) < 1e-5
+    assert route_noaux_tc([], [], 2, 1, 1) == []
+
+
+@pytest.mark.parametrize("E,ng,tkg,k,noaux", [(256, 8, 4, 8, True), (256, 8, 4, 8, False), (96, 7, None, 6, True),
+                                              (128, 1, 1, 8, True), (16, 8, 1, 4, True)])
+def test_route_grouped_vs_oracle(torch_cuda, E, ng, tkg, k, noaux):
+    """rmoe_route_grouped against the oracle's restatement on random logits and bias: ids equal
+    (a difference only where the two experts' sigmoid scores are within a few ulp: CUDA's and
+    glibc's expf may differ by an ulp), weights within 1e-5 relative; picks beyond the eligible
+    experts are empty (id 0xFFFFFFFF, weight 0)."""
+    from rusty_engine_b200.moe import route_grouped_batch
+
+    rng = np.random.default_rng(E * 31 + ng)
+    T = 300
+    logits = rng.standard_normal((T, E), dtype=np.float32)
+    bias = (rng.standard_normal(E, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    ids, w = route_grouped_batch(logits, bias, ng, k, tkg, noaux)
+    sig = (1.0 / (1.0 + np.exp(-(logits + bias).astype(np.float64)))).astype(np.float32)
+    for t in range(T):
+        ref = O.route_grouped(logits[t], bias, ng, k, tkg, noaux)
+        rid = np.array([i for i, _ in ref], dtype=np.int64)
+        rw = np.array([x for _, x in ref], dtype=np.float32)
+        n = len(ref)
+        assert (ids[t, n:] == 0xFFFFFFFF).all() and (w[t, n:] == 0).all()
+        got = ids[t, :n].astype(np.int64)
+        for j in np.nonzero(got != rid)[0]:
+            a, b = sig[t, got[j]], sig[t, rid[j]]
+            assert abs(float(a) - float(b)) <= 4 * np.spacing(np.float32(max(a, b))), (t, j, got[j], rid[j])
+        if (got == rid).all():
+            np.testing.assert_allclose(w[t, :n], rw, rtol=1e-5, atol=1e-7)
+
+
 @pytest.mark.parametrize("gate", [0, 1])
 def test_route_random_with_ties_bit_exact(torch_cuda, gate):
     from rusty_engine_b200.moe import Gate, RouterConfig, route_batch
