@@ -161,7 +161,8 @@ RMOE_API rmoe_status rmoe_dequant(uint32_t ggml_type, const void* src, uint64_t 
 /* QMat::matmul (src/qmat.rs:169-182) on the GPU: W[m x n] (GGUF bytes, host pointer, type t)
  * times X[rows x n] f32 -> Out[rows x m] f32.  X/Out are device pointers.  rows = 1 is
  * QMat::matvec (src/qmat.rs:80-82).  Weights are uploaded per call (a convenience path;
- * the layer handle keeps its weights resident). */
+ * the layer handle keeps its weights resident).  From 128 rows, with m % 128 == 0 and
+ * n % 256 == 0, the product runs on the tcgen05 kernel of the layer's down projection. */
 RMOE_API rmoe_status rmoe_qmat_matmul(uint32_t ggml_type, const void* w_host, uint64_t w_nbytes,
                              uint32_t m, uint32_t n, const float* x, uint32_t rows, float* out,
                              void* stream);

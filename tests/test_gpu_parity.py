@@ -165,6 +165,23 @@ def test_qmat_matmul_parity(torch_cuda, t):
     assert rel_l2(got, want) <= REL_L2
 
 
+@pytest.mark.parametrize("t", [12, 14, 2, 8, 0])
+def test_qmat_matmul_many_rows_tensor_cores(torch_cuda, t):
+    """QMat::matmul at prefill row counts (the tcgen05 path: rows >= 128, m % 128 == 0,
+    n % 256 == 0), ragged last tile, against the dequantized sequential-f32 matvec per row."""
+    from rusty_engine_b200.moe import QMat
+
+    rng = np.random.default_rng(200 + t)
+    m, n, rows = 256, 1024, 600
+    el, _ = synth.BLOCK[t]
+    raw = synth.gen_blocks(rng, t, m * n // el, 0.001, 0.01)
+    x = rng.standard_normal((rows, n)).astype(np.float32)
+    got = QMat.from_bytes(t, raw, m, n).matmul(x, rows)
+    deq = O.dequant(t, raw.tobytes()).reshape(m, n)
+    want = np.stack([O.matvec(deq, m, n, x[r]) for r in range(rows)])
+    assert rel_l2(got, want) <= REL_L2
+
+
 # ---- the layer --------------------------------------------------------------------------------
 def check_layer(got, lw, x, out, ids, w, what):
     """Fast-router contract: ids up to reported near-ties, outputs on the tokens routed alike."""
