@@ -161,11 +161,27 @@ RMOE_API rmoe_status rmoe_dequant(uint32_t ggml_type, const void* src, uint64_t 
 /* QMat::matmul (src/qmat.rs:169-182) on the GPU: W[m x n] (GGUF bytes, host pointer, type t)
  * times X[rows x n] f32 -> Out[rows x m] f32.  X/Out are device pointers.  rows = 1 is
  * QMat::matvec (src/qmat.rs:80-82).  Weights are uploaded per call (a convenience path;
- * the layer handle keeps its weights resident).  From 128 rows, with m % 128 == 0 and
- * n % 256 == 0, the product runs on the tcgen05 kernel of the layer's down projection. */
+ * the layer handle and rmoe_qmat keep their weights resident), synchronising the stream.
+ * From 128 rows, with m % 128 == 0 and n % 256 == 0, the product runs on the tcgen05 kernel of
+ * the layer's down projection. */
 RMOE_API rmoe_status rmoe_qmat_matmul(uint32_t ggml_type, const void* w_host, uint64_t w_nbytes,
                              uint32_t m, uint32_t n, const float* x, uint32_t rows, float* out,
                              void* stream);
+
+/* A resident quantized matrix (QMat, src/qmat.rs:30-58): W[m x n] GGUF bytes (host pointer)
+ * uploaded once to `device`; m % 64 == 0, n a multiple of the type's block. */
+typedef struct rmoe_qmat rmoe_qmat;
+RMOE_API rmoe_status rmoe_qmat_create(uint32_t ggml_type, const void* w_host, uint64_t w_nbytes, uint32_t m,
+                             uint32_t n, int32_t device, rmoe_qmat** out);
+/* QMat::matmul (src/qmat.rs:169-308): Out[rows x m] = X[rows x n] . W^T, device pointers,
+ * stream-ordered, no synchronisation (the workspace grows with cudaMalloc when rows exceed
+ * every earlier call's, and the call synchronises the device then).  From 128 rows, with
+ * m % 128 == 0 and n % 256 == 0, the tcgen05 kernel; below, the mma.sync kernel. */
+RMOE_API rmoe_status rmoe_qmat_forward(rmoe_qmat* q, const float* x, uint32_t rows, float* out, void* stream);
+/* Device errors of the forwards so far (an x value beyond the fp16 range, a timed-out wait);
+ * synchronises with the device.  RMOE_ERR_DEVICE clears the recorded status. */
+RMOE_API rmoe_status rmoe_qmat_status(rmoe_qmat* q);
+RMOE_API void rmoe_qmat_destroy(rmoe_qmat* q);
 
 /* route() (src/moe.rs:120-125) over T rows of E logits (device pointers): ids/weights are
  * T x k in chosen order. */

@@ -53,7 +53,7 @@ EXPORTS = [
     "rmoe_layer_create", "rmoe_layer_forward", "rmoe_layer_routing", "rmoe_layer_logits", "rmoe_layer_destroy",
     "rmoe_last_error", "rmoe_dequant", "rmoe_qmat_matmul", "rmoe_route", "rmoe_ep_unique_id",
     "rmoe_ep_layer_create", "rmoe_build_info", "rmoe_layer_stage_ms", "rmoe_layer_forward_noalloc",
-    "rmoe_route_grouped",
+    "rmoe_route_grouped", "rmoe_qmat_create", "rmoe_qmat_forward", "rmoe_qmat_status", "rmoe_qmat_destroy",
     "rmoe_gguf_open", "rmoe_gguf_close", "rmoe_gguf_tensor", "rmoe_gguf_meta_uint", "rmoe_gguf_moe_layer_desc",
 ]
 
@@ -85,6 +85,11 @@ def load():
         L.rmoe_dequant.argtypes = [u32, vp, u64, vp, vp]
         L.rmoe_qmat_matmul.argtypes = [u32, vp, u64, u32, u32, vp, u32, vp, vp]
         L.rmoe_route.argtypes = [vp, u32, u32, u32, u32, vp, vp, vp]
+        L.rmoe_qmat_create.argtypes = [u32, vp, u64, u32, u32, i32, C.POINTER(vp)]
+        L.rmoe_qmat_forward.argtypes = [vp, vp, u32, vp, vp]
+        L.rmoe_qmat_status.argtypes = [vp]
+        L.rmoe_qmat_destroy.argtypes = [vp]
+        L.rmoe_qmat_destroy.restype = None
         L.rmoe_route_grouped.argtypes = [vp, vp, u32, u32, u32, u32, u32, i32, i32, vp, vp, vp]
         L.rmoe_ep_unique_id.argtypes = [vp]
         L.rmoe_ep_layer_create.argtypes = [C.POINTER(LayerDesc), i32, i32, vp, C.POINTER(vp)]

@@ -717,65 +717,4 @@ rmoe_status rmoe_route_grouped(const float* logits, const float* bias, uint32_t 
     return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "grouped route launch");
 }
 
-rmoe_status rmoe_qmat_matmul(uint32_t t, const void* w_host, uint64_t w_nbytes, uint32_t m, uint32_t n, const float* x,
-                             uint32_t rows, float* out, void* stream) {
-    if (m % 64) return fail(RMOE_ERR_UNSUPPORTED, "m %u must be a multiple of 64", m);
-    rmoe_tensor tt{t, w_host, w_nbytes, {n, m, 1}};
-    Owned own;
-    DevMat W;
-    rmoe_status s = upload_mat(tt, m, n, 1, "qmat", own, W);
-    if (s) return s;
-    if (rows == 0) return RMOE_OK;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // many rows: the tcgen05 down-product kernel (256-row tiles, weights decoded once per tile
-    // and 128-row block); few rows: the mma.sync kernel (16-row tiles)
-    const bool tc = rows >= 128 && m % 128 == 0 && n % 256 == 0;
-    const int NT = tc ? tc_tile_rows() : 16;
-    const int ntiles = (int)((rows + NT - 1) / NT);
-    __half* xb = (__half*)own.alloc((size_t)rows * n * 2);
-    int* rowtok = (int*)own.alloc((size_t)rows * 4);
-    int* rowslot = (int*)own.alloc((size_t)rows * 4);
-    int8_t* hexp = (int8_t*)own.alloc((size_t)rows * (n / HBLK));
-    int* rexp = (int*)own.alloc((size_t)rows * 4);
-    int4* tiles = (int4*)own.alloc((size_t)ntiles * 16);
-    int* nt = (int*)own.alloc(16);
-    unsigned* status = (unsigned*)own.alloc(16);
-    if (!xb || !rowtok || !rowslot || !tiles || !nt || !hexp || !rexp || !status) return fail(RMOE_ERR_OOM, "qmat workspace");
-    cudaMemsetAsync(hexp, 0, (size_t)rows * (n / HBLK), st);
-    cudaMemsetAsync(rexp, 0, (size_t)rows * 4, st);
-    cudaMemsetAsync(rowslot, 0, (size_t)rows * 4, st);
-    cudaMemsetAsync(status, 0, 16, st);
-    std::vector<int4> ht(ntiles);
-    std::vector<int> hr(rows);
-    for (uint32_t i = 0; i < rows; i++) hr[i] = (int)i;
-    for (int i = 0; i < ntiles; i++) ht[i] = make_int4(0, i * NT, (int)std::min<uint32_t>(NT, rows - i * NT), 0);
-    cudaMemcpy(rowtok, hr.data(), rows * 4, cudaMemcpyHostToDevice);
-    cudaMemcpy(tiles, ht.data(), ntiles * 16, cudaMemcpyHostToDevice);
-    cudaMemcpy(nt, &ntiles, 4, cudaMemcpyHostToDevice);
-    cudaError_t e = launch_f32_to_f16(x, xb, (uint64_t)rows * n, st);
-    if (e != cudaSuccess) return cuda_fail(e, "convert");
-    GroupedParams gp{};
-    gp.down = W;
-    gp.sdown.type = -1;
-    gp.H = (int)m; gp.I = (int)n; gp.E = 1; gp.k = 1;
-    gp.h = xb; gp.hexp = hexp; gp.rowexp = rexp; gp.row_tok = rowtok; gp.row_slot = rowslot; gp.tiles = tiles;
-    gp.n_tiles = nt; gp.y = out; gp.status = status;
-    if (tc) {
-        TcMaps maps;
-        memset(&maps, 0, sizeof maps);
-        if (!make_weight_maps(W, maps.w[0][0]) || !make_rows_map(xb, rows, n, maps.b))
-            return fail(RMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the qmat operands");
-        if ((e = launch_tc_down(gp, maps, ntiles, st)) != cudaSuccess) return cuda_fail(e, "qmat launch");
-        unsigned hs = 0;
-        if ((e = cudaMemcpyAsync(&hs, status, 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
-            (e = cudaStreamSynchronize(st)) != cudaSuccess)
-            return cuda_fail(e, "qmat");
-        if (hs) return fail(RMOE_ERR_DEVICE, "qmat: device status 0x%x", hs);
-        return RMOE_OK;
-    }
-    if ((e = launch_small_down(gp, ntiles, NT, st)) != cudaSuccess) return cuda_fail(e, "qmat launch");
-    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(e, "qmat");
-    return RMOE_OK;
-}
-
 }  // extern "C"

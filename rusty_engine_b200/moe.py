@@ -207,17 +207,50 @@ class QMat:
     def cols(self) -> int:
         return self.n
 
+    def _handle(self):
+        """The resident device copy (rmoe_qmat_create), made on first use."""
+        h = getattr(self, "_h", None)
+        if h is None:
+            _require_cuda()
+            h = C.c_void_p()
+            b = self.bytes
+            _call(_lib.load().rmoe_qmat_create(self.ggml_type, b.ctypes.data, b.nbytes, self.m, self.n,
+                                               torch.cuda.current_device(), C.byref(h)))
+            self._h = h
+        return h
+
+    def matmul_device(self, x, out=None, *, stream=None):
+        """X [rows, n] f32 cuda tensor -> [rows, m] on the device (rmoe_qmat_forward: resident
+        weights, stream-ordered, no synchronisation)."""
+        rows = x.shape[0]
+        if x.shape[1] != self.n:
+            raise ValueError("matmul: X rows x n")
+        if out is None:
+            out = torch.empty((rows, self.m), dtype=torch.float32, device=x.device)
+        s = C.c_void_p(stream.cuda_stream) if stream is not None else _stream()
+        _call(_lib.load().rmoe_qmat_forward(self._handle(), x.data_ptr(), rows, out.data_ptr(), s))
+        return out
+
     def matmul(self, x, rows: int) -> np.ndarray:
         """W[m x n] . X[rows x n] -> [rows x m] (QMat::matmul, src/qmat.rs:169-182)."""
         _require_cuda()
         xd = _dev_f32(x).reshape(-1)
         if xd.numel() != rows * self.n:
             raise ValueError("matmul: X rows x n")
-        out = torch.empty((max(rows, 1), self.m), dtype=torch.float32, device="cuda")
-        b = self.bytes
-        _call(_lib.load().rmoe_qmat_matmul(self.ggml_type, b.ctypes.data, b.nbytes, self.m, self.n, xd.data_ptr(), rows,
-                                           out.data_ptr(), _stream()))
-        return out[:rows].cpu().numpy()
+        if rows == 0:
+            return np.zeros((0, self.m), np.float32)
+        out = self.matmul_device(xd.reshape(rows, self.n))
+        torch.cuda.synchronize()
+        _call(_lib.load().rmoe_qmat_status(self._handle()))
+        return out.cpu().numpy()
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            try:
+                _lib.load().rmoe_qmat_destroy(h)
+            except Exception:
+                pass
 
     def matvec(self, x) -> np.ndarray:
         return self.matmul(x, 1)[0]

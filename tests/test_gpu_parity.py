@@ -182,6 +182,22 @@ def test_qmat_matmul_many_rows_tensor_cores(torch_cuda, t):
     assert rel_l2(got, want) <= REL_L2
 
 
+def test_qmat_resident_handle_reuse(torch_cuda):
+    """One resident QMat (rmoe_qmat_create) driven with growing and shrinking row counts,
+    across both kernels: every product equals a fresh handle's, bit for bit."""
+    from rusty_engine_b200.moe import QMat
+
+    rng = np.random.default_rng(7)
+    m, n = 256, 1024
+    raw = synth.gen_blocks(rng, 12, m * n // 256, 0.001, 0.01)
+    q = QMat.from_bytes(12, raw, m, n)
+    for rows in (5, 300, 130, 1, 700, 64):
+        x = rng.standard_normal((rows, n)).astype(np.float32)
+        a = q.matmul(x, rows)
+        b = QMat.from_bytes(12, raw, m, n).matmul(x, rows)
+        np.testing.assert_array_equal(a, b)
+
+
 # ---- the layer --------------------------------------------------------------------------------
 def check_layer(got, lw, x, out, ids, w, what):
     """Fast-router contract: ids up to reported near-ties, outputs on the tokens routed alike."""
