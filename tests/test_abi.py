@@ -122,3 +122,37 @@ def test_forward_null_layer_invalid():
 def test_route_rejects_large_k():
     L = _lib.load()
     assert L.rmoe_route(None, 1, 64, 40, 0, None, None, None) == _lib.RMOE_ERR_UNSUPPORTED
+
+
+def test_route_grouped_host_validation():
+    """rmoe_route_grouped rejects unsupported shapes on the host, before any device call."""
+    L = _lib.load()
+    ids = np.zeros(64, np.uint32)
+    w = np.zeros(64, np.float32)
+    lg = np.zeros(64, np.float32)
+    cases = [
+        (dict(E=1024, k=8, ng=8, nbias=0), _lib.RMOE_ERR_UNSUPPORTED),  # E > 512
+        (dict(E=64, k=0, ng=8, nbias=0), _lib.RMOE_ERR_UNSUPPORTED),  # k = 0
+        (dict(E=64, k=33, ng=8, nbias=0), _lib.RMOE_ERR_UNSUPPORTED),  # k > 32
+        (dict(E=512, k=8, ng=65, nbias=0), _lib.RMOE_ERR_UNSUPPORTED),  # more than 64 groups
+        (dict(E=64, k=8, ng=8, nbias=4), _lib.RMOE_ERR_INVALID),  # a bias length with no bias
+    ]
+    for c, want in cases:
+        st = L.rmoe_route_grouped(lg.ctypes.data, None, c["nbias"], 1, c["E"], c["k"], c["ng"], 4, 1,
+                                  ids.ctypes.data, w.ctypes.data, None)
+        assert st == want, (c, L.rmoe_last_error())
+    # n_groups is clamped to E (n_groups.max(1).min(n), src/moe.rs:211): 65 groups of 32 experts is legal
+    assert L.rmoe_route_grouped(lg.ctypes.data, None, 0, 0, 32, 8, 65, 4, 1, ids.ctypes.data, w.ctypes.data,
+                                None) == _lib.RMOE_OK  # T = 0: nothing to do
+
+
+def test_qmat_host_validation():
+    L = _lib.load()
+    h = C.c_void_p()
+    raw = np.zeros(18 * 32, np.uint8)
+    st = L.rmoe_qmat_create(2, raw.ctypes.data, raw.nbytes, 32, 1024, 0, C.byref(h))
+    assert st == _lib.RMOE_ERR_UNSUPPORTED and b"multiple of 64" in L.rmoe_last_error()
+    assert L.rmoe_qmat_create(2, raw.ctypes.data, raw.nbytes, 64, 256, 0, None) == _lib.RMOE_ERR_INVALID
+    assert L.rmoe_qmat_forward(None, None, 4, None, None) == _lib.RMOE_ERR_INVALID
+    assert L.rmoe_qmat_status(None) == _lib.RMOE_ERR_INVALID
+    L.rmoe_qmat_destroy(None)  # a null handle is ignored
