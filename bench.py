@@ -1,17 +1,23 @@
 """MoE-layer throughput on B200: tokens/s of rusty-engine's moe_layer_forward hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c1|c3b1|c3b8|c3b32|c3b64|c5]
-                    [--impl ours|reference]
+                    [--impl ours|reference] [--no-cpu-baseline] [--no-sub]
 
 One step = one forward of the whole MoE layer (router, dispatch, gate/up+SwiGLU, down,
 combine) over one batch of synthetic tokens already resident in HBM; the timed region is
 bracketed by a barrier + synchronize, each step by CUDA events on the forward's stream, and
 L2 is flushed between steps outside the events (a 256 MiB write).  ``e2e`` is the same metric
 through the public host-buffer entry point (pinned host x in, host out, copies inside).
-``--impl reference`` times the CPU restatement of rusty-engine's pooled path (oracle/, all
-host threads) on the same config.  N > 1 runs one rank per GPU (torchrun); each rank serves
-its own batch (weak scaling) through an expert-parallel layer: experts split evenly over the
-ranks, tokens exchanged with NCCL (rmoe_ep_layer_create).
+
+N = 1 (no torchrun): the headline is config 2 (4096-token prefill); the same line carries
+``sub`` results for config 3 (decode batches 1, 8, 32, 64) and config 5 (the 235B-shaped layer,
+8192 tokens, Zipf(1.1) expert load), each with its roofline fraction.
+N > 1 (torchrun, one rank per GPU): config 5 as an expert-parallel layer, strong scaling: the
+8192 tokens are split evenly over the ranks (8192 / N each), experts dealt round-robin, tokens
+exchanged with NCCL; value = 8192 / (max over ranks of the step time).
+
+``--impl reference`` times the CPU restatement of rusty-engine's pooled path (oracle/, all host
+threads) on the same config: the whole 4096-token batch per step for config 2.
 """
 from __future__ import annotations
 
@@ -28,6 +34,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+C5_TOKENS = 8192
+
 CONFIGS = {
     # name: (builder, tokens, workload label)
     "c1": ("config_c1", 128, "c1 moe_layer_forward H1024 E16 k4 I512 Q4_0, 128 tokens"),
@@ -36,9 +44,11 @@ CONFIGS = {
     "c3b8": ("config_c2", 8, "c3 Qwen3-30B-A3B MoE layer decode batch 8"),
     "c3b32": ("config_c2", 32, "c3 Qwen3-30B-A3B MoE layer decode batch 32"),
     "c3b64": ("config_c2", 64, "c3 Qwen3-30B-A3B MoE layer decode batch 64"),
-    "c5": ("config_c5", 8192, "c5 Qwen3-235B-A22B MoE layer H4096 E128 k8 I1536 Q4_K/Q6_K, 8192 tokens, "
-                              "Zipf(1.1) expert load"),
+    "c5": ("config_c5", C5_TOKENS, "c5 Qwen3-235B-A22B MoE layer H4096 E128 k8 I1536 Q4_K/Q6_K, 8192 tokens, "
+                                   "Zipf(1.1) expert load"),
 }
+# reference-arm tokens per step: the whole batch, except config 5 (about 20 s of CPU per pass)
+REF_SAMPLE = {"c5": 1024}
 
 
 def kernels_per_forward(lw, T, world=1, rows_local=None):
@@ -66,6 +76,7 @@ NCU_TRAFFIC = {
     ("c3b1", "gateup"): 15.762e6,
     ("c3b1", "down"): 10.372e6,
 }
+STAGES = ["route_dispatch", "gateup", "down", "combine"]
 
 
 def load_peaks():
@@ -138,6 +149,20 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples), "src": "nvml, 2 ms poll"}
 
 
+def workload(cfg_name):
+    """(layer weights, the config's whole token batch) -- seeded synthetic data of the shapes
+    and distributions the config names."""
+    from rusty_engine_b200 import synth
+
+    builder, T, label = CONFIGS[cfg_name]
+    lw = getattr(synth, builder)()
+    if cfg_name == "c5":
+        lw, x = synth.zipf_workload(lw, T, seed=1)
+    else:
+        x = synth.activations(T, lw.H, seed=1)
+    return lw, x, label
+
+
 def cpu_baseline(cfg_name, lw, x, budget_s=15.0):
     """The oracle's pooled restatement of rusty-engine's CPU path on all host threads."""
     from oracle import oracle as O
@@ -173,6 +198,166 @@ def algorithmic(lw, T, ids=None):
     return flops_gateup, flops_down, bytes_total, gu_bytes, touched
 
 
+def reference_arm(args, rank, world):
+    """rusty-engine's pooled CPU path (C restatement, all host threads) on our arm's config:
+    rank 0 only; the whole batch per step (config 5: a 1024-token sample)."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    cfg = args.config if world == 1 else "c5"
+    lw, x, label = workload(cfg)
+    T = x.shape[0]
+    sample = min(T, REF_SAMPLE.get(cfg, T))
+    xs = np.ascontiguousarray(x[:sample])
+    threads = len(os.sched_getaffinity(0))
+    O.pool_init(threads)
+    for _ in range(args.warmup):
+        O.moe_layer_pooled(xs, lw)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.moe_layer_pooled(xs, lw)
+        times.append(time.perf_counter() - t0)
+    ms = statistics.mean(times) * 1e3
+    val = sample / (ms / 1e3)
+    what = "all" if sample == T else f"a {sample}-token sample of the"
+    print(json.dumps({
+        "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": val, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "min_ms_per_step": min(times) * 1e3,
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": label, "tokens": T, "sample_tokens": sample},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{what} {T} tokens per step (C restatement of the pooled AVX2 path)"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+class Bench:
+    """Timing helpers on one rank's GPU."""
+
+    def __init__(self, torch, dist):
+        self.torch, self.dist = torch, dist
+        self.flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+        self.stream = torch.cuda.current_stream()
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, v):
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def steps(self, layer, x, out, steps, warmup, sampler=None):
+        """Mean ms of `steps` forwards (CUDA events on the stream, L2 flushed in between)."""
+        torch = self.torch
+        for _ in range(warmup):
+            layer.forward(x, out)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        self.barrier()
+        if sampler:
+            sampler.start()
+        for i in range(steps):
+            self.flush.fill_(float(i))
+            starts[i].record(self.stream)
+            layer.forward(x, out)
+            ends[i].record(self.stream)
+        self.barrier()
+        clocks = sampler.stop() if sampler else None
+        ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+        return ms, clocks
+
+    def stages(self, layer, x, out, n):
+        """Per-stage ms from separate forwards (the events between stages serialise kernels
+        that otherwise overlap their launch through programmatic dependent launch)."""
+        from rusty_engine_b200 import _lib
+
+        stage = np.zeros(4)
+        for i in range(n):
+            self.flush.fill_(float(i))
+            layer.forward(x, out, flags=_lib.FLAG_STAGE_TIMING)
+            stage += np.array(layer.stage_ms())
+        return stage / n
+
+    def e2e(self, layer, x_np, n):
+        """Mean s of `n` host-buffer forwards (pinned x in, host out, copies inside the call)."""
+        import ctypes as C
+
+        from rusty_engine_b200 import _lib
+
+        torch = self.torch
+        xh = torch.from_numpy(x_np).pin_memory()
+        oh = torch.empty_like(xh).pin_memory()
+        L = _lib.load()
+        sptr = C.c_void_p(self.stream.cuda_stream)
+        T = x_np.shape[0]
+        for _ in range(2):
+            _lib.check(L.rmoe_layer_forward(layer._h, xh.data_ptr(), T, oh.data_ptr(), sptr, _lib.FLAG_HOST_IO))
+        self.barrier()
+        times = []
+        for _ in range(n):
+            self.flush.fill_(0.0)
+            torch.cuda.synchronize()
+            s0 = time.perf_counter()
+            _lib.check(L.rmoe_layer_forward(layer._h, xh.data_ptr(), T, oh.data_ptr(), sptr, _lib.FLAG_HOST_IO))
+            times.append(time.perf_counter() - s0)
+        return statistics.mean(times)
+
+
+def roofline_single(lw, T, ids, stage, peaks, cfg):
+    """Roofline of the dominant kernel (by stage time): tensor FLOPs for prefill (T >= 256),
+    HBM bytes for decode."""
+    fg, fd, nbytes, gu_bytes, touched = algorithmic(lw, T, ids)
+    dom = int(np.argmax(stage))
+    if T >= 256:
+        work = {1: fg, 2: fd}.get(dom, fg)
+        ach = work / (stage[dom] / 1e3) / 1e12
+        return {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": ach / peaks["bf16_tflops"], "traffic": NCU_TRAFFIC.get((cfg, STAGES[dom])),
+                "traffic_unit": "bytes per launch (ncu)", "kernel": STAGES[dom],
+                "peak_src": peaks["src"] + " burst bf16"}, touched
+    gb = (gu_bytes if dom == 1 else nbytes - gu_bytes) / (stage[dom] / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": gb, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": gb / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC.get((cfg, STAGES[dom])),
+            "traffic_unit": "bytes per launch (ncu)", "kernel": STAGES[dom],
+            "peak_src": peaks["src"] + " copy"}, touched
+
+
+def sub_result(B, lw, x_np, cfg, steps, warmup, peaks):
+    """One config's numbers on this GPU (N = 1 line's ``sub``)."""
+    from rusty_engine_b200 import _lib
+    from rusty_engine_b200.moe import MoELayer
+
+    torch = B.torch
+    T = x_np.shape[0]
+    layer = MoELayer(lw, device=torch.cuda.current_device())
+    x = torch.from_numpy(x_np).cuda()
+    out = torch.empty_like(x)
+    ms, _ = B.steps(layer, x, out, steps, warmup)
+    layer.forward(x, out, flags=_lib.FLAG_ROUTING_OUT)
+    torch.cuda.synchronize()
+    ids, _ = layer.routing(T)
+    stage = B.stages(layer, x, out, max(3, min(steps, 10)))
+    roof, touched = roofline_single(lw, T, ids, stage, peaks, cfg)
+    layer.close()
+    fg, fd, nbytes, _, _ = algorithmic(lw, T, ids)
+    res = {"workload": CONFIGS[cfg][2], "tokens": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+           "experts_touched": int(touched), "stage_ms": {n: float(v) for n, v in zip(STAGES, stage)},
+           "roofline": roof, "steps": steps, "warmup": warmup}
+    if T >= 256:
+        res["layer_tensor_frac"] = (fg + fd) / (ms / 1e3) / 1e12 / peaks["bf16_tflops"]
+    else:
+        res["layer_hbm_frac"] = nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -181,6 +366,7 @@ def main():
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true", help="N = 1: skip the config 3 / config 5 sub-results")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -189,38 +375,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
-    from rusty_engine_b200 import synth
-
-    builder, T, label = CONFIGS[args.config]
-
     if args.impl == "reference":
-        if rank != 0:
-            return
-        lw = getattr(synth, builder)()
-        x = synth.activations(T, lw.H)
-        from oracle import oracle as O
-
-        threads = len(os.sched_getaffinity(0))
-        O.pool_init(threads)
-        sample = min(T, 512)
-        for _ in range(max(1, min(args.warmup, 1))):
-            O.moe_layer_pooled(x[:sample], lw)
-        times = []
-        for _ in range(args.steps):
-            t0 = time.perf_counter()
-            O.moe_layer_pooled(x[:sample], lw)
-            times.append(time.perf_counter() - t0)
-        ms = statistics.mean(times) * 1e3
-        val = sample / (ms / 1e3)
-        print(json.dumps({
-            "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": val, "unit": "tokens/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": label, "tokens": T, "sample_tokens": sample},
-            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": f"{sample} of {T} tokens per step (C restatement of the pooled AVX2 path)"},
-            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }), flush=True)
+        reference_arm(args, rank, world)
         return
 
     import torch
@@ -238,137 +394,84 @@ def main():
     from rusty_engine_b200 import _lib
     from rusty_engine_b200.moe import MoELayer
 
-    lw = getattr(synth, builder)()
-    if args.config == "c5":
-        lw, x_np = synth.zipf_workload(lw, T, seed=1 + rank)
-    else:
-        x_np = synth.activations(T, lw.H, seed=1 + rank)
+    cfg = args.config if world == 1 else "c5"
+    lw, x_all, label = workload(cfg)
     if world > 1:
+        # strong scaling: this rank's share of the config's whole batch
+        T_all = x_all.shape[0]
+        per = (T_all + world - 1) // world
+        x_np = np.ascontiguousarray(x_all[rank * per:min(T_all, (rank + 1) * per)])
         from rusty_engine_b200.moe import ep_unique_id
 
         box = [ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         layer = MoELayer.expert_parallel(lw, rank, world, box[0], device=local)
     else:
+        T_all = x_all.shape[0]
+        x_np = x_all
         layer = MoELayer(lw, device=local)
+    T = x_np.shape[0]
+    B = Bench(torch, dist)
     x = torch.from_numpy(x_np).cuda()
     out = torch.empty_like(x)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
-
-    def flush_l2(v):
-        flush.fill_(v)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for _ in range(args.warmup):
-        layer.forward(x, out)
     layer.forward(x, out, flags=_lib.FLAG_ROUTING_OUT)
     torch.cuda.synchronize()
     ids, _ = layer.routing(T)
 
     sampler = ClockSampler(local)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    stage = np.zeros(4)
-    barrier()
-    sampler.start()
-    for i in range(args.steps):
-        flush_l2(float(i))
-        starts[i].record(stream)
-        layer.forward(x, out)
-        ends[i].record(stream)
-    barrier()
-    clocks = sampler.stop()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    ms = statistics.mean(step_ms)
-    # per-stage split, from separate forwards: the events between stages serialise kernels
-    # that otherwise overlap their launch (programmatic dependent launch)
-    if world == 1:
-        n_st = max(3, min(args.steps, 10))
-        for i in range(n_st):
-            flush_l2(float(i))
-            layer.forward(x, out, flags=_lib.FLAG_STAGE_TIMING)
-            stage += np.array(layer.stage_ms())
-        stage /= n_st
-    barrier()
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms, clocks = B.steps(layer, x, out, args.steps, args.warmup, sampler)
+    stage = B.stages(layer, x, out, max(3, min(args.steps, 10))) if world == 1 else None
+    B.barrier()
+    ms = B.max_over_ranks(ms)
+    e2e_s = B.max_over_ranks(B.e2e(layer, x_np, max(3, min(args.steps, 10))))
+    refined = layer.router_refined()
+    layer.close()
 
-    # end to end: pinned host x in, host out, copies inside the timed call
-    xh = torch.from_numpy(x_np).pin_memory()
-    oh = torch.empty_like(xh).pin_memory()
-    import ctypes as C
-
-    L = _lib.load()
-    sptr = C.c_void_p(stream.cuda_stream)
-    for _ in range(2):
-        _lib.check(L.rmoe_layer_forward(layer._h, xh.data_ptr(), T, oh.data_ptr(), sptr, _lib.FLAG_HOST_IO))
-    barrier()
-    e2e_steps = max(3, min(args.steps, 10))
-    e2e_times = []
-    for _ in range(e2e_steps):
-        flush_l2(0.0)
-        torch.cuda.synchronize()
-        s0 = time.perf_counter()
-        _lib.check(L.rmoe_layer_forward(layer._h, xh.data_ptr(), T, oh.data_ptr(), sptr, _lib.FLAG_HOST_IO))
-        e2e_times.append(time.perf_counter() - s0)
-    e2e_s = statistics.mean(e2e_times)
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    peaks = load_peaks()
+    subs = {}
+    if world == 1 and not args.no_sub and cfg == "c2":
+        for b in (1, 8, 32, 64):
+            subs[f"c3b{b}"] = sub_result(B, lw, x_all[:b].copy(), f"c3b{b}", args.steps, args.warmup, peaks)
+        lw5, x5, _ = workload("c5")
+        subs["c5"] = sub_result(B, lw5, x5, "c5", args.steps, args.warmup, peaks)
+        del lw5, x5
 
     if rank == 0:
-        peaks = load_peaks()
-        fg, fd, nbytes, gu_bytes, touched = algorithmic(lw, T, ids)
-        value = T * world / (ms / 1e3)
-        # dominant kernel by measured time share
-        names = ["route_dispatch", "gateup", "down", "combine"]
-        dom = int(np.argmax(stage))
+        lwr = lw
+        fg, fd, nbytes, gu_bytes, touched = algorithmic(lwr, T_all if world > 1 else T, None if world > 1 else ids)
+        value = T_all / (ms / 1e3)
         if world > 1:
-            # per rank: its share of the expert products over the whole step (exchanges included)
-            ach = (fg + fd) / (ms / 1e3) / 1e12
+            # the whole job: expert products of all 8192 tokens over the step, per GPU
+            ach = (fg + fd) / (ms / 1e3) / 1e12 / world
             roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                     "frac": ach / peaks["bf16_tflops_sustained"], "traffic": None,
-                    "kernel": "whole expert-parallel step per rank (router, exchanges, experts, combine)",
+                    "kernel": "whole expert-parallel step per GPU (router, exchanges, experts, combine)",
                     "peak_src": peaks["src"] + " sustained bf16"}
-        elif T >= 256:
-            work = {1: fg, 2: fd}.get(dom, fg)
-            ach = work / (stage[dom] / 1e3) / 1e12
-            roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                    "frac": ach / peaks["bf16_tflops"], "traffic": NCU_TRAFFIC.get((args.config, names[dom])),
-                    "traffic_unit": "bytes per launch (ncu)", "kernel": names[dom],
-                    "peak_src": peaks["src"] + " burst bf16"}
         else:
-            gb = (gu_bytes if dom == 1 else nbytes - gu_bytes) / (stage[dom] / 1e3) / 1e9
-            roof = {"bound": "hbm", "achieved": gb, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": gb / peaks["hbm_gbs"], "traffic": NCU_TRAFFIC.get((args.config, names[dom])),
-                    "traffic_unit": "bytes per launch (ncu)", "kernel": names[dom],
-                    "peak_src": peaks["src"] + " copy"}
+            roof, touched = roofline_single(lwr, T, ids, stage, peaks, cfg)
         line = {
             "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp16-mma/f32-acc/f32-router", "data": "synthetic",
-            "config": {"workload": label, "tokens_per_gpu": T, "experts_touched": int(touched),
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "fp16-mma/f32-acc/f32-router", "data": "synthetic",
+            "config": {"workload": label, "tokens_total": T_all, "tokens_per_gpu": T,
+                       "experts_touched": int(touched),
                        "l2": "flushed between steps (256 MiB write outside the events)",
                        "parallelism": f"ep{world}" if world > 1 else "single"},
-            "stage_ms": {n: float(v) for n, v in zip(names, stage)},
             "roofline": roof,
-            "e2e": {"value": T * world / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * lw.H * 4,
-                    "d2h_bytes_per_step": T * lw.H * 4},
-            "gpu_launches": kernels_per_forward(lw, T, world, T) * args.steps,
+            "e2e": {"value": T_all / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * lwr.H * 4,
+                    "d2h_bytes_per_step": T * lwr.H * 4},
+            "gpu_launches": kernels_per_forward(lwr, T, world, T) * args.steps,
+            "router_refined_tokens": refined,
             "clocks": clocks,
         }
+        if stage is not None:
+            line["stage_ms"] = {n: float(v) for n, v in zip(STAGES, stage)}
+        if subs:
+            line["sub"] = subs
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.config, lw, x_np)
+            line["cpu_baseline"] = cpu_baseline(cfg, lwr, x_np)
         print(json.dumps(line), flush=True)
-    layer.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -92,9 +92,10 @@ enum {
                                           f32 sums, src/moe.rs:271-277); without it the logits
                                           are sums in another order (FFMA, or from 1024 tokens
                                           tensor-core products of hi/lo-split fp32 operands)
-                                          within the f32 summation error of the exact sums, so
-                                          top-k can differ from the reference only at near-ties
-                                          of that size */
+                                          within the f32 summation error of the exact sums; a
+                                          token whose best k + 1 scores hold a near-tie of that
+                                          size has those logits rescored with the sequential
+                                          sums, so top-k ids match the reference either way */
 };
 
 /* Create a layer handle: validates the description on the host, copies router and expert
@@ -125,9 +126,18 @@ RMOE_API rmoe_status rmoe_layer_forward(rmoe_layer* layer, const float* x, uint3
  * H 2048 / E 128 / k 8 / I 768 layer).  The first call on a device looks up the array's
  * address (cudaGetSymbolAddress), so make that first call before any stream capture.  Every
  * call on a device shares the array: calls that overlap on the GPU race on it.  It does not
- * update what rmoe_layer_routing / rmoe_layer_logits / rmoe_layer_stage_ms report. */
+ * update what rmoe_layer_routing / rmoe_layer_logits / rmoe_layer_stage_ms report; its device
+ * errors are read with rmoe_noalloc_status. */
 RMOE_API rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* layer, const float* x, uint32_t T, float* out,
                                                 void* stream);
+
+/* Device errors of the last rmoe_layer_forward_noalloc call on `device` (an x value beyond the
+ * fp16 range, a tile-list overflow), which that call cannot report itself since it does not
+ * wait for its kernels.  Synchronises the device and reads the status word kept in the static
+ * scratch, allocating nothing; RMOE_ERR_DEVICE (then the word is cleared) when one is set.
+ * The next noalloc call on the device clears the word, so read it in between.  No counterpart
+ * in the reference (its CPU path has no device errors). */
+RMOE_API rmoe_status rmoe_noalloc_status(int32_t device);
 
 /* Routing of the last forward with RMOE_FLAG_ROUTING_OUT: expert ids (T x k, chosen order)
  * and weights (T x k), copied to host buffers.  Mirrors route() (src/moe.rs:120-125). */
@@ -137,6 +147,13 @@ RMOE_API rmoe_status rmoe_layer_routing(rmoe_layer* layer, uint32_t T, uint32_t*
  * last forward that had RMOE_FLAG_ROUTING_OUT, copied to a host buffer.  A debugging aid with no counterpart in
  * the reference (its logits never leave moe_layer_forward). */
 RMOE_API rmoe_status rmoe_layer_logits(rmoe_layer* layer, uint32_t T, float* logits);
+
+/* Tokens whose fast-router top-k met a near-tie since the last call (or since the handle's
+ * workspace was last sized), read and reset; synchronises the device.  For such a token the
+ * logits of the experts around its k-th pick are rescored with moe::matvec's sequential f32
+ * sums (src/moe.rs:271-277) before top-k, so its ids are the reference's.  A debugging aid
+ * with no counterpart in the reference. */
+RMOE_API rmoe_status rmoe_layer_router_refined(rmoe_layer* layer, uint32_t* count);
 
 /* Stage durations of the last forward that had RMOE_FLAG_STAGE_TIMING, in milliseconds,
  * from CUDA events recorded on the forward's stream: ms[0] route+dispatch, ms[1] gate/up

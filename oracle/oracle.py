@@ -87,6 +87,29 @@ def lib():
     return L
 
 
+# Layer-output parity bar: relative L2 <= 5e-3 and max-abs <= 2e-2.  The
+# absolute bar was set for outputs of the config-1 scale (RMS about 2); above that scale it is
+# held at the same size relative to the output: max-abs <= 1e-2 * RMS.  One rule for every test
+# and smoke(), continuous at RMS = 2.
+REL_L2 = 5e-3
+MAX_ABS = 2e-2
+MAX_ABS_RMS_REF = 2.0
+
+
+def max_abs_bound(rms: float) -> float:
+    return MAX_ABS * max(1.0, rms / MAX_ABS_RMS_REF)
+
+
+def layer_errors(got, want):
+    """(rel-L2, max-abs, output RMS) of a layer output against the oracle's."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    rms = float(np.sqrt(np.mean(want ** 2))) if want.size else 0.0
+    rel = float(np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30))
+    mx = float(np.abs(got - want).max()) if want.size else 0.0
+    return rel, mx, rms
+
+
 class OracleError(Exception):
     """Mirrors rusty-engine's EngineError{message} for the dequant dispatch."""
 

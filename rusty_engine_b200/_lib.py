@@ -55,6 +55,7 @@ EXPORTS = [
     "rmoe_ep_layer_create", "rmoe_build_info", "rmoe_layer_stage_ms", "rmoe_layer_forward_noalloc",
     "rmoe_route_grouped", "rmoe_qmat_create", "rmoe_qmat_forward", "rmoe_qmat_status", "rmoe_qmat_destroy",
     "rmoe_gguf_open", "rmoe_gguf_close", "rmoe_gguf_tensor", "rmoe_gguf_meta_uint", "rmoe_gguf_moe_layer_desc",
+    "rmoe_layer_router_refined", "rmoe_noalloc_status",
 ]
 
 NOALLOC_SCRATCH_BYTES = 8 << 20  # RMOE_NOALLOC_SCRATCH_BYTES
@@ -79,6 +80,8 @@ def load():
         L.rmoe_layer_routing.argtypes = [vp, u32, vp, vp]
         L.rmoe_layer_logits.argtypes = [vp, u32, vp]
         L.rmoe_layer_stage_ms.argtypes = [vp, vp]
+        L.rmoe_layer_router_refined.argtypes = [vp, vp]
+        L.rmoe_noalloc_status.argtypes = [i32]
         L.rmoe_layer_destroy.argtypes = [vp]
         L.rmoe_layer_destroy.restype = None
         L.rmoe_last_error.restype = C.c_char_p

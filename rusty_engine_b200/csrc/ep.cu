@@ -224,6 +224,7 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     rp.gate = (int)L->gate_kind; rp.xb = P.xb; rp.logits = P.logits; rp.topk_id = P.topk_id; rp.topk_w = P.topk_w;
     rp.logits_part = rp.exact ? nullptr : P.logits_part;
     rp.status = P.status; rp.ticket = P.ticket;
+    rp.router_wmax = L->router_wmax; rp.refined = P.status + 1;
     if (T && (e = launch_router_topk(rp, s)) != cudaSuccess) return cuda_fail(e, "ep router launch");
     // 2. plan
     ep_plan_kernel<<<G, 1024, 0, s>>>(P.topk_id, (int)T, k, El, G, P.pos, P.cnt);
@@ -302,6 +303,8 @@ rmoe_status ep_forward_host(rmoe_layer* L, const float* x, uint32_t T, float* ou
     if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "forward");
     return RMOE_OK;
 }
+
+unsigned* ep_status(rmoe_layer* L) { return L->ep ? L->ep->status : nullptr; }
 
 void ep_free(rmoe_layer* L) {
     delete L->ep;

@@ -69,6 +69,9 @@ struct RouteParams {
     int given;              // 1: topk_id / topk_w are filled in already (x and logits unused);
                             // ids >= E are empty picks and get no row
     int exact;              // 1: logits bit-identical to moe::matvec (sequential sums)
+    float router_wmax;      // max over experts of ||router row||_2 (sizes the fast router's
+                            // near-tie window; 0 turns the refinement off)
+    unsigned int* refined;  // optional counter of tokens whose near-tie logits were rescored
 };
 
 // Grouped expert products over the expert-sorted rows.

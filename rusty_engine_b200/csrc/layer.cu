@@ -8,6 +8,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
+#include <cmath>
 #include <string>
 #include <vector>
 
@@ -401,6 +403,14 @@ rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_
         return cuda_fail(e, "router split upload");
     L->router_wh = static_cast<float*>(rs);
     L->router_wl = L->router_wh + nw;
+    double wmax = 0.0;
+    for (uint32_t e2 = 0; e2 < d->n_experts; e2++) {
+        double ss = 0.0;
+        for (uint32_t i = 0; i < H; i++) ss += (double)d->router_w[(size_t)e2 * H + i] * d->router_w[(size_t)e2 * H + i];
+        wmax = std::max(wmax, std::sqrt(ss));
+    }
+    // rounded up a little so the window never undershoots the f32 sums it bounds
+    L->router_wmax = (float)(wmax * (1.0 + 1e-6));
     return RMOE_OK;
 }
 
@@ -472,6 +482,8 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.has_shared = L->has_shared;
     rp.given = given ? 1 : 0;
     rp.exact = (flags & RMOE_FLAG_EXACT_ROUTER) ? 1 : 0;
+    rp.router_wmax = L->router_wmax;
+    rp.refined = w.status + 1;
     rp.xb = w.xb;
     rp.rowexp = w.rowexp;
     rp.logits = given ? nullptr : w.logits;
@@ -647,6 +659,18 @@ rmoe_status rmoe_layer_logits(rmoe_layer* L, uint32_t T, float* logits) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpy(logits, L->ws.logits, (size_t)T * L->E * 4, cudaMemcpyDeviceToHost);
     return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "logits");
+}
+
+rmoe_status rmoe_layer_router_refined(rmoe_layer* L, uint32_t* count) {
+    if (!L || !count) return fail(RMOE_ERR_INVALID, "null layer / count");
+    *count = 0;
+    DeviceGuard g(L->device);
+    unsigned* st = L->ep ? ep_status(L) : L->ws.status;
+    if (!st) return RMOE_OK;  // no forward yet
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(count, st + 1, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(st + 1, 0, 4);
+    return e == cudaSuccess ? RMOE_OK : cuda_fail(e, "router refinement count");
 }
 
 rmoe_status rmoe_layer_stage_ms(rmoe_layer* L, float ms[4]) {

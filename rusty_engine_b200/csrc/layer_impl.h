@@ -72,6 +72,7 @@ struct rmoe_layer {
     float* router_w = nullptr;
     float* router_wh = nullptr;  // router_w split for the tensor-core logits (hi | lo, [E, H] each)
     float* router_wl = nullptr;
+    float router_wmax = 0.0f;    // max over experts of ||router row||_2 (fast-router near-tie window)
     rmoe::Owned own;       // weights
     rmoe::Owned ws_own;    // workspace
     rmoe::Workspace ws;
@@ -103,5 +104,6 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
 rmoe_status ep_forward_host(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags);
 rmoe_status ep_routing(rmoe_layer* L, uint32_t T, uint32_t* ids, float* weights, float* logits);
 void ep_free(rmoe_layer* L);
+unsigned* ep_status(rmoe_layer* L);  // the expert-parallel state's status words (null before a forward)
 int canon_type(uint32_t t);
 }  // namespace rmoe

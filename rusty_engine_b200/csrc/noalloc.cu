@@ -128,6 +128,7 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     rp.ticket = w.ticket; rp.expert_off = w.expert_off; rp.row_tok = w.row_tok; rp.row_slot = w.row_slot;
     rp.slot_row = w.slot_row; rp.n_rows = w.n_rows; rp.tiles = w.tiles; rp.n_tiles = w.n_tiles;
     rp.max_tiles = max_tiles; rp.tile_rows = nt; rp.status = w.status;
+    rp.router_wmax = L->router_wmax; rp.refined = w.status + 1;
     if ((e = launch_route_dispatch(rp, s)) != cudaSuccess) return cuda_fail(e, "noalloc route_dispatch launch");
 
     GroupedParams gp{};
@@ -141,6 +142,31 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     if (e != cudaSuccess) return cuda_fail(e, "noalloc gate/up launch");
     e = gv ? launch_gv_down(gp, max_tiles, nt, (int)T, s) : launch_small_down(gp, max_tiles, nt, s);
     if (e != cudaSuccess) return cuda_fail(e, "noalloc down launch");
+    return RMOE_OK;
+}
+
+// Device errors of the last rmoe_layer_forward_noalloc on `device`: the status word in the static
+// scratch, read with a plain copy (no allocation) after synchronising the device.
+rmoe_status rmoe_noalloc_status(int32_t device) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return fail(RMOE_ERR_INVALID, "device %d out of range", device);
+    DeviceGuard g(device);
+    unsigned char* base = nullptr;
+    rmoe_status st = scratch_on(device, &base);
+    if (st) return st;
+    Carver c{base};
+    c.take<unsigned>(64);  // the dispatch tickets, then the status words (the order carve() uses)
+    unsigned* status = c.take<unsigned>(16);
+    cudaError_t e = cudaDeviceSynchronize();
+    unsigned v = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&v, status, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "noalloc status read");
+    if (v) {
+        cudaMemset(status, 0, 4);
+        return fail(RMOE_ERR_DEVICE, "noalloc forward: device status 0x%x%s", v,
+                    (v & DERR_FP16_RANGE) ? " (an x value beyond the fp16 range)" : "");
+    }
     return RMOE_OK;
 }
 

@@ -16,16 +16,47 @@
 
 namespace rmoe {
 
-// rows i -> token i, slot 0, row exponent 0; the tile list (expert 0, first row, rows)
-__global__ void qmat_prep_kernel(int rows, int NT, int4* tiles, int* ntiles, int* rowtok, int* rowslot, int* rexp) {
+// rows i -> token i, slot 0; the tile list (expert 0, first row, rows)
+__global__ void qmat_prep_kernel(int rows, int NT, int4* tiles, int* ntiles, int* rowtok, int* rowslot) {
     const int ntl = (rows + NT - 1) / NT;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += gridDim.x * blockDim.x) {
         rowtok[i] = i;
         rowslot[i] = 0;
-        rexp[i] = 0;
         if (i < ntl) tiles[i] = make_int4(0, i * NT, min(NT, rows - i * NT), 0);
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) *ntiles = ntl;
+}
+
+// X rows -> the fp16 MMA operand, one warp per row.  QMat::matmul is f32 throughout
+// (src/qmat.rs:169-308), so a row whose largest |x| is at or beyond 2^15 is carried as
+// fp16 x 2^e: scaled by the exact power of two 2^-e that brings its maximum into [2^13, 2^14),
+// e written as the row exponent and as every block exponent, which the product kernels fold
+// back into the output (y * 2^e).  Rows inside the fp16 range keep e = 0 (no scaling).
+// Non-finite x cannot be carried and sets DERR_FP16_RANGE in the status word.
+__global__ void __launch_bounds__(256) qmat_x_kernel(const float* __restrict__ x, int rows, int n,
+                                                     __half* __restrict__ xb, int8_t* __restrict__ hexp,
+                                                     int* __restrict__ rexp, unsigned* status) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const float* xr = x + (size_t)r * n;
+    float mx = 0.0f;
+    bool finite = true;
+    for (int i = lane; i < n; i += 32) {
+        const float v = fabsf(__ldg(xr + i));
+        finite = finite && v <= 3.4028235e38f;
+        mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (!__all_sync(0xffffffffu, finite)) {
+        if (lane == 0) atomicOr(status, (unsigned)DERR_FP16_RANGE);
+        mx = 0.0f;
+    }
+    const int e = mx >= 32768.0f ? (int)((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13 : 0;
+    const float sc = exp2i(-e);  // exact
+    for (int i = lane; i < n; i += 32) xb[(size_t)r * n + i] = __float2half_rn(__fmul_rn(__ldg(xr + i), sc));
+    for (int b = lane; b < n / HBLK; b += 32) hexp[(size_t)r * (n / HBLK) + b] = (int8_t)e;
+    if (lane == 0) rexp[r] = e;
 }
 
 }  // namespace rmoe
@@ -104,6 +135,9 @@ RMOE_API rmoe_status rmoe_qmat_forward(rmoe_qmat* q, const float* x, uint32_t ro
     if (!q) return fail(RMOE_ERR_INVALID, "null qmat");
     if (rows == 0) return RMOE_OK;
     if (!x || !out) return fail(RMOE_ERR_INVALID, "null x / out");
+    // the product kernels store Out with 16-B vector stores; x is read as f32
+    if (reinterpret_cast<uintptr_t>(out) & 15) return fail(RMOE_ERR_INVALID, "device out must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(x) & 3) return fail(RMOE_ERR_INVALID, "device x must be 4-byte aligned");
     DeviceGuard g(q->device);
     rmoe_status st = qmat_workspace(q, rows);
     if (st) return st;
@@ -112,10 +146,12 @@ RMOE_API rmoe_status rmoe_qmat_forward(rmoe_qmat* q, const float* x, uint32_t ro
     const int NT = tc ? tc_tile_rows() : 16;
     const int ntiles = (int)((rows + NT - 1) / NT);
     qmat_prep_kernel<<<std::min<uint32_t>((rows + 255) / 256, 1024), 256, 0, s>>>((int)rows, NT, q->tiles, q->nt,
-                                                                              q->rowtok, q->rowslot, q->rexp);
+                                                                              q->rowtok, q->rowslot);
     cudaError_t e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaMemsetAsync(q->hexp, 0, (size_t)rows * (q->n / HBLK), s);
-    if (e == cudaSuccess) e = launch_f32_to_f16(x, q->xb, (uint64_t)rows * q->n, s);
+    if (e == cudaSuccess) {
+        qmat_x_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, (int)rows, (int)q->n, q->xb, q->hexp, q->rexp, q->status);
+        e = cudaGetLastError();
+    }
     if (e != cudaSuccess) return cuda_fail(e, "qmat prepare");
     GroupedParams gp{};
     gp.down = q->W;

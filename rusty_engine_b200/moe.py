@@ -356,6 +356,13 @@ class MoELayer:
         _call(_lib.load().rmoe_layer_logits(self._h, T, lg.ctypes.data))
         return lg
 
+    def router_refined(self) -> int:
+        """Tokens whose fast-router top-k met a near-tie (and were rescored with the
+        sequential sums) since the last call; reads and resets the count."""
+        n = C.c_uint32()
+        _call(_lib.load().rmoe_layer_router_refined(self._h, C.byref(n)))
+        return int(n.value)
+
     def stage_ms(self):
         """[route, gate/up, down, combine] ms of the last forward with FLAG_STAGE_TIMING."""
         ms = (C.c_float * 4)()

@@ -13,8 +13,7 @@ from rusty_engine_b200.moe import EngineError
 
 
 def small_layer(seed, gt=synth.GGML_Q4_K, dt=synth.GGML_Q6_K, shared=False, E=8, k=2):
-    # block scales of C1's order, so that outputs stay O(1) and the absolute parity bar applies
-    return synth.make_layer(512, 256, E, k, gate_t=gt, up_t=gt, down_t=dt, dlo=0.001, dhi=0.008, seed=seed,
+    return synth.make_layer(512, 256, E, k, gate_t=gt, up_t=gt, down_t=dt, dlo=0.001, dhi=0.02, seed=seed,
                             shared=shared)
 
 

@@ -30,12 +30,11 @@ def test_oracle_reproduces_golden(name):
 
 
 def _close_to_golden(out, want):
-    want = want.astype(np.float64)
-    rel = np.linalg.norm(out - want) / np.linalg.norm(want)
-    assert rel <= 5e-3, f"rel-L2 {rel:.3e}"
-    rms = float(np.sqrt(np.mean(want ** 2)))
-    bound = 2e-2 if rms < 50.0 else 2e-2 * rms  # K-quant layers have outputs ~1e5-1e6
-    assert np.abs(out - want).max() <= bound, f"max-abs {np.abs(out - want).max():.3e} (rms {rms:.3e})"
+    from oracle import oracle as O
+
+    rel, mx, rms = O.layer_errors(out, want)
+    assert rel <= O.REL_L2, f"rel-L2 {rel:.3e}"
+    assert mx <= O.max_abs_bound(rms), f"max-abs {mx:.3e} (rms {rms:.3e})"
 
 
 @pytest.mark.gpu
