@@ -46,6 +46,8 @@ CONFIGS = {
     "c3b64": ("config_c2", 64, "c3 Qwen3-30B-A3B MoE layer decode batch 64"),
     "c5": ("config_c5", C5_TOKENS, "c5 Qwen3-235B-A22B MoE layer H4096 E128 k8 I1536 Q4_K/Q6_K, 8192 tokens, "
                                    "Zipf(1.1) expert load"),
+    "c4": (None, 2048, "c4 random-init 48-layer Qwen3-30B-A3B-shaped stack (GQA 32/4, head_dim 128, RMSNorm, "
+                       "RoPE 1e6, vocab 151936, Q4_K_M mix), 2048-token prompt, MoE layers timed"),
 }
 # reference-arm tokens per step: the whole batch, except config 5 (about 20 s of CPU per pass)
 REF_SAMPLE = {"c5": 1024}
@@ -206,7 +208,15 @@ def reference_arm(args, rank, world):
     from oracle import oracle as O
 
     cfg = args.config if world == 1 else "c5"
-    lw, x, label = workload(cfg)
+    if cfg == "c4":
+        # per-layer work of the stack: one MoE layer of its shape over the 2048-token prompt
+        from rusty_engine_b200 import synth
+
+        lw = synth.config_c2(seed=100)
+        x = synth.activations(CONFIGS["c4"][1], lw.H, seed=1)
+        label = CONFIGS["c4"][2] + " (CPU: one MoE layer of the stack's shape per step)"
+    else:
+        lw, x, label = workload(cfg)
     T = x.shape[0]
     sample = min(T, REF_SAMPLE.get(cfg, T))
     xs = np.ascontiguousarray(x[:sample])
@@ -358,6 +368,66 @@ def sub_result(B, lw, x_np, cfg, steps, warmup, peaks):
     return res
 
 
+def bench_c4(args):
+    """Config 4: a 48-block stack (rusty_engine_b200.stack) over a 2048-token prompt of uniform
+    random ids; one step = one whole forward; only the MoE layers are timed (CUDA events around
+    each of the 48 MoE forwards, summed).  Layers are built and uploaded one at a time."""
+    import torch
+
+    from rusty_engine_b200 import synth
+    from rusty_engine_b200.stack import QWEN3_30B_A3B, QWEN3_30B_A3B_LAYERS, MoEStack, make_block
+
+    g = QWEN3_30B_A3B
+    T = CONFIGS["c4"][1]
+    torch.cuda.set_device(0)
+    base = synth.config_c2(seed=100)
+    stack = MoEStack(g, [make_block(g, 0, base_moe=base)], device=0)
+    for i in range(1, QWEN3_30B_A3B_LAYERS):
+        stack.add_layer(make_block(g, i, base_moe=base))
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    embed = torch.randn((g.vocab, g.d_model), generator=gen, device="cuda", dtype=torch.float32)
+    ids = torch.randint(0, g.vocab, (T,), generator=gen, device="cuda")
+    x = embed[ids].contiguous()
+    del embed
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    for _ in range(args.warmup):
+        stack.forward(x)
+    moe, whole = [], []
+    sampler = ClockSampler(0)
+    sampler.start()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        stack.forward(x)
+        e1.record()
+        torch.cuda.synchronize()
+        moe.append(sum(stack.moe_ms))
+        whole.append(e0.elapsed_time(e1))
+    clocks = sampler.stop()
+    per_layer = [m for m in stack.moe_ms]
+    stack.close()
+    moe_ms = statistics.mean(moe)
+    nl = QWEN3_30B_A3B_LAYERS
+    peaks = load_peaks()
+    flops = 6.0 * T * g.top_k * g.d_model * g.inter * nl
+    print(json.dumps({
+        "metric": "moe_layer_tokens_per_s", "value": T * nl / (moe_ms / 1e3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": moe_ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16-mma/f32-acc/f32-router", "data": "synthetic",
+        "config": {"workload": CONFIGS["c4"][2], "tokens": T, "layers": nl,
+                   "timed": "the 48 MoE layers of each forward (CUDA events around each MoE forward, summed); "
+                            "value = tokens x layers / that time",
+                   "l2": "flushed between steps (256 MiB write); every layer reads its own expert weights"},
+        "moe_ms_per_forward": moe_ms, "moe_ms_per_layer_mean": moe_ms / nl,
+        "moe_ms_per_layer_last_step": per_layer, "whole_forward_ms": statistics.mean(whole),
+        "roofline": {"bound": "tensor", "achieved": flops / (moe_ms / 1e3) / 1e12, "peak": peaks["bf16_tflops_sustained"],
+                     "unit": "TFLOP/s", "frac": flops / (moe_ms / 1e3) / 1e12 / peaks["bf16_tflops_sustained"],
+                     "kernel": "all 48 MoE layers of a forward", "peak_src": peaks["src"] + " sustained bf16"},
+        "clocks": clocks,
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -377,6 +447,10 @@ def main():
 
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.config == "c4":
+        if args.impl == "ours" and world == 1:
+            bench_c4(args)
         return
 
     import torch

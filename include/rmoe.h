@@ -227,7 +227,8 @@ RMOE_API rmoe_status rmoe_ep_unique_id(uint8_t id[128]);
  * the same id): experts are dealt round-robin, E / world_size per rank (rank r holds experts
  * r, r + W, r + 2W, ...), so a skewed load spreads over the ranks; the router is replicated.
  * desc carries the FULL tensors (each rank uploads only its experts).  E must divide by W,
- * W <= 16, no shared expert.  rmoe_layer_forward on the handle takes this rank's T tokens
+ * W <= 16.  A shared expert is replicated on every rank and applied by each rank to its own
+ * tokens.  rmoe_layer_forward on the handle takes this rank's T tokens
  * (device or RMOE_FLAG_HOST_IO buffers) and returns their complete layer outputs; it exchanges
  * rows with the other ranks over NCCL and reads the per-rank row counts back to the host
  * once (the call synchronises the stream there). */

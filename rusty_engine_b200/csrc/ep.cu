@@ -16,6 +16,9 @@
 //      tensor-core or small-batch kernels), producing per received row the weighted sum of its
 //      local picks' outputs (f32);
 //   6. those partial sums go back to the token's rank, which adds them in ascending rank order.
+// A shared expert (src/moe.rs:381-386) is replicated on every rank: each rank sends every one of
+// its tokens to itself and runs the shared expert on exactly those rows, so each token gets it
+// once, at weight 1, inside its own rank's partial sum.
 // There is no counterpart in the reference (its moe_layer_forward runs in one process,
 // src/moe.rs:360-388); the sum over a token's experts is regrouped by rank, which changes
 // only the f32 summation order.
@@ -60,9 +63,10 @@ struct EpState {
 
 static inline uint32_t row_bytes(uint32_t H, uint32_t k) { return (H * 2 + k * 8 + 15) & ~15u; }
 
-// 2. one CTA per destination: flags and the exclusive scan over tokens
+// 2. one CTA per destination: flags and the exclusive scan over tokens (every token goes to
+// rank `self_all` itself when that is >= 0: the shared expert runs there)
 __global__ void __launch_bounds__(1024) ep_plan_kernel(const int* topk_id, int T, int k, int E_local, int G, int* pos,
-                                                       int* cnt) {
+                                                       int* cnt, int self_all) {
     __shared__ int warp_sum[32];
     __shared__ int carry_s;
     const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -71,8 +75,10 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int* topk_id, int T
     for (int t0 = 0; t0 < T; t0 += 1024) {
         const int t = t0 + tid;
         int f = 0;
-        if (t < T)
+        if (t < T) {
             for (int j = 0; j < k; j++) f |= (topk_id[(size_t)t * k + j] % G) == d;
+            if (d == self_all) f = 1;
+        }
         int inc = f;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
@@ -227,7 +233,7 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     rp.router_wmax = L->router_wmax; rp.refined = P.status + 1;
     if (T && (e = launch_router_topk(rp, s)) != cudaSuccess) return cuda_fail(e, "ep router launch");
     // 2. plan
-    ep_plan_kernel<<<G, 1024, 0, s>>>(P.topk_id, (int)T, k, El, G, P.pos, P.cnt);
+    ep_plan_kernel<<<G, 1024, 0, s>>>(P.topk_id, (int)T, k, El, G, P.pos, P.cnt, L->has_shared ? P.rank : -1);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "ep plan launch");
     // 3. counts
     ncclResult_t r = ncclGroupStart();
@@ -268,7 +274,10 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
         ep_unpack_kernel<<<(unsigned)((R + 7) / 8), 256, 0, s>>>(P.recvbuf, (int)R, H, k, rb, L->ws.xb, L->ws.topk_id,
                                                                  L->ws.topk_w);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "ep unpack launch");
-        if ((st = layer_forward_device(L, nullptr, (uint32_t)R, P.part, s, flags & ~RMOE_FLAG_STAGE_TIMING, true)))
+        // the rows this rank sent itself (all its tokens, in token order, when the layer has a
+        // shared expert) also take the shared expert, at weight 1 (src/moe.rs:381-386)
+        if ((st = layer_forward_device(L, nullptr, (uint32_t)R, P.part, s, flags & ~RMOE_FLAG_STAGE_TIMING, true,
+                                       (uint32_t)roff[P.rank], L->has_shared ? (int64_t)P.h_cnt[G + P.rank] : 0)))
             return st;
     }
     // 6. partial sums back, combined in rank order
@@ -338,7 +347,6 @@ rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* d, int32_t rank, int32_t
         return fail(RMOE_ERR_INVALID, "rank %d / world size %d (1..16 ranks)", rank, world_size);
     if (d->n_experts % (uint32_t)world_size)
         return fail(RMOE_ERR_INVALID, "%u experts do not split evenly over %d ranks", d->n_experts, world_size);
-    if (d->has_shared) return fail(RMOE_ERR_UNSUPPORTED, "expert-parallel layers with a shared expert are not supported");
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(RMOE_ERR_CUDA, "no CUDA device");
     if (d->device < 0 || d->device >= ndev) return fail(RMOE_ERR_INVALID, "device %d out of range", d->device);
@@ -351,7 +359,7 @@ rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* d, int32_t rank, int32_t
     L->e_begin = (uint32_t)rank;
     L->k = d->top_k < d->n_experts ? d->top_k : d->n_experts;
     L->gate_kind = d->gate;
-    L->has_shared = 0;
+    L->has_shared = d->has_shared ? 1 : 0;  // the shared expert is replicated on every rank
     if ((s = layer_upload(d, L->e_begin, L->E, L, (uint32_t)world_size))) { delete L; return s; }
     L->ep = new EpState();
     L->ep->rank = rank;

@@ -42,6 +42,9 @@ struct RouteParams {
     const float* router_wh; // optional [E, H]: router_w with the 13 low mantissa bits cleared
     const float* router_wl; // optional [E, H]: router_w - router_wh (the tensor-core logits)
     int T, H, E, k, gate, has_shared;
+    int shared_t0, shared_n;  // tokens [shared_t0, shared_t0 + shared_n) get a shared-expert row
+                              // (all T normally; the expert-parallel local step gives the range
+                              // of the rows a rank sent to itself)
     __half* xb;             // [T, H] fp16 copy of x (GEMM B operand)
     int* rowexp;            // [rows] SwiGLU row exponents, set to -127 by the dispatch
     __half* xs;             // optional [rows, H]: x rows in expert-sorted order (tensor-core path)
@@ -98,7 +101,10 @@ struct CombineParams {
     const float* y;       // [rows, H]
     const int* slot_row;  // [T, k]
     const float* topk_w;  // [T, k]
-    int T, H, k, has_shared, shared_row0;
+    int T, H, k, has_shared;
+    int shared_t0, shared_n;  // tokens with a shared-expert row (see RouteParams)
+    const int* expert_off;    // [E + 2]: the shared expert's first row at expert_off[E]
+    int E;
     float* out;
 };
 

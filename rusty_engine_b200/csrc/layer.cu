@@ -466,7 +466,8 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
 }
 
 rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s,
-                                 uint32_t flags, bool given) {
+                                 uint32_t flags, bool given, uint32_t shared_t0, int64_t shared_n) {
+    if (shared_n < 0) shared_n = T;
     const bool det = flags & RMOE_FLAG_DETERMINISTIC;
     if (given) {
         if (T > L->ws_T || (det && !L->ws.y)) return fail(RMOE_ERR_INVALID, "given routing without its workspace");
@@ -480,6 +481,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     rp.router_w = L->router_w; rp.router_wh = L->router_wh; rp.router_wl = L->router_wl;
     rp.T = (int)T; rp.H = (int)L->H; rp.E = (int)L->E; rp.k = (int)L->k; rp.gate = (int)L->gate_kind;
     rp.has_shared = L->has_shared;
+    rp.shared_t0 = (int)shared_t0; rp.shared_n = (int)shared_n;
     rp.given = given ? 1 : 0;
     rp.exact = (flags & RMOE_FLAG_EXACT_ROUTER) ? 1 : 0;
     rp.router_wmax = L->router_wmax;
@@ -501,7 +503,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     // decode GEMV kernels where both expert types have register-fragment decoders
     const bool gv = !use_tc && gv_supported(L->wg.type, L->wd.type);
     const int tile_rows = use_tc ? tc_tile_rows() : gv ? gv_tile_rows((int)T) : small_tile_rows((int)T);
-    const uint64_t rows_T = (uint64_t)T * L->k + (L->has_shared ? T : 0);
+    const uint64_t rows_T = (uint64_t)T * L->k + (L->has_shared ? (uint64_t)shared_n : 0);
     // an expert with c rows takes at most c / tile_rows + 1 tiles, and at most rows_T experts
     // are touched: the grids launch no more tile slots than that
     const int max_tiles = (int)std::min<uint64_t>((uint64_t)L->max_tiles,
@@ -555,7 +557,7 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         CombineParams cp{};
         cp.y = w.y; cp.slot_row = w.slot_row; cp.topk_w = w.topk_w;
         cp.T = (int)T; cp.H = (int)L->H; cp.k = (int)L->k; cp.has_shared = L->has_shared;
-        cp.shared_row0 = (int)(T * L->k);
+        cp.shared_t0 = rp.shared_t0; cp.shared_n = rp.shared_n; cp.expert_off = w.expert_off; cp.E = (int)L->E;
         cp.out = out;
         if ((e = launch_combine(cp, s)) != cudaSuccess) return cuda_fail(e, "combine launch");
     }
@@ -598,6 +600,72 @@ rmoe_status rmoe_layer_create(const rmoe_layer_desc* d, rmoe_layer** out) {
     return RMOE_OK;
 }
 
+// Host buffers in and out.  Large batches are split into token chunks so that the copies
+// overlap the compute: chunk i's upload (copy-in stream), chunk i - 1's forward (the caller's
+// stream) and chunk i - 2's download (copy-out stream) run at once; the forwards of the chunks
+// run one after another on the caller's stream (they share the workspace).  A chunk keeps at
+// least HOSTIO_ROWS_PER_EXPERT routed rows per expert on average, so the tensor-core tiles stay
+// full; smaller batches, and calls that ask for routing or stage times, run as one chunk.
+static constexpr uint64_t HOSTIO_ROWS_PER_EXPERT = 64;
+static constexpr int HOSTIO_MAX_CHUNKS = 8;
+
+static rmoe_status forward_host_io(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s,
+                                   uint32_t flags) {
+    rmoe_status st = ensure_workspace(L, T, flags & RMOE_FLAG_DETERMINISTIC);
+    if (st) return st;
+    const size_t H = L->H;
+    uint64_t nc = (uint64_t)T * L->k / (HOSTIO_ROWS_PER_EXPERT * L->E);
+    if (flags & (RMOE_FLAG_ROUTING_OUT | RMOE_FLAG_STAGE_TIMING)) nc = 1;
+    nc = std::max<uint64_t>(1, std::min<uint64_t>(nc, HOSTIO_MAX_CHUNKS));
+    cudaError_t e = cudaSuccess;
+    if (nc == 1) {
+        e = cudaMemcpyAsync(L->ws.xin, x, (size_t)T * H * 4, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "x upload");
+        st = layer_forward_device(L, L->ws.xin, T, L->ws.xout, s, flags);
+        if (st) return st;
+        e = cudaMemcpyAsync(out, L->ws.xout, (size_t)T * H * 4, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return cuda_fail(e, "out download");
+    } else {
+        if (!L->io_stream[0]) {
+            for (auto& q : L->io_stream)
+                if ((e = cudaStreamCreateWithFlags(&q, cudaStreamNonBlocking)) != cudaSuccess)
+                    return cuda_fail(e, "host-IO copy stream");
+            for (auto& ev : L->io_ev)
+                if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
+                    return cuda_fail(e, "host-IO event");
+        }
+        cudaStream_t cin = L->io_stream[0], cout = L->io_stream[1];
+        cudaEvent_t* up = L->io_ev;            // chunk i uploaded
+        cudaEvent_t* done = L->io_ev + 8;      // chunk i computed
+        cudaEvent_t entry = L->io_ev[16];      // work queued on s before this call
+        // the staging buffers may still be read by work queued earlier on s
+        if ((e = cudaEventRecord(entry, s)) != cudaSuccess || (e = cudaStreamWaitEvent(cin, entry, 0)) != cudaSuccess)
+            return cuda_fail(e, "host-IO ordering");
+        const uint32_t per = (uint32_t)((T + nc - 1) / nc);
+        for (uint64_t i = 0; i < nc; i++) {
+            const uint32_t t0 = (uint32_t)i * per, n = std::min<uint32_t>(per, T - t0);
+            e = cudaMemcpyAsync(L->ws.xin + t0 * H, x + t0 * H, (size_t)n * H * 4, cudaMemcpyHostToDevice, cin);
+            if (e == cudaSuccess) e = cudaEventRecord(up[i], cin);
+            if (e != cudaSuccess) return cuda_fail(e, "x upload");
+        }
+        for (uint64_t i = 0; i < nc; i++) {
+            const uint32_t t0 = (uint32_t)i * per, n = std::min<uint32_t>(per, T - t0);
+            if ((e = cudaStreamWaitEvent(s, up[i], 0)) != cudaSuccess) return cuda_fail(e, "host-IO ordering");
+            if ((st = layer_forward_device(L, L->ws.xin + t0 * H, n, L->ws.xout + t0 * H, s, flags))) return st;
+            if ((e = cudaEventRecord(done[i], s)) != cudaSuccess || (e = cudaStreamWaitEvent(cout, done[i], 0)) != cudaSuccess)
+                return cuda_fail(e, "host-IO ordering");
+            e = cudaMemcpyAsync(out + t0 * H, L->ws.xout + t0 * H, (size_t)n * H * 4, cudaMemcpyDeviceToHost, cout);
+            if (e != cudaSuccess) return cuda_fail(e, "out download");
+        }
+        if ((e = cudaStreamSynchronize(cout)) != cudaSuccess) return cuda_fail(e, "out download");
+    }
+    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "forward");
+    unsigned status = 0;
+    cudaMemcpy(&status, L->ws.status, 4, cudaMemcpyDeviceToHost);
+    if (status) return fail(RMOE_ERR_DEVICE, "device status 0x%x", status);
+    return RMOE_OK;
+}
+
 rmoe_status rmoe_layer_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, void* stream, uint32_t flags) {
     if (!L) return fail(RMOE_ERR_INVALID, "null layer");
     if (T == 0) return RMOE_OK;
@@ -610,21 +678,7 @@ rmoe_status rmoe_layer_forward(rmoe_layer* L, const float* x, uint32_t T, float*
             return fail(RMOE_ERR_INVALID, "device x / out must be 16-byte aligned");
         return ep_forward(L, x, T, out, s, flags);
     }
-    if (flags & RMOE_FLAG_HOST_IO) {
-        rmoe_status st = ensure_workspace(L, T, flags & RMOE_FLAG_DETERMINISTIC);
-        if (st) return st;
-        cudaError_t e = cudaMemcpyAsync(L->ws.xin, x, (size_t)T * L->H * 4, cudaMemcpyHostToDevice, s);
-        if (e != cudaSuccess) return cuda_fail(e, "x upload");
-        st = layer_forward_device(L, L->ws.xin, T, L->ws.xout, s, flags);
-        if (st) return st;
-        e = cudaMemcpyAsync(out, L->ws.xout, (size_t)T * L->H * 4, cudaMemcpyDeviceToHost, s);
-        if (e != cudaSuccess) return cuda_fail(e, "out download");
-        if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "forward");
-        unsigned status = 0;
-        cudaMemcpy(&status, L->ws.status, 4, cudaMemcpyDeviceToHost);
-        if (status) return fail(RMOE_ERR_DEVICE, "device status 0x%x", status);
-        return RMOE_OK;
-    }
+    if (flags & RMOE_FLAG_HOST_IO) return forward_host_io(L, x, T, out, s, flags);
     // the router streams x and the combine writes out with 16-B vector accesses
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
         return fail(RMOE_ERR_INVALID, "device x / out must be 16-byte aligned");
@@ -699,6 +753,10 @@ void rmoe_layer_destroy(rmoe_layer* L) {
 rmoe_layer::~rmoe_layer() {
     for (auto& e : ev)
         if (e) cudaEventDestroy(e);
+    for (auto& e : io_ev)
+        if (e) cudaEventDestroy(e);
+    for (auto& q : io_stream)
+        if (q) cudaStreamDestroy(q);
     if (ep) rmoe::ep_free(this);
 }
 

@@ -83,6 +83,9 @@ struct rmoe_layer {
     bool last_tc = false;  // the last forward ran the tcgen05 kernels
     cudaEvent_t ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     bool ev_valid = false, ev_combine = false;
+    // host-IO pipeline: copy streams (in, out) and per-chunk events, made on first use
+    cudaStream_t io_stream[2] = {nullptr, nullptr};
+    cudaEvent_t io_ev[2 * 8 + 1] = {};
     ~rmoe_layer();
 };
 
@@ -98,8 +101,9 @@ rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_
 rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y);
 // given: the workspace's xb / topk_id / topk_w already hold T rows' routing (x unused; ids >= E
 // are empty picks) -- the expert-parallel local step
+// shared_t0 / shared_n: the tokens that get the shared expert (all T when shared_n < 0)
 rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags,
-                                 bool given = false);
+                                 bool given = false, uint32_t shared_t0 = 0, int64_t shared_n = -1);
 rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags);
 rmoe_status ep_forward_host(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags);
 rmoe_status ep_routing(rmoe_layer* L, uint32_t T, uint32_t* ids, float* weights, float* logits);

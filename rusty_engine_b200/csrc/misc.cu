@@ -14,7 +14,8 @@ __global__ void combine_kernel(CombineParams p) {
         float o = 0.0f;
         for (int j = 0; j < p.k; j++)
             if (sr[j] >= 0) o = __fadd_rn(o, __fmul_rn(wt[j], p.y[(size_t)sr[j] * p.H + i]));  // < 0: empty pick
-        if (p.has_shared) o = __fadd_rn(o, p.y[(size_t)(p.shared_row0 + t) * p.H + i]);
+        if (p.has_shared && t >= p.shared_t0 && t < p.shared_t0 + p.shared_n)
+            o = __fadd_rn(o, p.y[(size_t)(p.expert_off[p.E] + t - p.shared_t0) * p.H + i]);
         p.out[(size_t)t * p.H + i] = o;
     }
 }

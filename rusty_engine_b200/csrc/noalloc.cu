@@ -122,6 +122,7 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     rp.router_w = L->router_w;
     rp.T = (int)T; rp.H = (int)L->H; rp.E = (int)L->E; rp.k = (int)L->k; rp.gate = (int)L->gate_kind;
     rp.has_shared = L->has_shared;
+    rp.shared_t0 = 0; rp.shared_n = (int)T;
     rp.xb = w.xb; rp.rowexp = w.rowexp; rp.xs = nullptr; rp.logits = w.logits;
     rp.out_zero = out;  // the atomic combine accumulates into zeroed rows
     rp.topk_id = w.topk_id; rp.topk_w = w.topk_w; rp.local_rank = w.local_rank; rp.cta_cnt = w.cta_cnt;

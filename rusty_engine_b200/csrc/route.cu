@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(SC_THREADS) scan_counts_kernel(RouteParams p, 
     if (ticket_s != gridDim.x - 1) return;
     __threadfence();
     for (int i = tid; i < p.E; i += SC_THREADS) cnt_s[i] = __ldcg(p.expert_off + i);
-    if (tid == 0 && p.has_shared) cnt_s[p.E] = p.T;
+    if (tid == 0 && p.has_shared) cnt_s[p.E] = p.shared_n;
     __syncthreads();
     build_tiles(p, cnt_s, nullptr);
     if (tid == 0) *p.ticket = 0u;  // re-arm for the next launch (stream-ordered)
@@ -747,9 +747,10 @@ __global__ void __launch_bounds__(TK_THREADS) scatter_rows_kernel(RouteParams p)
         p.rowexp[pos] = -127;
     }
     if (p.has_shared) {
-        const int base = p.expert_off[p.E];
+        const int base = p.expert_off[p.E] - p.shared_t0;
         for (int tl = threadIdx.x; tl < TK_TOK && t0 + tl < p.T; tl += TK_THREADS) {
-            int t = t0 + tl;
+            const int t = t0 + tl;
+            if (t < p.shared_t0 || t >= p.shared_t0 + p.shared_n) continue;
             p.row_tok[base + t] = t;
             p.row_slot[base + t] = k;
             p.rowexp[base + t] = -127;
@@ -767,7 +768,8 @@ __global__ void __launch_bounds__(256) gather_x_kernel(RouteParams p) {
     if (t >= p.T) return;
     const int k = p.k, per = k + (p.has_shared ? 1 : 0), units = p.H / 8;
     const int dst_row = lane < k ? p.slot_row[(size_t)t * k + lane] : 0;  // lane j < k: row of pick j
-    const int shared_row = p.has_shared ? p.expert_off[p.E] + t : 0;
+    const int shared_row =
+        p.has_shared && t >= p.shared_t0 && t < p.shared_t0 + p.shared_n ? p.expert_off[p.E] + t - p.shared_t0 : -1;
     const uint4* src = reinterpret_cast<const uint4*>(p.xb + (size_t)t * p.H);
     for (int u0 = 0; u0 < units; u0 += 32 * GX_CHUNK) {
         uint4 v[GX_CHUNK];
@@ -830,7 +832,7 @@ __device__ void dispatch_small(const RouteParams& p, const int* ids_s, int* cnt_
         }
         cnt_s[e] = run;
     }
-    if (tid == 0 && p.has_shared) cnt_s[E] = T;
+    if (tid == 0 && p.has_shared) cnt_s[E] = p.shared_n;
     __syncthreads();
     build_tiles(p, cnt_s, off_s);
     __syncthreads();
@@ -847,8 +849,8 @@ __device__ void dispatch_small(const RouteParams& p, const int* ids_s, int* cnt_
         p.rowexp[pos] = -127;
     }
     if (p.has_shared)
-        for (int t = tid; t < T; t += nthr) {
-            const int pos = off_s[E] + t;
+        for (int t = p.shared_t0 + tid; t < p.shared_t0 + p.shared_n; t += nthr) {
+            const int pos = off_s[E] + t - p.shared_t0;
             p.row_tok[pos] = t;
             p.row_slot[pos] = k;
             p.rowexp[pos] = -127;

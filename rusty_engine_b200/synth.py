@@ -67,6 +67,28 @@ def _f16_bytes(v: np.ndarray) -> np.ndarray:
     return v.astype(np.float16).view(np.uint8).reshape(-1, 2)
 
 
+def pack_scale_min_k4(sc: np.ndarray, mn: np.ndarray) -> np.ndarray:
+    """The 12 packed bytes of eight 6-bit (scale, min) pairs: the inverse of get_scale_min_k4
+    (src/quant.rs:250-258)."""
+    q = np.zeros((sc.shape[0], 12), dtype=np.uint8)
+    q[:, 0:4] = sc[:, 0:4] | ((sc[:, 4:8] >> 4) << 6)
+    q[:, 4:8] = mn[:, 0:4] | ((mn[:, 4:8] >> 4) << 6)
+    q[:, 8:12] = (sc[:, 4:8] & 0xF) | ((mn[:, 4:8] & 0xF) << 4)
+    return q
+
+
+def gen_q4k_centered(rng: np.random.Generator, nblocks: int, dlo: float, dhi: float) -> np.ndarray:
+    """Q4_K superblocks whose weights have mean ~0 (dmin = d, min = 7.5 * scale rounded, scales
+    in 0..8), for projections where the uniform-scale draw's positive mean would make every
+    output the same large common mode."""
+    out = gen_blocks(rng, GGML_Q4_K, nblocks, dlo, dhi).reshape(nblocks, 144)
+    out[:, 2:4] = out[:, 0:2]
+    sc = rng.integers(0, 9, (nblocks, 8), dtype=np.uint8)
+    mn = np.rint(7.5 * sc).astype(np.uint8)
+    out[:, 4:16] = pack_scale_min_k4(sc, mn)
+    return out.reshape(-1)
+
+
 def gen_blocks(rng: np.random.Generator, t: int, nblocks: int, dlo: float, dhi: float) -> np.ndarray:
     """Random superblocks of type ``t`` (uint8 array of nblocks * block_bytes)."""
     e, b = BLOCK[t]
@@ -81,12 +103,7 @@ def gen_blocks(rng: np.random.Generator, t: int, nblocks: int, dlo: float, dhi: 
         out[:, 2:4] = _f16_bytes(rng.uniform(dlo, dhi, nblocks))
         sc = rng.integers(0, 64, (nblocks, 8), dtype=np.uint8)
         mn = rng.integers(0, 64, (nblocks, 8), dtype=np.uint8)
-        q = np.zeros((nblocks, 12), dtype=np.uint8)
-        # inverse of get_scale_min_k4 (src/quant.rs:250-258)
-        q[:, 0:4] = sc[:, 0:4] | ((sc[:, 4:8] >> 4) << 6)
-        q[:, 4:8] = mn[:, 0:4] | ((mn[:, 4:8] >> 4) << 6)
-        q[:, 8:12] = (sc[:, 4:8] & 0xF) | ((mn[:, 4:8] & 0xF) << 4)
-        out[:, 4:16] = q
+        out[:, 4:16] = pack_scale_min_k4(sc, mn)
     elif t == GGML_Q6_K:
         out[:, 192:208] = rng.integers(-32, 32, (nblocks, 16), dtype=np.int8).view(np.uint8)
         out[:, 208:210] = _f16_bytes(d)

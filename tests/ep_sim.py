@@ -11,14 +11,17 @@ import torch.distributed as dist
 from oracle import oracle as O
 
 
-def plan(ids: np.ndarray, G: int):
+def plan(ids: np.ndarray, G: int, self_all: int = -1):
     """pos[t, d] = row of token t in d's block (-1 when not sent), counts[d]; expert e lives
-    on rank e % G."""
+    on rank e % G; every token also goes to rank `self_all` when that is >= 0 (the home rank,
+    which runs the shared expert)."""
     T = ids.shape[0]
     flags = np.zeros((T, G), dtype=bool)
     for t in range(T):
         for e in ids[t]:
             flags[t, int(e) % G] = True
+        if self_all >= 0:
+            flags[t, self_all] = True
     pos = np.full((T, G), -1, dtype=np.int64)
     counts = np.zeros(G, dtype=np.int64)
     for d in range(G):
@@ -37,14 +40,15 @@ def a2a(rows: np.ndarray, send_counts, recv_counts, width: int) -> np.ndarray:
     return out.numpy()
 
 
-def ep_forward(x: np.ndarray, layer, experts_f32, rank: int, G: int) -> np.ndarray:
-    """This rank's tokens x [T, H] -> layer outputs [T, H]; experts_f32[e] = (gate, up, down)."""
+def ep_forward(x: np.ndarray, layer, experts_f32, rank: int, G: int, shared_f32=None) -> np.ndarray:
+    """This rank's tokens x [T, H] -> layer outputs [T, H]; experts_f32[e] = (gate, up, down);
+    shared_f32 = the shared expert's (gate, up, down), replicated on every rank."""
     T, H = x.shape
     E, k, I = layer.E, layer.k, layer.I
     El = E // G
     logits = O.router_logits(x, layer.router_w, E)
     ids, w = O.route_batch(logits, layer.gate, k)
-    pos, send_counts = plan(ids, G)
+    pos, send_counts = plan(ids, G, rank if shared_f32 is not None else -1)
     recv_counts = torch.empty(G, dtype=torch.int64)
     dist.all_to_all_single(recv_counts, torch.from_numpy(send_counts))
     recv_counts = recv_counts.numpy()
@@ -63,10 +67,14 @@ def ep_forward(x: np.ndarray, layer, experts_f32, rank: int, G: int) -> np.ndarr
                 rows[r, H + j] = int(ids[t, j]) // G if mine else El
                 rows[r, H + k + j] = w[t, j] if mine else 0.0
     got = a2a(rows, send_counts, recv_counts, width)
-    # local experts: per received row, the weighted sum of its picks held here
+    # local experts: per received row, the weighted sum of its picks held here; the rows this
+    # rank sent itself also take the shared expert at weight 1
+    roff = np.concatenate([[0], np.cumsum(recv_counts)])
     part = np.zeros((got.shape[0], H))
     for r in range(got.shape[0]):
         xr = got[r, :H].astype(np.float32)
+        if shared_f32 is not None and roff[rank] <= r < roff[rank + 1]:
+            part[r] += O.expert_ffn(xr, *shared_f32, H, I).astype(np.float64)
         for j in range(k):
             le = int(got[r, H + j])
             if le >= El:

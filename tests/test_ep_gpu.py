@@ -20,7 +20,7 @@ def _check(got, want, what):
     assert mx <= O.max_abs_bound(rms), f"{what}: max-abs {mx:.3e} (rms {rms:.3e})"
 
 
-def _rank(rank, world, uid, tokens):
+def _rank(rank, world, uid, tokens, shared=False):
     import torch
 
     from oracle import oracle as O
@@ -28,7 +28,8 @@ def _rank(rank, world, uid, tokens):
     from rusty_engine_b200.moe import MoELayer
 
     torch.cuda.set_device(rank)
-    lw = synth.config_c1()
+    lw = synth.config_c1() if not shared else synth.make_layer(
+        1024, 512, 16, 4, gate_t=12, up_t=12, down_t=14, dlo=0.001, dhi=0.004, seed=3, shared=True)
     layer = MoELayer.expert_parallel(lw, rank, world, uid, device=rank)
     for T in tokens:
         x = synth.activations(T, lw.H, seed=10 * rank + T)
@@ -41,11 +42,12 @@ def _rank(rank, world, uid, tokens):
     layer.close()
 
 
-def _run(world, tokens, timeout_s=300):
+def _run(world, tokens, timeout_s=300, shared=False):
     from rusty_engine_b200.moe import ep_unique_id
 
     uid = ep_unique_id()
-    ctx = mp.start_processes(_rank, args=(world, uid, tokens), nprocs=world, start_method="spawn", join=False)
+    ctx = mp.start_processes(_rank, args=(world, uid, tokens, shared), nprocs=world, start_method="spawn",
+                             join=False)
     deadline = time.time() + timeout_s
     while not ctx.join(timeout=5):
         if time.time() > deadline:
@@ -62,3 +64,13 @@ def test_ep_two_gpus_matches_oracle(gpu):
         pytest.skip("needs two GPUs")
     # 3 and 16 tokens: small-batch local path; 512: tensor-core local path
     _run(2, (3, 16, 512))
+
+
+def test_ep_two_gpus_shared_expert(gpu):
+    """A layer with a shared expert (replicated on both ranks, applied by each rank to its own
+    tokens) against the oracle's whole layer, small-batch and tensor-core local paths."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _run(2, (5, 300), shared=True)

@@ -33,7 +33,7 @@ def _experts_f32(lw):
     return out
 
 
-def _rank(rank, world, port, tokens, seed, bias_to):
+def _rank(rank, world, port, tokens, seed, bias_to, shared=False):
     import torch.distributed as dist
 
     from oracle import oracle as O
@@ -42,12 +42,16 @@ def _rank(rank, world, port, tokens, seed, bias_to):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
         lw = synth.make_layer(256, 256, 8, 3, gate_t=GGML_Q4_K, up_t=GGML_Q4_K, down_t=GGML_Q6_K, dlo=0.001,
-                              dhi=0.01, seed=seed, name="ep-sim")
+                              dhi=0.01, seed=seed, name="ep-sim", shared=shared)
         if bias_to is not None:  # every token's picks on one rank's experts (e % 2 == bias_to)
             lw.router_w[bias_to::2] += np.float32(0.5)
         ex = _experts_f32(lw)
         x = synth.activations(tokens[rank], lw.H, seed=100 + rank) if tokens[rank] else np.zeros((0, lw.H), np.float32)
-        got = ep_sim.ep_forward(x, lw, ex, rank, world)
+        sh = None
+        if shared:
+            sh = tuple(O.dequant(q.ggml_type, q.data).reshape(r, c)
+                       for q, r, c in zip(lw.shared, (lw.I, lw.I, lw.H), (lw.H, lw.H, lw.I)))
+        got = ep_sim.ep_forward(x, lw, ex, rank, world, sh)
         if tokens[rank]:
             want = O.moe_layer_q_exact(x, lw)[0]
             rel = np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want)
@@ -59,3 +63,11 @@ def _rank(rank, world, port, tokens, seed, bias_to):
 @pytest.mark.parametrize("tokens,bias_to", [((5, 3), None), ((4, 0), None), ((3, 6), 1)])
 def test_ep_exchange_matches_whole_layer(tokens, bias_to):
     mp.start_processes(_rank, args=(2, _free_port(), tokens, 7, bias_to), nprocs=2, start_method="spawn", join=True)
+
+
+@pytest.mark.parametrize("tokens", [(5, 3), (4, 0)])
+def test_ep_exchange_with_shared_expert(tokens):
+    """The shared expert replicated on both ranks: every token is also sent to its own rank,
+    which adds the shared expert's output to that row's partial sum (src/moe.rs:381-386)."""
+    mp.start_processes(_rank, args=(2, _free_port(), tokens, 9, None, True), nprocs=2, start_method="spawn",
+                       join=True)

@@ -430,6 +430,23 @@ def test_host_io_matches_device_path(torch_cuda):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+@pytest.mark.parametrize("T", [1024, 1500])
+def test_host_io_chunked_pipeline(torch_cuda, T):
+    """Large host-buffer forwards are split into token chunks whose copies overlap the compute
+    (four / five chunks here): outputs equal the one-shot device-buffer forward (deterministic
+    combine, so both sum each token's experts in the same order) and the oracle."""
+    from rusty_engine_b200.moe import MoELayer
+
+    lw = synth.config_c1()
+    x = synth.activations(T, lw.H, seed=T)
+    layer = MoELayer(lw, device=0)
+    a = layer.forward_host(x, flags=_lib.FLAG_DETERMINISTIC)
+    b = layer.forward(torch_cuda.from_numpy(x).cuda(), flags=_lib.FLAG_DETERMINISTIC).cpu().numpy()
+    layer.close()
+    np.testing.assert_allclose(a, b, rtol=1e-6, atol=1e-6)
+    assert_layer_close(a, O.moe_layer_q_exact(x, lw)[0], f"host-IO chunked T={T}")
+
+
 def test_reference_layer_kats_f32_experts(torch_cuda):
     """moe_layer_routes_to_best_expert / moe_layer_adds_shared_expert (src/moe.rs:773-801)
     through the f32-ExpertWeights signature (zero-padded to the kernel widths)."""
