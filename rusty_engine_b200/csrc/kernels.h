@@ -129,6 +129,14 @@ int gv_tile_rows(int T);
 cudaError_t launch_gv_gateup(const GroupedParams& p, int max_tiles, int nt, int T, cudaStream_t s);
 cudaError_t launch_gv_down(const GroupedParams& p, int max_tiles, int nt, int T, cudaStream_t s);
 
+// The whole layer for a decode batch (T <= 16, Q4_K / Q6_K experts, fast router, atomic
+// combine) in one cooperative launch (layer_small.cu).  bar: two zeroed words that persist
+// between launches; grid_cache: three ints (0 at first use) caching the co-resident grid size.
+// cudaErrorNotSupported where the shapes or the device do not allow it.
+bool layer_small_supported(int gate_type, int down_type, int T, int E, int k);
+cudaError_t launch_layer_small(const RouteParams& r, const GroupedParams& g, unsigned* bar, int* grid_cache,
+                               cudaStream_t s);
+
 // TMA descriptors of one weight-matrix stack: main plane (viewed as u16, 128-row boxes), the
 // block-scale plane and the Q5_0 high-bit plane (both [block][row], 128-row boxes).
 struct WMaps {

@@ -510,6 +510,27 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
                                                   rows_T / tile_rows + std::min<uint64_t>(L->E + 2, rows_T));
     rp.max_tiles = max_tiles; rp.tile_rows = tile_rows; rp.status = w.status;
     const bool timing = flags & RMOE_FLAG_STAGE_TIMING;
+    // decode batches of Q4_K / Q6_K experts: the whole layer in one launch where the flags allow
+    // (fast router, atomic combine, no stage events)
+    if (gv && !given && !det && !timing && !rp.exact &&
+        layer_small_supported(L->wg.type, L->wd.type, (int)T, (int)L->E, (int)L->k)) {
+        GroupedParams gp{};
+        gp.gate = L->wg; gp.up = L->wu; gp.down = L->wd;
+        gp.sgate = L->swg; gp.sup = L->swu; gp.sdown = L->swd;
+        gp.H = (int)L->H; gp.I = (int)L->I; gp.E = (int)L->E; gp.k = (int)L->k;
+        gp.xb = w.xb; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp; gp.y = nullptr; gp.out = out;
+        gp.status = w.status;
+        cudaError_t e = launch_layer_small(rp, gp, w.ticket + 14, L->small_grid, s);
+        if (e == cudaSuccess) {
+            L->last_tc = false;
+            L->ev_valid = false;
+            L->ev_combine = false;
+            L->last_T = T;
+            return RMOE_OK;
+        }
+        if (e != cudaErrorNotSupported && e != cudaErrorCooperativeLaunchTooLarge) return cuda_fail(e, "small layer launch");
+        cudaGetLastError();  // not for this shape or device: the multi-launch path below
+    }
     if (timing && !L->ev[0])
         for (auto& ev : L->ev) cudaEventCreate(&ev);
     auto mark = [&](int i) {

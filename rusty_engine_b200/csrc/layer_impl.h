@@ -81,6 +81,7 @@ struct rmoe_layer {
     int max_tiles = 0;
     uint32_t last_T = 0;
     bool last_tc = false;  // the last forward ran the tcgen05 kernels
+    int small_grid[3] = {0, 0, 0};  // co-resident grid sizes of the one-launch decode layer
     cudaEvent_t ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     bool ev_valid = false, ev_combine = false;
     // host-IO pipeline: copy streams (in, out) and per-chunk events, made on first use

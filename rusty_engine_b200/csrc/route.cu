@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 namespace rmoe {
 
@@ -357,214 +358,7 @@ __device__ __forceinline__ void logit_row(const RouteParams& p, int t, int lane,
     __syncwarp();
 }
 
-// ---------------------------------------------------------------------------------------
-// top-k of one token's E logits (one warp)
-// ---------------------------------------------------------------------------------------
-// Routing weights of one token's k picks (one warp; lane j < k holds pick j's score and writes
-// w_out[j]).  The sums run in pick order on every lane (the same sequential f32 additions as
-// the reference), each lane then forms its own weight.
-__device__ __forceinline__ void pick_weights(float chosen_score, int k, int gate, int lane, float* w_out) {
-    if (gate == 1) {
-        float wsum = 0.0f;
-        for (int j = 0; j < k; j++) wsum = __fadd_rn(wsum, __shfl_sync(0xffffffffu, chosen_score, j));
-        if (lane < k) w_out[lane] = (wsum == 0.0f) ? 0.0f : __fdiv_rn(chosen_score, wsum);
-    } else {
-        // softmax_in_place (src/moe.rs:61-72): max fold, exp(v - max), sequential sum, divide
-        float mx = -INFINITY;
-        for (int j = 0; j < k; j++) mx = fmaxf(mx, __shfl_sync(0xffffffffu, chosen_score, j));
-        const float ex = (lane < k) ? expf(__fsub_rn(chosen_score, mx)) : 0.0f;
-        float sum = 0.0f;
-        for (int j = 0; j < k; j++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, ex, j));
-        if (lane < k) w_out[lane] = (sum != 0.0f) ? __fdiv_rn(ex, sum) : ex;
-    }
-}
-
-// The score top-k ranks: the logit, or its sigmoid (src/moe.rs:44-46) for the sigmoid gate.
-__device__ __forceinline__ float gate_score(float x, int gate) { return gate == 1 ? 1.0f / (1.0f + expf(-x)) : x; }
-
-// Scores as unsigned keys in the same order (-0 and +0 equal, as the float compare has them);
-// 0 is left free to mark a taken or absent entry.
-__device__ __forceinline__ unsigned score_key(float v) {
-    const unsigned u = __float_as_uint(v + 0.0f);
-    const unsigned k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return k ? k : 1u;
-}
-__device__ __forceinline__ float key_score(unsigned k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
-}
-
-// The n best scores of one token's E logits (one warp).  Order = stable descending argsort
-// (larger first, ties to the lower index), the rusty-engine top_k / top_k_sigmoid contract
-// (src/moe.rs:75-117).  Lane j < n gets the j-th expert id and its score.
-template <int NS>  // NS >= ceil(E / 32) logits per lane
-__device__ __forceinline__ void warp_select_n(const float* lg, int E, int n, int gate, int lane, float& chosen_score,
-                                              int& chosen_id) {
-    unsigned key[NS];
-#pragma unroll
-    for (int s = 0; s < NS; s++) {
-        const int e = lane + 32 * s;
-        key[s] = e < E ? score_key(gate_score(lg[e], gate)) : 0u;
-    }
-    chosen_score = 0.0f;
-    chosen_id = 0;
-    for (int j = 0; j < n; j++) {
-        // this lane's best (s ascending = index ascending, so a strict '>' keeps the lower
-        // index), then the warp's largest key and, among the lanes holding it, the lowest index
-        unsigned bk = 0u;
-        int bs = 0;
-#pragma unroll
-        for (int s = 0; s < NS; s++)
-            if (key[s] > bk) {
-                bk = key[s];
-                bs = s;
-            }
-        const unsigned m = __reduce_max_sync(0xffffffffu, bk);
-        const int win = (int)__reduce_min_sync(0xffffffffu, bk == m ? (unsigned)(lane + 32 * bs) : 0xffffffffu);
-        if ((win & 31) == lane)
-#pragma unroll
-            for (int s = 0; s < NS; s++)
-                if (s == (win >> 5)) key[s] = 0u;
-        if (lane == j) {
-            chosen_score = key_score(m);
-            chosen_id = win;
-        }
-    }
-}
-
-// One token's top-k (one warp): lane j < k returns the j-th expert id and writes pick j's
-// weight to w_out[j].
-template <int NS>
-__device__ int warp_topk_n(const float* lg, int E, int k, int gate, int lane, float* w_out) {
-    float chosen_score;
-    int chosen_id;
-    warp_select_n<NS>(lg, E, k, gate, lane, chosen_score, chosen_id);
-    pick_weights(chosen_score, k, gate, lane, w_out);
-    return chosen_id;
-}
-
-__device__ int warp_topk(const float* lg, int E, int k, int gate, int lane, float* w_out) {
-    const int ns = (E + 31) / 32;
-    if (ns <= 1) return warp_topk_n<1>(lg, E, k, gate, lane, w_out);
-    if (ns <= 2) return warp_topk_n<2>(lg, E, k, gate, lane, w_out);
-    if (ns <= 4) return warp_topk_n<4>(lg, E, k, gate, lane, w_out);
-    if (ns <= 8) return warp_topk_n<8>(lg, E, k, gate, lane, w_out);
-    return warp_topk_n<MAX_E / 32>(lg, E, k, gate, lane, w_out);
-}
-
-// ---------------------------------------------------------------------------------------
-// Near-tie refinement of the fast router.
-//
-// A fast logit differs from moe::matvec's sequential f32 sum (src/moe.rs:271-277) by
-// summation error.  Both sums are within a few units of u * ||w_e|| * ||x_t|| (u = 2^-24) of
-// the exact value (at the BASELINE shapes the largest distance seen is about 4 units), so a
-// top-k choice made on fast logits can differ from the reference's only where two of the
-// k + 1 best scores lie within that distance.  For a token where any two adjacent scores of
-// its k + 1 best are closer than tau = REFINE_UNITS units (the ratio of tau to the largest
-// error is what the GPU tests check), every expert whose fast score lies within tau of the
-// (k+1)-th best is rescored with the exact sequential chain, bit-identical to moe::matvec, and
-// top-k runs again: experts further down are more than tau / 2 below k + 1 others under any
-// of the sums and cannot be chosen.  The ids are then the reference's, near-ties included.
-// For the sigmoid gate the distances are taken between scores (sigmoid has slope <= 1/4,
-// plus a few ulp for the rounding of the score itself).
-// ---------------------------------------------------------------------------------------
-static constexpr float REFINE_UNITS = 32.0f;
-
-// moe::matvec's logit of expert e for token t: products rounded, then added in ascending k
-// to a running f32 sum that starts at 0, with no contraction.
-__device__ __noinline__ float exact_logit(const float* __restrict__ w, const float* __restrict__ x, int H) {
-    const float4* w4 = reinterpret_cast<const float4*>(w);
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    float s = 0.0f;
-#pragma unroll 8
-    for (int i = 0; i < H / 4; i++) {
-        const float4 a = __ldg(w4 + i), b = __ldg(x4 + i);
-        s = __fadd_rn(s, __fmul_rn(a.x, b.x));
-        s = __fadd_rn(s, __fmul_rn(a.y, b.y));
-        s = __fadd_rn(s, __fmul_rn(a.z, b.z));
-        s = __fadd_rn(s, __fmul_rn(a.w, b.w));
-    }
-    return s;
-}
-
-// ||x_t||_2 (one warp; f32 partial sums, used only to size the refinement window).
-__device__ __forceinline__ float warp_row_norm(const float* __restrict__ x, int H, int lane) {
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    float s = 0.0f;
-#pragma unroll 4
-    for (int j = lane; j < H / 4; j += 32) {
-        const float4 v = __ldg(x4 + j);
-        s = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, s))));
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    return sqrtf(s);
-}
-
-// Top-k of token t from its fast logits in row[0 .. E) (warp-private shared memory), with the
-// near-tie refinement above.  Refined logits replace the fast ones in row and in p.logits.
-template <int NS>
-__device__ int warp_topk_refined_n(const RouteParams& p, int t, float* row, int lane, float* w_out) {
-    const int E = p.E, k = p.k, gate = p.gate, H = p.H;
-    const float* xt = p.x + (size_t)t * H;
-    const float xn = warp_row_norm(xt, H, lane);
-    const int n = min(k + 1, E);
-    float sc;
-    int id;
-    warp_select_n<NS>(row, E, n, gate, lane, sc, id);
-    const float tau_l = REFINE_UNITS * 5.9604645e-8f * p.router_wmax * xn;
-    const float tau = gate == 1 ? 0.25f * tau_l + 4.7683716e-7f : tau_l;  // + 8 ulp of 1.0
-    const float next = __shfl_down_sync(0xffffffffu, sc, 1);
-    const bool close = lane + 1 < n && !(sc - next >= tau);
-    if (__any_sync(0xffffffffu, close)) {
-        // every expert at or above (k+1)-th score - tau (all of them when k = E: only the
-        // order can change then)
-        const float thr = k < E ? __shfl_sync(0xffffffffu, sc, n - 1) - tau : -INFINITY;
-        unsigned mb = 0u;  // bit s: expert lane + 32 s is rescored
-#pragma unroll
-        for (int s = 0; s < NS; s++) {
-            const int e = lane + 32 * s;
-            if (e < E && !(gate_score(row[e], gate) < thr)) mb |= 1u << s;
-        }
-        int total = 0;
-#pragma unroll
-        for (int s = 0; s < NS; s++) total += __popc(__ballot_sync(0xffffffffu, (mb >> s) & 1u));
-        for (int pass = 0; pass * 32 < total; pass++) {
-            // the rescored experts in ascending order, one per lane
-            const int want = lane + 32 * pass;
-            int mine = -1, base = 0;
-#pragma unroll
-            for (int s = 0; s < NS; s++) {
-                const unsigned m = __ballot_sync(0xffffffffu, (mb >> s) & 1u);
-                const int c = __popc(m);
-                if (want >= base && want < base + c) mine = 32 * s + (int)__fns(m, 0, want - base + 1);
-                base += c;
-            }
-            const float v = mine >= 0 ? exact_logit(p.router_w + (size_t)mine * H, xt, H) : 0.0f;
-            __syncwarp();
-            if (mine >= 0) {
-                row[mine] = v;
-                if (p.logits) p.logits[(size_t)t * E + mine] = v;
-            }
-            __syncwarp();
-        }
-        if (lane == 0 && p.refined) atomicAdd(p.refined, 1u);
-        warp_select_n<NS>(row, E, k, gate, lane, sc, id);
-    }
-    pick_weights(sc, k, gate, lane, w_out);
-    return id;
-}
-
-// The fast router's top-k of token t (refined near ties); plain top-k for exact logits.
-__device__ int warp_topk_fast(const RouteParams& p, int t, float* row, int lane, float* w_out) {
-    const int E = p.E;
-    if (p.exact || !p.x || !(p.router_wmax > 0.0f)) return warp_topk(row, E, p.k, p.gate, lane, w_out);
-    const int ns = (E + 31) / 32;
-    if (ns <= 1) return warp_topk_refined_n<1>(p, t, row, lane, w_out);
-    if (ns <= 2) return warp_topk_refined_n<2>(p, t, row, lane, w_out);
-    if (ns <= 4) return warp_topk_refined_n<4>(p, t, row, lane, w_out);
-    if (ns <= 8) return warp_topk_refined_n<8>(p, t, row, lane, w_out);
-    return warp_topk_refined_n<MAX_E / 32>(p, t, row, lane, w_out);
-}
+// (top-k of one token and the near-tie refinement of the fast router: topk.cuh)
 
 // ---------------------------------------------------------------------------------------
 // top-k + counts (+ last-CTA scan and tile list)

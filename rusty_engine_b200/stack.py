@@ -187,15 +187,19 @@ class MoEStack:
         p = torch.softmax(scores, dim=-1)
         return torch.matmul(p, vh).transpose(0, 1).reshape(T, g.n_heads * g.head_dim)
 
-    def forward(self, x, pos_start: int = 0, time_moe: bool = True):
+    def forward(self, x, pos_start: int = 0, time_moe: bool = True, collect: bool = False):
         """x: [T, d_model] f32 cuda tensor -> [T, d_model]; self.moe_ms gets the MoE layers'
-        times (ms, CUDA events on the current stream)."""
+        times (ms, CUDA events on the current stream).  collect: also keep every block's input
+        in self.block_inputs (for per-block checks)."""
         g = self.g
         T = x.shape[0]
         cos, sin = (torch.from_numpy(a).to(x.device) for a in rope_tables(g, T, pos_start))
         stream = torch.cuda.current_stream()
         events = []
+        self.block_inputs = []
         for L in self.layers:
+            if collect:
+                self.block_inputs.append(x.clone())
             xn = self._rmsnorm(x, L["attn_norm"])
             q = L["q"].matmul_device(xn)
             k = L["k"].matmul_device(xn)

