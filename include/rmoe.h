@@ -261,6 +261,14 @@ RMOE_API rmoe_status rmoe_gguf_meta_uint(const rmoe_gguf* g, const char* key, ui
  * points into the mapping: pass it to rmoe_layer_create before rmoe_gguf_close. */
 RMOE_API rmoe_status rmoe_gguf_moe_layer_desc(rmoe_gguf* g, uint32_t block, rmoe_layer_desc* out);
 
+/* Self-test of the tensor-core kernels' bounded waits (no counterpart in the reference): one
+ * CTA on `device` allocates tensor memory, waits on an mbarrier that nothing arrives at with a
+ * limit of limit_us (1 .. 1000000) instead of the kernels' 1 s, then records DERR_TIMEOUT,
+ * frees the tensor memory and returns, as the product kernels do when a wait runs out.
+ * Returns RMOE_ERR_DEVICE with the timeout in the message (what a product call whose wait ran
+ * out reports); the context stays usable.  RMOE_ERR_CUDA for any other outcome. */
+RMOE_API rmoe_status rmoe_selftest_bounded_wait(int32_t device, uint32_t limit_us);
+
 /* Build info: "sm_100a <git-describe> <kernels...>". */
 RMOE_API const char* rmoe_build_info(void);
 

@@ -55,7 +55,7 @@ EXPORTS = [
     "rmoe_ep_layer_create", "rmoe_build_info", "rmoe_layer_stage_ms", "rmoe_layer_forward_noalloc",
     "rmoe_route_grouped", "rmoe_qmat_create", "rmoe_qmat_forward", "rmoe_qmat_status", "rmoe_qmat_destroy",
     "rmoe_gguf_open", "rmoe_gguf_close", "rmoe_gguf_tensor", "rmoe_gguf_meta_uint", "rmoe_gguf_moe_layer_desc",
-    "rmoe_layer_router_refined", "rmoe_noalloc_status",
+    "rmoe_layer_router_refined", "rmoe_noalloc_status", "rmoe_selftest_bounded_wait",
 ]
 
 NOALLOC_SCRATCH_BYTES = 8 << 20  # RMOE_NOALLOC_SCRATCH_BYTES
@@ -82,6 +82,7 @@ def load():
         L.rmoe_layer_stage_ms.argtypes = [vp, vp]
         L.rmoe_layer_router_refined.argtypes = [vp, vp]
         L.rmoe_noalloc_status.argtypes = [i32]
+        L.rmoe_selftest_bounded_wait.argtypes = [i32, u32]
         L.rmoe_layer_destroy.argtypes = [vp]
         L.rmoe_layer_destroy.restype = None
         L.rmoe_last_error.restype = C.c_char_p

@@ -32,14 +32,15 @@ __device__ __forceinline__ uint64_t globaltimer() {
     asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
     return t;
 }
-// Wait for the phase with the given parity to complete; gives up after ~1 s (the kernel then
-// records DERR_TIMEOUT and winds down instead of hanging the GPU).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Wait for the phase with the given parity to complete; gives up after limit_ns (~1 s in the
+// product kernels; the kernel then records DERR_TIMEOUT and winds down instead of hanging the
+// GPU).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_t limit_ns = 1000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t i = 0;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255) == 255 && globaltimer() - t0 > 1000000000ull) return false;
+        if ((i & 255) == 255 && globaltimer() - t0 > limit_ns) return false;
     }
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
