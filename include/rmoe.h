@@ -231,7 +231,12 @@ RMOE_API rmoe_status rmoe_ep_unique_id(uint8_t id[128]);
  * tokens.  rmoe_layer_forward on the handle takes this rank's T tokens
  * (device or RMOE_FLAG_HOST_IO buffers) and returns their complete layer outputs; it exchanges
  * rows with the other ranks over NCCL and reads the per-rank row counts back to the host
- * once (the call synchronises the stream there). */
+ * once (the call synchronises the stream there).
+ * Failure detection: the communicator is non-blocking; the create (which waits for every
+ * rank to join) and every host wait of a forward give up after RMOE_EP_TIMEOUT_MS
+ * milliseconds without progress (environment variable, default 120000), or at once on an NCCL
+ * error: the communicator is then aborted (its kernels end) and the call returns
+ * RMOE_ERR_NCCL, as does every later forward on the handle. */
 RMOE_API rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* desc, int32_t rank, int32_t world_size,
                                  const uint8_t id[128], rmoe_layer** out);
 

@@ -60,6 +60,23 @@ def attention(q, k, v, g):
     return ctx
 
 
+def attention_residual(g, b, x, cos, sin):
+    """y = x + o(attention(rmsnorm(x))): the block before its MoE FFN, float64 inside."""
+    qd, kvd = g.n_heads * g.head_dim, g.n_kv_heads * g.head_dim
+    x = x.astype(np.float32)
+    xn = rmsnorm(x, b.attn_norm, g.rms_eps)
+    q = rope(proj(b.q, qd, g.d_model, xn), g.n_heads, g.head_dim, cos, sin)
+    k = rope(proj(b.k, kvd, g.d_model, xn), g.n_kv_heads, g.head_dim, cos, sin)
+    v = proj(b.v, kvd, g.d_model, xn)
+    ctx = attention(q, k, v, g)
+    return (x.astype(np.float64) + proj(b.o, g.d_model, qd, ctx)).astype(np.float32)
+
+
+def moe_residual(g, b, y):
+    """The MoE FFN of a block on its attention residual y: moe_layer_forward(rmsnorm(y))."""
+    return O.moe_layer_q_exact(rmsnorm(y, b.ffn_norm, g.rms_eps), b.moe)[0]
+
+
 def stack_forward(g, blocks, x, cos, sin):
     """Hidden states after every block, [T, d_model] f32 each (last one = the output)."""
     outs = []

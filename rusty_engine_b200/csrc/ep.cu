@@ -23,7 +23,10 @@
 // src/moe.rs:360-388); the sum over a token's experts is regrouped by rank, which changes
 // only the f32 summation order.
 #include <nccl.h>
+#include <stdlib.h>
 
+#include <chrono>
+#include <thread>
 #include <vector>
 
 #include "../../include/rmoe.h"
@@ -55,7 +58,10 @@ struct EpState {
     float* ret = nullptr;    // [send rows][H] partial sums coming back
     uint8_t* recvbuf = nullptr;
     float* part = nullptr;   // [recv rows][H] partial sums computed here
+    int timeout_ms = 120000;      // no progress for this long: the communicator is aborted
+    cudaEvent_t ev = nullptr;     // host waits go through this event
     ~EpState() {
+        if (ev) cudaEventDestroy(ev);
         if (h_cnt) cudaFreeHost(h_cnt);
         if (comm) ncclCommDestroy(comm);
     }
@@ -173,6 +179,52 @@ static rmoe_status nccl_fail(ncclResult_t r, const char* what) {
     return fail(RMOE_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
 }
 
+// Failure detection.  The communicator is non-blocking, and every host wait of an
+// expert-parallel call polls both the GPU work and the communicator's asynchronous error: an
+// NCCL error, or no progress for timeout_ms (a peer rank that stopped, so the exchange kernels
+// wait for it), aborts the communicator -- which ends its kernels -- and the call returns
+// RMOE_ERR_NCCL; every later call on the handle returns the same.
+static rmoe_status ep_abort(EpState& P, rmoe_status st) {
+    if (P.comm) ncclCommAbort(P.comm);
+    P.comm = nullptr;
+    return st;
+}
+
+static rmoe_status ep_poll(EpState& P, const char* what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t q = P.ev ? cudaEventQuery(P.ev) : cudaSuccess;
+        ncclResult_t a = ncclSuccess;
+        if (ncclCommGetAsyncError(P.comm, &a) != ncclSuccess || (a != ncclSuccess && a != ncclInProgress))
+            return ep_abort(P, nccl_fail(a, what));
+        if (q == cudaSuccess && a == ncclSuccess) return RMOE_OK;
+        if (q != cudaSuccess && q != cudaErrorNotReady) return cuda_fail(q, what);
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (ms > P.timeout_ms)
+            return ep_abort(P, fail(RMOE_ERR_NCCL, "%s: no progress for %d ms (a peer rank stopped?); the communicator "
+                                                   "was aborted", what, P.timeout_ms));
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// After ncclGroupEnd on the non-blocking communicator: wait until the group is enqueued.
+static rmoe_status ep_enqueued(EpState& P, ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return RMOE_OK;
+    if (r != ncclInProgress) return ep_abort(P, nccl_fail(r, what));
+    cudaEvent_t keep = P.ev;
+    P.ev = nullptr;  // poll the communicator alone
+    rmoe_status st = ep_poll(P, what);
+    P.ev = keep;
+    return st;
+}
+
+// Wait, bounded, for the work queued on s so far.
+static rmoe_status ep_sync(EpState& P, cudaStream_t s, const char* what) {
+    cudaError_t e = cudaEventRecord(P.ev, s);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return ep_poll(P, what);
+}
+
 static rmoe_status ep_token_buffers(rmoe_layer* L, uint32_t T) {
     EpState& P = *L->ep;
     if (T <= P.capT) return RMOE_OK;
@@ -220,6 +272,7 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     EpState& P = *L->ep;
     const int G = P.world, H = (int)L->H, k = (int)L->k, El = (int)L->E;
     const uint32_t rb = row_bytes(L->H, L->k);
+    if (!P.comm) return fail(RMOE_ERR_NCCL, "expert-parallel layer: the communicator was aborted by an earlier failure");
     rmoe_status st = ep_token_buffers(L, T ? T : 1);
     if (st) return st;
     cudaError_t e;
@@ -242,10 +295,11 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
         if (r == ncclSuccess) r = ncclRecv(P.cnt + G + q, 1, ncclInt32, q, P.comm, s);
     }
     ncclResult_t r2 = ncclGroupEnd();
-    if (r != ncclSuccess || r2 != ncclSuccess) return nccl_fail(r != ncclSuccess ? r : r2, "ep counts exchange");
-    if ((e = cudaMemcpyAsync(P.h_cnt, P.cnt, 2 * G * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess ||
-        (e = cudaStreamSynchronize(s)) != cudaSuccess)
+    if (r != ncclSuccess) return ep_abort(P, nccl_fail(r, "ep counts exchange"));
+    if ((st = ep_enqueued(P, r2, "ep counts exchange"))) return st;
+    if ((e = cudaMemcpyAsync(P.h_cnt, P.cnt, 2 * G * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
         return cuda_fail(e, "ep counts");
+    if ((st = ep_sync(P, s, "ep counts"))) return st;
     std::vector<uint64_t> soff(G + 1, 0), roff(G + 1, 0);
     for (int q = 0; q < G; q++) {
         soff[q + 1] = soff[q] + (uint64_t)P.h_cnt[q];
@@ -267,7 +321,8 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
             r = ncclRecv(P.recvbuf + roff[q] * rb, (size_t)P.h_cnt[G + q] * rb, ncclUint8, q, P.comm, s);
     }
     r2 = ncclGroupEnd();
-    if (r != ncclSuccess || r2 != ncclSuccess) return nccl_fail(r != ncclSuccess ? r : r2, "ep dispatch exchange");
+    if (r != ncclSuccess) return ep_abort(P, nccl_fail(r, "ep dispatch exchange"));
+    if ((st = ep_enqueued(P, r2, "ep dispatch exchange"))) return st;
     // 5. local experts over the received rows
     if (R) {
         if ((st = ensure_workspace(L, (uint32_t)R, flags & RMOE_FLAG_DETERMINISTIC))) return st;
@@ -289,7 +344,8 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
             r = ncclRecv(P.ret + soff[q] * H, (size_t)P.h_cnt[q] * H, ncclFloat32, q, P.comm, s);
     }
     r2 = ncclGroupEnd();
-    if (r != ncclSuccess || r2 != ncclSuccess) return nccl_fail(r != ncclSuccess ? r : r2, "ep combine exchange");
+    if (r != ncclSuccess) return ep_abort(P, nccl_fail(r, "ep combine exchange"));
+    if ((st = ep_enqueued(P, r2, "ep combine exchange"))) return st;
     if (T) {
         ep_combine_kernel<<<T, 256, 0, s>>>(P.ret, P.pos, P.cnt, (int)T, H, G, out);
         if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "ep combine launch");
@@ -302,6 +358,7 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
 // Host buffers in and out, copies inside the call (synchronises the stream).
 rmoe_status ep_forward_host(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags) {
     EpState& P = *L->ep;
+    if (!P.comm) return fail(RMOE_ERR_NCCL, "expert-parallel layer: the communicator was aborted by an earlier failure");
     rmoe_status st = ep_token_buffers(L, T ? T : 1);
     if (st) return st;
     cudaError_t e = cudaMemcpyAsync(P.xin, x, (size_t)T * L->H * 4, cudaMemcpyHostToDevice, s);
@@ -309,7 +366,7 @@ rmoe_status ep_forward_host(rmoe_layer* L, const float* x, uint32_t T, float* ou
     if ((st = ep_forward(L, P.xin, T, P.xout, s, flags & ~RMOE_FLAG_HOST_IO))) return st;
     if ((e = cudaMemcpyAsync(out, P.xout, (size_t)T * L->H * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
         return cuda_fail(e, "out download");
-    if ((e = cudaStreamSynchronize(s)) != cudaSuccess) return cuda_fail(e, "forward");
+    if ((st = ep_sync(P, s, "forward"))) return st;
     return RMOE_OK;
 }
 
@@ -368,13 +425,34 @@ rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* d, int32_t rank, int32_t
         delete L;
         return fail(RMOE_ERR_OOM, "pinned count buffer");
     }
+    if (const char* t = getenv("RMOE_EP_TIMEOUT_MS")) {
+        const long v = strtol(t, nullptr, 10);
+        if (v > 0) L->ep->timeout_ms = (int)v;
+    }
+    if (cudaEventCreateWithFlags(&L->ep->ev, cudaEventDisableTiming) != cudaSuccess) {
+        delete L;
+        return fail(RMOE_ERR_CUDA, "expert-parallel event");
+    }
     ncclUniqueId u;
     for (int i = 0; i < 128; i++) u.internal[i] = (char)id[i];
-    ncclResult_t r = ncclCommInitRank(&L->ep->comm, world_size, u, rank);
-    if (r != ncclSuccess) {
+    // non-blocking communicator: the init (which waits for every rank) and every later wait are
+    // polled with the timeout instead of blocking for good on a rank that never comes
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = ncclCommInitRankConfig(&L->ep->comm, world_size, u, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        if (L->ep->comm) ncclCommAbort(L->ep->comm);
         L->ep->comm = nullptr;
         delete L;
-        return nccl_fail(r, "ncclCommInitRank");
+        return nccl_fail(r, "ncclCommInitRankConfig");
+    }
+    cudaEvent_t keep = L->ep->ev;
+    L->ep->ev = nullptr;
+    rmoe_status ist = ep_poll(*L->ep, "ncclCommInitRankConfig (waiting for every rank to join)");
+    L->ep->ev = keep;
+    if (ist) {
+        delete L;
+        return ist;
     }
     *out = L;
     return RMOE_OK;

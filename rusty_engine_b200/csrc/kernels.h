@@ -75,6 +75,7 @@ struct RouteParams {
     float router_wmax;      // max over experts of ||router row||_2 (sizes the fast router's
                             // near-tie window; 0 turns the refinement off)
     unsigned int* refined;  // optional counter of tokens whose near-tie logits were rescored
+    int stage_floats;       // dynamic shared memory the top-k kernel has for rescoring (floats)
 };
 
 // Grouped expert products over the expert-sorted rows.

@@ -36,6 +36,7 @@ struct SmallLayerParams {
     GroupedParams g;     // expert stacks, h / hexp / rowexp, out
     unsigned* bar;       // grid barrier words: arrivals, generation (zero at first use)
     int depth_gu, ring_gu, depth_dn, ring_dn;
+    int stage_floats;    // shared memory after the logit rows, for rescoring near-ties
 };
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
@@ -148,11 +149,35 @@ __global__ void __launch_bounds__(GV_THREADS, 2) layer_small_kernel(SmallLayerPa
     RouteParams rp = p;
     rp.logits = nullptr;
     if (blockIdx.x != 0) rp.refined = nullptr;
+    __shared__ int amb_t[LS_MAX_T], amb_n;
+    __shared__ float amb_thr[LS_MAX_T];
+    if (tid == 0) amb_n = 0;
+    __syncthreads();
     for (int t = warp; t < T; t += GV_THREADS / 32) {
-        const int id = warp_topk_fast(rp, t, rows_s + (size_t)t * E, lane, s_wts + t * k);
+        int id;
+        float thr;
+        if (!refine_on(rp)) {
+            id = warp_topk(rows_s + (size_t)t * E, E, k, p.gate, lane, s_wts + t * k);
+        } else if (!warp_topk_try(rp, t, rows_s + (size_t)t * E, lane, s_wts + t * k, id, thr)) {
+            if (lane == 0) {  // near-tie: rescored by the whole CTA below
+                const int i = atomicAdd(&amb_n, 1);
+                amb_t[i] = t;
+                amb_thr[i] = thr;
+            }
+            continue;
+        }
         if (lane < k) s_ids[t * k + lane] = id;
     }
     __syncthreads();
+    for (int i = 0; i < amb_n; i++) {  // CTA-uniform; the stage follows the logit rows
+        const int t = amb_t[i];
+        cta_rescore(rp, t, rows_s + (size_t)t * E, amb_thr[i], rows_s + ((T * E + 3) & ~3), sp.stage_floats);
+        if (warp == 0) {
+            const int id = warp_topk(rows_s + (size_t)t * E, E, k, p.gate, lane, s_wts + t * k);
+            if (lane < k) s_ids[t * k + lane] = id;
+        }
+        __syncthreads();
+    }
     const int np = T * k, nrows = np + (p.has_shared ? T : 0);
     if (blockIdx.x == 0)
         for (int i = tid; i < np; i += GV_THREADS) {
@@ -247,8 +272,10 @@ static cudaError_t go_small(SmallLayerParams sp, int* grid_cache, cudaStream_t s
     size_t sm_gu, sm_dn;
     gv_layout<TG, NT, 2, KSG>(H, sp.depth_gu, sp.ring_gu, sm_gu);
     gv_layout<TD, NT, 1, KSD>(I, sp.depth_dn, sp.ring_dn, sm_dn);
-    const size_t sm_route = (size_t)sp.r.T * sp.r.E * 4;
+    const int rows_floats = (sp.r.T * sp.r.E + 3) & ~3;
+    const size_t sm_route = (size_t)(rows_floats + rescore_stage_floats(sp.r.H)) * 4;
     const size_t smem = std::max(std::max(sm_gu, sm_dn), sm_route);
+    sp.stage_floats = (int)(smem / 4) - rows_floats;
     if (smem > 227 * 1024) return cudaErrorNotSupported;
     auto kfn = layer_small_kernel<TG, TD, NT, KSG, KSD>;
     cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -438,13 +438,19 @@ __device__ void build_tiles(const RouteParams& p, const int* cnt_s, int* off_s) 
 }
 
 __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
+    extern __shared__ __align__(16) float tk_stage[];  // rescoring stage (p.stage_floats)
     __shared__ int ids_s[TK_TOK * MAX_K];
     __shared__ float row_s[TK_THREADS / 32][MAX_E];
+    __shared__ int amb_tl[TK_TOK], amb_n;
+    __shared__ float amb_thr[TK_TOK];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = blockIdx.x * TK_TOK;
     const int E = p.E, H = p.H, k = p.k;
     const int ntok = min(TK_TOK, p.T - t0);
     const int ncta = gridDim.x;
+    const bool refine = !p.given && refine_on(p);
+    if (tid == 0) amb_n = 0;
+    __syncthreads();
 
     for (int tl = warp; tl < ntok; tl += TK_THREADS / 32) {
         int t = t0 + tl;
@@ -453,12 +459,39 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
             continue;
         }
         logit_row(p, t, lane, row_s[warp]);
-        int id = warp_topk_fast(p, t, row_s[warp], lane, p.topk_w + (size_t)t * k);
+        int id;
+        float thr;
+        if (!refine) {
+            id = warp_topk(row_s[warp], E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+        } else if (!warp_topk_try(p, t, row_s[warp], lane, p.topk_w + (size_t)t * k, id, thr)) {
+            if (lane == 0) {  // near-tie: rescored by the whole CTA below
+                const int i = atomicAdd(&amb_n, 1);
+                amb_tl[i] = tl;
+                amb_thr[i] = thr;
+            }
+            __syncwarp();
+            continue;
+        }
         if (lane < k) {
             p.topk_id[(size_t)t * k + lane] = id;
             ids_s[tl * k + lane] = id;
         }
         __syncwarp();  // the row is read before the warp's next token overwrites it
+    }
+    __syncthreads();
+    for (int i = 0; i < amb_n; i++) {  // CTA-uniform
+        const int tl = amb_tl[i], t = t0 + tl;
+        float* row = row_s[0];
+        for (int q = tid; q < E; q += TK_THREADS) row[q] = __ldcg(p.logits + (size_t)t * E + q);
+        cta_rescore(p, t, row, amb_thr[i], tk_stage, p.stage_floats);
+        if (warp == 0) {
+            const int id = warp_topk(row, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+            if (lane < k) {
+                p.topk_id[(size_t)t * k + lane] = id;
+                ids_s[tl * k + lane] = id;
+            }
+        }
+        __syncthreads();
     }
     // zero the output rows this CTA owns when the combine accumulates with atomics (the x
     // gather kernel does it instead when it runs)
@@ -725,8 +758,10 @@ __global__ void __launch_bounds__(RS_THREADS) route_small_kernel(RouteParams p) 
 static constexpr int RF_EXP = 8, RF_TOK = 8, RF_THREADS = 256;
 static constexpr int RF_WCH = 16;  // float4 of the expert row each lane holds at a time
 
+static int rf_stage_off(int E) { return (RF_TOK * E + 3) & ~3; }  // floats before the rescoring stage
 static size_t route_fused_smem(int T, int H, int E, int k) {
-    return std::max(std::max((size_t)RF_TOK * H * 4, (size_t)RF_TOK * E * 4), dispatch_small_scratch(T, E, k));
+    const size_t need = std::max(std::max((size_t)RF_TOK * H * 4, (size_t)RF_TOK * E * 4), dispatch_small_scratch(T, E, k));
+    return std::max(need, (size_t)(rf_stage_off(E) + rescore_stage_floats(H)) * 4);
 }
 
 template <int MODE>  // 0: logits (and the fp16 copy) only; 1: + top-k; 2: + the dispatch
@@ -831,13 +866,42 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     float* lg = fsm;  // the group's logits, read past L1 (other CTAs wrote them)
     for (int q = tid; q < nt * E; q += RF_THREADS) lg[q] = __ldcg(p.logits + (size_t)t0 * E + q);
     __syncthreads();
+    __shared__ int amb_w[RF_TOK], amb_n;
+    __shared__ float amb_thr[RF_TOK];
+    if (tid == 0) amb_n = 0;
+    __syncthreads();
     if (warp < nt) {
         const int t = t0 + warp;
-        const int id = warp_topk_fast(p, t, lg + warp * E, lane, p.topk_w + (size_t)t * k);
-        if (lane < k) {
+        int id;
+        float thr;
+        bool done = true;
+        if (!refine_on(p)) {
+            id = warp_topk(lg + warp * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+        } else if (!warp_topk_try(p, t, lg + warp * E, lane, p.topk_w + (size_t)t * k, id, thr)) {
+            done = false;
+            if (lane == 0) {  // near-tie: rescored by the whole CTA below
+                const int i = atomicAdd(&amb_n, 1);
+                amb_w[i] = warp;
+                amb_thr[i] = thr;
+            }
+        }
+        if (done && lane < k) {
             p.topk_id[(size_t)t * k + lane] = id;
             ids_s[t * k + lane] = id;
         }
+    }
+    __syncthreads();
+    for (int i = 0; i < amb_n; i++) {  // CTA-uniform; the stage follows the group's logit rows
+        const int w = amb_w[i], t = t0 + w;
+        cta_rescore(p, t, lg + w * E, amb_thr[i], fsm + ((RF_TOK * E + 3) & ~3), p.stage_floats);
+        if (warp == 0) {
+            const int id = warp_topk(lg + w * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+            if (lane < k) {
+                p.topk_id[(size_t)t * k + lane] = id;
+                ids_s[t * k + lane] = id;
+            }
+        }
+        __syncthreads();
     }
 
     // 4. the last token group: dispatch of the whole batch (a single group is its own last)
@@ -860,13 +924,27 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     }
 }
 
-static cudaError_t launch_route_fused(const RouteParams& p, int mode, cudaStream_t s) {
+static cudaError_t launch_route_fused(const RouteParams& p0, int mode, cudaStream_t s) {
+    RouteParams p = p0;
     const size_t sm = mode == 0 ? (size_t)RF_TOK * p.H * 4 : route_fused_smem(p.T, p.H, p.E, p.k);
+    p.stage_floats = (int)(sm / 4) - rf_stage_off(p.E);
     auto k = mode == 0 ? route_fused_small_kernel<0> : mode == 1 ? route_fused_small_kernel<1> : route_fused_small_kernel<2>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) return e;
     k<<<dim3((p.E + RF_EXP - 1) / RF_EXP, (p.T + RF_TOK - 1) / RF_TOK), RF_THREADS, sm, s>>>(p);
     return cudaGetLastError();
+}
+
+// Dynamic shared memory of a top-k kernel that may rescore near-ties (sets p.stage_floats).
+template <typename K>
+static cudaError_t rescore_smem(K kernel, RouteParams& p, size_t& sm) {
+    sm = 0;
+    p.stage_floats = 0;
+    if (!refine_on(p) || p.given) return cudaSuccess;
+    p.stage_floats = rescore_stage_floats(p.H);
+    sm = (size_t)p.stage_floats * 4;
+    return sm > 48 * 1024 ? cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
+                          : cudaSuccess;
 }
 
 int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
@@ -906,12 +984,40 @@ __global__ void route_only_kernel(const float* logits, int T, int E, int k, int 
 // Top-k of every token's logits (one warp per token), summing the K-split partials first when
 // the split product made them.
 __global__ void __launch_bounds__(256) route_rows_kernel(RouteParams p) {
+    extern __shared__ __align__(16) float rr_stage[];  // rescoring stage (p.stage_floats)
     __shared__ float row_s[8][MAX_E];
+    __shared__ int amb_w[8], amb_n;
+    __shared__ float amb_thr[8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = blockIdx.x * 8 + warp;
-    if (t >= p.T) return;
-    logit_row(p, t, lane, row_s[warp]);
-    const int id = warp_topk_fast(p, t, row_s[warp], lane, p.topk_w + (size_t)t * p.k);
-    if (lane < p.k) p.topk_id[(size_t)t * p.k + lane] = id;
+    if (threadIdx.x == 0) amb_n = 0;
+    __syncthreads();
+    if (t < p.T) {
+        logit_row(p, t, lane, row_s[warp]);
+        int id;
+        float thr;
+        bool done = true;
+        if (!refine_on(p)) {
+            id = warp_topk(row_s[warp], p.E, p.k, p.gate, lane, p.topk_w + (size_t)t * p.k);
+        } else if (!warp_topk_try(p, t, row_s[warp], lane, p.topk_w + (size_t)t * p.k, id, thr)) {
+            done = false;
+            if (lane == 0) {
+                const int i = atomicAdd(&amb_n, 1);
+                amb_w[i] = warp;
+                amb_thr[i] = thr;
+            }
+        }
+        if (done && lane < p.k) p.topk_id[(size_t)t * p.k + lane] = id;
+    }
+    __syncthreads();
+    for (int i = 0; i < amb_n; i++) {  // CTA-uniform
+        const int w = amb_w[i], tt = blockIdx.x * 8 + w;
+        cta_rescore(p, tt, row_s[w], amb_thr[i], rr_stage, p.stage_floats);
+        if (warp == 0) {
+            const int id = warp_topk(row_s[w], p.E, p.k, p.gate, lane, p.topk_w + (size_t)tt * p.k);
+            if (lane < p.k) p.topk_id[(size_t)tt * p.k + lane] = id;
+        }
+        __syncthreads();
+    }
 }
 
 cudaError_t launch_router_topk(const RouteParams& p0, cudaStream_t s) {
@@ -920,7 +1026,9 @@ cudaError_t launch_router_topk(const RouteParams& p0, cudaStream_t s) {
     if (!use_split(p)) p.logits_part = nullptr;
     cudaError_t e = launch_logits(p, s);
     if (e != cudaSuccess || p.T <= 0) return e;
-    route_rows_kernel<<<(p.T + 7) / 8, 256, 0, s>>>(p);
+    size_t sm;
+    if ((e = rescore_smem(route_rows_kernel, p, sm)) != cudaSuccess) return e;
+    route_rows_kernel<<<(p.T + 7) / 8, 256, sm, s>>>(p);
     return cudaGetLastError();
 }
 
@@ -941,7 +1049,9 @@ cudaError_t launch_route_dispatch(const RouteParams& p0, cudaStream_t s) {
                 return e;
             route_small_kernel<<<1, RS_THREADS, sm, s>>>(p);  // the whole dispatch in one CTA
         } else {
-            topk_count_kernel<<<route_grid(p.T), TK_THREADS, 0, s>>>(p);
+            size_t sm;
+            if ((e = rescore_smem(topk_count_kernel, p, sm)) != cudaSuccess) return e;
+            topk_count_kernel<<<route_grid(p.T), TK_THREADS, sm, s>>>(p);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
             scan_counts_kernel<<<p.E, SC_THREADS, 0, s>>>(p, route_grid(p.T));
             if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -114,48 +114,13 @@ __device__ __forceinline__ int warp_topk(const float* lg, int E, int k, int gate
 // (k+1)-th best is rescored with the exact sequential chain, bit-identical to moe::matvec, and
 // top-k runs again: experts further down are more than tau / 2 below k + 1 others under any
 // of the sums and cannot be chosen.  The ids are then the reference's, near-ties included.
+// Two steps: each warp checks its tokens (warp_topk_try) and defers the close ones; after the
+// CTA's warps are done, the whole CTA rescores each deferred token (cta_rescore), so the rows
+// come in with the CTA's full memory parallelism and only the chain itself is serial.
 // For the sigmoid gate the distances are taken between scores (sigmoid has slope <= 1/4,
 // plus a few ulp for the rounding of the score itself).
 // ---------------------------------------------------------------------------------------
 static constexpr float REFINE_UNITS = 64.0f;
-
-// moe::matvec's logit of expert e for token t: products rounded, then added in ascending k
-// to a running f32 sum that starts at 0, with no contraction.  The additions are one serial
-// chain (about 4 cycles each); to keep the loads off it, the rows are streamed through L1 with
-// prefetches RF_PF lines (128 B) ahead, so the loads inside the chain hit L1.  Every lane of a
-// warp may run its own chain; they read the same x line at once (one broadcast).
-static constexpr int RF_PF = 16;
-__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];\n" ::"l"(p)); }
-static __device__ __noinline__ float exact_logit(const float* __restrict__ w, const float* __restrict__ x, int H) {
-    for (int l = 0; l < RF_PF && 32 * l < H; l++) {
-        prefetch_l1(w + 32 * l);
-        prefetch_l1(x + 32 * l);
-    }
-    const float4* w4 = reinterpret_cast<const float4*>(w);
-    const float4* x4 = reinterpret_cast<const float4*>(x);
-    float s = 0.0f;
-#pragma unroll 2
-    for (int i = 0; i < H; i += 32) {
-        if (i + 32 * RF_PF < H) {
-            prefetch_l1(w + i + 32 * RF_PF);
-            prefetch_l1(x + i + 32 * RF_PF);
-        }
-        float4 a[8], b[8];
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-            a[q] = __ldg(w4 + i / 4 + q);
-            b[q] = __ldg(x4 + i / 4 + q);
-        }
-#pragma unroll
-        for (int q = 0; q < 8; q++) {
-            s = __fadd_rn(s, __fmul_rn(a[q].x, b[q].x));
-            s = __fadd_rn(s, __fmul_rn(a[q].y, b[q].y));
-            s = __fadd_rn(s, __fmul_rn(a[q].z, b[q].z));
-            s = __fadd_rn(s, __fmul_rn(a[q].w, b[q].w));
-        }
-    }
-    return s;
-}
 
 // ||x_t||_2 (one warp) from the token's fp16 copy (written by the logits step before any top-k
 // runs; 16-B loads through L2, all of a lane's in flight at once).  It only sizes the
@@ -178,71 +143,110 @@ __device__ __forceinline__ float warp_row_norm(const __half* __restrict__ xb, in
     return sqrtf(s);
 }
 
-// Top-k of token t from its fast logits in row[0 .. E) (warp-private shared memory), with the
-// near-tie refinement above.  Refined logits replace the fast ones in row and in p.logits.
+// Whether the fast router refines at all (exact logits need no refinement).
+__host__ __device__ __forceinline__ bool refine_on(const RouteParams& p) {
+    return !p.exact && p.x && p.xb && p.router_wmax > 0.0f;
+}
+
+// First step, one warp per token: top-k of token t from its fast logits in row[0 .. E).  When
+// no two of the k + 1 best scores are within the window, lane j < k gets the j-th id in `id`,
+// the weights are written to w_out, and the call returns true.  Otherwise it returns false
+// with `thr`, the score from which experts must be rescored (the (k+1)-th best minus the
+// window; -inf when k = E, where only the order can change); the caller then runs
+// cta_rescore and warp_topk on the row.
 template <int NS>
-__device__ int warp_topk_refined_n(const RouteParams& p, int t, float* row, int lane, float* w_out) {
-    const int E = p.E, k = p.k, gate = p.gate, H = p.H;
-    const float* xt = p.x + (size_t)t * H;
-    const float xn = warp_row_norm(p.xb + (size_t)t * H, H, lane);
+__device__ bool warp_topk_try_n(const RouteParams& p, int t, const float* row, int lane, float* w_out, int& id,
+                                float& thr) {
+    const int E = p.E, k = p.k, gate = p.gate;
+    const float xn = warp_row_norm(p.xb + (size_t)t * p.H, p.H, lane);
     const int n = min(k + 1, E);
     float sc;
-    int id;
     warp_select_n<NS>(row, E, n, gate, lane, sc, id);
     const float tau_l = REFINE_UNITS * 5.9604645e-8f * p.router_wmax * xn;
     const float tau = gate == 1 ? 0.25f * tau_l + 4.7683716e-7f : tau_l;  // + 8 ulp of 1.0
     const float next = __shfl_down_sync(0xffffffffu, sc, 1);
     const bool close = lane + 1 < n && !(sc - next >= tau);
     if (__any_sync(0xffffffffu, close)) {
-        // every expert at or above (k+1)-th score - tau (all of them when k = E: only the
-        // order can change then)
-        const float thr = k < E ? __shfl_sync(0xffffffffu, sc, n - 1) - tau : -INFINITY;
-        unsigned mb = 0u;  // bit s: expert lane + 32 s is rescored
-#pragma unroll
-        for (int s = 0; s < NS; s++) {
-            const int e = lane + 32 * s;
-            if (e < E && !(gate_score(row[e], gate) < thr)) mb |= 1u << s;
-        }
-        int total = 0;
-#pragma unroll
-        for (int s = 0; s < NS; s++) total += __popc(__ballot_sync(0xffffffffu, (mb >> s) & 1u));
-        for (int pass = 0; pass * 32 < total; pass++) {
-            // the rescored experts in ascending order, one per lane
-            const int want = lane + 32 * pass;
-            int mine = -1, base = 0;
-#pragma unroll
-            for (int s = 0; s < NS; s++) {
-                const unsigned m = __ballot_sync(0xffffffffu, (mb >> s) & 1u);
-                const int c = __popc(m);
-                if (want >= base && want < base + c) mine = 32 * s + (int)__fns(m, 0, want - base + 1);
-                base += c;
-            }
-            const float v = mine >= 0 ? exact_logit(p.router_w + (size_t)mine * H, xt, H) : 0.0f;
-            __syncwarp();
-            if (mine >= 0) {
-                row[mine] = v;
-                if (p.logits) p.logits[(size_t)t * E + mine] = v;
-            }
-            __syncwarp();
-        }
-        if (lane == 0 && p.refined) atomicAdd(p.refined, 1u);
-        warp_select_n<NS>(row, E, k, gate, lane, sc, id);
+        thr = k < E ? __shfl_sync(0xffffffffu, sc, n - 1) - tau : -INFINITY;
+        return false;
     }
     pick_weights(sc, k, gate, lane, w_out);
-    return id;
+    return true;
 }
 
-// The fast router's top-k of token t (refined near ties); plain top-k for exact logits.
-__device__ __forceinline__ int warp_topk_fast(const RouteParams& p, int t, float* row, int lane, float* w_out) {
-    const int E = p.E;
-    if (p.exact || !p.x || !p.xb || !(p.router_wmax > 0.0f)) return warp_topk(row, E, p.k, p.gate, lane, w_out);
-    const int ns = (E + 31) / 32;
-    if (ns <= 1) return warp_topk_refined_n<1>(p, t, row, lane, w_out);
-    if (ns <= 2) return warp_topk_refined_n<2>(p, t, row, lane, w_out);
-    if (ns <= 4) return warp_topk_refined_n<4>(p, t, row, lane, w_out);
-    if (ns <= 8) return warp_topk_refined_n<8>(p, t, row, lane, w_out);
-    return warp_topk_refined_n<MAX_E / 32>(p, t, row, lane, w_out);
+__device__ __forceinline__ bool warp_topk_try(const RouteParams& p, int t, const float* row, int lane, float* w_out,
+                                              int& id, float& thr) {
+    const int ns = (p.E + 31) / 32;
+    if (ns <= 1) return warp_topk_try_n<1>(p, t, row, lane, w_out, id, thr);
+    if (ns <= 2) return warp_topk_try_n<2>(p, t, row, lane, w_out, id, thr);
+    if (ns <= 4) return warp_topk_try_n<4>(p, t, row, lane, w_out, id, thr);
+    if (ns <= 8) return warp_topk_try_n<8>(p, t, row, lane, w_out, id, thr);
+    return warp_topk_try_n<MAX_E / 32>(p, t, row, lane, w_out, id, thr);
 }
 
+// Second step, the whole CTA (every thread calls it): the experts of token t scoring at least
+// thr are rescored with moe::matvec's sequential chain (src/moe.rs:271-277): products rounded,
+// then added in ascending k to a running f32 sum that starts at 0, no contraction.  The CTA
+// loads x_t and as many of those experts' router rows as `stage` holds (stage_floats floats of
+// shared memory, at least 2 H) with 16-B loads all in flight at once, then one thread per
+// expert runs its chain from shared memory (the chain itself is the floor: H dependent adds).
+// The exact logits replace the fast ones in row (and in p.logits when set).
+static __device__ void cta_rescore(const RouteParams& p, int t, float* row, float thr, float* stage, int stage_floats) {
+    __shared__ int s_mem[MAX_E];
+    __shared__ int s_nm;
+    const int E = p.E, H = p.H, gate = p.gate;
+    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31;
+    __syncthreads();
+    if (tid < 32) {
+        int base = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const bool m = e < E && !(gate_score(row[e], gate) < thr);
+            const unsigned b = __ballot_sync(0xffffffffu, m);
+            if (m) s_mem[base + __popc(b & ((1u << lane) - 1u))] = e;
+            base += __popc(b);
+        }
+        if (lane == 0) s_nm = base;
+    }
+    __syncthreads();
+    const int nm = s_nm, cap = stage_floats / H - 1;
+    const float4* x4 = reinterpret_cast<const float4*>(p.x + (size_t)t * H);
+    float4* st4 = reinterpret_cast<float4*>(stage);
+    const int h4 = H / 4;
+    for (int m0 = 0; m0 < nm; m0 += cap) {
+        const int mc = min(cap, nm - m0);
+        for (int q = tid; q < (1 + mc) * h4; q += nthr) {
+            const int r = q / h4, j = q - r * h4;
+            const float4* src = r == 0 ? x4 : reinterpret_cast<const float4*>(p.router_w + (size_t)s_mem[m0 + r - 1] * H);
+            st4[q] = __ldg(src + j);
+        }
+        __syncthreads();
+        if (tid < mc) {
+            const float4* xs = st4;
+            const float4* ws = st4 + (size_t)(1 + tid) * h4;
+            float s = 0.0f;
+#pragma unroll 4
+            for (int j = 0; j < h4; j++) {
+                const float4 a = ws[j], b = xs[j];
+                s = __fadd_rn(s, __fmul_rn(a.x, b.x));
+                s = __fadd_rn(s, __fmul_rn(a.y, b.y));
+                s = __fadd_rn(s, __fmul_rn(a.z, b.z));
+                s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+            }
+            const int e = s_mem[m0 + tid];
+            row[e] = s;
+            if (p.logits) p.logits[(size_t)t * E + e] = s;
+        }
+        __syncthreads();
+    }
+    if (tid == 0 && p.refined) atomicAdd(p.refined, 1u);
+}
+
+// Shared memory the rescoring stage needs for rows of H floats: x and up to four expert rows
+// (at least one).
+__host__ __device__ inline int rescore_stage_floats(int H) {
+    const int rows = 1 + (H <= 2048 ? 4 : H <= 4096 ? 2 : 1);
+    return rows * H;
+}
 
 }  // namespace rmoe

@@ -190,13 +190,14 @@ class MoEStack:
     def forward(self, x, pos_start: int = 0, time_moe: bool = True, collect: bool = False):
         """x: [T, d_model] f32 cuda tensor -> [T, d_model]; self.moe_ms gets the MoE layers'
         times (ms, CUDA events on the current stream).  collect: also keep every block's input
-        in self.block_inputs (for per-block checks)."""
+        in self.block_inputs and every block's attention residual (before the MoE FFN) in
+        self.block_mids (for per-part checks)."""
         g = self.g
         T = x.shape[0]
         cos, sin = (torch.from_numpy(a).to(x.device) for a in rope_tables(g, T, pos_start))
         stream = torch.cuda.current_stream()
         events = []
-        self.block_inputs = []
+        self.block_inputs, self.block_mids = [], []
         for L in self.layers:
             if collect:
                 self.block_inputs.append(x.clone())
@@ -208,6 +209,8 @@ class MoEStack:
             k = self._rope(k, g.n_kv_heads, cos, sin)
             ctx = self._attention(q, k, v).contiguous()
             y = x + L["o"].matmul_device(ctx)
+            if collect:
+                self.block_mids.append(y.clone())
             yn = self._rmsnorm(y, L["ffn_norm"]).contiguous()
             if time_moe:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

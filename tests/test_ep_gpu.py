@@ -74,3 +74,38 @@ def test_ep_two_gpus_shared_expert(gpu):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     _run(2, (5, 300), shared=True)
+
+
+def _create_alone(q):
+    """Rank 0 of a two-rank layer whose other rank never calls in (child process)."""
+    import os
+    import time
+
+    os.environ["RMOE_EP_TIMEOUT_MS"] = "3000"
+    from rusty_engine_b200.moe import MoELayer, ep_unique_id
+
+    t0 = time.time()
+    try:
+        MoELayer.expert_parallel(synth.config_c1(), 0, 2, ep_unique_id(), device=0)
+        q.put((0, "created", time.time() - t0))
+    except Exception as e:  # RmoeError: "rmoe NCCL: <message>"
+        q.put((-1, f"{type(e).__name__}: {e}", time.time() - t0))
+
+
+def test_ep_create_times_out_when_a_rank_never_joins(gpu):
+    """Failure made on the host: rank 0 of a two-rank expert-parallel layer is created while
+    rank 1 never calls in.  The non-blocking NCCL communicator init gives up after
+    RMOE_EP_TIMEOUT_MS (3 s here), aborts, and the create fails with RMOE_ERR_NCCL instead of
+    blocking for good.  Runs in a child process, itself bounded by a timeout."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_create_alone, args=(q,))
+    p.start()
+    p.join(120)
+    if p.is_alive():
+        p.kill()
+        pytest.fail("the create did not return within 120 s")
+    code, msg, dt = q.get(timeout=10)
+    assert code != 0, msg
+    assert "NCCL" in msg and "no progress" in msg, msg
+    assert dt < 60, dt
