@@ -82,7 +82,8 @@ struct Gv<T_Q4_K> {
     __device__ static int off8(int, int c, int) { return 8 * (c >> 1); }
     // y = d*sc*q - dmin*m: q lands in 1024 + q (low nibble) or 1024 + 16 q (high nibble), both
     // exact; 1024 is taken off / the 16 divided out exactly, then one fma with the fp16 pair.
-    __device__ static void decode(const uint4* q16, const uint2* q8, int, uint16_t, uint32_t (&a)[8][2]) {
+    template <int R>
+    __device__ static void decode(const uint4* q16, const uint2* q8, int, uint16_t, uint32_t (&a)[8][4]) {
         const uint4 q = q16[0];
         const uint2 dm = q8[0];
         const __half2 Dl = as_h2(__byte_perm(dm.x, 0, 0x1010)), Ml = as_h2(__byte_perm(dm.x, 0, 0x3232));
@@ -97,10 +98,10 @@ struct Gv<T_Q4_K> {
             const __half2 l13 = __hsub2(as_h2((v8 & 0x000F000Fu) | 0x64006400u), K1024);
             const __half2 h02 = __hfma2(as_h2((v & 0x00F000F0u) | 0x64006400u), S16, M64);
             const __half2 h13 = __hfma2(as_h2((v8 & 0x00F000F0u) | 0x64006400u), S16, M64);
-            a[2 * i][0] = as_u32(__hfma2(l02, Dl, Ml));
-            a[2 * i][1] = as_u32(__hfma2(l13, Dl, Ml));
-            a[2 * i + 1][0] = as_u32(__hfma2(h02, Dh, Mh));
-            a[2 * i + 1][1] = as_u32(__hfma2(h13, Dh, Mh));
+            a[2 * i][R] = as_u32(__hfma2(l02, Dl, Ml));
+            a[2 * i][2 + R] = as_u32(__hfma2(l13, Dl, Ml));
+            a[2 * i + 1][R] = as_u32(__hfma2(h02, Dh, Mh));
+            a[2 * i + 1][2 + R] = as_u32(__hfma2(h13, Dh, Mh));
         }
     }
 };
@@ -128,7 +129,8 @@ struct Gv<T_Q6_K> {
     // q6 lands in 1024 + q6 (low bits at mantissa 0..3, high at 4..5) or 1024 + 16 q6 (4..7 and
     // 8..9), whichever needs fewer shifts for that quadrant and byte pair; q6 - 32 is recovered
     // exactly and multiplied by the scale d * sc (rounded once to fp16, as the other kernels).
-    __device__ static void decode(const uint4*, const uint2* q8, int c, uint16_t dbits, uint32_t (&a)[8][2]) {
+    template <int R>
+    __device__ static void decode(const uint4*, const uint2* q8, int c, uint16_t dbits, uint32_t (&a)[8][4]) {
         const uint2 A8 = q8[0], B8 = q8[1], H8 = q8[2], S8 = q8[3];
         const __half2 d2 = __half2half2(__ushort_as_half(dbits));
         const int sh = 8 * (c >> 1);
@@ -154,14 +156,14 @@ struct Gv<T_Q6_K> {
             const __half2 q1b = __hfma2(as_h2(((B >> 4) & 0x00F000F0u) | ((H >> 2) & 0x03000300u) | C), S16, M96);
             const __half2 q2b = __hfma2(as_h2(((A >> 8) & 0x00F000F0u) | ((H >> 4) & 0x03000300u) | C), S16, M96);
             const __half2 q3b = __hfma2(as_h2(((B >> 8) & 0x00F000F0u) | ((H >> 6) & 0x03000300u) | C), S16, M96);
-            a[4 * w + 0][0] = as_u32(__hmul2(q0a, sq[0]));
-            a[4 * w + 0][1] = as_u32(__hmul2(q0b, sq[0]));
-            a[4 * w + 1][0] = as_u32(__hmul2(q1a, sq[1]));
-            a[4 * w + 1][1] = as_u32(__hmul2(q1b, sq[1]));
-            a[4 * w + 2][0] = as_u32(__hmul2(q2a, sq[2]));
-            a[4 * w + 2][1] = as_u32(__hmul2(q2b, sq[2]));
-            a[4 * w + 3][0] = as_u32(__hmul2(q3a, sq[3]));
-            a[4 * w + 3][1] = as_u32(__hmul2(q3b, sq[3]));
+            a[4 * w + 0][R] = as_u32(__hmul2(q0a, sq[0]));
+            a[4 * w + 0][2 + R] = as_u32(__hmul2(q0b, sq[0]));
+            a[4 * w + 1][R] = as_u32(__hmul2(q1a, sq[1]));
+            a[4 * w + 1][2 + R] = as_u32(__hmul2(q1b, sq[1]));
+            a[4 * w + 2][R] = as_u32(__hmul2(q2a, sq[2]));
+            a[4 * w + 2][2 + R] = as_u32(__hmul2(q2b, sq[2]));
+            a[4 * w + 3][R] = as_u32(__hmul2(q3a, sq[3]));
+            a[4 * w + 3][2 + R] = as_u32(__hmul2(q3b, sq[3]));
         }
     }
 };
@@ -354,7 +356,9 @@ __device__ __forceinline__ void gv_tile(const GroupedParams& p, int e, int row0,
         const uint2* bu = bsm + (size_t)u * 8 * NTT * 32 + lane;
 #pragma unroll
         for (int m = 0; m < NMAT; m++) {
-            uint32_t a0[8][2], a1[8][2];
+            // A fragments in the register order mma.sync takes them: (row g, k pair 0), (row g + 8,
+            // pair 0), (row g, pair 1), (row g + 8, pair 1) -- each decoder writes its row's two
+            uint32_t afr[8][4];
 #pragma unroll
             for (int r = 0; r < 2; r++) {
                 uint4 q16[D::N16 > 0 ? D::N16 : 1];
@@ -367,12 +371,12 @@ __device__ __forceinline__ void gv_tile(const GroupedParams& p, int e, int row0,
                     q8[j] = *reinterpret_cast<const uint2*>(sl + G::OFF8 + ((m * 2 + r) * D::N8 + j) * (GV_THREADS * 8) +
                                                             tid * 8);
                 const uint16_t db = D::DPL ? dsm[(m * nsb + (u >> 1)) * RB + 16 * rg + g + 8 * r] : 0;
-                if (r == 0) D::decode(q16, q8, c, db, a0);
-                else D::decode(q16, q8, c, db, a1);
+                if (r == 0) D::template decode<0>(q16, q8, c, db, afr);
+                else D::template decode<1>(q16, q8, c, db, afr);
             }
 #pragma unroll
             for (int s = 0; s < 8; s++) {
-                const uint32_t a[4] = {a0[s][0], a1[s][0], a0[s][1], a1[s][1]};
+                const uint32_t* a = afr[s];
 #pragma unroll
                 for (int t = 0; t < NTT; t++) {
                     if (NTT == 1 || t < ntl) {  // a tile always has a live first n-tile

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -512,7 +513,11 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
     const bool timing = flags & RMOE_FLAG_STAGE_TIMING;
     // decode batches of Q4_K / Q6_K experts: the whole layer in one launch where the flags allow
     // (fast router, atomic combine, no stage events)
-    if (gv && !given && !det && !timing && !rp.exact &&
+    static const bool small_on = [] {  // RMOE_SMALL_LAYER=0 keeps decode batches on the multi-launch path
+        const char* v = getenv("RMOE_SMALL_LAYER");
+        return !(v && v[0] == '0');
+    }();
+    if (small_on && gv && !given && !det && !timing && !rp.exact &&
         layer_small_supported(L->wg.type, L->wd.type, (int)T, (int)L->E, (int)L->k)) {
         GroupedParams gp{};
         gp.gate = L->wg; gp.up = L->wu; gp.down = L->wd;

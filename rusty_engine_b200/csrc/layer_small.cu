@@ -28,6 +28,8 @@
 namespace rmoe {
 
 static constexpr int LS_MAX_T = 16;
+static constexpr int LS_WCH = 16;            // float4 of a router row a lane holds at a time
+static constexpr int LS_XSTAGE = 64 * 1024;  // shared memory for staged token rows (bytes)
 static constexpr int LS_MAX_ROWS = LS_MAX_T * (MAX_K + 1);
 
 struct SmallLayerParams {
@@ -67,12 +69,11 @@ __device__ void ls_grid_barrier(unsigned* bar, unsigned* status) {
             st_release_gpu(bar + 1, gen + 1);
         } else {
             const uint64_t t0 = ls_globaltimer();
-            while (ld_acquire_gpu(bar + 1) == gen) {
-                if (ls_globaltimer() - t0 > 1000000000ull) {
+            for (uint32_t i = 0; ld_acquire_gpu(bar + 1) == gen; i++) {
+                if ((i & 255) == 255 && ls_globaltimer() - t0 > 1000000000ull) {
                     atomicOr(status, (unsigned)DERR_TIMEOUT);
                     break;
                 }
-                __nanosleep(64);
             }
         }
         __threadfence();
@@ -96,33 +97,82 @@ __global__ void __launch_bounds__(GV_THREADS, 2) layer_small_kernel(SmallLayerPa
     const int n4 = H / 4;
 
     // ---- A. logits (lane l sums elements 4 l + 128 j of its expert for every token) ----------
-    for (int e = gwarp; e < E; e += gwarps) {
-        float acc[LS_MAX_T];
+    // CTA b < ceil(E / 8): warp w scores expert 8 b + w.  Its first router chunk (16 float4 a
+    // lane) is loaded before anything waits; the tokens are staged in shared memory LS_XG at a
+    // time (every load of a group in flight at once), so no load sits behind an FMA chain.
+    if (blockIdx.x * 8 < E) {
+        const int e = blockIdx.x * 8 + warp;
+        const float4* wr = reinterpret_cast<const float4*>(p.router_w + (size_t)min(e, E - 1) * H);
+        float4 wv[LS_WCH];
 #pragma unroll
-        for (int t = 0; t < LS_MAX_T; t++) acc[t] = 0.0f;
-        const float4* wr = reinterpret_cast<const float4*>(p.router_w + (size_t)e * H);
-        for (int j = lane; j < n4; j += 32) {
-            const float4 a = __ldg(wr + j);
-#pragma unroll
-            for (int t = 0; t < LS_MAX_T; t++)
-                if (t < T) {
-                    const float4 b = __ldg(reinterpret_cast<const float4*>(p.x + (size_t)t * H) + j);
-                    acc[t] = fmaf(a.x, b.x, acc[t]);
-                    acc[t] = fmaf(a.y, b.y, acc[t]);
-                    acc[t] = fmaf(a.z, b.z, acc[t]);
-                    acc[t] = fmaf(a.w, b.w, acc[t]);
-                }
+        for (int u = 0; u < LS_WCH; u++) {
+            const int j = lane + 32 * u;
+            wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        float4* xs4 = reinterpret_cast<float4*>(smem);
+        const int G = max(1, min(T, LS_XSTAGE / (H * 4)));
         float mine = 0.0f;
+        for (int tg = 0; tg < T; tg += G) {
+            const int ng = min(G, T - tg);
+            __syncthreads();  // the previous group's rows are no longer read
+            const float4* xg = reinterpret_cast<const float4*>(p.x + (size_t)tg * H);
+            for (int q0 = 0; q0 < ng * n4; q0 += 8 * GV_THREADS) {
+                float4 v[8];
 #pragma unroll
-        for (int t = 0; t < LS_MAX_T; t++)
-            if (t < T) {
-                float v = acc[t];
+                for (int u = 0; u < 8; u++) {
+                    const int q = q0 + u * GV_THREADS + tid;
+                    v[u] = q < ng * n4 ? __ldg(xg + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-                if (lane == t) mine = v;
+                for (int u = 0; u < 8; u++) {
+                    const int q = q0 + u * GV_THREADS + tid;
+                    if (q < ng * n4) xs4[q] = v[u];
+                }
             }
-        if (lane < T) p.logits[(size_t)lane * E + e] = mine;
+            __syncthreads();
+            if (e < E) {
+                float acc[LS_MAX_T];
+#pragma unroll
+                for (int t = 0; t < LS_MAX_T; t++) acc[t] = 0.0f;
+                for (int j0 = 0; j0 < n4; j0 += 32 * LS_WCH) {
+                    if (j0 > 0)
+#pragma unroll
+                        for (int u = 0; u < LS_WCH; u++) {
+                            const int j = j0 + lane + 32 * u;
+                            wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                    for (int u = 0; u < LS_WCH; u++) {
+                        const int j = j0 + lane + 32 * u;
+                        if (j < n4)
+#pragma unroll
+                            for (int t = 0; t < LS_MAX_T; t++)
+                                if (t < ng) {
+                                    const float4 a = wv[u], b = xs4[t * n4 + j];
+                                    acc[t] = fmaf(a.x, b.x, acc[t]);
+                                    acc[t] = fmaf(a.y, b.y, acc[t]);
+                                    acc[t] = fmaf(a.z, b.z, acc[t]);
+                                    acc[t] = fmaf(a.w, b.w, acc[t]);
+                                }
+                    }
+                }
+#pragma unroll
+                for (int t = 0; t < LS_MAX_T; t++)
+                    if (t < ng) {
+                        float v = acc[t];
+#pragma unroll
+                        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                        if (lane == tg + t) mine = v;
+                    }
+                if (n4 > 32 * LS_WCH)  // the chunk registers hold the last chunk: reload the first
+#pragma unroll
+                    for (int u = 0; u < LS_WCH; u++) {
+                        const int j = lane + 32 * u;
+                        wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+            }
+        }
+        if (e < E && lane < T) p.logits[(size_t)lane * E + e] = mine;
     }
     {
         // fp16 MMA operand (|x| beyond the fp16 range is reported, never silently inf), zeroed
@@ -274,7 +324,8 @@ static cudaError_t go_small(SmallLayerParams sp, int* grid_cache, cudaStream_t s
     gv_layout<TD, NT, 1, KSD>(I, sp.depth_dn, sp.ring_dn, sm_dn);
     const int rows_floats = (sp.r.T * sp.r.E + 3) & ~3;
     const size_t sm_route = (size_t)(rows_floats + rescore_stage_floats(sp.r.H)) * 4;
-    const size_t smem = std::max(std::max(sm_gu, sm_dn), sm_route);
+    const int xg = std::max(1, std::min(sp.r.T, LS_XSTAGE / (H * 4)));  // staged token rows (phase A)
+    const size_t smem = std::max(std::max(std::max(sm_gu, sm_dn), sm_route), (size_t)xg * H * 4);
     sp.stage_floats = (int)(smem / 4) - rows_floats;
     if (smem > 227 * 1024) return cudaErrorNotSupported;
     auto kfn = layer_small_kernel<TG, TD, NT, KSG, KSD>;

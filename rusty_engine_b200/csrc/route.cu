@@ -943,8 +943,8 @@ static cudaError_t rescore_smem(K kernel, RouteParams& p, size_t& sm) {
     if (!refine_on(p) || p.given) return cudaSuccess;
     p.stage_floats = rescore_stage_floats(p.H);
     sm = (size_t)p.stage_floats * 4;
-    return sm > 48 * 1024 ? cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm)
-                          : cudaSuccess;
+    // static + dynamic beyond 48 KB needs the opt-in, whatever the dynamic part alone is
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
 }
 
 int route_grid(int T) { return (T + TK_TOK - 1) / TK_TOK; }
