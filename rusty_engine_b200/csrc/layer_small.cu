@@ -199,30 +199,25 @@ __global__ void __launch_bounds__(GV_THREADS, 2) layer_small_kernel(SmallLayerPa
     RouteParams rp = p;
     rp.logits = nullptr;
     if (blockIdx.x != 0) rp.refined = nullptr;
-    __shared__ int amb_t[LS_MAX_T], amb_n;
-    __shared__ float amb_thr[LS_MAX_T];
+    __shared__ AmbTok amb[LS_MAX_T];
+    __shared__ int amb_list[LS_MAX_T], amb_n;
     if (tid == 0) amb_n = 0;
     __syncthreads();
     for (int t = warp; t < T; t += GV_THREADS / 32) {
         int id;
-        float thr;
         if (!refine_on(rp)) {
             id = warp_topk(rows_s + (size_t)t * E, E, k, p.gate, lane, s_wts + t * k);
-        } else if (!warp_topk_try(rp, t, rows_s + (size_t)t * E, lane, s_wts + t * k, id, thr)) {
-            if (lane == 0) {  // near-tie: rescored by the whole CTA below
-                const int i = atomicAdd(&amb_n, 1);
-                amb_t[i] = t;
-                amb_thr[i] = thr;
-            }
+        } else if (!warp_topk_try(rp, t, rows_s + (size_t)t * E, lane, s_wts + t * k, id, amb[t])) {
+            if (lane == 0) amb_list[atomicAdd(&amb_n, 1)] = t;  // near-tie: rescored below
             continue;
         }
         if (lane < k) s_ids[t * k + lane] = id;
     }
     __syncthreads();
-    for (int i = 0; i < amb_n; i++) {  // CTA-uniform; the stage follows the logit rows
-        const int t = amb_t[i];
-        cta_rescore(rp, t, rows_s + (size_t)t * E, amb_thr[i], rows_s + ((T * E + 3) & ~3), sp.stage_floats);
-        if (warp == 0) {
+    if (amb_n) {  // CTA-uniform; the stage follows the logit rows, which it updates
+        cta_rescore_batch(rp, amb, amb_list, amb_n, rows_s + ((T * E + 3) & ~3), sp.stage_floats, rows_s, 0, E);
+        for (int i = warp; i < amb_n; i += GV_THREADS / 32) {
+            const int t = amb_list[i];
             const int id = warp_topk(rows_s + (size_t)t * E, E, k, p.gate, lane, s_wts + t * k);
             if (lane < k) s_ids[t * k + lane] = id;
         }

@@ -441,8 +441,8 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
     extern __shared__ __align__(16) float tk_stage[];  // rescoring stage (p.stage_floats)
     __shared__ int ids_s[TK_TOK * MAX_K];
     __shared__ float row_s[TK_THREADS / 32][MAX_E];
-    __shared__ int amb_tl[TK_TOK], amb_n;
-    __shared__ float amb_thr[TK_TOK];
+    __shared__ AmbTok amb[TK_TOK];
+    __shared__ int amb_list[TK_TOK], amb_n;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int t0 = blockIdx.x * TK_TOK;
     const int E = p.E, H = p.H, k = p.k;
@@ -460,15 +460,10 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
         }
         logit_row(p, t, lane, row_s[warp]);
         int id;
-        float thr;
         if (!refine) {
             id = warp_topk(row_s[warp], E, k, p.gate, lane, p.topk_w + (size_t)t * k);
-        } else if (!warp_topk_try(p, t, row_s[warp], lane, p.topk_w + (size_t)t * k, id, thr)) {
-            if (lane == 0) {  // near-tie: rescored by the whole CTA below
-                const int i = atomicAdd(&amb_n, 1);
-                amb_tl[i] = tl;
-                amb_thr[i] = thr;
-            }
+        } else if (!warp_topk_try(p, t, row_s[warp], lane, p.topk_w + (size_t)t * k, id, amb[tl])) {
+            if (lane == 0) amb_list[atomicAdd(&amb_n, 1)] = tl;  // near-tie: rescored below
             __syncwarp();
             continue;
         }
@@ -479,17 +474,18 @@ __global__ void __launch_bounds__(TK_THREADS) topk_count_kernel(RouteParams p) {
         __syncwarp();  // the row is read before the warp's next token overwrites it
     }
     __syncthreads();
-    for (int i = 0; i < amb_n; i++) {  // CTA-uniform
-        const int tl = amb_tl[i], t = t0 + tl;
-        float* row = row_s[0];
-        for (int q = tid; q < E; q += TK_THREADS) row[q] = __ldcg(p.logits + (size_t)t * E + q);
-        cta_rescore(p, t, row, amb_thr[i], tk_stage, p.stage_floats);
-        if (warp == 0) {
-            const int id = warp_topk(row, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
+    if (amb_n) {  // CTA-uniform
+        cta_rescore_batch(p, amb, amb_list, amb_n, tk_stage, p.stage_floats, p.logits, 0, E);
+        for (int i = warp; i < amb_n; i += TK_THREADS / 32) {
+            const int tl = amb_list[i], t = t0 + tl;
+            for (int e = lane; e < E; e += 32) row_s[warp][e] = p.logits[(size_t)t * E + e];
+            __syncwarp();
+            const int id = warp_topk(row_s[warp], E, k, p.gate, lane, p.topk_w + (size_t)t * k);
             if (lane < k) {
                 p.topk_id[(size_t)t * k + lane] = id;
                 ids_s[tl * k + lane] = id;
             }
+            __syncwarp();
         }
         __syncthreads();
     }
@@ -866,24 +862,19 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     float* lg = fsm;  // the group's logits, read past L1 (other CTAs wrote them)
     for (int q = tid; q < nt * E; q += RF_THREADS) lg[q] = __ldcg(p.logits + (size_t)t0 * E + q);
     __syncthreads();
-    __shared__ int amb_w[RF_TOK], amb_n;
-    __shared__ float amb_thr[RF_TOK];
+    __shared__ AmbTok amb[RF_TOK];
+    __shared__ int amb_list[RF_TOK], amb_n;
     if (tid == 0) amb_n = 0;
     __syncthreads();
     if (warp < nt) {
         const int t = t0 + warp;
         int id;
-        float thr;
         bool done = true;
         if (!refine_on(p)) {
             id = warp_topk(lg + warp * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
-        } else if (!warp_topk_try(p, t, lg + warp * E, lane, p.topk_w + (size_t)t * k, id, thr)) {
+        } else if (!warp_topk_try(p, t, lg + warp * E, lane, p.topk_w + (size_t)t * k, id, amb[warp])) {
             done = false;
-            if (lane == 0) {  // near-tie: rescored by the whole CTA below
-                const int i = atomicAdd(&amb_n, 1);
-                amb_w[i] = warp;
-                amb_thr[i] = thr;
-            }
+            if (lane == 0) amb_list[atomicAdd(&amb_n, 1)] = warp;  // near-tie: rescored below
         }
         if (done && lane < k) {
             p.topk_id[(size_t)t * k + lane] = id;
@@ -891,10 +882,10 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
         }
     }
     __syncthreads();
-    for (int i = 0; i < amb_n; i++) {  // CTA-uniform; the stage follows the group's logit rows
-        const int w = amb_w[i], t = t0 + w;
-        cta_rescore(p, t, lg + w * E, amb_thr[i], fsm + ((RF_TOK * E + 3) & ~3), p.stage_floats);
-        if (warp == 0) {
+    if (amb_n) {  // CTA-uniform; the stage follows the group's logit rows, which it updates
+        cta_rescore_batch(p, amb, amb_list, amb_n, fsm + ((RF_TOK * E + 3) & ~3), p.stage_floats, lg, t0, E);
+        for (int i = warp; i < amb_n; i += RF_THREADS / 32) {
+            const int w = amb_list[i], t = t0 + w;
             const int id = warp_topk(lg + w * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
             if (lane < k) {
                 p.topk_id[(size_t)t * k + lane] = id;
@@ -986,37 +977,31 @@ __global__ void route_only_kernel(const float* logits, int T, int E, int k, int 
 __global__ void __launch_bounds__(256) route_rows_kernel(RouteParams p) {
     extern __shared__ __align__(16) float rr_stage[];  // rescoring stage (p.stage_floats)
     __shared__ float row_s[8][MAX_E];
-    __shared__ int amb_w[8], amb_n;
-    __shared__ float amb_thr[8];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = blockIdx.x * 8 + warp;
+    __shared__ AmbTok amb[8];
+    __shared__ int amb_list[8], amb_n;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t0 = blockIdx.x * 8, t = t0 + warp;
     if (threadIdx.x == 0) amb_n = 0;
     __syncthreads();
     if (t < p.T) {
         logit_row(p, t, lane, row_s[warp]);
         int id;
-        float thr;
         bool done = true;
         if (!refine_on(p)) {
             id = warp_topk(row_s[warp], p.E, p.k, p.gate, lane, p.topk_w + (size_t)t * p.k);
-        } else if (!warp_topk_try(p, t, row_s[warp], lane, p.topk_w + (size_t)t * p.k, id, thr)) {
+        } else if (!warp_topk_try(p, t, row_s[warp], lane, p.topk_w + (size_t)t * p.k, id, amb[warp])) {
             done = false;
-            if (lane == 0) {
-                const int i = atomicAdd(&amb_n, 1);
-                amb_w[i] = warp;
-                amb_thr[i] = thr;
-            }
+            if (lane == 0) amb_list[atomicAdd(&amb_n, 1)] = warp;  // near-tie: rescored below
         }
         if (done && lane < p.k) p.topk_id[(size_t)t * p.k + lane] = id;
     }
     __syncthreads();
-    for (int i = 0; i < amb_n; i++) {  // CTA-uniform
-        const int w = amb_w[i], tt = blockIdx.x * 8 + w;
-        cta_rescore(p, tt, row_s[w], amb_thr[i], rr_stage, p.stage_floats);
-        if (warp == 0) {
+    if (amb_n) {  // CTA-uniform; rows of row_s are this CTA's tokens, MAX_E apart
+        cta_rescore_batch(p, amb, amb_list, amb_n, rr_stage, p.stage_floats, &row_s[0][0], t0, MAX_E);
+        for (int i = warp; i < amb_n; i += 8) {
+            const int w = amb_list[i], tt = t0 + w;
             const int id = warp_topk(row_s[w], p.E, p.k, p.gate, lane, p.topk_w + (size_t)tt * p.k);
             if (lane < p.k) p.topk_id[(size_t)tt * p.k + lane] = id;
         }
-        __syncthreads();
     }
 }
 

@@ -115,7 +115,7 @@ __device__ __forceinline__ int warp_topk(const float* lg, int E, int k, int gate
 // top-k runs again: experts further down are more than tau / 2 below k + 1 others under any
 // of the sums and cannot be chosen.  The ids are then the reference's, near-ties included.
 // Two steps: each warp checks its tokens (warp_topk_try) and defers the close ones; after the
-// CTA's warps are done, the whole CTA rescores each deferred token (cta_rescore), so the rows
+// CTA's warps are done, the whole CTA rescores the deferred tokens (cta_rescore_batch), so the rows
 // come in with the CTA's full memory parallelism and only the chain itself is serial.
 // For the sigmoid gate the distances are taken between scores (sigmoid has slope <= 1/4,
 // plus a few ulp for the rounding of the score itself).
@@ -148,15 +148,27 @@ __host__ __device__ __forceinline__ bool refine_on(const RouteParams& p) {
     return !p.exact && p.x && p.xb && p.router_wmax > 0.0f;
 }
 
+// One token whose fast top-k met a near-tie, as the first step hands it to the second: the
+// experts to rescore (at most RF_MAXM; nm = -1: more than that, then every expert scoring at
+// least thr is rescored).
+static constexpr int RF_MAXM = 32;
+struct AmbTok {
+    int t, nm;
+    float thr;
+    int mem[RF_MAXM];
+};
+
 // First step, one warp per token: top-k of token t from its fast logits in row[0 .. E).  When
 // no two of the k + 1 best scores are within the window, lane j < k gets the j-th id in `id`,
-// the weights are written to w_out, and the call returns true.  Otherwise it returns false
-// with `thr`, the score from which experts must be rescored (the (k+1)-th best minus the
-// window; -inf when k = E, where only the order can change); the caller then runs
-// cta_rescore and warp_topk on the row.
+// the weights are written to w_out, and the call returns true.  Otherwise it fills `a` (a
+// shared-memory slot) and returns false; the CTA then rescores (cta_rescore_batch) and reruns
+// warp_topk on the token's row.  The sorted k + 1 best split into groups at every gap of at
+// least the window; only groups of two or more can be misordered, so only their experts are
+// rescored, plus, when such a group reaches the (k+1)-th best, every expert below it within
+// the window (one of them may belong in the top k).
 template <int NS>
 __device__ bool warp_topk_try_n(const RouteParams& p, int t, const float* row, int lane, float* w_out, int& id,
-                                float& thr) {
+                                AmbTok& a) {
     const int E = p.E, k = p.k, gate = p.gate;
     const float xn = warp_row_norm(p.xb + (size_t)t * p.H, p.H, lane);
     const int n = min(k + 1, E);
@@ -165,81 +177,149 @@ __device__ bool warp_topk_try_n(const RouteParams& p, int t, const float* row, i
     const float tau_l = REFINE_UNITS * 5.9604645e-8f * p.router_wmax * xn;
     const float tau = gate == 1 ? 0.25f * tau_l + 4.7683716e-7f : tau_l;  // + 8 ulp of 1.0
     const float next = __shfl_down_sync(0xffffffffu, sc, 1);
-    const bool close = lane + 1 < n && !(sc - next >= tau);
-    if (__any_sync(0xffffffffu, close)) {
-        thr = k < E ? __shfl_sync(0xffffffffu, sc, n - 1) - tau : -INFINITY;
-        return false;
+    const bool close = lane + 1 < n && !(sc - next >= tau);  // ranks lane and lane + 1
+    const unsigned cm = __ballot_sync(0xffffffffu, close);
+    if (!cm) {
+        pick_weights(sc, k, gate, lane, w_out);
+        return true;
     }
-    pick_weights(sc, k, gate, lane, w_out);
-    return true;
+    const bool in = lane < n && (((cm >> lane) & 1u) || (lane > 0 && ((cm >> (lane - 1)) & 1u)));
+    const unsigned im = __ballot_sync(0xffffffffu, in);
+    int nm = __popc(im);
+    if (in) a.mem[__popc(im & ((1u << lane) - 1u))] = id;
+    const float sk = __shfl_sync(0xffffffffu, sc, n - 1);
+    const float thr = k < E ? sk - tau : -INFINITY;
+    if (k < E && ((cm >> (n - 2)) & 1u)) {  // the group reaches the (k+1)-th best
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            bool top = false;  // one of the k + 1 best already
+            for (int j = 0; j < n; j++) top |= __shfl_sync(0xffffffffu, id, j) == e;
+            const float se = e < E ? gate_score(row[e], gate) : -INFINITY;
+            const bool b = e < E && !top && !(se < thr);
+            const unsigned bm = __ballot_sync(0xffffffffu, b);
+            const int at = nm + __popc(bm & ((1u << lane) - 1u));
+            if (b && at < RF_MAXM) a.mem[at] = e;
+            nm += __popc(bm);
+        }
+    }
+    if (lane == 0) {
+        a.t = t;
+        a.nm = nm <= RF_MAXM ? nm : -1;
+        a.thr = thr;
+    }
+    __syncwarp();
+    return false;
 }
 
 __device__ __forceinline__ bool warp_topk_try(const RouteParams& p, int t, const float* row, int lane, float* w_out,
-                                              int& id, float& thr) {
+                                              int& id, AmbTok& a) {
     const int ns = (p.E + 31) / 32;
-    if (ns <= 1) return warp_topk_try_n<1>(p, t, row, lane, w_out, id, thr);
-    if (ns <= 2) return warp_topk_try_n<2>(p, t, row, lane, w_out, id, thr);
-    if (ns <= 4) return warp_topk_try_n<4>(p, t, row, lane, w_out, id, thr);
-    if (ns <= 8) return warp_topk_try_n<8>(p, t, row, lane, w_out, id, thr);
-    return warp_topk_try_n<MAX_E / 32>(p, t, row, lane, w_out, id, thr);
+    if (ns <= 1) return warp_topk_try_n<1>(p, t, row, lane, w_out, id, a);
+    if (ns <= 2) return warp_topk_try_n<2>(p, t, row, lane, w_out, id, a);
+    if (ns <= 4) return warp_topk_try_n<4>(p, t, row, lane, w_out, id, a);
+    if (ns <= 8) return warp_topk_try_n<8>(p, t, row, lane, w_out, id, a);
+    return warp_topk_try_n<MAX_E / 32>(p, t, row, lane, w_out, id, a);
 }
 
-// Second step, the whole CTA (every thread calls it): the experts of token t scoring at least
-// thr are rescored with moe::matvec's sequential chain (src/moe.rs:271-277): products rounded,
-// then added in ascending k to a running f32 sum that starts at 0, no contraction.  The CTA
-// loads x_t and as many of those experts' router rows as `stage` holds (stage_floats floats of
-// shared memory, at least 2 H) with 16-B loads all in flight at once, then one thread per
-// expert runs its chain from shared memory (the chain itself is the floor: H dependent adds).
-// The exact logits replace the fast ones in row (and in p.logits when set).
-static __device__ void cta_rescore(const RouteParams& p, int t, float* row, float thr, float* stage, int stage_floats) {
-    __shared__ int s_mem[MAX_E];
-    __shared__ int s_nm;
-    const int E = p.E, H = p.H, gate = p.gate;
-    const int tid = threadIdx.x, nthr = blockDim.x, lane = tid & 31;
-    __syncthreads();
-    if (tid < 32) {
-        int base = 0;
-        for (int e0 = 0; e0 < E; e0 += 32) {
-            const int e = e0 + lane;
-            const bool m = e < E && !(gate_score(row[e], gate) < thr);
-            const unsigned b = __ballot_sync(0xffffffffu, m);
-            if (m) s_mem[base + __popc(b & ((1u << lane) - 1u))] = e;
-            base += __popc(b);
-        }
-        if (lane == 0) s_nm = base;
-    }
-    __syncthreads();
-    const int nm = s_nm, cap = stage_floats / H - 1;
-    const float4* x4 = reinterpret_cast<const float4*>(p.x + (size_t)t * H);
+// Second step, the whole CTA (every thread calls it, with the same arguments): the listed
+// experts of the deferred tokens are rescored with moe::matvec's sequential chain
+// (src/moe.rs:271-277): products rounded, then added in ascending k to a running f32 sum that
+// starts at 0, no contraction.  As many tokens as `stage` (stage_floats floats of shared
+// memory, at least 2 H) holds go at once: their x rows and listed router rows are loaded with
+// 16-B loads all in flight, every thread forms products in place, and one thread per
+// (token, expert) adds its products in ascending k -- only those chains are serial, and they
+// run side by side.  A token with more than RF_MAXM experts to rescore (nm = -1) goes alone,
+// in rounds, over every expert scoring at least its thr (its row read back from `logits`).
+// The tokens are slots[list[0 .. na)]; token t's logits are row t - row0 of `logits` (row
+// stride ld, global or shared memory, holding the fast ones on entry), where the exact ones
+// are written.
+static constexpr int RF_JMAX = 128;  // (token, expert) chains per round
+static __device__ void cta_rescore_batch(const RouteParams& p, const AmbTok* slots, const int* list, int na,
+                                         float* stage, int stage_floats, float* logits, int row0, int ld) {
+    __shared__ int s_tok[RF_JMAX], s_e[RF_JMAX], s_xrow[RF_JMAX], s_erow[RF_JMAX];
+    __shared__ int s_nj, s_next, s_cursor;
+    const int E = p.E, H = p.H, gate = p.gate, h4 = H / 4;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int cap = min(stage_floats / H, RF_JMAX + 1);  // rows the stage holds
     float4* st4 = reinterpret_cast<float4*>(stage);
-    const int h4 = H / 4;
-    for (int m0 = 0; m0 < nm; m0 += cap) {
-        const int mc = min(cap, nm - m0);
-        for (int q = tid; q < (1 + mc) * h4; q += nthr) {
-            const int r = q / h4, j = q - r * h4;
-            const float4* src = r == 0 ? x4 : reinterpret_cast<const float4*>(p.router_w + (size_t)s_mem[m0 + r - 1] * H);
-            st4[q] = __ldg(src + j);
-        }
+    __syncthreads();
+    if (tid == 0) s_cursor = 0;
+    int i0 = 0;
+    while (i0 < na) {
         __syncthreads();
-        if (tid < mc) {
-            const float4* xs = st4;
-            const float4* ws = st4 + (size_t)(1 + tid) * h4;
-            float s = 0.0f;
-#pragma unroll 4
-            for (int j = 0; j < h4; j++) {
-                const float4 a = ws[j], b = xs[j];
-                s = __fadd_rn(s, __fmul_rn(a.x, b.x));
-                s = __fadd_rn(s, __fmul_rn(a.y, b.y));
-                s = __fadd_rn(s, __fmul_rn(a.z, b.z));
-                s = __fadd_rn(s, __fmul_rn(a.w, b.w));
+        if (tid == 0) {
+            int nj = 0, i = i0, rows = 0;
+            if (slots[list[i0]].nm < 0) {  // the over-full token alone: a round of experts from the cursor
+                int e = s_cursor;
+                for (; e < E && nj < cap - 1; e++) {
+                    const float se = gate_score(logits[(size_t)(slots[list[i0]].t - row0) * ld + e], gate);
+                    if (!(se < slots[list[i0]].thr)) {
+                        s_tok[nj] = i0;
+                        s_e[nj] = e;
+                        s_xrow[nj] = 0;
+                        s_erow[nj] = 1 + nj;
+                        nj++;
+                    }
+                }
+                s_cursor = e < E ? e : 0;
+                i = e < E ? i0 : i0 + 1;
+            } else {  // whole tokens while their rows fit
+                for (; i < na && slots[list[i]].nm >= 0; i++) {
+                    const int nm = slots[list[i]].nm;
+                    if (rows + 1 + nm > cap || nj + nm > RF_JMAX) break;
+                    for (int j = 0; j < nm; j++) {
+                        s_tok[nj + j] = i;
+                        s_e[nj + j] = slots[list[i]].mem[j];
+                        s_xrow[nj + j] = rows;
+                        s_erow[nj + j] = rows + 1 + j;
+                    }
+                    rows += 1 + nm;
+                    nj += nm;
+                }
             }
-            const int e = s_mem[m0 + tid];
-            row[e] = s;
-            if (p.logits) p.logits[(size_t)t * E + e] = s;
+            s_nj = nj;
+            s_next = i;
         }
         __syncthreads();
+        const int nj = s_nj;
+        // the x rows (one per token of the round: its first job loads it) and the expert rows,
+        // every 16-B load of the round issued before any is used
+        for (int q = tid; q < 2 * nj * h4; q += nthr) {
+            const int j = q / (2 * h4), r = q - j * 2 * h4, w = r >= h4, c = r - w * h4;
+            if (!w && j > 0 && s_tok[j - 1] == s_tok[j]) continue;  // x row loaded by the token's first job
+            const float* src = w ? p.router_w + (size_t)s_e[j] * H : p.x + (size_t)slots[list[s_tok[j]]].t * H;
+            st4[(size_t)(w ? s_erow[j] : s_xrow[j]) * h4 + c] = __ldg(reinterpret_cast<const float4*>(src) + c);
+        }
+        __syncthreads();
+        for (int q = tid; q < nj * h4; q += nthr) {  // products, each rounded, in place
+            const int j = q / h4, c = q - j * h4;
+            float4 a = st4[(size_t)s_erow[j] * h4 + c];
+            const float4 b = st4[(size_t)s_xrow[j] * h4 + c];
+            a.x = __fmul_rn(a.x, b.x);
+            a.y = __fmul_rn(a.y, b.y);
+            a.z = __fmul_rn(a.z, b.z);
+            a.w = __fmul_rn(a.w, b.w);
+            st4[(size_t)s_erow[j] * h4 + c] = a;
+        }
+        __syncthreads();
+        for (int j = tid; j < nj; j += nthr) {  // the chains, side by side
+            const float4* pr = st4 + (size_t)s_erow[j] * h4;
+            float s = 0.0f;
+#pragma unroll 8
+            for (int c = 0; c < h4; c++) {
+                const float4 a = pr[c];
+                s = __fadd_rn(s, a.x);
+                s = __fadd_rn(s, a.y);
+                s = __fadd_rn(s, a.z);
+                s = __fadd_rn(s, a.w);
+            }
+            logits[(size_t)(slots[list[s_tok[j]]].t - row0) * ld + s_e[j]] = s;
+        }
+        __syncthreads();
+        if (tid == 0 && p.refined) atomicAdd(p.refined, (unsigned)(s_next - i0));
+        i0 = s_next;
     }
-    if (tid == 0 && p.refined) atomicAdd(p.refined, 1u);
+    __syncthreads();
 }
 
 // Shared memory the rescoring stage needs for rows of H floats: x and up to four expert rows
