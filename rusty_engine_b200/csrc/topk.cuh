@@ -242,31 +242,52 @@ static __device__ void cta_rescore_batch(const RouteParams& p, const AmbTok* slo
     const int tid = threadIdx.x, nthr = blockDim.x;
     const int cap = min(stage_floats / H, RF_JMAX + 1);  // rows the stage holds
     float4* st4 = reinterpret_cast<float4*>(stage);
+    if (cap < 2) {  // no room for x and one expert row: the tokens keep their fast logits
+        if (tid == 0 && p.status) atomicOr(p.status, (unsigned)DERR_TIMEOUT);
+        __syncthreads();
+        return;
+    }
     __syncthreads();
     if (tid == 0) s_cursor = 0;
     int i0 = 0;
-    while (i0 < na) {
+    // every round consumes at least one expert of token i0 or moves past it, so the rounds are
+    // bounded; the bound is enforced all the same (status word, then the remaining tokens keep
+    // their fast logits)
+    const int max_rounds = na * (E + 2);
+    for (int round = 0; i0 < na; round++) {
+        if (round >= max_rounds) {
+            if (tid == 0 && p.status) atomicOr(p.status, (unsigned)DERR_TIMEOUT);
+            break;
+        }
         __syncthreads();
         if (tid == 0) {
             int nj = 0, i = i0, rows = 0;
-            if (slots[list[i0]].nm < 0) {  // the over-full token alone: a round of experts from the cursor
-                int e = s_cursor;
-                for (; e < E && nj < cap - 1; e++) {
-                    const float se = gate_score(logits[(size_t)(slots[list[i0]].t - row0) * ld + e], gate);
-                    if (!(se < slots[list[i0]].thr)) {
-                        s_tok[nj] = i0;
-                        s_e[nj] = e;
-                        s_xrow[nj] = 0;
-                        s_erow[nj] = 1 + nj;
-                        nj++;
+            const AmbTok& a0 = slots[list[i0]];
+            if (s_cursor > 0 || a0.nm < 0 || 1 + a0.nm > cap) {
+                // token i0 alone, a round of at most cap - 1 of its experts from the cursor:
+                // its list, or (over-full list) every expert scoring at least thr
+                int c = s_cursor;
+                if (a0.nm >= 0) {
+                    for (; c < a0.nm && nj < cap - 1; c++, nj++) s_e[nj] = a0.mem[c];
+                    s_cursor = c < a0.nm ? c : 0;
+                    i = c < a0.nm ? i0 : i0 + 1;
+                } else {
+                    for (; c < E && nj < cap - 1; c++) {
+                        const float se = gate_score(logits[(size_t)(a0.t - row0) * ld + c], gate);
+                        if (!(se < a0.thr)) s_e[nj++] = c;
                     }
+                    s_cursor = c < E ? c : 0;
+                    i = c < E ? i0 : i0 + 1;
                 }
-                s_cursor = e < E ? e : 0;
-                i = e < E ? i0 : i0 + 1;
+                for (int j = 0; j < nj; j++) {
+                    s_tok[j] = i0;
+                    s_xrow[j] = 0;
+                    s_erow[j] = 1 + j;
+                }
             } else {  // whole tokens while their rows fit
-                for (; i < na && slots[list[i]].nm >= 0; i++) {
+                for (; i < na; i++) {
                     const int nm = slots[list[i]].nm;
-                    if (rows + 1 + nm > cap || nj + nm > RF_JMAX) break;
+                    if (nm < 0 || rows + 1 + nm > cap || nj + nm > RF_JMAX) break;
                     for (int j = 0; j < nm; j++) {
                         s_tok[nj + j] = i;
                         s_e[nj + j] = slots[list[i]].mem[j];
@@ -316,7 +337,7 @@ static __device__ void cta_rescore_batch(const RouteParams& p, const AmbTok* slo
             logits[(size_t)(slots[list[s_tok[j]]].t - row0) * ld + s_e[j]] = s;
         }
         __syncthreads();
-        if (tid == 0 && p.refined) atomicAdd(p.refined, (unsigned)(s_next - i0));
+        if (tid == 0 && p.refined && s_next > i0) atomicAdd(p.refined, (unsigned)(s_next - i0));
         i0 = s_next;
     }
     __syncthreads();
