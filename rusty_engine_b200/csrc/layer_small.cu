@@ -318,7 +318,7 @@ static cudaError_t go_small(SmallLayerParams sp, int* grid_cache, cudaStream_t s
     gv_layout<TG, NT, 2, KSG>(H, sp.depth_gu, sp.ring_gu, sm_gu);
     gv_layout<TD, NT, 1, KSD>(I, sp.depth_dn, sp.ring_dn, sm_dn);
     const int rows_floats = (sp.r.T * sp.r.E + 3) & ~3;
-    const size_t sm_route = (size_t)(rows_floats + rescore_stage_floats(sp.r.H)) * 4;
+    const size_t sm_route = (size_t)(rows_floats + 2 * sp.r.H) * 4;  // the rescoring stage takes what is left
     const int xg = std::max(1, std::min(sp.r.T, LS_XSTAGE / (H * 4)));  // staged token rows (phase A)
     const size_t smem = std::max(std::max(std::max(sm_gu, sm_dn), sm_route), (size_t)xg * H * 4);
     sp.stage_floats = (int)(smem / 4) - rows_floats;

@@ -343,10 +343,10 @@ static __device__ void cta_rescore_batch(const RouteParams& p, const AmbTok* slo
     __syncthreads();
 }
 
-// Shared memory the rescoring stage needs for rows of H floats: x and up to four expert rows
-// (at least one).
+// Shared memory the rescoring stage takes for rows of H floats: about 88 KB (11 rows at
+// H = 2048, 5 at H = 4096; at least 2), so that a CTA's deferred tokens usually go in one round.
 __host__ __device__ inline int rescore_stage_floats(int H) {
-    const int rows = 1 + (H <= 2048 ? 4 : H <= 4096 ? 2 : 1);
+    const int rows = max(2, min(16, 90112 / (4 * H)));
     return rows * H;
 }
 

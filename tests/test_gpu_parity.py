@@ -372,6 +372,24 @@ def test_c3_decode_parity(torch_cuda, c2_weights, T):
         check_layer(got, lw, x, out, ids, w, f"c3 b={T} det={det}")
 
 
+@pytest.mark.parametrize("T", [1, 5, 8, 16])
+def test_one_launch_decode_layer(torch_cuda, c2_weights, T, monkeypatch):
+    """The whole decode layer as one cooperative launch (RMOE_SMALL_LAYER=1): the C2 layer at
+    up to 16 tokens, and a sigmoid-gate layer with a shared expert, against the oracle."""
+    monkeypatch.setenv("RMOE_SMALL_LAYER", "1")
+    lw = c2_weights
+    x = synth.activations(T, lw.H, seed=200 + T)
+    out, ids, w, _ = O.moe_layer_q_exact(x, lw)
+    got = run_layer(torch_cuda, lw, x)
+    check_layer(got, lw, x, out, ids, w, f"one-launch b={T}")
+    ls = synth.make_layer(512, 256, 16, 4, gate_t=12, up_t=12, down_t=14, dlo=0.001, dhi=0.01, seed=9, gate=1,
+                          shared=True)
+    xs = synth.activations(T, ls.H, seed=9)
+    out, ids, w, _ = O.moe_layer_q_exact(xs, ls)
+    got = run_layer(torch_cuda, ls, xs)
+    check_layer(got, ls, xs, out, ids, w, f"one-launch sigmoid+shared b={T}")
+
+
 @pytest.mark.parametrize("T", [1, 3, 127])
 def test_ragged_token_counts(torch_cuda, T):
     lw = synth.config_c1()
