@@ -633,7 +633,7 @@ rmoe_status rmoe_layer_create(const rmoe_layer_desc* d, rmoe_layer** out) {
 // run one after another on the caller's stream (they share the workspace).  A chunk keeps at
 // least HOSTIO_ROWS_PER_EXPERT routed rows per expert on average, so the tensor-core tiles stay
 // full; smaller batches, and calls that ask for routing or stage times, run as one chunk.
-static constexpr uint64_t HOSTIO_ROWS_PER_EXPERT = 64;
+static constexpr uint64_t HOSTIO_ROWS_PER_EXPERT = 128;
 static constexpr int HOSTIO_MAX_CHUNKS = 8;
 
 static rmoe_status forward_host_io(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s,

@@ -109,3 +109,64 @@ def test_ep_create_times_out_when_a_rank_never_joins(gpu):
     assert code != 0, msg
     assert "NCCL" in msg and "no progress" in msg, msg
     assert dt < 60, dt
+
+
+def _leave_rank(rank, world, uid, q, left):
+    """Both ranks run one forward; then rank 1 closes its layer and leaves (between steps,
+    nothing in flight) while rank 0 runs a second forward, which must fail within the
+    communicator timeout instead of waiting for good."""
+    import os
+    import time
+
+    os.environ["RMOE_EP_TIMEOUT_MS"] = "5000"
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+
+    from rusty_engine_b200.moe import MoELayer
+
+    torch.cuda.set_device(rank)
+    lw = synth.config_c1()
+    layer = MoELayer.expert_parallel(lw, rank, world, uid, device=rank)
+    x = torch.from_numpy(synth.activations(8, lw.H, seed=rank)).cuda()
+    layer.forward(x)
+    torch.cuda.synchronize()
+    if rank == 1:
+        layer.close()
+        left.set()
+        return
+    left.wait(60)
+    t0 = time.time()
+    try:
+        layer.forward(x)
+        torch.cuda.synchronize()
+        q.put((0, "forward returned", time.time() - t0))
+    except Exception as e:
+        q.put((-1, f"{type(e).__name__}: {e}", time.time() - t0))
+    layer.close()
+
+
+def test_ep_peer_leaves_forward_fails_within_timeout(gpu):
+    """Failure made on the host, on two GPUs: a rank leaves between steps; the other rank's next
+    forward ends with RMOE_ERR_NCCL (an NCCL error, or no progress for RMOE_EP_TIMEOUT_MS, then
+    the communicator is aborted) instead of hanging.  NVLS off, as for every such test."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from rusty_engine_b200.moe import ep_unique_id
+
+    ctx = mp.get_context("spawn")
+    q, left = ctx.Queue(), ctx.Event()
+    uid = ep_unique_id()
+    procs = [ctx.Process(target=_leave_rank, args=(r, 2, uid, q, left)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank did not finish within 180 s"
+    code, msg, dt = q.get(timeout=10)
+    assert code != 0 and "NCCL" in msg, msg
+    assert dt < 60, dt
