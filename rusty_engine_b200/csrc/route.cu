@@ -680,37 +680,60 @@ __device__ void dispatch_small(const RouteParams& p, const int* ids_s, int* cnt_
         }
 }
 
-// Dispatch of at most 32 picks (no shared expert, every expert's rows within one tile) by one
-// warp: a pick's expert-sorted row is its rank by (expert, pick index), each expert one tile.
+// Dispatch of at most 64 picks (no shared expert, every expert's rows within one tile) by one
+// warp, two picks per lane: a pick's expert-sorted row is its rank by (expert, pick index), and
+// each touched expert is one tile, placed by the number of touched experts below it.  Short
+// rolled loops over the picks in shared memory (this code runs once per launch).
+static constexpr int DT_MAX = 64;
 __device__ void dispatch_tiny(const RouteParams& p, const int* ids_s, int lane) {
+    __shared__ int first_s[DT_MAX];
     const int np = p.T * p.k;
-    const bool live = lane < np;
-    const int id = live ? ids_s[lane] : 0x7fffffff;
-    int pos = 0, below = 0;  // picks before this one in expert order; experts below this one
-    bool first = true;       // this lane holds its expert's first pick
-    for (int j = 0; j < np; j++) {
-        const int o = __shfl_sync(0xffffffffu, id, j);
-        pos += (o < id) || (o == id && j < lane);
-        if (o == id && j < lane) first = false;
+    int id[2], pos[2] = {0, 0}, rows[2] = {0, 0};
+    bool first[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int i = lane + 32 * h;
+        id[h] = i < np ? ids_s[i] : 0x7fffffff;
+        first[h] = i < np;
     }
-    const unsigned heads = __ballot_sync(0xffffffffu, live && first);
     for (int j = 0; j < np; j++) {
-        const int o = __shfl_sync(0xffffffffu, id, j);
-        below += ((heads >> j) & 1u) && o < id;
+        const int o = ids_s[j];  // the same word for every lane: a broadcast
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const bool before = j < lane + 32 * h;
+            pos[h] += (o < id[h]) || (o == id[h] && before);
+            rows[h] += o == id[h];
+            if (o == id[h] && before) first[h] = false;
+        }
     }
-    const int rows = __popc(__match_any_sync(0xffffffffu, id));
-    if (live) {
-        const int t = lane / p.k;
-        p.row_tok[pos] = t;
-        p.row_slot[pos] = lane - t * p.k;
-        p.slot_row[lane] = pos;
-        p.rowexp[pos] = -127;
-        if (first) p.tiles[below] = make_int4(id, pos, rows, 0);
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+        if (lane + 32 * h < DT_MAX) first_s[lane + 32 * h] = first[h];
+    __syncwarp();
+    int below[2] = {0, 0};  // touched experts with a smaller id
+    for (int j = 0; j < np; j++) {
+        const int o = ids_s[j], f = first_s[j];
+#pragma unroll
+        for (int h = 0; h < 2; h++) below[h] += f && o < id[h];
+    }
+    const unsigned heads0 = __ballot_sync(0xffffffffu, first[0]), heads1 = __ballot_sync(0xffffffffu, first[1]);
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int i = lane + 32 * h;
+        if (i < np) {
+            const int t = i / p.k;
+            p.row_tok[pos[h]] = t;
+            p.row_slot[pos[h]] = i - t * p.k;
+            p.slot_row[i] = pos[h];
+            p.rowexp[pos[h]] = -127;
+            if (first[h]) p.tiles[below[h]] = make_int4(id[h], pos[h], rows[h], 0);
+        }
     }
     if (lane == 0) {
         *p.n_rows = np;
-        *p.n_tiles = __popc(heads);
+        *p.n_tiles = __popc(heads0) + __popc(heads1);
     }
+    __syncwarp();
 }
 
 static size_t dispatch_small_scratch(int T, int E, int k) {
@@ -782,37 +805,60 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
         wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 
-    // 1. the token group's rows -> shared memory (+ fp16 copy and zeroed output rows)
+    // 1. the token group's rows -> shared memory: 16-B asynchronous copies, every one in flight
+    //    before any is waited for (a short rolled loop: this code runs once per launch, and
+    //    straight-line code fetched once costs more than the copies themselves)
     float4* xs4 = reinterpret_cast<float4*>(fsm);
     const float4* xg = reinterpret_cast<const float4*>(p.x + (size_t)t0 * H);
-    for (int q0 = 0; q0 < nt * n4; q0 += 4 * RF_THREADS) {  // four loads in flight per thread
-        float4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int q = q0 + u * RF_THREADS + tid;
-            v[u] = q < nt * n4 ? __ldg(xg + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int q = q0 + u * RF_THREADS + tid;
-            if (q >= nt * n4) continue;
-            xs4[q] = v[u];
-            if (blockIdx.x == 0) {
-                // fp16 MMA operand; |x| beyond the fp16 range is reported, never silently inf
-                if (!(fabsf(v[u].x) <= 65504.f && fabsf(v[u].y) <= 65504.f && fabsf(v[u].z) <= 65504.f &&
-                      fabsf(v[u].w) <= 65504.f))
-                    atomicOr(p.status, (unsigned)DERR_FP16_RANGE);
-                *reinterpret_cast<uint2*>(p.xb + (size_t)t0 * H + 4 * q) =
-                    make_uint2(pack_f16x2(v[u].x, v[u].y), pack_f16x2(v[u].z, v[u].w));
-                if (MODE == 2 && p.out_zero)
-                    *reinterpret_cast<float4*>(p.out_zero + (size_t)t0 * H + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-    }
+    for (int q = tid; q < nt * n4; q += RF_THREADS)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(xs4 + q)), "l"(xg + q) : "memory");
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
     __syncthreads();
+    if (blockIdx.x == 0)  // fp16 MMA operand (|x| beyond the fp16 range is reported, never silently inf)
+        for (int q = tid; q < nt * n4; q += RF_THREADS) {
+            const float4 v = xs4[q];
+            if (!(fabsf(v.x) <= 65504.f && fabsf(v.y) <= 65504.f && fabsf(v.z) <= 65504.f && fabsf(v.w) <= 65504.f))
+                atomicOr(p.status, (unsigned)DERR_FP16_RANGE);
+            *reinterpret_cast<uint2*>(p.xb + (size_t)t0 * H + 4 * q) =
+                make_uint2(pack_f16x2(v.x, v.y), pack_f16x2(v.z, v.w));
+            if (MODE == 2 && p.out_zero)
+                *reinterpret_cast<float4*>(p.out_zero + (size_t)t0 * H + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 
-    // 2. logits: lane l sums K elements 4 l + 128 j of its expert for every token of the group
-    if (e < E) {
+    // 2. logits: lane l sums K elements 4 l + 128 j of its expert for every token of the group.
+    //    Rows of at most 32 * RF_WCH float4 stay in registers and the token loop is rolled (four
+    //    partial sums per lane, so the FMA chains are short); warp 0 also forms ||x_t||^2 for the
+    //    near-tie window of the top-k step.
+    __shared__ float xn2_s[RF_TOK];
+    if (e < E && n4 <= 32 * RF_WCH) {
+        float mine = 0.0f;
+        for (int t = 0; t < nt; t++) {
+            const float4* xr = xs4 + t * n4 + lane;
+            float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, q0 = 0.f, q1 = 0.f;
+#pragma unroll
+            for (int u = 0; u < RF_WCH; u++)
+                if (lane + 32 * u < n4) {
+                    const float4 a = wv[u], b = xr[32 * u];
+                    s0 = fmaf(a.x, b.x, s0);
+                    s1 = fmaf(a.y, b.y, s1);
+                    s2 = fmaf(a.z, b.z, s2);
+                    s3 = fmaf(a.w, b.w, s3);
+                    if (warp == 0) {
+                        q0 = fmaf(b.x, b.x, fmaf(b.y, b.y, q0));
+                        q1 = fmaf(b.z, b.z, fmaf(b.w, b.w, q1));
+                    }
+                }
+            float v = (s0 + s1) + (s2 + s3), n2 = q0 + q1;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                v += __shfl_xor_sync(0xffffffffu, v, off);
+                n2 += __shfl_xor_sync(0xffffffffu, n2, off);
+            }
+            if (lane == t) mine = v;
+            if (warp == 0 && lane == 0) xn2_s[t] = n2;
+        }
+        if (lane < nt) p.logits[(size_t)(t0 + lane) * E + e] = mine;
+    } else if (e < E) {
         float acc[RF_TOK];
 #pragma unroll
         for (int t = 0; t < RF_TOK; t++) acc[t] = 0.0f;
@@ -848,6 +894,17 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
                 if (lane == t) mine = v;
             }
         if (lane < nt) p.logits[(size_t)(t0 + lane) * E + e] = mine;
+        if (warp == 0)  // ||x_t||^2 for the top-k step, one token at a time
+            for (int t = 0; t < nt; t++) {
+                float n2 = 0.0f;
+                for (int j = lane; j < n4; j += 32) {
+                    const float4 b = xs4[t * n4 + j];
+                    n2 = fmaf(b.x, b.x, fmaf(b.y, b.y, fmaf(b.z, b.z, fmaf(b.w, b.w, n2))));
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, off);
+                if (lane == 0) xn2_s[t] = n2;
+            }
     }
 
     // 3. the token group's last CTA: top-k of its tokens
@@ -872,7 +929,8 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
         bool done = true;
         if (!refine_on(p)) {
             id = warp_topk(lg + warp * E, E, k, p.gate, lane, p.topk_w + (size_t)t * k);
-        } else if (!warp_topk_try(p, t, lg + warp * E, lane, p.topk_w + (size_t)t * k, id, amb[warp])) {
+        } else if (!warp_topk_try(p, t, lg + warp * E, lane, p.topk_w + (size_t)t * k, id, amb[warp],
+                                  sqrtf(xn2_s[warp]))) {
             done = false;
             if (lane == 0) amb_list[atomicAdd(&amb_n, 1)] = warp;  // near-tie: rescored below
         }
@@ -908,7 +966,7 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
         if (tid == 0) p.ticket[0] = 0u;  // every token group has taken its ticket
     }
     __syncthreads();
-    if (T * k <= 32 && !p.has_shared && T <= p.tile_rows) {
+    if (T * k <= DT_MAX && !p.has_shared && T <= p.tile_rows) {
         if (warp == 0) dispatch_tiny(p, ids_s, lane);
     } else {
         dispatch_small(p, ids_s, cnt_s, off_s, reinterpret_cast<int*>(fsm));

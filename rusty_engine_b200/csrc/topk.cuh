@@ -168,9 +168,9 @@ struct AmbTok {
 // the window (one of them may belong in the top k).
 template <int NS>
 __device__ bool warp_topk_try_n(const RouteParams& p, int t, const float* row, int lane, float* w_out, int& id,
-                                AmbTok& a) {
+                                AmbTok& a, float xn) {
     const int E = p.E, k = p.k, gate = p.gate;
-    const float xn = warp_row_norm(p.xb + (size_t)t * p.H, p.H, lane);
+    if (xn < 0.0f) xn = warp_row_norm(p.xb + (size_t)t * p.H, p.H, lane);
     const int n = min(k + 1, E);
     float sc;
     warp_select_n<NS>(row, E, n, gate, lane, sc, id);
@@ -211,14 +211,15 @@ __device__ bool warp_topk_try_n(const RouteParams& p, int t, const float* row, i
     return false;
 }
 
+// xn: ||x_t||_2 where the caller has it, else negative (the warp reads the token's fp16 copy).
 __device__ __forceinline__ bool warp_topk_try(const RouteParams& p, int t, const float* row, int lane, float* w_out,
-                                              int& id, AmbTok& a) {
+                                              int& id, AmbTok& a, float xn = -1.0f) {
     const int ns = (p.E + 31) / 32;
-    if (ns <= 1) return warp_topk_try_n<1>(p, t, row, lane, w_out, id, a);
-    if (ns <= 2) return warp_topk_try_n<2>(p, t, row, lane, w_out, id, a);
-    if (ns <= 4) return warp_topk_try_n<4>(p, t, row, lane, w_out, id, a);
-    if (ns <= 8) return warp_topk_try_n<8>(p, t, row, lane, w_out, id, a);
-    return warp_topk_try_n<MAX_E / 32>(p, t, row, lane, w_out, id, a);
+    if (ns <= 1) return warp_topk_try_n<1>(p, t, row, lane, w_out, id, a, xn);
+    if (ns <= 2) return warp_topk_try_n<2>(p, t, row, lane, w_out, id, a, xn);
+    if (ns <= 4) return warp_topk_try_n<4>(p, t, row, lane, w_out, id, a, xn);
+    if (ns <= 8) return warp_topk_try_n<8>(p, t, row, lane, w_out, id, a, xn);
+    return warp_topk_try_n<MAX_E / 32>(p, t, row, lane, w_out, id, a, xn);
 }
 
 // Second step, the whole CTA (every thread calls it, with the same arguments): the listed
