@@ -118,17 +118,6 @@ bool make_f32_rows_map(const float* base, uint64_t rows, uint32_t width, uint32_
                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// ---------------------------------------------------------------------------------------------
-// device: TMA 2-D tile load (no multicast)
-// ---------------------------------------------------------------------------------------------
-__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];\n" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
 template <int TYPE, int NMAT>
 struct TcGeom {
     static_assert(NMAT == 2, "the gate and up matrices");

@@ -152,6 +152,12 @@ struct alignas(64) TcMaps {
     CUtensorMap b;
 };
 
+// The same decode products with the weight stream on TMA (gemv_tma.cu): CTA = (tile, 128-row
+// block), weights from the stacks' maps (maps.w), same tiles, h layout and launch order as the
+// gv launchers.  cudaErrorNotSupported where the shapes do not fit (then use those).
+cudaError_t launch_gvt_gateup(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s);
+cudaError_t launch_gvt_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s);
+
 // Build the maps of one stack (after upload_mat) / of the h workspace; false on a driver error.
 bool make_weight_maps(const DevMat& M, WMaps& out);
 bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMap& out);

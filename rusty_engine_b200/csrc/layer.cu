@@ -20,6 +20,9 @@
 
 namespace rmoe {
 
+// decode batches of at least this many tokens use the TMA-streamed decode kernels
+static constexpr uint32_t GVT_MIN_T = 2;
+
 static thread_local std::string g_err;
 
 rmoe_status fail(rmoe_status s, const char* fmt, ...) {
@@ -563,9 +566,21 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         maps.w[1][1] = L->smu;
         maps.b = L->xsmap;
     }
-    e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s)
-        : gv   ? launch_gv_gateup(gp, max_tiles, tile_rows, (int)T, s)
-               : launch_small_gateup(gp, max_tiles, tile_rows, s);
+    // decode batches of several tokens stream the weights with TMA (gemv_tma.cu); single tokens
+    // (a few tiles) keep the per-lane copies of gv_kernel, whose K-split CTAs fill the GPU
+    const bool gvt = gv && T >= GVT_MIN_T;
+    TcMaps gmaps;
+    if (gvt) {
+        memset(&gmaps, 0, sizeof gmaps);
+        gmaps.w[0][0] = L->mg;
+        gmaps.w[0][1] = L->mu;
+        gmaps.w[1][0] = L->smg;
+        gmaps.w[1][1] = L->smu;
+    }
+    e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : cudaErrorNotSupported;
+    if (!use_tc && gvt) e = launch_gvt_gateup(gp, gmaps, max_tiles, tile_rows, s);
+    if (!use_tc && e == cudaErrorNotSupported)
+        e = gv ? launch_gv_gateup(gp, max_tiles, tile_rows, (int)T, s) : launch_small_gateup(gp, max_tiles, tile_rows, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");
     mark(2);
     if (use_tc && (e = launch_rescale_h(gp, (int)rows_T, s)) != cudaSuccess) return cuda_fail(e, "h rescale launch");
@@ -574,9 +589,14 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         maps.w[1][0] = L->smd;
         maps.b = L->hmap;
     }
-    e = use_tc ? launch_tc_down(gp, maps, max_tiles, s)
-        : gv   ? launch_gv_down(gp, max_tiles, tile_rows, (int)T, s)
-               : launch_small_down(gp, max_tiles, tile_rows, s);
+    if (gvt) {
+        gmaps.w[0][0] = L->md;
+        gmaps.w[1][0] = L->smd;
+    }
+    e = use_tc ? launch_tc_down(gp, maps, max_tiles, s) : cudaErrorNotSupported;
+    if (!use_tc && gvt) e = launch_gvt_down(gp, gmaps, max_tiles, tile_rows, s);
+    if (!use_tc && e == cudaErrorNotSupported)
+        e = gv ? launch_gv_down(gp, max_tiles, tile_rows, (int)T, s) : launch_small_down(gp, max_tiles, tile_rows, s);
     if (e != cudaSuccess) return cuda_fail(e, "down launch");
     L->last_tc = use_tc;
     mark(3);

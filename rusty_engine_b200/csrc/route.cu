@@ -682,11 +682,10 @@ __device__ void dispatch_small(const RouteParams& p, const int* ids_s, int* cnt_
 
 // Dispatch of at most 64 picks (no shared expert, every expert's rows within one tile) by one
 // warp, two picks per lane: a pick's expert-sorted row is its rank by (expert, pick index), and
-// each touched expert is one tile, placed by the number of touched experts below it.  Short
-// rolled loops over the picks in shared memory (this code runs once per launch).
+// each touched expert is one tile, placed by the number of touched experts below it (short
+// rolled loops over the picks, exchanged by shuffles).
 static constexpr int DT_MAX = 64;
 __device__ void dispatch_tiny(const RouteParams& p, const int* ids_s, int lane) {
-    __shared__ int first_s[DT_MAX];
     const int np = p.T * p.k;
     int id[2], pos[2] = {0, 0}, rows[2] = {0, 0};
     bool first[2];
@@ -697,7 +696,7 @@ __device__ void dispatch_tiny(const RouteParams& p, const int* ids_s, int lane) 
         first[h] = i < np;
     }
     for (int j = 0; j < np; j++) {
-        const int o = ids_s[j];  // the same word for every lane: a broadcast
+        const int o = __shfl_sync(0xffffffffu, j < 32 ? id[0] : id[1], j & 31);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const bool before = j < lane + 32 * h;
@@ -706,17 +705,14 @@ __device__ void dispatch_tiny(const RouteParams& p, const int* ids_s, int lane) 
             if (o == id[h] && before) first[h] = false;
         }
     }
-#pragma unroll
-    for (int h = 0; h < 2; h++)
-        if (lane + 32 * h < DT_MAX) first_s[lane + 32 * h] = first[h];
-    __syncwarp();
+    const unsigned heads0 = __ballot_sync(0xffffffffu, first[0]), heads1 = __ballot_sync(0xffffffffu, first[1]);
     int below[2] = {0, 0};  // touched experts with a smaller id
     for (int j = 0; j < np; j++) {
-        const int o = ids_s[j], f = first_s[j];
+        const int o = __shfl_sync(0xffffffffu, j < 32 ? id[0] : id[1], j & 31);
+        const bool f = ((j < 32 ? heads0 : heads1) >> (j & 31)) & 1u;
 #pragma unroll
         for (int h = 0; h < 2; h++) below[h] += f && o < id[h];
     }
-    const unsigned heads0 = __ballot_sync(0xffffffffu, first[0]), heads1 = __ballot_sync(0xffffffffu, first[1]);
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         const int i = lane + 32 * h;
@@ -733,7 +729,6 @@ __device__ void dispatch_tiny(const RouteParams& p, const int* ids_s, int lane) 
         *p.n_rows = np;
         *p.n_tiles = __popc(heads0) + __popc(heads1);
     }
-    __syncwarp();
 }
 
 static size_t dispatch_small_scratch(int T, int E, int k) {
@@ -768,14 +763,18 @@ __global__ void __launch_bounds__(RS_THREADS) route_small_kernel(RouteParams p) 
 
 // ---------------------------------------------------------------------------------------
 // Whole routing of a small batch in fast mode, one launch.  CTA (expert group, token group) =
-// 8 experts (a warp each) x 8 tokens: the token rows are staged in shared memory (the first
-// expert group also writes their fp16 copy and zeroes their output rows) and every warp forms
-// its expert's logits from FFMA partial sums over K folded by shuffles.  The last CTA of each
-// token group to finish (atomic ticket, no waiting) runs top-k for those tokens; the last of
-// those runs dispatch_small for the whole batch and resets the tickets.
+// 8 / KQ experts x 8 tokens, a warp per (expert, K slice): the token rows are staged in shared
+// memory (the first expert group also writes their fp16 copy and zeroes their output rows),
+// every warp forms its slice's partial logits from FFMA sums folded by shuffles, and the
+// slices are added in slice order.  Routing proper (KQ = 4: 2 experts per CTA) spreads the
+// router rows and the shared-memory reads of x over E / 2 CTAs; the logits-only mode for
+// mid-size batches (KQ = 1: 8 experts per CTA) keeps the x staging per CTA low.  The last CTA
+// of each token group to finish (atomic ticket, no waiting) runs top-k for those tokens; the
+// last of those runs the dispatch for the whole batch and resets the tickets.
 // ---------------------------------------------------------------------------------------
-static constexpr int RF_EXP = 8, RF_TOK = 8, RF_THREADS = 256;
+static constexpr int RF_WARPS = 8, RF_TOK = 8, RF_THREADS = 32 * RF_WARPS;
 static constexpr int RF_WCH = 16;  // float4 of the expert row each lane holds at a time
+__host__ __device__ constexpr int rf_kq(int mode) { return mode == 0 ? 1 : 4; }
 
 static int rf_stage_off(int E) { return (RF_TOK * E + 3) & ~3; }  // floats before the rescoring stage
 static size_t route_fused_smem(int T, int H, int E, int k) {
@@ -783,11 +782,22 @@ static size_t route_fused_smem(int T, int H, int E, int k) {
     return std::max(need, (size_t)(rf_stage_off(E) + rescore_stage_floats(H)) * 4);
 }
 
+// A read-only 16-B load issued exactly once: the router rows are reused by every token of the
+// group from registers, and a plain __ldg may be re-issued inside the token loop (to save
+// registers), which puts a global-memory round trip in every iteration.
+__device__ __forceinline__ float4 ldg_once(const float4* src) {
+    float4 v;
+    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];\n" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(src));
+    return v;
+}
+
 template <int MODE>  // 0: logits (and the fp16 copy) only; 1: + top-k; 2: + the dispatch
 __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RouteParams p) {
+    constexpr int KQ = rf_kq(MODE), NEXP = RF_WARPS / KQ, JS = 32 * KQ;  // JS: float4 stride of a lane
     extern __shared__ __align__(16) float fsm[];
     __shared__ int ids_s[RS_MAX_T * MAX_K];
     __shared__ int cnt_s[MAX_E + 2], off_s[MAX_E + 2];
+    __shared__ float part_s[RF_WARPS][RF_TOK], pn_s[KQ][RF_TOK];
     __shared__ unsigned ticket_s;
     pdl_trigger();  // the expert kernels may take their SM slots now; they wait for this grid
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -795,15 +805,15 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
     const int t0 = blockIdx.y * RF_TOK, nt = min(RF_TOK, T - t0);
     const int n4 = H / 4;
 
-    // 0. this warp's expert row: its first 16 float4 per lane in flight before anything waits
-    const int e = blockIdx.x * RF_EXP + warp;
-    const float4* wr = reinterpret_cast<const float4*>(p.router_w + (size_t)min(e, E - 1) * H);
+    // 0. this warp's slice of its expert row (float4 kq * 32 + lane + JS u): the first RF_WCH
+    //    per lane in flight before anything waits
+    const int el = warp / KQ, kq = warp % KQ;
+    const int e = blockIdx.x * NEXP + el;
+    const float4* wr = reinterpret_cast<const float4*>(p.router_w + (size_t)min(e, E - 1) * H) + kq * 32 + lane;
+    const int nj = (n4 - kq * 32 - lane + JS - 1) / JS;  // float4 of the slice this lane holds
     float4 wv[RF_WCH];
 #pragma unroll
-    for (int u = 0; u < RF_WCH; u++) {
-        const int j = lane + 32 * u;
-        wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    for (int u = 0; u < RF_WCH; u++) wv[u] = u < nj ? ldg_once(wr + JS * u) : make_float4(0.f, 0.f, 0.f, 0.f);
 
     // 1. the token group's rows -> shared memory: 16-B asynchronous copies, every one in flight
     //    before any is waited for (a short rolled loop: this code runs once per launch, and
@@ -825,25 +835,25 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
                 *reinterpret_cast<float4*>(p.out_zero + (size_t)t0 * H + 4 * q) = make_float4(0.f, 0.f, 0.f, 0.f);
         }
 
-    // 2. logits: lane l sums K elements 4 l + 128 j of its expert for every token of the group.
-    //    Rows of at most 32 * RF_WCH float4 stay in registers and the token loop is rolled (four
-    //    partial sums per lane, so the FMA chains are short); warp 0 also forms ||x_t||^2 for the
-    //    near-tie window of the top-k step.
-    __shared__ float xn2_s[RF_TOK];
-    if (e < E && n4 <= 32 * RF_WCH) {
-        float mine = 0.0f;
+    // 2. logits: the lane's float4 of the slice against every token of the group; a slice of
+    //    at most RF_WCH float4 per lane stays in registers and the token loop is rolled (four
+    //    partial sums per lane, so the FMA chains are short), longer rows go in chunks of
+    //    RF_WCH with the token sums carried in registers.  The first expert's warps also form
+    //    ||x_t||^2 slice by slice for the near-tie window of the top-k step.
+    const float4* xl = xs4 + kq * 32 + lane;
+    if (e < E && nj <= RF_WCH) {
         for (int t = 0; t < nt; t++) {
-            const float4* xr = xs4 + t * n4 + lane;
+            const float4* xr = xl + t * n4;
             float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f, q0 = 0.f, q1 = 0.f;
 #pragma unroll
             for (int u = 0; u < RF_WCH; u++)
-                if (lane + 32 * u < n4) {
-                    const float4 a = wv[u], b = xr[32 * u];
+                if (u < nj) {
+                    const float4 a = wv[u], b = xr[JS * u];
                     s0 = fmaf(a.x, b.x, s0);
                     s1 = fmaf(a.y, b.y, s1);
                     s2 = fmaf(a.z, b.z, s2);
                     s3 = fmaf(a.w, b.w, s3);
-                    if (warp == 0) {
+                    if (el == 0) {
                         q0 = fmaf(b.x, b.x, fmaf(b.y, b.y, q0));
                         q1 = fmaf(b.z, b.z, fmaf(b.w, b.w, q1));
                     }
@@ -854,57 +864,62 @@ __global__ void __launch_bounds__(RF_THREADS) route_fused_small_kernel(RoutePara
                 v += __shfl_xor_sync(0xffffffffu, v, off);
                 n2 += __shfl_xor_sync(0xffffffffu, n2, off);
             }
-            if (lane == t) mine = v;
-            if (warp == 0 && lane == 0) xn2_s[t] = n2;
+            if (lane == 0) {
+                part_s[warp][t] = v;
+                if (el == 0) pn_s[kq][t] = n2;
+            }
         }
-        if (lane < nt) p.logits[(size_t)(t0 + lane) * E + e] = mine;
     } else if (e < E) {
-        float acc[RF_TOK];
+        float acc[RF_TOK], nacc[RF_TOK];
 #pragma unroll
-        for (int t = 0; t < RF_TOK; t++) acc[t] = 0.0f;
-        for (int j0 = 0; j0 < n4; j0 += 32 * RF_WCH) {
-            if (j0 > 0)
+        for (int t = 0; t < RF_TOK; t++) acc[t] = nacc[t] = 0.0f;
+        for (int u0 = 0; u0 < nj; u0 += RF_WCH) {
+            if (u0 > 0)
 #pragma unroll
-                for (int u = 0; u < RF_WCH; u++) {
-                    const int j = j0 + lane + 32 * u;
-                    wv[u] = j < n4 ? __ldg(wr + j) : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
+                for (int u = 0; u < RF_WCH; u++)
+                    wv[u] = u0 + u < nj ? ldg_once(wr + JS * (u0 + u)) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int u = 0; u < RF_WCH; u++) {
-                const int j = j0 + lane + 32 * u;
-                if (j < n4)
+            for (int u = 0; u < RF_WCH; u++)
+                if (u0 + u < nj)
 #pragma unroll
                     for (int t = 0; t < RF_TOK; t++)
                         if (t < nt) {
-                            const float4 a = wv[u], b = xs4[t * n4 + j];
+                            const float4 a = wv[u], b = xl[t * n4 + JS * (u0 + u)];
                             acc[t] = fmaf(a.x, b.x, acc[t]);
                             acc[t] = fmaf(a.y, b.y, acc[t]);
                             acc[t] = fmaf(a.z, b.z, acc[t]);
                             acc[t] = fmaf(a.w, b.w, acc[t]);
+                            if (el == 0) nacc[t] = fmaf(b.x, b.x, fmaf(b.y, b.y, fmaf(b.z, b.z, fmaf(b.w, b.w, nacc[t]))));
                         }
-            }
         }
-        float mine = 0.0f;
 #pragma unroll
         for (int t = 0; t < RF_TOK; t++)
             if (t < nt) {
-                float v = acc[t];
+                float v = acc[t], n2 = nacc[t];
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-                if (lane == t) mine = v;
-            }
-        if (lane < nt) p.logits[(size_t)(t0 + lane) * E + e] = mine;
-        if (warp == 0)  // ||x_t||^2 for the top-k step, one token at a time
-            for (int t = 0; t < nt; t++) {
-                float n2 = 0.0f;
-                for (int j = lane; j < n4; j += 32) {
-                    const float4 b = xs4[t * n4 + j];
-                    n2 = fmaf(b.x, b.x, fmaf(b.y, b.y, fmaf(b.z, b.z, fmaf(b.w, b.w, n2))));
+                for (int off = 16; off > 0; off >>= 1) {
+                    v += __shfl_xor_sync(0xffffffffu, v, off);
+                    n2 += __shfl_xor_sync(0xffffffffu, n2, off);
                 }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, off);
-                if (lane == 0) xn2_s[t] = n2;
+                if (lane == 0) {
+                    part_s[warp][t] = v;
+                    if (el == 0) pn_s[kq][t] = n2;
+                }
             }
+    }
+    __syncthreads();
+    __shared__ float xn2_s[RF_TOK];
+    if (kq == 0 && e < E && lane < nt) {  // the slices in slice order
+        float v = part_s[warp][lane];
+#pragma unroll
+        for (int q = 1; q < KQ; q++) v += part_s[warp + q][lane];
+        p.logits[(size_t)(t0 + lane) * E + e] = v;
+    }
+    if (warp == 0 && lane < nt) {
+        float n2 = pn_s[0][lane];
+#pragma unroll
+        for (int q = 1; q < KQ; q++) n2 += pn_s[q][lane];
+        xn2_s[lane] = n2;
     }
 
     // 3. the token group's last CTA: top-k of its tokens
@@ -980,7 +995,8 @@ static cudaError_t launch_route_fused(const RouteParams& p0, int mode, cudaStrea
     auto k = mode == 0 ? route_fused_small_kernel<0> : mode == 1 ? route_fused_small_kernel<1> : route_fused_small_kernel<2>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) return e;
-    k<<<dim3((p.E + RF_EXP - 1) / RF_EXP, (p.T + RF_TOK - 1) / RF_TOK), RF_THREADS, sm, s>>>(p);
+    const int nexp = RF_WARPS / rf_kq(mode);
+    k<<<dim3((p.E + nexp - 1) / nexp, (p.T + RF_TOK - 1) / RF_TOK), RF_THREADS, sm, s>>>(p);
     return cudaGetLastError();
 }
 

@@ -2,6 +2,7 @@
 // use: mbarriers (with bounded waits), bulk async copies, cp.async, TMEM allocation, tcgen05
 // MMA / commit / ld / st and the UMMA descriptors.
 #pragma once
+#include <cuda.h>
 #include <stdint.h>
 
 #include "common.cuh"
@@ -56,6 +57,15 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
                  "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
+}
+// 2-D tensor-map tile load global -> shared (no multicast), completion counted in bytes on `bar`
+// (x: innermost coordinate in elements of the map's type)
+__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
 }
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
