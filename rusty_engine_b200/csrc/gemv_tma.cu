@@ -12,13 +12,19 @@
 // stage; eight consumer warps (16 rows each) read their fragments from the stage, decode,
 // multiply and release the stage (one arrival per warp) for the producer to refill.
 //
-// CTA = (tile of <= NT expert-sorted rows, 128-row block of the expert's weights), K whole:
+// Items = (tile of <= NT expert-sorted rows, 128-row block of the expert's weights), K whole.
+// Gate/up runs one item per CTA; down is persistent (two CTAs per SM), each CTA walking a
+// contiguous range of items: the producer streams the raw blocks of one item after another
+// through the same ring, and the consumers stage a tile's token rows once for all of its row
+// blocks in the range.
 //   gate/up: h[row, f] = silu(gate_f . x) * (up_f . x)      (src/moe.rs:280-299), stored as fp16
 //            x 2^e with e per (row, 16-feature block); the row's largest e goes to rowexp[row]
 //   down:    y = down . h[row], every h block brought to the row's exponent while it is staged;
 //            out[tok] += w_slot * y * 2^rowexp                  (src/moe.rs:373-380)
 // Every mbarrier wait is bounded: on a timeout the CTA records DERR_TIMEOUT, stops, and the
 // producer waits (bounded) for the copies it issued before the CTA exits.
+#include <algorithm>
+
 #include "gemv.cuh"
 #include "tc_ptx.cuh"
 
@@ -29,6 +35,8 @@ static constexpr int GVT_CONS = 8;                       // consumer warps (row 
 static constexpr int GVT_THREADS = 32 * (GVT_CONS + 1);  // + the producer warp
 static constexpr int GVT_RB = 16 * GVT_CONS;             // weight rows per CTA (= the maps' box rows)
 static constexpr int GVT_MAXD = 8;                       // ring stages at most
+
+__host__ __device__ constexpr bool gvt_persistent(int nmat) { return nmat == 1; }
 
 template <int TYPE, int NMAT>
 struct GvtGeom {
@@ -61,17 +69,27 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
         pdl_wait();
         pdl_trigger();
     }
-    const int tile = blockIdx.y;
-    if (tile >= *p.n_tiles) return;  // uniform exit before any barrier
-    const int4 ti = p.tiles[tile];
-    const int e = ti.x, row0 = ti.y, nrows = ti.z, rblk = blockIdx.x;
-    const bool sh = e >= p.E;
-    const DevMat& M0 = NMAT == 2 ? (sh ? p.sgate : p.gate) : (sh ? p.sdown : p.down);
+    // this CTA's items (tile * nrb + row block).  Down (persistent): a contiguous range, so that
+    // consecutive items share their tile's token rows (staged once) and the weight ring streams
+    // across items.  Gate/up: one item per CTA (grid = row blocks x tile slots), which measured
+    // faster for its 16-stage items than the persistent walk.
+    constexpr bool PERSIST = gvt_persistent(NMAT);
+    const int rows_out = NMAT == 2 ? p.I : p.H, nrb = rows_out / GVT_RB;
+    int it0, it1;
+    if (PERSIST) {
+        const int n_items = *p.n_tiles * nrb;
+        it0 = (int)((long long)blockIdx.x * n_items / gridDim.x);
+        it1 = (int)((long long)(blockIdx.x + 1) * n_items / gridDim.x);  // ranges differ by one item at most
+    } else {
+        it0 = (int)blockIdx.y < *p.n_tiles ? (int)blockIdx.y * nrb + (int)blockIdx.x : 0;
+        it1 = (int)blockIdx.y < *p.n_tiles ? it0 + 1 : 0;
+    }
+    if (it0 >= it1) return;  // uniform exit before any barrier
     const int K = NMAT == 2 ? p.H : p.I;
     const int nraw = K / R::RK;
-    const int grow0 = (sh ? 0 : e) * (int)M0.rows + rblk * GVT_RB;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t ring = smem_u32(smem) + (uint32_t)ring_off;
+    const int total_stages = (it1 - it0) * nraw;
 
     if (tid == 0) {
         for (int i = 0; i < depth; i++) {
@@ -79,167 +97,188 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
             mbar_init(smem_u32(&empty[i]), GVT_CONS);
         }
         s_abort = 0;
-        s_consumed = nraw;
+        s_consumed = total_stages;
         fence_mbar_init();
     }
     __syncthreads();
 
-    int issued = 0;  // producer: raw blocks whose copies were issued
+    int issued = 0;  // producer: stages whose copies were issued
     if (warp == GVT_CONS) {
         // ---------------- producer: one raw block of every matrix per stage ----------------
         if (lane == 0) {
-            for (int j = 0; j < nraw; j++) {
-                const int s = j % depth;
-                if (j >= depth && !mbar_wait(smem_u32(&empty[s]), ((j / depth) + 1) & 1)) {
-                    s_abort = 1;
-                    atomicOr(p.status, (unsigned)DERR_TIMEOUT);
-                    break;
-                }
-                if (s_abort) break;
-                const uint32_t bar = smem_u32(&full[s]);
-                mbar_arrive_expect_tx(bar, (uint32_t)G::STAGE);
+            int gj = 0;
+            for (int item = it0; item < it1 && !s_abort; item++) {
+                const int4 ti = p.tiles[item / nrb];
+                const bool sh = ti.x >= p.E;
+                const DevMat& M0 = NMAT == 2 ? (sh ? p.sgate : p.gate) : (sh ? p.sdown : p.down);
+                const int grow0 = (sh ? 0 : ti.x) * (int)M0.rows + (item % nrb) * GVT_RB;
+                for (int j = 0; j < nraw; j++, gj++) {
+                    const int s = gj % depth;
+                    if (gj >= depth && !mbar_wait(smem_u32(&empty[s]), ((gj / depth) + 1) & 1)) {
+                        s_abort = 1;
+                        atomicOr(p.status, (unsigned)DERR_TIMEOUT);
+                        break;
+                    }
+                    if (s_abort) break;
+                    const uint32_t bar = smem_u32(&full[s]);
+                    mbar_arrive_expect_tx(bar, (uint32_t)G::STAGE);
 #pragma unroll
-                for (int m = 0; m < NMAT; m++) {
-                    const WMaps& wm = maps.w[sh ? 1 : 0][m];
-                    const uint32_t dst = ring + (uint32_t)(s * G::STAGE + m * RS::BYTES);
-                    tma_2d(dst, &wm.main, j * (R::MB / 2), grow0, bar);
-                    if (R::DBLK) tma_2d(dst + RS::DOFF, &wm.d, grow0, j * R::DBLK, bar);
+                    for (int m = 0; m < NMAT; m++) {
+                        const WMaps& wm = maps.w[sh ? 1 : 0][m];
+                        const uint32_t dst = ring + (uint32_t)(s * G::STAGE + m * RS::BYTES);
+                        tma_2d(dst, &wm.main, j * (R::MB / 2), grow0, bar);
+                        if (R::DBLK) tma_2d(dst + RS::DOFF, &wm.d, grow0, j * R::DBLK, bar);
+                    }
+                    issued = gj + 1;
                 }
-                issued = j + 1;
             }
         }
     } else {
         // ---------------- consumers ----------------
         const int rg = warp, g = lane >> 2, c = lane & 3;
-        for (int n = tid; n < NT; n += NCT) {
-            int tok = 0;
-            float w = 0.0f;
-            if (n < nrows) {
-                const int r = row0 + n;
-                tok = p.row_tok[r];
-                if (NMAT == 1) {
-                    const int slot = p.row_slot[r];
-                    w = slot < p.k ? p.topk_w[(size_t)tok * p.k + slot] : 1.0f;
-                }
-            }
-            s_tok[n] = tok;
-            s_w[n] = w;
-        }
-        if (NMAT == 1) {
-            pdl_wait();
-            for (int n = tid; n < NT; n += NCT) s_rexp[n] = n < nrows ? __ldcg(p.rowexp + row0 + n) : 0;
-        }
-        asm volatile("bar.sync 1, %0;\n" ::"n"(NCT) : "memory");
-
-        // token operand in fragment order (as gv_tile): entry ((u * 8 + s) * NTT + t) * 32 + lane
         uint2* bsm = reinterpret_cast<uint2*>(smem);
-        {
-            const int cpr = K / 8;
-            const int hstride = p.I / GV_EBLK;
-            const int total = nrows * cpr;
-            constexpr int SB = 4;
-            for (int i0 = 0; i0 < total; i0 += SB * NCT) {
-                uint4 v[SB];
-                int d[SB];
+        int cur_tile = -1, row0 = 0, nrows = 0, gj = 0;
+        int s = 0;               // ring slot of stage gj (kept incrementally: depth is a runtime value)
+        uint32_t phase = 0;      // parity of the full[s] phase stage gj completes
+        if (NMAT == 1) pdl_wait();  // h, its exponents and the row exponents are gate/up's output
+        for (int item = it0; item < it1; item++) {
+            const int tile = item / nrb, rblk = item % nrb;
+            if (tile != cur_tile) {
+                // the previous tile's token rows and tables are no longer read by any warp
+                asm volatile("bar.sync 1, %0;\n" ::"n"(NCT) : "memory");
+                const int4 ti = p.tiles[tile];
+                cur_tile = tile;
+                row0 = ti.y;
+                nrows = ti.z;
+                for (int n = tid; n < NT; n += NCT) {
+                    int tok = 0, rexp = 0;
+                    float w = 0.0f;
+                    if (n < nrows) {
+                        const int r = row0 + n;
+                        tok = p.row_tok[r];
+                        if (NMAT == 1) {
+                            const int slot = p.row_slot[r];
+                            w = slot < p.k ? p.topk_w[(size_t)tok * p.k + slot] : 1.0f;
+                            rexp = __ldcg(p.rowexp + r);
+                        }
+                    }
+                    s_tok[n] = tok;
+                    s_w[n] = w;
+                    s_rexp[n] = rexp;
+                }
+                asm volatile("bar.sync 1, %0;\n" ::"n"(NCT) : "memory");
+                // token operand in fragment order (as gv_tile): entry ((u * 8 + s) * NTT + t) * 32 + lane
+                const int cpr = K / 8;
+                const int hstride = p.I / GV_EBLK;
+                const int total = nrows * cpr;
+                constexpr int SB = 4;
+                for (int i0 = 0; i0 < total; i0 += SB * NCT) {
+                    uint4 v[SB];
+                    int d[SB];
 #pragma unroll
-                for (int u = 0; u < SB; u++) {
-                    const int i = i0 + u * NCT + tid;
-                    d[u] = 0;
-                    if (i < total) {
+                    for (int u = 0; u < SB; u++) {
+                        const int i = i0 + u * NCT + tid;
+                        d[u] = 0;
+                        if (i < total) {
+                            const int n = i / cpr, j = i - n * cpr;
+                            if (NMAT == 2) {
+                                v[u] = __ldcg(reinterpret_cast<const uint4*>(p.xb + (size_t)s_tok[n] * K + 8 * j));
+                            } else {
+                                const size_t r = (size_t)(row0 + n);
+                                v[u] = __ldcg(reinterpret_cast<const uint4*>(p.h + r * p.I + 8 * j));
+                                d[u] = (int)__ldcg(p.hexp + r * hstride + (8 * j) / GV_EBLK);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < SB; u++) {
+                        const int i = i0 + u * NCT + tid;
+                        if (i >= total) continue;
                         const int n = i / cpr, j = i - n * cpr;
-                        if (NMAT == 2) {
-                            v[u] = __ldcg(reinterpret_cast<const uint4*>(p.xb + (size_t)s_tok[n] * K + 8 * j));
-                        } else {
-                            const size_t r = (size_t)(row0 + n);
-                            v[u] = __ldcg(reinterpret_cast<const uint4*>(p.h + r * p.I + 8 * j));
-                            d[u] = (int)__ldcg(p.hexp + r * hstride + (8 * j) / GV_EBLK);
+                        uint4 w = v[u];
+                        if (NMAT == 1) {
+                            const int dd = d[u] - s_rexp[n];
+                            const uint2 lo = gv_scale4(make_uint2(w.x, w.y), dd), hi = gv_scale4(make_uint2(w.z, w.w), dd);
+                            w = make_uint4(lo.x, lo.y, hi.x, hi.y);
+                        }
+#pragma unroll
+                        for (int hf = 0; hf < 2; hf++) {
+                            const int kk = 8 * j + 4 * hf;
+                            int cc, st;
+                            D::inv(kk & (GV_UK - 1), cc, st);
+                            const uint32_t x01 = hf ? w.z : w.x, x23 = hf ? w.w : w.y;
+                            bsm[(((kk / GV_UK) * 8 + st) * NTT + (n >> 3)) * 32 + (n & 7) * 4 + cc] =
+                                make_uint2(__byte_perm(x01, x23, 0x5410), __byte_perm(x01, x23, 0x7632));
                         }
                     }
                 }
-#pragma unroll
-                for (int u = 0; u < SB; u++) {
-                    const int i = i0 + u * NCT + tid;
-                    if (i >= total) continue;
-                    const int n = i / cpr, j = i - n * cpr;
-                    uint4 w = v[u];
-                    if (NMAT == 1) {
-                        const int dd = d[u] - s_rexp[n];
-                        const uint2 lo = gv_scale4(make_uint2(w.x, w.y), dd), hi = gv_scale4(make_uint2(w.z, w.w), dd);
-                        w = make_uint4(lo.x, lo.y, hi.x, hi.y);
-                    }
-#pragma unroll
-                    for (int hf = 0; hf < 2; hf++) {
-                        const int kk = 8 * j + 4 * hf;
-                        int cc, st;
-                        D::inv(kk & (GV_UK - 1), cc, st);
-                        const uint32_t x01 = hf ? w.z : w.x, x23 = hf ? w.w : w.y;
-                        bsm[(((kk / GV_UK) * 8 + st) * NTT + (n >> 3)) * 32 + (n & 7) * 4 + cc] =
-                            make_uint2(__byte_perm(x01, x23, 0x5410), __byte_perm(x01, x23, 0x7632));
-                    }
-                }
+                asm volatile("bar.sync 1, %0;\n" ::"n"(NCT) : "memory");
             }
-        }
-        asm volatile("bar.sync 1, %0;\n" ::"n"(NCT) : "memory");
 
-        float acc[NMAT][NTT][4];
+            float acc[NMAT][NTT][4];
 #pragma unroll
-        for (int m = 0; m < NMAT; m++)
+            for (int m = 0; m < NMAT; m++)
 #pragma unroll
-            for (int t = 0; t < NTT; t++)
+                for (int t = 0; t < NTT; t++)
 #pragma unroll
-                for (int q = 0; q < 4; q++) acc[m][t][q] = 0.0f;
-        const int ntl = (nrows + 7) >> 3;  // n-tiles holding live token rows
+                    for (int q = 0; q < 4; q++) acc[m][t][q] = 0.0f;
+            const int ntl = (nrows + 7) >> 3;  // n-tiles holding live token rows
 
-        for (int j = 0; j < nraw; j++) {
-            const int s = j % depth;
-            if (s_abort || !mbar_wait(smem_u32(&full[s]), (j / depth) & 1)) {
-                if (!s_abort) {
-                    s_abort = 1;
-                    atomicOr(p.status, (unsigned)DERR_TIMEOUT);
-                }
-                if (lane == 0) atomicMin(&s_consumed, j);
-                break;
-            }
-            const uint8_t* st = smem + ring_off + (size_t)s * G::STAGE;
-#pragma unroll
-            for (int uu = 0; uu < UPB; uu++) {
-                const int u = j * UPB + uu;
-                const uint2* bu = bsm + (size_t)u * 8 * NTT * 32 + lane;
-#pragma unroll
-                for (int m = 0; m < NMAT; m++) {
-                    uint32_t afr[8][4];
-#pragma unroll
-                    for (int r = 0; r < 2; r++) {
-                        const int row = 16 * rg + g + 8 * r;
-                        const uint8_t* rp = st + m * RS::BYTES + row * R::PITCH;
-                        uint4 q16[D::N16 > 0 ? D::N16 : 1];
-                        uint2 q8[D::N8 > 0 ? D::N8 : 1];
-#pragma unroll
-                        for (int jj = 0; jj < D::N16; jj++) q16[jj] = *reinterpret_cast<const uint4*>(rp + D::off16(uu, c, jj));
-#pragma unroll
-                        for (int jj = 0; jj < D::N8; jj++) q8[jj] = *reinterpret_cast<const uint2*>(rp + D::off8(uu, c, jj));
-                        const uint16_t db =
-                            D::DPL ? *reinterpret_cast<const uint16_t*>(st + m * RS::BYTES + RS::DOFF + row * 2) : 0;
-                        if (r == 0) D::template decode<0>(q16, q8, c, db, afr);
-                        else D::template decode<1>(q16, q8, c, db, afr);
+            for (int j = 0; j < nraw; j++, gj++) {
+                if (s_abort || !mbar_wait(smem_u32(&full[s]), phase)) {
+                    if (!s_abort) {
+                        s_abort = 1;
+                        atomicOr(p.status, (unsigned)DERR_TIMEOUT);
                     }
+                    if (lane == 0) atomicMin(&s_consumed, gj);
+                    break;
+                }
+                const uint8_t* st = smem + ring_off + (size_t)s * G::STAGE;
 #pragma unroll
-                    for (int s8 = 0; s8 < 8; s8++) {
+                for (int uu = 0; uu < UPB; uu++) {
+                    const int u = j * UPB + uu;
+                    const uint2* bu = bsm + (size_t)u * 8 * NTT * 32 + lane;
 #pragma unroll
-                        for (int t = 0; t < NTT; t++) {
-                            if (NTT == 1 || t < ntl) {
-                                const uint2 b = bu[(s8 * NTT + t) * 32];
-                                mma_f16_16816(acc[m][t], afr[s8], b.x, b.y);
+                    for (int m = 0; m < NMAT; m++) {
+                        uint32_t afr[8][4];
+#pragma unroll
+                        for (int r = 0; r < 2; r++) {
+                            const int row = 16 * rg + g + 8 * r;
+                            const uint8_t* rp = st + m * RS::BYTES + row * R::PITCH;
+                            uint4 q16[D::N16 > 0 ? D::N16 : 1];
+                            uint2 q8[D::N8 > 0 ? D::N8 : 1];
+#pragma unroll
+                            for (int jj = 0; jj < D::N16; jj++) q16[jj] = *reinterpret_cast<const uint4*>(rp + D::off16(uu, c, jj));
+#pragma unroll
+                            for (int jj = 0; jj < D::N8; jj++) q8[jj] = *reinterpret_cast<const uint2*>(rp + D::off8(uu, c, jj));
+                            const uint16_t db =
+                                D::DPL ? *reinterpret_cast<const uint16_t*>(st + m * RS::BYTES + RS::DOFF + row * 2) : 0;
+                            if (r == 0) D::template decode<0>(q16, q8, c, db, afr);
+                            else D::template decode<1>(q16, q8, c, db, afr);
+                        }
+#pragma unroll
+                        for (int s8 = 0; s8 < 8; s8++) {
+#pragma unroll
+                            for (int t = 0; t < NTT; t++) {
+                                if (NTT == 1 || t < ntl) {
+                                    const uint2 b = bu[(s8 * NTT + t) * 32];
+                                    mma_f16_16816(acc[m][t], afr[s8], b.x, b.y);
+                                }
                             }
                         }
                     }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with the stage
+                if (++s == depth) {
+                    s = 0;
+                    phase ^= 1u;
+                }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with the stage
-        }
+            // after a timeout the warps skip the stages and the stores but keep walking the items,
+            // so that every consumer warp takes the same named-barrier steps
+            if (s_abort) continue;
 
-        if (!s_abort) {
             // accumulator (m, t, q): weight row 16 rg + g + 8 (q >> 1), token row 8 t + 2 c + (q & 1)
             const int fb = rblk * GVT_CONS + rg;  // 16-row block of the output features
             const int f = fb * 16 + g;
@@ -310,7 +349,17 @@ static cudaError_t go_gvt(const GroupedParams& p, const TcMaps& maps, int max_ti
     auto k = gvt_kernel<TYPE, NT, NMAT>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k, dim3(rows / GVT_RB, max_tiles), dim3(GVT_THREADS), smem, s, p, maps, depth, (int)ring_off);
+    // down: persistent, two CTAs per SM (the shared-memory budget), each walking a range of items
+    static int n_sm = 0;
+    if (!n_sm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+        if (n_sm <= 0) n_sm = 148;
+    }
+    const int items = max_tiles * (rows / GVT_RB);
+    const dim3 grid = gvt_persistent(NMAT) ? dim3(std::min(items, 2 * n_sm)) : dim3(rows / GVT_RB, max_tiles);
+    return launch_pdl(k, grid, dim3(GVT_THREADS), smem, s, p, maps, depth, (int)ring_off);
 }
 
 template <int NMAT>

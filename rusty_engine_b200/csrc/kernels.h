@@ -155,6 +155,9 @@ struct alignas(64) TcMaps {
 // The same decode products with the weight stream on TMA (gemv_tma.cu): CTA = (tile, 128-row
 // block), weights from the stacks' maps (maps.w), same tiles, h layout and launch order as the
 // gv launchers.  cudaErrorNotSupported where the shapes do not fit (then use those).
+// Decode batches of at least GVT_MIN_T tokens use them (a single token fills the GPU only with
+// the K-split CTAs of gv_kernel).
+static constexpr uint32_t GVT_MIN_T = 2;
 cudaError_t launch_gvt_gateup(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s);
 cudaError_t launch_gvt_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s);
 

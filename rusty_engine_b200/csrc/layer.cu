@@ -20,9 +20,6 @@
 
 namespace rmoe {
 
-// decode batches of at least this many tokens use the TMA-streamed decode kernels
-static constexpr uint32_t GVT_MIN_T = 2;
-
 static thread_local std::string g_err;
 
 rmoe_status fail(rmoe_status s, const char* fmt, ...) {

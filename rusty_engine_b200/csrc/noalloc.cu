@@ -16,6 +16,8 @@
 // status word) on the caller's stream and the kernels overwrite everything else before reading
 // it.  All calls on a device share the one array, so calls that overlap on the GPU (different
 // streams, or different layers on concurrent streams) race on it.
+#include <string.h>
+
 #include <mutex>
 
 #include <algorithm>
@@ -139,9 +141,21 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     gp.xb = w.xb; gp.row_tok = w.row_tok; gp.row_slot = w.row_slot; gp.tiles = w.tiles; gp.n_tiles = w.n_tiles;
     gp.topk_w = w.topk_w; gp.h = w.h; gp.hexp = w.hexp; gp.rowexp = w.rowexp;
     gp.y = nullptr; gp.out = out; gp.status = w.status;
-    e = gv ? launch_gv_gateup(gp, max_tiles, nt, (int)T, s) : launch_small_gateup(gp, max_tiles, nt, s);
+    // the layer's own kernel choice: TMA-streamed decode kernels from GVT_MIN_T tokens (their
+    // tensor maps live in the layer), the per-lane-copy ones below, the generic small kernels
+    // for the other formats
+    const bool gvt = gv && T >= GVT_MIN_T;
+    TcMaps gmaps;
+    memset(&gmaps, 0, sizeof gmaps);
+    gmaps.w[0][0] = L->mg; gmaps.w[0][1] = L->mu; gmaps.w[1][0] = L->smg; gmaps.w[1][1] = L->smu;
+    e = gvt ? launch_gvt_gateup(gp, gmaps, max_tiles, nt, s) : cudaErrorNotSupported;
+    if (e == cudaErrorNotSupported)
+        e = gv ? launch_gv_gateup(gp, max_tiles, nt, (int)T, s) : launch_small_gateup(gp, max_tiles, nt, s);
     if (e != cudaSuccess) return cuda_fail(e, "noalloc gate/up launch");
-    e = gv ? launch_gv_down(gp, max_tiles, nt, (int)T, s) : launch_small_down(gp, max_tiles, nt, s);
+    gmaps.w[0][0] = L->md; gmaps.w[1][0] = L->smd;
+    e = gvt ? launch_gvt_down(gp, gmaps, max_tiles, nt, s) : cudaErrorNotSupported;
+    if (e == cudaErrorNotSupported)
+        e = gv ? launch_gv_down(gp, max_tiles, nt, (int)T, s) : launch_small_down(gp, max_tiles, nt, s);
     if (e != cudaSuccess) return cuda_fail(e, "noalloc down launch");
     return RMOE_OK;
 }
