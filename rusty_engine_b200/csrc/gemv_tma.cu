@@ -5,7 +5,8 @@
 // The products, fragment order and decode are those of gemv.cuh (dequantisation in the
 // registers that feed mma.sync); what changes is how the weights arrive.  At decode batch sizes
 // the per-lane cp.async ring of gv_kernel issues a few 8- and 16-byte requests per lane per
-// unit, and the number of requests in flight per SM, not the bytes, caps its HBM rate.  Here
+// unit, and its copy stream, not the decode, caps its HBM rate (with the decode taken out it
+// still reached only ~2.5 TB/s at 64 tokens).  Here
 // one producer warp brings each raw block of the CTA's 128 weight rows (the tensor-core path's
 // weight maps: 128 rows x one Q4_K unit / one Q6_K superblock, plus the Q6_K d plane) into a
 // ring of shared-memory stages with 2-D TMA copies, completion counted on an mbarrier per
