@@ -86,8 +86,10 @@ struct Gv<T_Q4_K> {
     __device__ static void decode(const uint4* q16, const uint2* q8, int, uint16_t, uint32_t (&a)[8][4]) {
         const uint4 q = q16[0];
         const uint2 dm = q8[0];
-        const __half2 Dl = as_h2(__byte_perm(dm.x, 0, 0x1010)), Ml = as_h2(__byte_perm(dm.x, 0, 0x3232));
-        const __half2 Dh = as_h2(__byte_perm(dm.y, 0, 0x1010)), Mh = as_h2(__byte_perm(dm.y, 0, 0x3232));
+        // the scale pairs splatted as half2: half selections the fma takes as operand forms (no
+        // separate byte permutes; one ALU instruction per MMA fewer at 64 tokens)
+        const __half2 Dl = __low2half2(as_h2(dm.x)), Ml = __high2half2(as_h2(dm.x));
+        const __half2 Dh = __low2half2(as_h2(dm.y)), Mh = __high2half2(as_h2(dm.y));
         const __half2 K1024 = __float2half2_rn(1024.0f), S16 = __float2half2_rn(0.0625f),
                       M64 = __float2half2_rn(-64.0f);
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
