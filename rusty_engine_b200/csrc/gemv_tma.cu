@@ -10,10 +10,11 @@
 // one producer warp brings each raw block of the CTA's 128 weight rows (the tensor-core path's
 // weight maps: 128 rows x one Q4_K unit / one Q6_K superblock, plus the Q6_K d plane) into a
 // ring of shared-memory stages with 2-D TMA copies, completion counted on an mbarrier per
-// stage; eight consumer warps (16 rows each) read their fragments from the stage, decode,
-// multiply and release the stage (one arrival per warp) for the producer to refill.
+// stage; the consumer warps (16 rows each: eight for 128-row blocks, four for gate/up's 64-row
+// blocks) read their fragments from the stage, decode, multiply and release the stage (one
+// arrival per warp) for the producer to refill.
 //
-// Items = (tile of <= NT expert-sorted rows, 128-row block of the expert's weights), K whole.
+// Items = (tile of <= NT expert-sorted rows, block of RB weight rows of the expert), K whole.
 // Gate/up runs one item per CTA; down is persistent (two CTAs per SM), each CTA walking a
 // contiguous range of items: the producer streams the raw blocks of one item after another
 // through the same ring, and the consumers stage a tile's token rows once for all of its row
@@ -32,30 +33,33 @@
 namespace rmoe {
 using namespace tc;
 
-static constexpr int GVT_CONS = 8;                       // consumer warps (row groups of 16 rows)
-static constexpr int GVT_THREADS = 32 * (GVT_CONS + 1);  // + the producer warp
-static constexpr int GVT_RB = 16 * GVT_CONS;             // weight rows per CTA (= the maps' box rows)
-static constexpr int GVT_MAXD = 8;                       // ring stages at most
+// CTA = CONS consumer warps (row groups of 16 rows: RB = 16 CONS weight rows, the height of the
+// maps' boxes) + one producer warp.  CONS = 8 (128 rows, two CTAs per SM) everywhere; gate/up
+// with 8-row tiles also has CONS = 4 (64 rows, three CTAs per SM): twice the items, so the last
+// partial wave of a launch is half as long.
+static constexpr int GVT_MAXD = 8;  // ring stages at most
+__host__ __device__ constexpr int gvt_ctas_per_sm(int cons) { return cons == 4 ? 3 : 2; }
 
 __host__ __device__ constexpr bool gvt_persistent(int nmat) { return nmat == 1; }
 
-template <int TYPE, int NMAT>
+template <int TYPE, int NMAT, int RB>
 struct GvtGeom {
     using R = Raw<TYPE>;
-    using RS = RawStage<TYPE, GVT_RB>;
+    using RS = RawStage<TYPE, RB>;
     static constexpr int STAGE = NMAT * RS::BYTES;  // one raw block of every matrix
     static constexpr int UPB = R::RK / GV_UK;       // 128-element units per raw block
     static_assert(R::RK % GV_UK == 0 && RS::BYTES % 128 == 0, "stage geometry");
 };
 
-template <int TYPE, int NT, int NMAT>
-__global__ void __launch_bounds__(GVT_THREADS, 2)
+template <int TYPE, int NT, int NMAT, int CONS>
+__global__ void __launch_bounds__(32 * (CONS + 1), gvt_ctas_per_sm(CONS))
     gvt_kernel(const __grid_constant__ GroupedParams p, const __grid_constant__ TcMaps maps, int depth, int ring_off) {
+    constexpr int RB = 16 * CONS;
     using D = Gv<TYPE>;
-    using G = GvtGeom<TYPE, NMAT>;
+    using G = GvtGeom<TYPE, NMAT, RB>;
     using RS = typename G::RS;
     using R = Raw<TYPE>;
-    constexpr int NTT = NT / 8, UPB = G::UPB, NCT = 32 * GVT_CONS;
+    constexpr int NTT = NT / 8, UPB = G::UPB, NCT = 32 * CONS;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[GVT_MAXD], empty[GVT_MAXD];
     __shared__ int s_tok[NT], s_rexp[NT];
@@ -75,7 +79,7 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
     // across items.  Gate/up: one item per CTA (grid = row blocks x tile slots), which measured
     // faster for its 16-stage items than the persistent walk.
     constexpr bool PERSIST = gvt_persistent(NMAT);
-    const int rows_out = NMAT == 2 ? p.I : p.H, nrb = rows_out / GVT_RB;
+    const int rows_out = NMAT == 2 ? p.I : p.H, nrb = rows_out / RB;
     int it0, it1;
     if (PERSIST) {
         const int n_items = *p.n_tiles * nrb;
@@ -95,7 +99,7 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
     if (tid == 0) {
         for (int i = 0; i < depth; i++) {
             mbar_init(smem_u32(&full[i]), 1);
-            mbar_init(smem_u32(&empty[i]), GVT_CONS);
+            mbar_init(smem_u32(&empty[i]), CONS);
         }
         s_abort = 0;
         s_consumed = total_stages;
@@ -104,7 +108,7 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
     __syncthreads();
 
     int issued = 0;  // producer: stages whose copies were issued
-    if (warp == GVT_CONS) {
+    if (warp == CONS) {
         // ---------------- producer: one raw block of every matrix per stage ----------------
         if (lane == 0) {
             int gj = 0;
@@ -112,7 +116,7 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
                 const int4 ti = p.tiles[item / nrb];
                 const bool sh = ti.x >= p.E;
                 const DevMat& M0 = NMAT == 2 ? (sh ? p.sgate : p.gate) : (sh ? p.sdown : p.down);
-                const int grow0 = (sh ? 0 : ti.x) * (int)M0.rows + (item % nrb) * GVT_RB;
+                const int grow0 = (sh ? 0 : ti.x) * (int)M0.rows + (item % nrb) * RB;
                 for (int j = 0; j < nraw; j++, gj++) {
                     const int s = gj % depth;
                     if (gj >= depth && !mbar_wait(smem_u32(&empty[s]), ((gj / depth) + 1) & 1)) {
@@ -281,7 +285,7 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
             if (s_abort) continue;
 
             // accumulator (m, t, q): weight row 16 rg + g + 8 (q >> 1), token row 8 t + 2 c + (q & 1)
-            const int fb = rblk * GVT_CONS + rg;  // 16-row block of the output features
+            const int fb = rblk * CONS + rg;  // 16-row block of the output features
             const int f = fb * 16 + g;
             if (NMAT == 2) {
                 const int hstride = p.I / GV_EBLK;
@@ -330,7 +334,7 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
     }
     // a CTA that stopped early exits only after the copies it issued have landed
     __syncthreads();
-    if (warp == GVT_CONS && lane == 0 && s_abort)
+    if (warp == CONS && lane == 0 && s_abort)
         for (int j = s_consumed; j < issued; j++)
             if (!mbar_wait(smem_u32(&full[j % depth]), (j / depth) & 1, 100000000ull)) break;
 }
@@ -338,16 +342,20 @@ __global__ void __launch_bounds__(GVT_THREADS, 2)
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-template <int TYPE, int NT, int NMAT>
+template <int TYPE, int NT, int NMAT, int CONS>
 static cudaError_t go_gvt(const GroupedParams& p, const TcMaps& maps, int max_tiles, cudaStream_t s) {
-    using G = GvtGeom<TYPE, NMAT>;
+    constexpr int RB = 16 * CONS;
+    using G = GvtGeom<TYPE, NMAT, RB>;
     const int K = NMAT == 2 ? p.H : p.I, rows = NMAT == 2 ? p.I : p.H;
-    if (rows % GVT_RB || K % Raw<TYPE>::RK) return cudaErrorNotSupported;
+    if (rows % RB || K % Raw<TYPE>::RK) return cudaErrorNotSupported;
     const size_t ring_off = ((size_t)K * NT * 2 + 127) & ~(size_t)127;
-    int depth = (int)std::min<size_t>(GVT_MAXD, (GV_SMEM_TWO - ring_off) / G::STAGE);
+    // shared memory that keeps gvt_ctas_per_sm CTAs on an SM
+    const size_t budget = CONS == 4 ? (size_t)74 * 1024 : (size_t)GV_SMEM_TWO;
+    if (ring_off >= budget) return cudaErrorNotSupported;
+    int depth = (int)std::min<size_t>(GVT_MAXD, (budget - ring_off) / G::STAGE);
     if (depth < 2) return cudaErrorNotSupported;
     const size_t smem = ring_off + (size_t)depth * G::STAGE;
-    auto k = gvt_kernel<TYPE, NT, NMAT>;
+    auto k = gvt_kernel<TYPE, NT, NMAT, CONS>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     // down: persistent, two CTAs per SM (the shared-memory budget), each walking a range of items
@@ -358,31 +366,40 @@ static cudaError_t go_gvt(const GroupedParams& p, const TcMaps& maps, int max_ti
         cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
         if (n_sm <= 0) n_sm = 148;
     }
-    const int items = max_tiles * (rows / GVT_RB);
-    const dim3 grid = gvt_persistent(NMAT) ? dim3(std::min(items, 2 * n_sm)) : dim3(rows / GVT_RB, max_tiles);
-    return launch_pdl(k, grid, dim3(GVT_THREADS), smem, s, p, maps, depth, (int)ring_off);
+    const int items = max_tiles * (rows / RB);
+    const dim3 grid = gvt_persistent(NMAT) ? dim3(std::min(items, 2 * n_sm)) : dim3(rows / RB, max_tiles);
+    return launch_pdl(k, grid, dim3(32 * (CONS + 1)), smem, s, p, maps, depth, (int)ring_off);
 }
 
-template <int NMAT>
+template <int NMAT, int CONS>
 static cudaError_t go_gvt_type(int type, const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt,
                                cudaStream_t s) {
     switch (type) {
-        case T_Q4_K: return nt == 8 ? go_gvt<T_Q4_K, 8, NMAT>(p, maps, max_tiles, s) : go_gvt<T_Q4_K, 16, NMAT>(p, maps, max_tiles, s);
-        case T_Q6_K: return nt == 8 ? go_gvt<T_Q6_K, 8, NMAT>(p, maps, max_tiles, s) : go_gvt<T_Q6_K, 16, NMAT>(p, maps, max_tiles, s);
+        case T_Q4_K:
+            return nt == 8 ? go_gvt<T_Q4_K, 8, NMAT, CONS>(p, maps, max_tiles, s)
+                           : go_gvt<T_Q4_K, 16, NMAT, CONS>(p, maps, max_tiles, s);
+        case T_Q6_K:
+            return nt == 8 ? go_gvt<T_Q6_K, 8, NMAT, CONS>(p, maps, max_tiles, s)
+                           : go_gvt<T_Q6_K, 16, NMAT, CONS>(p, maps, max_tiles, s);
         default: return cudaErrorNotSupported;
     }
 }
 
-cudaError_t launch_gvt_gateup(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s) {
+cudaError_t launch_gvt_gateup(const GroupedParams& p, const TcMaps& maps, const TcMaps* maps64, int max_tiles, int nt,
+                              cudaStream_t s) {
     if (max_tiles <= 0) return cudaSuccess;
     if (nt != 8 && nt != 16) return cudaErrorInvalidValue;
-    return go_gvt_type<2>(p.gate.type, p, maps, max_tiles, nt, s);
+    if (maps64 && nt == 8) {
+        const cudaError_t e = go_gvt_type<2, 4>(p.gate.type, p, *maps64, max_tiles, nt, s);
+        if (e != cudaErrorNotSupported) return e;
+    }
+    return go_gvt_type<2, 8>(p.gate.type, p, maps, max_tiles, nt, s);
 }
 
 cudaError_t launch_gvt_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s) {
     if (max_tiles <= 0) return cudaSuccess;
     if (nt != 8 && nt != 16) return cudaErrorInvalidValue;
-    return go_gvt_type<1>(p.down.type, p, maps, max_tiles, nt, s);
+    return go_gvt_type<1, 8>(p.down.type, p, maps, max_tiles, nt, s);
 }
 
 }  // namespace rmoe

@@ -78,31 +78,31 @@ static bool encode2d(CUtensorMap& m, CUtensorMapDataType dt, const void* base, u
 }
 
 template <int TYPE>
-static bool maps_for(const DevMat& M, WMaps& o) {
+static bool maps_for(const DevMat& M, WMaps& o, uint32_t rows) {
     using R = Raw<TYPE>;
-    // main plane as u16 [trows][main_stride / 2]; box = PITCH bytes x 128 rows (past the row end
-    // the box reads zeros)
+    // main plane as u16 [trows][main_stride / 2]; box = PITCH bytes x `rows` rows (past the row
+    // end the box reads zeros)
     bool ok = encode2d(o.main, CU_TENSOR_MAP_DATA_TYPE_UINT16, M.main, M.main_stride / 2, M.trows, M.main_stride,
-                       R::PITCH / 2, TC_M, CU_TENSOR_MAP_SWIZZLE_NONE);
+                       R::PITCH / 2, rows, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (R::DBLK)
-        ok = ok && encode2d(o.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, M.dpl, M.trows, M.dstride, M.trows * 2, TC_M, R::DBLK,
+        ok = ok && encode2d(o.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, M.dpl, M.trows, M.dstride, M.trows * 2, rows, R::DBLK,
                             CU_TENSOR_MAP_SWIZZLE_NONE);
     if (R::AUX)
-        ok = ok && encode2d(o.aux, CU_TENSOR_MAP_DATA_TYPE_UINT32, M.aux, M.trows, M.dstride, M.trows * 4, TC_M, R::AUX,
+        ok = ok && encode2d(o.aux, CU_TENSOR_MAP_DATA_TYPE_UINT32, M.aux, M.trows, M.dstride, M.trows * 4, rows, R::AUX,
                             CU_TENSOR_MAP_SWIZZLE_NONE);
     return ok;
 }
 
-bool make_weight_maps(const DevMat& M, WMaps& out) {
+bool make_weight_maps(const DevMat& M, WMaps& out, uint32_t rows) {
     memset(&out, 0, sizeof out);
     switch (M.type) {
-        case T_Q4_K: return maps_for<T_Q4_K>(M, out);
-        case T_Q5_K: return maps_for<T_Q5_K>(M, out);
-        case T_Q6_K: return maps_for<T_Q6_K>(M, out);
-        case T_Q4_0: return maps_for<T_Q4_0>(M, out);
-        case T_Q5_0: return maps_for<T_Q5_0>(M, out);
-        case T_Q8_0: return maps_for<T_Q8_0>(M, out);
-        case T_DENSE: return maps_for<T_DENSE>(M, out);
+        case T_Q4_K: return maps_for<T_Q4_K>(M, out, rows);
+        case T_Q5_K: return maps_for<T_Q5_K>(M, out, rows);
+        case T_Q6_K: return maps_for<T_Q6_K>(M, out, rows);
+        case T_Q4_0: return maps_for<T_Q4_0>(M, out, rows);
+        case T_Q5_0: return maps_for<T_Q5_0>(M, out, rows);
+        case T_Q8_0: return maps_for<T_Q8_0>(M, out, rows);
+        case T_DENSE: return maps_for<T_DENSE>(M, out, rows);
         default: return false;
     }
 }

@@ -158,11 +158,16 @@ struct alignas(64) TcMaps {
 // Decode batches of at least GVT_MIN_T tokens use them (a single token fills the GPU only with
 // the K-split CTAs of gv_kernel).
 static constexpr uint32_t GVT_MIN_T = 2;
-cudaError_t launch_gvt_gateup(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s);
+// ... and gate/up runs 64-row blocks (maps64) for batches of at most GVT64_MAX_T tokens
+static constexpr uint32_t GVT64_MAX_T = 16;
+// maps64: the same stacks with 64-row boxes (null: none); 8-row tiles of gate/up then run
+// 64-row blocks, three CTAs per SM (finer items, so the last wave is shorter)
+cudaError_t launch_gvt_gateup(const GroupedParams& p, const TcMaps& maps, const TcMaps* maps64, int max_tiles, int nt,
+                              cudaStream_t s);
 cudaError_t launch_gvt_down(const GroupedParams& p, const TcMaps& maps, int max_tiles, int nt, cudaStream_t s);
 
 // Build the maps of one stack (after upload_mat) / of the h workspace; false on a driver error.
-bool make_weight_maps(const DevMat& M, WMaps& out);
+bool make_weight_maps(const DevMat& M, WMaps& out, uint32_t rows = 128);  // rows: box height
 bool make_rows_map(const __half* base, uint64_t rows, uint32_t width, CUtensorMap& out);
 // fp32 [rows, width] row-major, 128-B-swizzled boxes of box_w (32) x box_rows
 bool make_f32_rows_map(const float* base, uint64_t rows, uint32_t width, uint32_t box_w, uint32_t box_rows,

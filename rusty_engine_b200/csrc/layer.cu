@@ -380,6 +380,9 @@ rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_
         maps_ok = maps_ok && make_weight_maps(L->swg, L->smg) && make_weight_maps(L->swu, L->smu) &&
                   make_weight_maps(L->swd, L->smd);
     if (!maps_ok) return fail(RMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed for an expert stack");
+    // 64-row boxes of gate/up for the decode kernels' finer row blocks
+    L->maps64 = make_weight_maps(L->wg, L->mg64, 64) && make_weight_maps(L->wu, L->mu64, 64) &&
+                (!d->has_shared || (make_weight_maps(L->swg, L->smg64, 64) && make_weight_maps(L->swu, L->smu64, 64)));
     void* rw = L->own.alloc((size_t)d->n_experts * H * 4);
     if (!rw) return fail(RMOE_ERR_OOM, "router cudaMalloc failed");
     cudaError_t e = cudaMemcpy(rw, d->router_w, (size_t)d->n_experts * H * 4, cudaMemcpyHostToDevice);
@@ -574,8 +577,19 @@ rmoe_status layer_forward_device(rmoe_layer* L, const float* x, uint32_t T, floa
         gmaps.w[1][0] = L->smg;
         gmaps.w[1][1] = L->smu;
     }
+    TcMaps gmaps64;
+    if (gvt && L->maps64) {
+        memset(&gmaps64, 0, sizeof gmaps64);
+        gmaps64.w[0][0] = L->mg64;
+        gmaps64.w[0][1] = L->mu64;
+        gmaps64.w[1][0] = L->smg64;
+        gmaps64.w[1][1] = L->smu64;
+    }
     e = use_tc ? launch_tc_gateup(gp, maps, max_tiles, s) : cudaErrorNotSupported;
-    if (!use_tc && gvt) e = launch_gvt_gateup(gp, gmaps, max_tiles, tile_rows, s);
+    // 64-row gate/up blocks for batches of up to GVT64_MAX_T tokens (few tiles: the finer items
+    // shorten the last wave); larger batches keep the 128-row blocks, which measured faster there
+    const bool use64 = L->maps64 && T <= GVT64_MAX_T;
+    if (!use_tc && gvt) e = launch_gvt_gateup(gp, gmaps, use64 ? &gmaps64 : nullptr, max_tiles, tile_rows, s);
     if (!use_tc && e == cudaErrorNotSupported)
         e = gv ? launch_gv_gateup(gp, max_tiles, tile_rows, (int)T, s) : launch_small_gateup(gp, max_tiles, tile_rows, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate/up launch");

@@ -68,6 +68,8 @@ struct rmoe_layer {
     rmoe::EpState* ep = nullptr;  // expert-parallel state (null for a whole layer)
     rmoe::DevMat wg{}, wu{}, wd{}, swg{}, swu{}, swd{};
     rmoe::WMaps mg{}, mu{}, md{}, smg{}, smu{}, smd{};  // TMA maps of the stacks above
+    rmoe::WMaps mg64{}, mu64{}, smg64{}, smu64{};       // gate/up with 64-row boxes (decode kernels)
+    bool maps64 = false;
     CUtensorMap hmap{}, xsmap{};                          // TMA maps of the workspace h and xs
     float* router_w = nullptr;
     float* router_wh = nullptr;  // router_w split for the tensor-core logits (hi | lo, [E, H] each)

@@ -148,7 +148,11 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     TcMaps gmaps;
     memset(&gmaps, 0, sizeof gmaps);
     gmaps.w[0][0] = L->mg; gmaps.w[0][1] = L->mu; gmaps.w[1][0] = L->smg; gmaps.w[1][1] = L->smu;
-    e = gvt ? launch_gvt_gateup(gp, gmaps, max_tiles, nt, s) : cudaErrorNotSupported;
+    TcMaps gmaps64;
+    memset(&gmaps64, 0, sizeof gmaps64);
+    gmaps64.w[0][0] = L->mg64; gmaps64.w[0][1] = L->mu64; gmaps64.w[1][0] = L->smg64; gmaps64.w[1][1] = L->smu64;
+    e = gvt ? launch_gvt_gateup(gp, gmaps, (L->maps64 && T <= GVT64_MAX_T) ? &gmaps64 : nullptr, max_tiles, nt, s)
+            : cudaErrorNotSupported;
     if (e == cudaErrorNotSupported)
         e = gv ? launch_gv_gateup(gp, max_tiles, nt, (int)T, s) : launch_small_gateup(gp, max_tiles, nt, s);
     if (e != cudaSuccess) return cuda_fail(e, "noalloc gate/up launch");
