@@ -13,8 +13,9 @@ N = 1 (no torchrun): the headline is config 2 (4096-token prefill); the same lin
 ``sub`` results for config 3 (decode batches 1, 8, 32, 64) and config 5 (the 235B-shaped layer,
 8192 tokens, Zipf(1.1) expert load), each with its roofline fraction.
 N > 1 (torchrun, one rank per GPU): config 5 as an expert-parallel layer, strong scaling: the
-8192 tokens are split evenly over the ranks (8192 / N each), experts dealt round-robin, tokens
-exchanged with NCCL; value = 8192 / (max over ranks of the step time).
+8192 tokens are split evenly over the ranks (8192 / N each), experts placed by the pick counts
+of a separate calibration batch (largest load first to the least-loaded rank), tokens exchanged
+with NCCL; value = 8192 / (max over ranks of the step time).
 
 ``--impl reference`` times the CPU restatement of rusty-engine's pooled path (oracle/, all host
 threads) on the same config: the whole 4096-token batch per step for config 2.
@@ -163,6 +164,20 @@ def workload(cfg_name):
     else:
         x = synth.activations(T, lw.H, seed=1)
     return lw, x, label
+
+
+def ep_placement(lw, world, T_cal=2048):
+    """Expert placement for the expert-parallel step: the per-expert pick counts of a separate
+    calibration batch of the config's distribution (another seed; routed on the host in
+    float64), spread over the ranks largest-first (ep_balanced_placement).  The same on every
+    rank, with no exchange."""
+    from rusty_engine_b200 import synth
+    from rusty_engine_b200.moe import ep_balanced_placement
+
+    x = synth.activations(T_cal, lw.H, seed=7) + np.float32(1.0)  # zipf_workload's activations
+    logits = x.astype(np.float64) @ np.asarray(lw.router_w, dtype=np.float64).reshape(lw.E, lw.H).T
+    ids = np.argpartition(-logits, lw.k - 1, axis=1)[:, :lw.k]
+    return ep_balanced_placement(np.bincount(ids.ravel(), minlength=lw.E), world)
 
 
 def cpu_baseline(cfg_name, lw, x, budget_s=15.0):
@@ -479,7 +494,8 @@ def main():
 
         box = [ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
-        layer = MoELayer.expert_parallel(lw, rank, world, box[0], device=local)
+        placement = ep_placement(lw, world)
+        layer = MoELayer.expert_parallel(lw, rank, world, box[0], device=local, placement=placement)
     else:
         T_all = x_all.shape[0]
         x_np = x_all
@@ -533,6 +549,8 @@ def main():
                        "experts_touched": int(touched),
                        "l2": "flushed between steps (256 MiB write outside the events)",
                        "parallelism": f"ep{world}" if world > 1 else "single"},
+            **({"placement": "experts placed by the pick counts of a 2048-token calibration batch "
+                             "(another seed), largest load first to the least-loaded rank"} if world > 1 else {}),
             "roofline": roof,
             "e2e": {"value": T_all / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": T * lwr.H * 4,
                     "d2h_bytes_per_step": T * lwr.H * 4},

@@ -240,6 +240,18 @@ RMOE_API rmoe_status rmoe_ep_unique_id(uint8_t id[128]);
 RMOE_API rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* desc, int32_t rank, int32_t world_size,
                                  const uint8_t id[128], rmoe_layer** out);
 
+/* rmoe_ep_layer_create with the caller's expert placement: expert_rank[e] (n_experts entries,
+ * the same table on every rank) is the rank that holds expert e; every rank must hold at least
+ * one expert, and the experts need not split evenly.  A rank numbers its experts in ascending
+ * global order.  Placing by measured expert loads (e.g. the per-expert pick counts of a
+ * calibration batch, spread by a greedy largest-first fill) keeps the busiest rank near the
+ * mean under skewed routing, where the round-robin deal can leave one rank with 1.5x the mean
+ * at 8 ranks.  expert_rank == NULL is the round-robin deal.  No counterpart in the reference
+ * (its MoE layer runs in one process). */
+RMOE_API rmoe_status rmoe_ep_layer_create_placed(const rmoe_layer_desc* desc, int32_t rank, int32_t world_size,
+                                                 const uint8_t id[128], const int32_t* expert_rank,
+                                                 rmoe_layer** out);
+
 /* ---- GGUF expert binding (MmapModel::open / tensor_bytes, src/loader.rs:33-102; the MoE
  *      tensors of a block, src/model.rs:366-391) ---------------------------------------------- */
 

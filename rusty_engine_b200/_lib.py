@@ -52,7 +52,7 @@ class LayerDesc(C.Structure):
 EXPORTS = [
     "rmoe_layer_create", "rmoe_layer_forward", "rmoe_layer_routing", "rmoe_layer_logits", "rmoe_layer_destroy",
     "rmoe_last_error", "rmoe_dequant", "rmoe_qmat_matmul", "rmoe_route", "rmoe_ep_unique_id",
-    "rmoe_ep_layer_create", "rmoe_build_info", "rmoe_layer_stage_ms", "rmoe_layer_forward_noalloc",
+    "rmoe_ep_layer_create", "rmoe_ep_layer_create_placed", "rmoe_build_info", "rmoe_layer_stage_ms", "rmoe_layer_forward_noalloc",
     "rmoe_route_grouped", "rmoe_qmat_create", "rmoe_qmat_forward", "rmoe_qmat_status", "rmoe_qmat_destroy",
     "rmoe_gguf_open", "rmoe_gguf_close", "rmoe_gguf_tensor", "rmoe_gguf_meta_uint", "rmoe_gguf_moe_layer_desc",
     "rmoe_layer_router_refined", "rmoe_noalloc_status", "rmoe_selftest_bounded_wait",
@@ -97,6 +97,7 @@ def load():
         L.rmoe_route_grouped.argtypes = [vp, vp, u32, u32, u32, u32, u32, i32, i32, vp, vp, vp]
         L.rmoe_ep_unique_id.argtypes = [vp]
         L.rmoe_ep_layer_create.argtypes = [C.POINTER(LayerDesc), i32, i32, vp, C.POINTER(vp)]
+        L.rmoe_ep_layer_create_placed.argtypes = [C.POINTER(LayerDesc), i32, i32, vp, vp, C.POINTER(vp)]
         L.rmoe_build_info.restype = C.c_char_p
         L.rmoe_gguf_open.argtypes = [C.c_char_p, C.POINTER(vp)]
         L.rmoe_gguf_close.argtypes = [vp]

@@ -1,17 +1,21 @@
 // ep.cu -- expert-parallel layers: the experts split over G ranks (one GPU each), NCCL
 // send/recv exchanges between them.
 //
-// Rank r holds experts r, r + G, r + 2G, ... (dealt round-robin, so the most popular experts
-// of a skewed load land on different ranks; local id = e / G) and the whole router.  A forward
-// on rank r takes r's own T tokens:
+// Each rank holds a subset of the experts and the whole router.  The placement is either the
+// caller's (expert_rank[e] = the rank holding e, e.g. balanced by measured expert loads) or
+// round-robin (rank r holds experts r, r + G, r + 2G, ..., so the most popular experts of a
+// skewed load land on different ranks); a rank's local ids number its experts in ascending
+// global order.  A forward on rank r takes r's own T tokens:
 //   1. router logits + top-k over all E experts (the same kernels as a whole layer);
 //   2. plan: for every destination rank d, which tokens have at least one pick on d (each such
 //      token is sent to d once, however many of its picks d holds) and their order (token
 //      order, by a per-destination scan);
 //   3. counts exchange (one int per peer) and one device-to-host read of the counts, which
-//      size the payload calls;
+//      size the payload calls (the pack of step 4 is queued behind that read and runs while the
+//      host waits);
 //   4. pack + exchange: a row per (token, destination): the token's fp16 activations followed
-//      by its k picks as seen by d (d's local expert id e / G, or the empty id E/G, and the weight);
+//      by its k picks as seen by d (d's local expert id, or the empty id = d's expert count, and
+//      the weight);
 //   5. d runs its local experts over the rows it received with the given routing (the grouped
 //      tensor-core or small-batch kernels), producing per received row the weighted sum of its
 //      local picks' outputs (f32);
@@ -52,6 +56,7 @@ struct EpState {
     unsigned* status = nullptr;
     unsigned* ticket = nullptr;  // router last-CTA counters (0 between launches)
     int* h_cnt = nullptr;    // pinned copy of cnt
+    int* map = nullptr;      // device [E rank of e][E local id of e][G experts on rank d]
     Owned send_own, recv_own;
     uint64_t cap_send = 0, cap_recv = 0;  // rows
     uint8_t* sendbuf = nullptr;
@@ -69,10 +74,14 @@ struct EpState {
 
 static inline uint32_t row_bytes(uint32_t H, uint32_t k) { return (H * 2 + k * 8 + 15) & ~15u; }
 
+// Largest worst-case send buffer (tokens x ranks rows) that is allocated so that the pack can
+// be queued before the host has read the counts.
+static constexpr uint64_t PACK_EARLY_BYTES = 1ull << 30;
+
 // 2. one CTA per destination: flags and the exclusive scan over tokens (every token goes to
 // rank `self_all` itself when that is >= 0: the shared expert runs there)
-__global__ void __launch_bounds__(1024) ep_plan_kernel(const int* topk_id, int T, int k, int E_local, int G, int* pos,
-                                                       int* cnt, int self_all) {
+__global__ void __launch_bounds__(1024) ep_plan_kernel(const int* topk_id, int T, int k, const int* rank_of, int G,
+                                                       int* pos, int* cnt, int self_all) {
     __shared__ int warp_sum[32];
     __shared__ int carry_s;
     const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -82,7 +91,7 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int* topk_id, int T
         const int t = t0 + tid;
         int f = 0;
         if (t < T) {
-            for (int j = 0; j < k; j++) f |= (topk_id[(size_t)t * k + j] % G) == d;
+            for (int j = 0; j < k; j++) f |= rank_of[topk_id[(size_t)t * k + j]] == d;
             if (d == self_all) f = 1;
         }
         int inc = f;
@@ -114,8 +123,8 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int* topk_id, int T
 
 // 4. one warp per (token, destination): the row for d
 __global__ void __launch_bounds__(256) ep_pack_kernel(const __half* xb, const int* topk_id, const float* topk_w,
-                                                      const int* pos, const int* cnt, int T, int H, int k, int E_local,
-                                                      int G, uint32_t rb, uint8_t* sendbuf) {
+                                                      const int* pos, const int* cnt, int T, int H, int k,
+                                                      const int* map, int E, int G, uint32_t rb, uint8_t* sendbuf) {
     const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (wid >= T * G) return;
     const int t = wid / G, d = wid - t * G;
@@ -129,8 +138,8 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __half* xb, const in
     for (int u = lane; u < H / 8; u += 32) dst[u] = src[u];
     if (lane < k) {
         const int id = topk_id[(size_t)t * k + lane];
-        const bool mine = id % G == d;
-        reinterpret_cast<int*>(row + (size_t)H * 2)[lane] = mine ? id / G : E_local;
+        const bool mine = map[id] == d;
+        reinterpret_cast<int*>(row + (size_t)H * 2)[lane] = mine ? map[E + id] : map[2 * E + d];
         reinterpret_cast<float*>(row + (size_t)H * 2 + k * 4)[lane] = mine ? topk_w[(size_t)t * k + lane] : 0.0f;
     }
 }
@@ -192,6 +201,9 @@ static rmoe_status ep_abort(EpState& P, rmoe_status st) {
 
 static rmoe_status ep_poll(EpState& P, const char* what) {
     const auto t0 = std::chrono::steady_clock::now();
+    // The count read of every forward waits here for tens of microseconds: the first 2 ms of a
+    // wait poll back to back (a 50-us sleep would add its whole length to each forward), later
+    // polls sleep between queries.
     for (;;) {
         cudaError_t q = P.ev ? cudaEventQuery(P.ev) : cudaSuccess;
         ncclResult_t a = ncclSuccess;
@@ -203,7 +215,8 @@ static rmoe_status ep_poll(EpState& P, const char* what) {
         if (ms > P.timeout_ms)
             return ep_abort(P, fail(RMOE_ERR_NCCL, "%s: no progress for %d ms (a peer rank stopped?); the communicator "
                                                    "was aborted", what, P.timeout_ms));
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (ms < 2) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
@@ -270,7 +283,7 @@ static rmoe_status grow(Owned& own, uint64_t rows, uint64_t& cap, uint32_t rb, u
 
 rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cudaStream_t s, uint32_t flags) {
     EpState& P = *L->ep;
-    const int G = P.world, H = (int)L->H, k = (int)L->k, El = (int)L->E;
+    const int G = P.world, H = (int)L->H, k = (int)L->k;
     const uint32_t rb = row_bytes(L->H, L->k);
     if (!P.comm) return fail(RMOE_ERR_NCCL, "expert-parallel layer: the communicator was aborted by an earlier failure");
     rmoe_status st = ep_token_buffers(L, T ? T : 1);
@@ -286,7 +299,7 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     rp.router_wmax = L->router_wmax; rp.refined = P.status + 1;
     if (T && (e = launch_router_topk(rp, s)) != cudaSuccess) return cuda_fail(e, "ep router launch");
     // 2. plan
-    ep_plan_kernel<<<G, 1024, 0, s>>>(P.topk_id, (int)T, k, El, G, P.pos, P.cnt, L->has_shared ? P.rank : -1);
+    ep_plan_kernel<<<G, 1024, 0, s>>>(P.topk_id, (int)T, k, P.map, G, P.pos, P.cnt, L->has_shared ? P.rank : -1);
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "ep plan launch");
     // 3. counts
     ncclResult_t r = ncclGroupStart();
@@ -299,7 +312,22 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     if ((st = ep_enqueued(P, r2, "ep counts exchange"))) return st;
     if ((e = cudaMemcpyAsync(P.h_cnt, P.cnt, 2 * G * 4, cudaMemcpyDeviceToHost, s)) != cudaSuccess)
         return cuda_fail(e, "ep counts");
-    if ((st = ep_sync(P, s, "ep counts"))) return st;
+    if ((e = cudaEventRecord(P.ev, s)) != cudaSuccess) return cuda_fail(e, "ep counts");
+    // 4a. pack: it needs only the device-side counts, so with a send buffer sized for the worst
+    // case (every token sent to every rank; up to PACK_EARLY_BYTES) it is queued behind the
+    // count read and runs while the host waits for the counts
+    const bool early = T && (uint64_t)T * G * rb <= PACK_EARLY_BYTES;
+    auto pack = [&]() -> rmoe_status {
+        ep_pack_kernel<<<(T * G + 7) / 8, 256, 0, s>>>(P.xb, P.topk_id, P.topk_w, P.pos, P.cnt, (int)T, H, k, P.map,
+                                                       (int)L->E_router, G, rb, P.sendbuf);
+        cudaError_t le = cudaGetLastError();
+        return le == cudaSuccess ? RMOE_OK : cuda_fail(le, "ep pack launch");
+    };
+    if (early) {
+        if ((st = grow(P.send_own, (uint64_t)T * G, P.cap_send, rb, L->H, &P.sendbuf, &P.ret))) return st;
+        if ((st = pack())) return st;
+    }
+    if ((st = ep_poll(P, "ep counts"))) return st;
     std::vector<uint64_t> soff(G + 1, 0), roff(G + 1, 0);
     for (int q = 0; q < G; q++) {
         soff[q + 1] = soff[q] + (uint64_t)P.h_cnt[q];
@@ -308,12 +336,8 @@ rmoe_status ep_forward(rmoe_layer* L, const float* x, uint32_t T, float* out, cu
     const uint64_t S = soff[G], R = roff[G];
     if ((st = grow(P.send_own, S, P.cap_send, rb, L->H, &P.sendbuf, &P.ret))) return st;
     if ((st = grow(P.recv_own, R, P.cap_recv, rb, L->H, &P.recvbuf, &P.part))) return st;
-    // 4. pack + exchange
-    if (T) {
-        ep_pack_kernel<<<(T * G + 7) / 8, 256, 0, s>>>(P.xb, P.topk_id, P.topk_w, P.pos, P.cnt, (int)T, H, k, El, G, rb,
-                                                       P.sendbuf);
-        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "ep pack launch");
-    }
+    // 4b. pack (when not queued early) + exchange
+    if (T && !early && (st = pack())) return st;
     r = ncclGroupStart();
     for (int q = 0; q < G && r == ncclSuccess; q++) {
         if (P.h_cnt[q]) r = ncclSend(P.sendbuf + soff[q] * rb, (size_t)P.h_cnt[q] * rb, ncclUint8, q, P.comm, s);
@@ -395,6 +419,13 @@ rmoe_status rmoe_ep_unique_id(uint8_t id[128]) {
 
 rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* d, int32_t rank, int32_t world_size, const uint8_t id[128],
                                  rmoe_layer** out) {
+    if (d && world_size >= 1 && d->n_experts % (uint32_t)world_size)
+        return fail(RMOE_ERR_INVALID, "%u experts do not split evenly over %d ranks", d->n_experts, world_size);
+    return rmoe_ep_layer_create_placed(d, rank, world_size, id, nullptr, out);
+}
+
+rmoe_status rmoe_ep_layer_create_placed(const rmoe_layer_desc* d, int32_t rank, int32_t world_size,
+                                        const uint8_t id[128], const int32_t* expert_rank, rmoe_layer** out) {
     if (!out) return fail(RMOE_ERR_INVALID, "null output handle pointer");
     *out = nullptr;
     rmoe_status s = validate_desc(d);
@@ -402,8 +433,20 @@ rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* d, int32_t rank, int32_t
     if (!id) return fail(RMOE_ERR_INVALID, "null NCCL unique id");
     if (world_size < 1 || world_size > 16 || rank < 0 || rank >= world_size)
         return fail(RMOE_ERR_INVALID, "rank %d / world size %d (1..16 ranks)", rank, world_size);
-    if (d->n_experts % (uint32_t)world_size)
-        return fail(RMOE_ERR_INVALID, "%u experts do not split evenly over %d ranks", d->n_experts, world_size);
+    // the placement table: rank of each expert, its local id there, the expert count per rank
+    const uint32_t E = d->n_experts, G = (uint32_t)world_size;
+    std::vector<int> map(2 * E + G, 0);
+    std::vector<uint32_t> mine;
+    for (uint32_t e = 0; e < E; e++) {
+        const int32_t r = expert_rank ? expert_rank[e] : (int32_t)(e % G);
+        if (r < 0 || r >= world_size)
+            return fail(RMOE_ERR_INVALID, "expert_rank[%u] = %d is not a rank of %d", e, r, world_size);
+        map[e] = r;
+        map[E + e] = map[2 * E + r]++;
+        if (r == rank) mine.push_back(e);
+    }
+    for (uint32_t r = 0; r < G; r++)
+        if (!map[2 * E + r]) return fail(RMOE_ERR_INVALID, "rank %u holds no expert (every rank needs at least one)", r);
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(RMOE_ERR_CUDA, "no CUDA device");
     if (d->device < 0 || d->device >= ndev) return fail(RMOE_ERR_INVALID, "device %d out of range", d->device);
@@ -412,13 +455,17 @@ rmoe_status rmoe_ep_layer_create(const rmoe_layer_desc* d, int32_t rank, int32_t
     L->device = d->device;
     L->H = d->hidden; L->I = d->inter;
     L->E_router = d->n_experts;
-    L->E = L->E_local = d->n_experts / (uint32_t)world_size;
-    L->e_begin = (uint32_t)rank;
+    L->E = L->E_local = (uint32_t)mine.size();
     L->k = d->top_k < d->n_experts ? d->top_k : d->n_experts;
     L->gate_kind = d->gate;
     L->has_shared = d->has_shared ? 1 : 0;  // the shared expert is replicated on every rank
-    if ((s = layer_upload(d, L->e_begin, L->E, L, (uint32_t)world_size))) { delete L; return s; }
+    if ((s = layer_upload(d, mine.data(), L->E, L))) { delete L; return s; }
+    int* dmap = static_cast<int*>(L->own.alloc(map.size() * sizeof(int)));
+    if (!dmap) { delete L; return fail(RMOE_ERR_OOM, "expert placement table"); }
+    cudaError_t me = cudaMemcpy(dmap, map.data(), map.size() * sizeof(int), cudaMemcpyHostToDevice);
+    if (me != cudaSuccess) { delete L; return cuda_fail(me, "expert placement table"); }
     L->ep = new EpState();
+    L->ep->map = dmap;
     L->ep->rank = rank;
     L->ep->world = world_size;
     if (cudaMallocHost(&L->ep->h_cnt, 2 * world_size * sizeof(int)) != cudaSuccess) {

@@ -334,15 +334,14 @@ rmoe_status validate_desc(const rmoe_layer_desc* d) {
 }
 
 
-rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_count, rmoe_layer* L,
-                         uint32_t e_stride) {
+rmoe_status layer_upload(const rmoe_layer_desc* d, const uint32_t* ids, uint32_t e_count, rmoe_layer* L) {
     const uint32_t H = d->hidden, I = d->inter;
     if (canon_type(d->gate_exps.ggml_type) != canon_type(d->up_exps.ggml_type))
         return fail(RMOE_ERR_UNSUPPORTED, "gate (%s) and up (%s) expert types differ", type_name(d->gate_exps.ggml_type),
                     type_name(d->up_exps.ggml_type));
     uint32_t el, by;
     rmoe_status s;
-    // experts e_begin + j * e_stride, j < e_count (gathered on the host when strided)
+    // experts ids[j], j < e_count (gathered on the host), or 0 .. e_count - 1 when ids is null
     std::vector<uint8_t> gathered;
     auto slice = [&](const rmoe_tensor& t, uint32_t rows, uint32_t K) {
         rmoe_tensor u = t;
@@ -350,12 +349,11 @@ rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_
         uint64_t per = (uint64_t)rows * (K / el) * by;
         if (t.nbytes == per * d->n_experts && t.data) {
             const uint8_t* src = static_cast<const uint8_t*>(t.data);
-            if (e_stride == 1) {
-                u.data = src + per * e_begin;
+            if (!ids) {
+                u.data = src;
             } else {
                 gathered.resize(per * e_count);
-                for (uint32_t j = 0; j < e_count; j++)
-                    memcpy(gathered.data() + per * j, src + per * (e_begin + (uint64_t)j * e_stride), per);
+                for (uint32_t j = 0; j < e_count; j++) memcpy(gathered.data() + per * j, src + per * ids[j], per);
                 u.data = gathered.data();
             }
             u.nbytes = per * e_count;
@@ -653,7 +651,7 @@ rmoe_status rmoe_layer_create(const rmoe_layer_desc* d, rmoe_layer** out) {
     L->has_shared = d->has_shared ? 1 : 0;
     L->E_local = L->E;
     L->E_router = L->E;
-    if ((s = layer_upload(d, 0, d->n_experts, L, 1))) { delete L; return s; }
+    if ((s = layer_upload(d, nullptr, d->n_experts, L))) { delete L; return s; }
     *out = L;
     return RMOE_OK;
 }

@@ -64,7 +64,6 @@ struct rmoe_layer {
     int has_shared = 0;
     uint32_t E_local = 0;
     uint32_t E_router = 0;      // experts the router scores (E, or all experts of an EP layer)
-    uint32_t e_begin = 0;       // first global expert id held here (EP: experts e_begin + j * ranks)
     rmoe::EpState* ep = nullptr;  // expert-parallel state (null for a whole layer)
     rmoe::DevMat wg{}, wu{}, wd{}, swg{}, swu{}, swd{};
     rmoe::WMaps mg{}, mu{}, md{}, smg{}, smu{}, smd{};  // TMA maps of the stacks above
@@ -99,8 +98,7 @@ bool block_geom(uint32_t t, uint32_t& el, uint32_t& by);
 rmoe_status upload_mat(const rmoe_tensor& t, uint32_t rows, uint32_t K, uint32_t experts, const char* name, Owned& own,
                        DevMat& out);
 rmoe_status validate_desc(const rmoe_layer_desc* d);
-rmoe_status layer_upload(const rmoe_layer_desc* d, uint32_t e_begin, uint32_t e_count, rmoe_layer* L,
-                         uint32_t e_stride);
+rmoe_status layer_upload(const rmoe_layer_desc* d, const uint32_t* ids, uint32_t e_count, rmoe_layer* L);
 rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y);
 // given: the workspace's xb / topk_id / topk_w already hold T rows' routing (x unused; ids >= E
 // are empty picks) -- the expert-parallel local step

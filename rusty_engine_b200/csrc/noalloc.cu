@@ -96,7 +96,7 @@ rmoe_status rmoe_layer_forward_noalloc(rmoe_layer* L, const float* x, uint32_t T
     if (!x || !out) return fail(RMOE_ERR_INVALID, "null x / out");
     if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
         return fail(RMOE_ERR_INVALID, "device x / out must be 16-byte aligned");
-    if (L->E_local != L->E) return fail(RMOE_ERR_UNSUPPORTED, "noalloc forward: expert-parallel layers are not supported");
+    if (L->ep) return fail(RMOE_ERR_UNSUPPORTED, "noalloc forward: expert-parallel layers are not supported");
     const uint64_t rows = (uint64_t)T * L->k + (L->has_shared ? T : 0);
     const bool gv = gv_supported(L->wg.type, L->wd.type);
     const int nt = gv ? gv_tile_rows((int)T) : small_tile_rows((int)T);

@@ -277,15 +277,39 @@ def ep_unique_id() -> bytes:
     return bytes(buf)
 
 
+def ep_balanced_placement(load: Sequence[float], world: int) -> np.ndarray:
+    """An expert placement for rmoe_ep_layer_create_placed from per-expert loads (e.g. the pick
+    counts of a calibration batch, summed over the ranks): largest load first, each expert to
+    the rank with the least load so far (then the fewest experts, then the lowest rank), so
+    every rank gets at least one expert when there are at least `world` experts.  Returns
+    placement[e] = rank."""
+    load = np.asarray(load, dtype=np.float64)
+    E = load.shape[0]
+    if world < 1 or E < world:
+        raise EngineError(f"{E} experts cannot be placed on {world} ranks (each rank needs one)")
+    acc = np.zeros(world)
+    n = np.zeros(world, dtype=np.int64)
+    out = np.empty(E, dtype=np.int32)
+    for e in sorted(range(E), key=lambda i: (-load[i], i)):
+        r = min(range(world), key=lambda q: (acc[q], n[q], q))
+        out[e] = r
+        acc[r] += load[e]
+        n[r] += 1
+    return out
+
+
 class MoELayer:
     """A resident MoE layer on one GPU (rmoe_layer_create / rmoe_layer_forward)."""
 
     @classmethod
-    def expert_parallel(cls, lw: LayerWeights, rank: int, world: int, uid: bytes, device: Optional[int] = None):
-        """This rank's shard of an expert-parallel layer (rmoe_ep_layer_create): experts
-        [rank E/world, (rank + 1) E/world) on `device`; every rank calls it with the same uid.
-        forward() then takes this rank's tokens and returns their full layer outputs."""
-        return cls(lw, device, _ep=(rank, world, uid))
+    def expert_parallel(cls, lw: LayerWeights, rank: int, world: int, uid: bytes, device: Optional[int] = None,
+                        placement=None):
+        """This rank's shard of an expert-parallel layer on `device`; every rank calls it with
+        the same uid (and the same placement).  placement[e] is the rank holding expert e
+        (rmoe_ep_layer_create_placed, e.g. from ep_balanced_placement); None deals the experts
+        round-robin (rmoe_ep_layer_create: rank r holds r, r + world, ...).  forward() then
+        takes this rank's tokens and returns their full layer outputs."""
+        return cls(lw, device, _ep=(rank, world, uid, placement))
 
     def __init__(self, lw: LayerWeights, device: Optional[int] = None, *, _ep=None):
         _require_cuda()
@@ -307,9 +331,15 @@ class MoELayer:
         if _ep is None:
             _call(L.rmoe_layer_create(C.byref(d), C.byref(h)))
         else:
-            rank, world, uid = _ep
+            rank, world, uid, placement = _ep
             idbuf = (C.c_uint8 * 128).from_buffer_copy(bytes(uid))
-            _call(L.rmoe_ep_layer_create(C.byref(d), rank, world, idbuf, C.byref(h)))
+            if placement is None:
+                _call(L.rmoe_ep_layer_create(C.byref(d), rank, world, idbuf, C.byref(h)))
+            else:
+                pl = np.ascontiguousarray(placement, dtype=np.int32)
+                if pl.shape != (lw.E,):
+                    raise EngineError(f"placement has {pl.size} entries for {lw.E} experts")
+                _call(L.rmoe_ep_layer_create_placed(C.byref(d), rank, world, idbuf, pl.ctypes.data, C.byref(h)))
         self._h = h
 
     @classmethod

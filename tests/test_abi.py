@@ -156,3 +156,27 @@ def test_qmat_host_validation():
     assert L.rmoe_qmat_forward(None, None, 4, None, None) == _lib.RMOE_ERR_INVALID
     assert L.rmoe_qmat_status(None) == _lib.RMOE_ERR_INVALID
     L.rmoe_qmat_destroy(None)  # a null handle is ignored
+
+
+def test_ep_placement_host_validation(tiny):
+    """rmoe_ep_layer_create_placed checks the placement table before touching a device: every
+    entry a rank of the world, every rank holding at least one expert."""
+    d, keep = _desc(tiny)
+    uid = (C.c_uint8 * 128)()
+    L = _lib.load()
+
+    def create(pl, rank=0, world=2):
+        h = C.c_void_p()
+        arr = np.ascontiguousarray(pl, dtype=np.int32)
+        st = L.rmoe_ep_layer_create_placed(C.byref(d), rank, world, uid, arr.ctypes.data, C.byref(h))
+        return st, L.rmoe_last_error().decode()
+
+    st, msg = create([0, 1, 2, 0])
+    assert st == _lib.RMOE_ERR_INVALID and "expert_rank[2] = 2" in msg, msg
+    st, msg = create([0, 0, 0, 0])
+    assert st == _lib.RMOE_ERR_INVALID and "rank 1 holds no expert" in msg, msg
+    st, msg = create([-1, 0, 1, 1])
+    assert st == _lib.RMOE_ERR_INVALID and "expert_rank[0] = -1" in msg, msg
+    h = C.c_void_p()
+    st = L.rmoe_ep_layer_create(C.byref(d), 0, 3, uid, C.byref(h))
+    assert st == _lib.RMOE_ERR_INVALID and "split evenly" in L.rmoe_last_error().decode()

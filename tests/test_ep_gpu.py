@@ -20,7 +20,7 @@ def _check(got, want, what):
     assert mx <= O.max_abs_bound(rms), f"{what}: max-abs {mx:.3e} (rms {rms:.3e})"
 
 
-def _rank(rank, world, uid, tokens, shared=False):
+def _rank(rank, world, uid, tokens, shared=False, placement=None):
     import torch
 
     from oracle import oracle as O
@@ -30,7 +30,7 @@ def _rank(rank, world, uid, tokens, shared=False):
     torch.cuda.set_device(rank)
     lw = synth.config_c1() if not shared else synth.make_layer(
         1024, 512, 16, 4, gate_t=12, up_t=12, down_t=14, dlo=0.001, dhi=0.004, seed=3, shared=True)
-    layer = MoELayer.expert_parallel(lw, rank, world, uid, device=rank)
+    layer = MoELayer.expert_parallel(lw, rank, world, uid, device=rank, placement=placement)
     for T in tokens:
         x = synth.activations(T, lw.H, seed=10 * rank + T)
         out = layer.forward(torch.from_numpy(x).cuda())
@@ -42,11 +42,11 @@ def _rank(rank, world, uid, tokens, shared=False):
     layer.close()
 
 
-def _run(world, tokens, timeout_s=300, shared=False):
+def _run(world, tokens, timeout_s=300, shared=False, placement=None):
     from rusty_engine_b200.moe import ep_unique_id
 
     uid = ep_unique_id()
-    ctx = mp.start_processes(_rank, args=(world, uid, tokens, shared), nprocs=world, start_method="spawn",
+    ctx = mp.start_processes(_rank, args=(world, uid, tokens, shared, placement), nprocs=world, start_method="spawn",
                              join=False)
     deadline = time.time() + timeout_s
     while not ctx.join(timeout=5):
@@ -74,6 +74,19 @@ def test_ep_two_gpus_shared_expert(gpu):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     _run(2, (5, 300), shared=True)
+
+
+def test_ep_two_gpus_placed(gpu):
+    """A caller-given placement (rmoe_ep_layer_create_placed): rank 0 holds 3 of the 16
+    experts, rank 1 the other 13, on the small-batch and the tensor-core local paths."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    placement = [1] * 16
+    for e in (2, 7, 11):
+        placement[e] = 0
+    _run(2, (6, 512), placement=placement)
 
 
 def _create_alone(q):

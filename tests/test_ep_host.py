@@ -33,7 +33,7 @@ def _experts_f32(lw):
     return out
 
 
-def _rank(rank, world, port, tokens, seed, bias_to, shared=False):
+def _rank(rank, world, port, tokens, seed, bias_to, shared=False, placement=None):
     import torch.distributed as dist
 
     from oracle import oracle as O
@@ -51,7 +51,7 @@ def _rank(rank, world, port, tokens, seed, bias_to, shared=False):
         if shared:
             sh = tuple(O.dequant(q.ggml_type, q.data).reshape(r, c)
                        for q, r, c in zip(lw.shared, (lw.I, lw.I, lw.H), (lw.H, lw.H, lw.I)))
-        got = ep_sim.ep_forward(x, lw, ex, rank, world, sh)
+        got = ep_sim.ep_forward(x, lw, ex, rank, world, sh, placement)
         if tokens[rank]:
             want = O.moe_layer_q_exact(x, lw)[0]
             rel = np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want)
@@ -71,3 +71,29 @@ def test_ep_exchange_with_shared_expert(tokens):
     which adds the shared expert's output to that row's partial sum (src/moe.rs:381-386)."""
     mp.start_processes(_rank, args=(2, _free_port(), tokens, 9, None, True), nprocs=2, start_method="spawn",
                        join=True)
+
+
+@pytest.mark.parametrize("placement", [[1, 1, 1, 1, 1, 1, 1, 0], [0, 0, 1, 0, 1, 1, 0, 1]])
+def test_ep_exchange_with_placement(placement):
+    """A caller-given expert placement (rmoe_ep_layer_create_placed): uneven expert counts per
+    rank, local ids in ascending global order, the empty id = the destination's expert count."""
+    mp.start_processes(_rank, args=(2, _free_port(), (5, 4), 11, None, False, placement), nprocs=2,
+                       start_method="spawn", join=True)
+
+
+def test_balanced_placement_spreads_load():
+    """ep_balanced_placement: largest-first fill to the least-loaded rank; every rank holds an
+    expert even when most loads are zero; the busiest rank stays near the mean on a Zipf load."""
+    from rusty_engine_b200.moe import EngineError, ep_balanced_placement
+
+    p = ep_balanced_placement([0, 0, 0, 0, 0, 9, 0, 0], 4)
+    assert sorted(set(p.tolist())) == [0, 1, 2, 3] and p[5] == 0
+    load = 1.0 / np.arange(1, 129) ** 1.1
+    for G in (2, 4, 8):
+        p = ep_balanced_placement(load, G)
+        per = np.bincount(p, weights=load, minlength=G)
+        rr = np.array([load[r::G].sum() for r in range(G)])
+        assert per.max() <= rr.max() + 1e-12
+        assert per.max() <= max(per.mean() * 1.02, load.max())
+    with pytest.raises(EngineError):
+        ep_balanced_placement([1.0, 2.0], 4)
