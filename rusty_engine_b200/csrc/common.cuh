@@ -30,6 +30,10 @@ enum GgmlType : int {
     T_DENSE = 100  // device-only: an fp16 plane holding F32/F16/BF16 experts
 };
 
+// Storage position of K index i in the K-permuted operand order of the tensor-core Q6_K down
+// product (positions 1 and 2 of every group of four swapped; its own inverse).
+__host__ __device__ __forceinline__ int kperm_pos(int i) { return (i & ~3) | ((i & 1) << 1) | ((i >> 1) & 1); }
+
 // Status word bits written by kernels when a device-side check fails (never trap).
 enum DevErr : uint32_t { DERR_NONE = 0, DERR_BAD_EXPERT = 1, DERR_ROWS_OVERFLOW = 2, DERR_TILES_OVERFLOW = 4,
                          DERR_TIMEOUT = 8, DERR_FP16_RANGE = 16 };

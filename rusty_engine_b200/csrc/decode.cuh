@@ -142,6 +142,53 @@ struct Slice<T_Q6_K, ROWS> {
     }
 };
 
+// Q6_K for the tensor-core down product, in the K-permuted operand order: inside every group of
+// four K positions the stored order is (k, k+2, k+1, k+3) (kperm_pos), so a packed pair is bytes
+// 0 and 2 (or 1 and 3) of one quant word and needs no byte permute (about 2.8 instructions per
+// weight against 4 for slice32).  The other operand (h, or QMat's x) is stored in the same order,
+// so the products are unchanged, and the decoded fp16 values are slice32's: q6 - 32 is formed
+// exactly, either as (1024 + q6) - 1056 or as (1024 + 16 q6) / 16 - 96, then rounded once by the
+// scale product.
+template <int ROWS>
+__device__ __forceinline__ void slice32_q6k_kperm(const uint8_t* p, const uint8_t* dq, int sub, int half,
+                                                  uint32_t* v) {
+    const float q6d = h2f(*reinterpret_cast<const uint16_t*>(dq));
+    const int h = sub >> 1, odd = sub & 1, qd = 2 * odd + half;
+    const uint4* ql = reinterpret_cast<const uint4*>(p + h * 64 + half * 32);
+    const uint4* qh = reinterpret_cast<const uint4*>(p + 128 + h * 32);
+    const uint4 l0 = ql[0], l1 = ql[1], h0 = qh[0], h1 = qh[1];
+    const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+    const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    const int8_t* sc = reinterpret_cast<const int8_t*>(p + 192 + h * 8);
+    const __half2 s0 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qd * 2]));
+    const __half2 s1 = __float2half2_rn(__fmul_rn(q6d, (float)sc[qd * 2 + 1]));
+    const __half2 K1056 = __float2half2_rn(1056.0f), S16 = __float2half2_rn(0.0625f),
+                  M96 = __float2half2_rn(-96.0f);
+    const uint32_t C = 0x64006400u;
+    // the quadrant's two high bits (at 2 qd of each qh byte) go to mantissa bit 4 (pair 0, 2 of a
+    // low-nibble quadrant) or 8 (every other pair): a left shift by 4 - 2 half for pair (0, 2),
+    // a right shift by 2 qd for pair (1, 3)
+    const int hl = 4 - 2 * half, hr = 2 * qd;
+    const int lsh = odd ? 8 : 4;  // pair (1, 3): the byte's nibble to mantissa bits 4..7
+#pragma unroll
+    for (int i = 0; i < 8; i++) {  // l = 4i .. 4i+3
+        const __half2 s = (i < 4) ? s0 : s1;
+        const uint32_t L = lw[i], Hh = hw[i];
+        __half2 y02;
+        if (!odd) {
+            const uint32_t c = lop_or3(L & 0x000F000Fu, (Hh << hl) & 0x00300030u, C);
+            y02 = __hsub2(as_h2(c), K1056);
+        } else {
+            const uint32_t c = lop_or3(L & 0x00F000F0u, (Hh << hl) & 0x03000300u, C);
+            y02 = __hfma2(as_h2(c), S16, M96);
+        }
+        const uint32_t c13 = lop_or3((L >> lsh) & 0x00F000F0u, (Hh >> hr) & 0x03000300u, C);
+        const __half2 y13 = __hfma2(as_h2(c13), S16, M96);
+        v[2 * i] = as_u32(__hmul2(y02, s));
+        v[2 * i + 1] = as_u32(__hmul2(y13, s));
+    }
+}
+
 // Q4_0 main plane row: qs[8 x 16]; half = block 2*sub + half (low nibbles -> elements 0..15,
 // high nibbles -> 16..31).
 template <int ROWS>

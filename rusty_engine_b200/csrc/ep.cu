@@ -251,7 +251,7 @@ static rmoe_status ep_token_buffers(rmoe_layer* L, uint32_t T) {
     P.xin = (float*)A((size_t)cap * L->H * 4);
     P.xout = (float*)A((size_t)cap * L->H * 4);
     P.logits = (float*)A((size_t)cap * L->E_router * 4);
-    P.logits_part = (float*)A((size_t)8 * cap * L->E_router * 4);
+    P.logits_part = (float*)A((size_t)LOGIT_SPLITS * cap * L->E_router * 4);
     P.topk_id = (int*)A((size_t)cap * L->k * 4);
     P.topk_w = (float*)A((size_t)cap * L->k * 4);
     P.pos = (int*)A((size_t)cap * G * 4);

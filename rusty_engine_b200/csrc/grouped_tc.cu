@@ -357,8 +357,10 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
             }
             asm volatile("bar.sync 1, %0;\n" ::"n"(G::CONV) : "memory");
             if (work) {
-                // per (row, 64-feature block): exponent, fp16 values, block/row exponents
+                // per (row, 64-feature block): exponent, fp16 values, block/row exponents; h is
+                // written in the down kernel's operand order (K-permuted for a Q6_K down stack)
                 const int nblk = p.I / HBLK;
+                const bool kperm = p.down.type == T_Q6_K;
                 const int ct = tid - 128;
                 for (int pi = ct; pi < nrows * 2; pi += G::CONV) {
                     const int blk = pi >= nrows ? 1 : 0, n = pi - blk * nrows;  // consecutive lanes: rows
@@ -379,13 +381,24 @@ __global__ void __launch_bounds__(TcGeom<TYPE, NMAT>::THREADS, TcGeom<TYPE, NMAT
                     const float sc = exp2i(-ex);
                     const size_t rr = (size_t)(row0 + n);
                     uint4* dst = reinterpret_cast<uint4*>(p.h + rr * p.I + fb * TC_M + blk * 64);
+                    if (kperm) {  // features in tc_down's Q6_K operand order (kperm_pos)
 #pragma unroll
-                    for (int j2 = 0; j2 < 8; j2++) {
-                        const float4 a = s4[2 * j2], b = s4[2 * j2 + 1];
-                        dst[j2] = make_uint4(pack_f16x2(__fmul_rn(a.x, sc), __fmul_rn(a.y, sc)),
-                                             pack_f16x2(__fmul_rn(a.z, sc), __fmul_rn(a.w, sc)),
-                                             pack_f16x2(__fmul_rn(b.x, sc), __fmul_rn(b.y, sc)),
-                                             pack_f16x2(__fmul_rn(b.z, sc), __fmul_rn(b.w, sc)));
+                        for (int j2 = 0; j2 < 8; j2++) {
+                            const float4 a = s4[2 * j2], b = s4[2 * j2 + 1];
+                            dst[j2] = make_uint4(pack_f16x2(__fmul_rn(a.x, sc), __fmul_rn(a.z, sc)),
+                                                 pack_f16x2(__fmul_rn(a.y, sc), __fmul_rn(a.w, sc)),
+                                                 pack_f16x2(__fmul_rn(b.x, sc), __fmul_rn(b.z, sc)),
+                                                 pack_f16x2(__fmul_rn(b.y, sc), __fmul_rn(b.w, sc)));
+                        }
+                    } else {
+#pragma unroll
+                        for (int j2 = 0; j2 < 8; j2++) {
+                            const float4 a = s4[2 * j2], b = s4[2 * j2 + 1];
+                            dst[j2] = make_uint4(pack_f16x2(__fmul_rn(a.x, sc), __fmul_rn(a.y, sc)),
+                                                 pack_f16x2(__fmul_rn(a.z, sc), __fmul_rn(a.w, sc)),
+                                                 pack_f16x2(__fmul_rn(b.x, sc), __fmul_rn(b.y, sc)),
+                                                 pack_f16x2(__fmul_rn(b.z, sc), __fmul_rn(b.w, sc)));
+                        }
                     }
                     p.hexp[rr * nblk + fb * 2 + blk] = (int8_t)ex;
                     atomicMax(p.rowexp + rr, ex);
@@ -650,8 +663,13 @@ __global__ void __launch_bounds__(512, 1)
                 if (gk >= NA && !mbar_wait(smem_u32(&bar_a_empty[s]), ((gk / NA) + 1) & 1)) { fail(); ok = false; break; }
                 const uint8_t* mat = raw_g + (size_t)rs * RS::BYTES;
                 uint32_t v[32];
-                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 0, v);
-                slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 1, v + 16);
+                if constexpr (TYPE == T_Q6_K) {  // K-permuted pairs: the h / x operand is stored to match
+                    slice32_q6k_kperm<TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, sub, 0, v);
+                    slice32_q6k_kperm<TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, sub, 1, v + 16);
+                } else {
+                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 0, v);
+                    slice32<TYPE, TC_M>(mat + r * PITCH, mat + RS::DOFF + r * 2, mat + RS::AOFF + r * 4, sub, 1, v + 16);
+                }
                 if (sub == SUBS - 2 + g) {  // this group's last read of the raw slot
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(&bar_raw_empty[rs]));

@@ -32,7 +32,7 @@ static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 b
 }
 
 static constexpr int MAX_E = 512;  // experts per layer this build supports
-static constexpr int LOGIT_SPLITS = 8;  // K-splits of the large-batch fast router (logits_part planes)
+static constexpr int LOGIT_SPLITS = 4;  // K-splits of the large-batch fast router (logits_part planes)
 static constexpr int MAX_K = 32;   // top-k this build supports
 static constexpr int RG_MAX_G = 64; // expert groups the group router supports
 

@@ -453,7 +453,7 @@ rmoe_status ensure_workspace(rmoe_layer* L, uint32_t T, bool need_y) {
     w.hexp = (int8_t*)A(rows * (I / GV_EBLK));
     w.rowexp = (int*)A(rows * 4);
     w.logits = (float*)A((size_t)cap * E * 4);
-    w.logits_part = (float*)A((size_t)8 * cap * E * 4);
+    w.logits_part = (float*)A((size_t)LOGIT_SPLITS * cap * E * 4);
     if (need_y || L->ws_had_y) w.y = (float*)A(rows * H * 4);
     if (!ok) return fail(RMOE_ERR_OOM, "workspace cudaMalloc failed for %u tokens", cap);
     if (!make_rows_map(w.h, rows, I, L->hmap) || !make_rows_map(w.xs, rows, H, L->xsmap))

@@ -32,10 +32,11 @@ __global__ void qmat_prep_kernel(int rows, int NT, int4* tiles, int* ntiles, int
 // fp16 x 2^e: scaled by the exact power of two 2^-e that brings its maximum into [2^13, 2^14),
 // e written as the row exponent and as every block exponent, which the product kernels fold
 // back into the output (y * 2^e).  Rows inside the fp16 range keep e = 0 (no scaling).
-// Non-finite x cannot be carried and sets DERR_FP16_RANGE in the status word.
+// Non-finite x cannot be carried and sets DERR_FP16_RANGE in the status word.  kperm: the row
+// is stored in the tensor-core down kernel's K-permuted order for a Q6_K matrix (kperm_pos).
 __global__ void __launch_bounds__(256) qmat_x_kernel(const float* __restrict__ x, int rows, int n,
                                                      __half* __restrict__ xb, int8_t* __restrict__ hexp,
-                                                     int* __restrict__ rexp, unsigned* status) {
+                                                     int* __restrict__ rexp, unsigned* status, int kperm) {
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= rows) return;
     const float* xr = x + (size_t)r * n;
@@ -54,7 +55,8 @@ __global__ void __launch_bounds__(256) qmat_x_kernel(const float* __restrict__ x
     }
     const int e = mx >= 32768.0f ? (int)((__float_as_uint(mx) >> 23) & 0xffu) - 127 - 13 : 0;
     const float sc = exp2i(-e);  // exact
-    for (int i = lane; i < n; i += 32) xb[(size_t)r * n + i] = __float2half_rn(__fmul_rn(__ldg(xr + i), sc));
+    for (int i = lane; i < n; i += 32)
+        xb[(size_t)r * n + (kperm ? kperm_pos(i) : i)] = __float2half_rn(__fmul_rn(__ldg(xr + i), sc));
     for (int b = lane; b < n / HBLK; b += 32) hexp[(size_t)r * (n / HBLK) + b] = (int8_t)e;
     if (lane == 0) rexp[r] = e;
 }
@@ -149,7 +151,8 @@ RMOE_API rmoe_status rmoe_qmat_forward(rmoe_qmat* q, const float* x, uint32_t ro
                                                                               q->rowtok, q->rowslot);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) {
-        qmat_x_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, (int)rows, (int)q->n, q->xb, q->hexp, q->rexp, q->status);
+        qmat_x_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, (int)rows, (int)q->n, q->xb, q->hexp, q->rexp, q->status,
+                                                     tc && q->W.type == T_Q6_K ? 1 : 0);
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return cuda_fail(e, "qmat prepare");
