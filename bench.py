@@ -166,6 +166,13 @@ def workload(cfg_name):
     return lw, x, label
 
 
+def host_expert_rows(lw, x):
+    """Rows per expert of a batch (its top-k picks, routed on the host in float64)."""
+    logits = x.astype(np.float64) @ np.asarray(lw.router_w, dtype=np.float64).reshape(lw.E, lw.H).T
+    ids = np.argpartition(-logits, lw.k - 1, axis=1)[:, :lw.k]
+    return np.bincount(ids.ravel(), minlength=lw.E)
+
+
 def ep_placement(lw, world, T_cal=2048):
     """Expert placement for the expert-parallel step: the per-expert pick counts of a separate
     calibration batch of the config's distribution (another seed; routed on the host in
@@ -175,9 +182,7 @@ def ep_placement(lw, world, T_cal=2048):
     from rusty_engine_b200.moe import ep_balanced_placement
 
     x = synth.activations(T_cal, lw.H, seed=7) + np.float32(1.0)  # zipf_workload's activations
-    logits = x.astype(np.float64) @ np.asarray(lw.router_w, dtype=np.float64).reshape(lw.E, lw.H).T
-    ids = np.argpartition(-logits, lw.k - 1, axis=1)[:, :lw.k]
-    return ep_balanced_placement(np.bincount(ids.ravel(), minlength=lw.E), world)
+    return ep_balanced_placement(host_expert_rows(lw, x), world)
 
 
 def cpu_baseline(cfg_name, lw, x, budget_s=15.0):
@@ -560,6 +565,11 @@ def main():
         }
         if stage is not None:
             line["stage_ms"] = {n: float(v) for n, v in zip(STAGES, stage)}
+        if world > 1:
+            # per-GPU load of the timed batch: expert rows each rank computes (host routing)
+            rows = np.bincount(placement, weights=host_expert_rows(lw, x_all), minlength=world)
+            line["ep_expert_rows_per_rank"] = [int(r) for r in rows]
+            line["ep_busiest_over_mean"] = float(rows.max() / rows.mean())
         if subs:
             line["sub"] = subs
         if world == 1 and not args.no_cpu_baseline:
