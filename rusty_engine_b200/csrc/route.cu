@@ -32,7 +32,7 @@
 
 namespace rmoe {
 
-static constexpr int TK_TOK = 8;  // tokens per top-k CTA (8: C2 route 0.111 ms; 16: 0.118; 32: 0.143)
+static constexpr int TK_TOK = 8;  // tokens per top-k CTA (C2 route: 4: 0.117 ms; 8: 0.111; 16: 0.118; 32: 0.143)
 static constexpr int TK_THREADS = 256;
 
 // ---------------------------------------------------------------------------------------
