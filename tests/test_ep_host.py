@@ -97,3 +97,22 @@ def test_balanced_placement_spreads_load():
         assert per.max() <= max(per.mean() * 1.02, load.max())
     with pytest.raises(EngineError):
         ep_balanced_placement([1.0, 2.0], 4)
+
+
+def test_bench_expert_placement_on_a_zipf_layer():
+    """The expert-parallel bench's placement (bench.ep_placement: pick counts of a calibration
+    batch of another seed, routed on the host, spread largest-first) gives every rank an expert
+    and keeps the busiest rank of the timed batch no busier than the round-robin deal does."""
+    import bench
+
+    lw0 = synth.make_layer(256, 256, 16, 4, gate_t=GGML_Q4_K, up_t=GGML_Q4_K, down_t=GGML_Q6_K, dlo=0.001,
+                           dhi=0.01, seed=3, name="zipf-small")
+    lw, x = synth.zipf_workload(lw0, 1024, seed=1)
+    rows_e = bench.host_expert_rows(lw, x)
+    assert rows_e.sum() == 1024 * lw.k
+    for G in (2, 4):
+        pl = bench.ep_placement(lw, G, T_cal=1024)
+        assert pl.shape == (lw.E,) and sorted(set(pl.tolist())) == list(range(G))
+        busiest = np.bincount(pl, weights=rows_e, minlength=G).max()
+        rr = np.bincount(np.arange(lw.E) % G, weights=rows_e, minlength=G).max()
+        assert busiest <= rr, (G, busiest, rr)
