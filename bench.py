@@ -70,12 +70,13 @@ def kernels_per_forward(lw, T, world=1, rows_local=None):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernels,
-# from one ncu --set full capture each of the same bench command on a B200
+# from one ncu --set full capture each of the same bench command on a B200 (the summaries under
+# profiles/: tc_kernels_c2_prefill.md, gvt_kernels_c3_decode_b64.md, decode_b1_kernels.md)
 NCU_TRAFFIC = {
     ("c2", "gateup"): 386.080e6 + 42.816e6,
-    ("c2", "down"): 265.979e6 + 27.879e6,
-    ("c3b64", "gateup"): 246.148e6 + 4.643e6,
-    ("c3b64", "down"): 162.667e6 + 6.531e6,
+    ("c2", "down"): 268.007e6 + 30.732e6,
+    ("c3b64", "gateup"): 246.296e6 + 4.087e6,
+    ("c3b64", "down"): 164.055e6 + 3.826e6,
     ("c3b1", "gateup"): 15.762e6,
     ("c3b1", "down"): 10.372e6,
 }
