@@ -70,8 +70,7 @@ def kernels_per_forward(lw, T, world=1, rows_local=None):
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the dominant kernels,
-# from one ncu --set full capture each of the same bench command on a B200 (the summaries under
-# profiles/: tc_kernels_c2_prefill.md, gvt_kernels_c3_decode_b64.md, decode_b1_kernels.md)
+# from one ncu --set full capture each of the same bench command on a B200
 NCU_TRAFFIC = {
     ("c2", "gateup"): 386.080e6 + 42.816e6,
     ("c2", "down"): 268.007e6 + 30.732e6,
