@@ -12,6 +12,8 @@ through the public host-buffer entry point (pinned host x in, host out, copies i
 N = 1 (no torchrun): the headline is config 2 (4096-token prefill); the same line carries
 ``sub`` results for config 3 (decode batches 1, 8, 32, 64) and config 5 (the 235B-shaped layer,
 8192 tokens, Zipf(1.1) expert load), each with its roofline fraction.
+Launched by torchrun (the scaling run) at N = 1: config 5 on one GPU (the plain layer), the
+base of the scaling curve.
 N > 1 (torchrun, one rank per GPU): config 5 as an expert-parallel layer, strong scaling: the
 8192 tokens are split evenly over the ranks (8192 / N each), experts placed by the pick counts
 of a separate calibration batch (largest load first to the least-loaded rank), tokens exchanged
@@ -220,6 +222,13 @@ def algorithmic(lw, T, ids=None):
     return flops_gateup, flops_down, bytes_total, gu_bytes, touched
 
 
+def arm_config(args, world):
+    """The workload of this run: config 5 (the expert-parallel layer of the scaling curve) at
+    every N launched by torchrun, including N = 1, where it is the plain one-GPU layer, the base
+    of that curve; the --config choice (config 2, the headline, by default) otherwise."""
+    return "c5" if world > 1 or "TORCHELASTIC_RUN_ID" in os.environ else args.config
+
+
 def reference_arm(args, rank, world):
     """rusty-engine's pooled CPU path (C restatement, all host threads) on our arm's config:
     rank 0 only; the whole batch per step (config 5: a 1024-token sample)."""
@@ -227,7 +236,7 @@ def reference_arm(args, rank, world):
         return
     from oracle import oracle as O
 
-    cfg = args.config if world == 1 else "c5"
+    cfg = arm_config(args, world)
     if cfg == "c4":
         # per-layer work of the stack: one MoE layer of its shape over the 2048-token prompt
         from rusty_engine_b200 import synth
@@ -488,7 +497,7 @@ def main():
     from rusty_engine_b200 import _lib
     from rusty_engine_b200.moe import MoELayer
 
-    cfg = args.config if world == 1 else "c5"
+    cfg = arm_config(args, world)
     lw, x_all, label = workload(cfg)
     if world > 1:
         # strong scaling: this rank's share of the config's whole batch
@@ -548,7 +557,7 @@ def main():
         line = {
             "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "scaling": "strong" if cfg == "c5" else "weak", "vs_baseline": None,
             "dtype": "fp16-mma/f32-acc/f32-router", "data": "synthetic",
             "config": {"workload": label, "tokens_total": T_all, "tokens_per_gpu": T,
                        "experts_touched": int(touched),
